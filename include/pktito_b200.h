@@ -1,0 +1,123 @@
+/* libpktito_b200: libpktito's int8 path (activation quantization, the
+ * int8 x int8 -> int32 block sums, the float32 scale epilogue) on B200
+ * (sm_100a), behind a C ABI.
+ *
+ * Two layers of entry points:
+ *
+ *  - pkb_*_host: the reference's backend contract, host pointers in and out,
+ *    synchronous. These are what the cuda-b200 entry of the reference's
+ *    backend table calls (libpktito_b200/csrc/cuda_b200.c exports
+ *    `pk_kernels_cuda_b200`, the table of backend/kernels.h:242-278).
+ *
+ *  - pkb_*_dev: the same arithmetic on device-resident buffers, enqueued on a
+ *    caller's CUDA stream and returning at once; for callers that keep a
+ *    batch of segments on the GPU.
+ *
+ * Every function returns PKB_OK (0) or a nonzero pkb_status; the message of
+ * the calling thread's last failure is pkb_last_error(). Nothing falls back
+ * to the CPU: without a usable sm_100 device every compute entry fails with
+ * PKB_ENODEV.
+ *
+ * Results are the reference `ref` backend's bits (backend/ref/kernels.c), in
+ * whichever of the four IEEE rounding modes the caller names: rmode is one
+ * of PKB_RN, PKB_RD, PKB_RU, PKB_RZ, and the table entry passes the mode its
+ * caller's fegetround() reports, as the reference's own arithmetic follows it.
+ */
+#ifndef PKTITO_B200_H
+#define PKTITO_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    PKB_OK = 0,
+    PKB_EINVAL = 1,   /* a shape, stride, alignment or pointer the contract rules out */
+    PKB_ECUDA = 2,    /* a CUDA runtime or driver call failed */
+    PKB_ENOMEM = 3,   /* device or pinned host memory could not be had */
+    PKB_ETIMEOUT = 4, /* a kernel's bounded wait ran out; its results are not to be used */
+    PKB_ENODEV = 5    /* no sm_100 device */
+} pkb_status;
+
+enum { PKB_RN = 0, PKB_RD = 1, PKB_RU = 2, PKB_RZ = 3 };
+
+/* The widest input a product may have, in blocks of 32: the reference's
+ * PK_MAX_BLOCKS (backend/kernels.h:83) times 32. */
+#define PKB_MAX_N 16384u
+
+/* ------------------------------------------------------------ library -- */
+
+/* The calling thread's last failure, "" if none. */
+const char *pkb_last_error(void);
+
+/* sm_100 devices this process can use (0 without a GPU or a driver). */
+int pkb_device_count(void);
+
+/* The device this thread's host-pointer calls run on (default 0). A pool
+ * spread over several GPUs binds each of its threads to one. */
+int pkb_set_thread_device(int device);
+
+/* Reads and clears the device-side error word of `device`: nonzero after a
+ * kernel's bounded wait ran out (bit 0) or it met an argument it refused
+ * (bit 1). pkb_*_host check it on every call; pkb_*_dev callers check it
+ * after synchronising. */
+int pkb_device_errors(int device, uint32_t *word);
+
+/* ---------------------------------------------- host-pointer contract -- */
+
+/* pk_k_quantize (backend/kernels.h:47-58; ref backend/ref/kernels.c:24-58):
+ * T columns of n floats, column t at x + t*xs, quantized in blocks of qb
+ * (qb a multiple of 32 dividing n, n <= PKB_MAX_N) into q [T][n] and
+ * d [T][n/qb]. T == 0 touches nothing. */
+int pkb_quantize_host(int8_t *q, float *d, uint32_t n, uint32_t qb, uint32_t T, const float *x,
+                      size_t xs, int rmode);
+
+/* pk_k_gemm_q8 (backend/kernels.h:60-78; ref backend/ref/kernels.c:60-86):
+ * out[t*os + r] for r < rows, t < T, from the PK_Q8 matrix w (core/pkf.h:28-41;
+ * rows a multiple of 16, w at its first row), scales ws, optional bias, and
+ * the activations q/d of n inputs in blocks of qb. The floats of out between
+ * rows and os are left as they were. The matrix is uploaded once and kept on
+ * the device, keyed by its host address and checked against a host copy of
+ * its bytes on every call; pkb_forget drops it. */
+int pkb_gemm_q8_host(float *out, size_t os, const int8_t *w, const float *ws, const float *bias,
+                     uint32_t rows, const int8_t *q, const float *d, uint32_t n, uint32_t qb,
+                     uint32_t T, int add, int rmode);
+
+/* Drops every cached matrix whose host bytes overlap [p, p + bytes), on
+ * every device; for a caller about to unmap or rewrite weights. Not to be
+ * called while another thread runs a product on those weights. */
+int pkb_forget(const void *p, size_t bytes);
+
+/* ------------------------------------------------ device-resident path -- */
+
+/* Bytes of the device layout pkb_repack_q8_dev writes for a rows x n matrix:
+ * rows of n int8, row r at r*n (rows a multiple of 16, n of 32). */
+size_t pkb_wpack_bytes(uint32_t rows, uint32_t n);
+
+/* PK_Q8 panels (device copy of the reference's bytes, core/pkf.h:28-41) to
+ * the row-major layout the product's TMA tiles read; once per matrix. */
+int pkb_repack_q8_dev(void *stream, int8_t *wpack, const int8_t *w_pk, uint32_t rows, uint32_t n);
+
+/* pkb_quantize_host's arithmetic on device buffers, enqueued on stream. */
+int pkb_quantize_dev(void *stream, int8_t *q, float *d, const float *x, size_t xs, uint32_t T,
+                     uint32_t n, uint32_t qb, int rmode);
+
+/* pkb_gemm_q8_host's arithmetic on device buffers, enqueued on stream, with
+ * the weights repacked by pkb_repack_q8_dev (wpack at its first row). q and
+ * wpack must be 16-byte aligned; out may have any stride os >= rows. */
+int pkb_gemm_q8_dev(void *stream, float *out, size_t os, const int8_t *wpack, const float *ws,
+                    const float *bias, uint32_t rows, const int8_t *q, const float *d, uint32_t n,
+                    uint32_t qb, uint32_t T, int add, int rmode);
+
+/* Launches of libpktito_b200 kernels since the process started, on every
+ * device: the evidence a benchmark reports for its own kernels' work. */
+uint64_t pkb_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PKTITO_B200_H */

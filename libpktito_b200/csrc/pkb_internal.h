@@ -1,0 +1,37 @@
+// Declarations shared by the CUDA sources of libpktito_b200 (not installed).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace pkb {
+
+// Arguments of the product kernel (pkb_gemm.cu) besides its two tensor maps.
+struct GemmArgs {
+    float* out;            // out[t*os + r]
+    const float* ws;       // [rows] row scales
+    const float* bias;     // [rows] or null
+    const float* d;        // [T][n/qb] block scales
+    uint32_t* err;         // device-side error word
+    unsigned long long os;
+    uint32_t rows, n, qb, T, add;
+    uint32_t tiles_m, tiles_n;
+    long long timeout;     // SM clock cycles a wait may last
+};
+
+int gemm_tile_rows();   // frames a tile (TMA box of the activations)
+int gemm_tile_cols();   // output rows a tile (TMA box of the weights)
+int gemm_box_k();       // inputs of K a TMA box
+
+cudaError_t launch_gemm_q8(const CUtensorMap& map_a, const CUtensorMap& map_b, const GemmArgs& g, int num_sms,
+                           int rmode, cudaStream_t stream);
+
+cudaError_t launch_quantize(int8_t* q, float* d, const float* x, size_t xs, uint32_t T, uint32_t n, uint32_t qb,
+                            int rmode, int num_sms, cudaStream_t stream);
+
+cudaError_t launch_repack_q8(int8_t* wpack, const int8_t* w_pk, uint32_t rows, uint32_t n, int num_sms,
+                             cudaStream_t stream);
+
+}  // namespace pkb

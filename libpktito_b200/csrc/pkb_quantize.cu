@@ -1,0 +1,180 @@
+// Activation quantization and the weights' one-time repack, sm_100a.
+//
+// quantize: the reference's k_quantize (backend/ref/kernels.c:24-58,
+// contract backend/kernels.h:47-58). For each column t and block b of qb
+// inputs:
+//
+//   a block holding a NaN or an infinity, or whose amax = max |x| is below
+//   2^-121:                                    q = 0, d = 0
+//   otherwise:  d = amax / 127,  id = 127 / amax,  q = (int8)rint(x * id)
+//
+// each operation rounded once in the mode RM (rint rounds to an integer in
+// that mode). The maximum is exact in any order, so the reduction's shape
+// is free. HBM-bound: 4 bytes read and 1 + 4/qb written an input.
+//
+// Layout of the work: a block of 32 is 8 threads of 4 inputs (one 16-byte
+// load each), a block of 64 is 16 threads, so a warp takes 4 or 2 blocks at
+// once and reduces each within its thread group by shuffles; wider blocks
+// (qb = n, up to 16384) take a warp each, in two passes over the block.
+// Warps stride over the blocks, grid sized to the SMs.
+//
+// repack: PK_Q8 panels (core/pkf.h:28-41: 16 rows by 4 inputs in 64-byte
+// groups) to plain rows of n bytes, which the product's TMA tiles read.
+
+#include "pkb_device.cuh"
+#include "pkb_internal.h"
+
+namespace pkb {
+
+namespace {
+
+__device__ __forceinline__ float4 load4(const float* p, bool vec) {
+    if (vec) return __ldg(reinterpret_cast<const float4*>(p));
+    return make_float4(__ldg(p), __ldg(p + 1), __ldg(p + 2), __ldg(p + 3));
+}
+
+__device__ __forceinline__ bool finite4(float4 v) {
+    return isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w);
+}
+
+__device__ __forceinline__ float amax4(float4 v) {
+    return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+}
+
+// Four quantized bytes, packed little-endian in the inputs' order.
+template <int RM>
+__device__ __forceinline__ uint32_t quant4(float4 v, float id) {
+    const uint32_t b0 = static_cast<uint8_t>(static_cast<int8_t>(f2i_r<RM>(mul_r<RM>(v.x, id))));
+    const uint32_t b1 = static_cast<uint8_t>(static_cast<int8_t>(f2i_r<RM>(mul_r<RM>(v.y, id))));
+    const uint32_t b2 = static_cast<uint8_t>(static_cast<int8_t>(f2i_r<RM>(mul_r<RM>(v.z, id))));
+    const uint32_t b3 = static_cast<uint8_t>(static_cast<int8_t>(f2i_r<RM>(mul_r<RM>(v.w, id))));
+    return b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+}
+
+// Blocks of G*4 inputs (G = 8 or 16 threads a block).
+template <int RM, int G>
+__global__ void __launch_bounds__(256) quantize_narrow(int8_t* __restrict__ q, float* __restrict__ d,
+                                                       const float* __restrict__ x, size_t xs, uint32_t T,
+                                                       uint32_t n, bool vec) {
+    constexpr uint32_t QB = 4 * G;
+    constexpr uint32_t PER_WARP = 32 / G;
+    const uint32_t nb = n / QB;
+    const size_t total = static_cast<size_t>(T) * nb;
+    const uint32_t lane = threadIdx.x & 31, lg = lane % G;
+    const size_t warp0 = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32;
+    const size_t nwarps = static_cast<size_t>(gridDim.x) * blockDim.x / 32;
+    for (size_t wb = warp0 * PER_WARP; wb < total; wb += nwarps * PER_WARP) {  // warp-uniform
+        const size_t blk = wb + lane / G;
+        const bool valid = blk < total;
+        const size_t t = valid ? blk / nb : 0, b = valid ? blk % nb : 0;
+        const float4 v = valid ? load4(x + t * xs + b * QB + 4 * lg, vec) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float amax = amax4(v);
+        uint32_t bad = finite4(v) ? 0u : 1u;
+#pragma unroll
+        for (int off = G / 2; off >= 1; off >>= 1) {
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+            bad |= __shfl_xor_sync(0xffffffffu, bad, off);
+        }
+        if (!valid) continue;
+        uint32_t packed = 0;
+        float scale = 0.0f;
+        if (!bad && amax >= 0x1p-121f) {
+            scale = div_r<RM>(amax, 127.0f);
+            packed = quant4<RM>(v, div_r<RM>(127.0f, amax));
+        }
+        *reinterpret_cast<uint32_t*>(q + t * n + b * QB + 4 * lg) = packed;
+        if (lg == 0) d[t * nb + b] = scale;
+    }
+}
+
+// Blocks of any multiple of 32 inputs, a warp each.
+template <int RM>
+__global__ void __launch_bounds__(256) quantize_wide(int8_t* __restrict__ q, float* __restrict__ d,
+                                                     const float* __restrict__ x, size_t xs, uint32_t T,
+                                                     uint32_t n, uint32_t qb, bool vec) {
+    const uint32_t nb = n / qb;
+    const size_t total = static_cast<size_t>(T) * nb;
+    const uint32_t lane = threadIdx.x & 31;
+    const size_t warp0 = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32;
+    const size_t nwarps = static_cast<size_t>(gridDim.x) * blockDim.x / 32;
+    for (size_t blk = warp0; blk < total; blk += nwarps) {  // warp-uniform
+        const size_t t = blk / nb, b = blk % nb;
+        const float* v = x + t * xs + b * qb;
+        float amax = 0.0f;
+        uint32_t bad = 0;
+        for (uint32_t i = 4 * lane; i < qb; i += 128) {
+            const float4 f = load4(v + i, vec);
+            amax = fmaxf(amax, amax4(f));
+            bad |= finite4(f) ? 0u : 1u;
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+            bad |= __shfl_xor_sync(0xffffffffu, bad, off);
+        }
+        int8_t* qo = q + t * n + b * qb;
+        const bool zero = bad || !(amax >= 0x1p-121f);
+        const float id = zero ? 0.0f : div_r<RM>(127.0f, amax);
+        for (uint32_t i = 4 * lane; i < qb; i += 128)
+            *reinterpret_cast<uint32_t*>(qo + i) = zero ? 0u : quant4<RM>(load4(v + i, vec), id);
+        if (lane == 0) d[t * nb + b] = zero ? 0.0f : div_r<RM>(amax, 127.0f);
+    }
+}
+
+template <int RM>
+cudaError_t quantize_rm(int8_t* q, float* d, const float* x, size_t xs, uint32_t T, uint32_t n, uint32_t qb,
+                        int num_sms, cudaStream_t stream) {
+    const bool vec = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (xs % 4 == 0);
+    const size_t blocks = static_cast<size_t>(T) * (n / qb);
+    const size_t per_cta = qb == 32 ? 8 * 4 : qb == 64 ? 8 * 2 : 8;  // blocks a 256-thread CTA takes per pass
+    size_t grid = (blocks + per_cta - 1) / per_cta;
+    const size_t cap = static_cast<size_t>(num_sms) * 8;
+    if (grid > cap) grid = cap;
+    if (grid == 0) grid = 1;
+    if (qb == 32)
+        quantize_narrow<RM, 8><<<static_cast<unsigned>(grid), 256, 0, stream>>>(q, d, x, xs, T, n, vec);
+    else if (qb == 64)
+        quantize_narrow<RM, 16><<<static_cast<unsigned>(grid), 256, 0, stream>>>(q, d, x, xs, T, n, vec);
+    else
+        quantize_wide<RM><<<static_cast<unsigned>(grid), 256, 0, stream>>>(q, d, x, xs, T, n, qb, vec);
+    return cudaGetLastError();
+}
+
+__global__ void __launch_bounds__(256) repack_q8(uint32_t* __restrict__ dst, const uint32_t* __restrict__ src,
+                                                 uint32_t rows, uint32_t n) {
+    // word (r, k/4) of the plain rows from word ((r/16)*(n/4) + k/4)*16 + r%16
+    // of the panels
+    const uint32_t n4 = n / 4;
+    const size_t total = static_cast<size_t>(rows) * n4;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const size_t r = i / n4, k4 = i % n4;
+        dst[i] = __ldg(src + ((r / 16) * n4 + k4) * 16 + (r % 16));
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_quantize(int8_t* q, float* d, const float* x, size_t xs, uint32_t T, uint32_t n, uint32_t qb,
+                            int rmode, int num_sms, cudaStream_t stream) {
+    switch (rmode) {
+    case 1: return quantize_rm<1>(q, d, x, xs, T, n, qb, num_sms, stream);
+    case 2: return quantize_rm<2>(q, d, x, xs, T, n, qb, num_sms, stream);
+    case 3: return quantize_rm<3>(q, d, x, xs, T, n, qb, num_sms, stream);
+    default: return quantize_rm<0>(q, d, x, xs, T, n, qb, num_sms, stream);
+    }
+}
+
+cudaError_t launch_repack_q8(int8_t* wpack, const int8_t* w_pk, uint32_t rows, uint32_t n, int num_sms,
+                             cudaStream_t stream) {
+    const size_t words = static_cast<size_t>(rows) * (n / 4);
+    size_t grid = (words + 255) / 256;
+    const size_t cap = static_cast<size_t>(num_sms) * 16;
+    if (grid > cap) grid = cap;
+    if (grid == 0) grid = 1;
+    repack_q8<<<static_cast<unsigned>(grid), 256, 0, stream>>>(reinterpret_cast<uint32_t*>(wpack),
+                                                              reinterpret_cast<const uint32_t*>(w_pk), rows, n);
+    return cudaGetLastError();
+}
+
+}  // namespace pkb

@@ -1,0 +1,207 @@
+"""The CUDA path against the oracle, bit for bit, through the C ABI.
+
+Every comparison is of bytes (float32 bit patterns, int8 values): the
+reference's contract is ref's bits, not ref's answer to a tolerance
+(backend/kernels.h:9-24). Cases follow the reference's own checks:
+tests/q8check.c (edges, output stride 35, rounding modes, no columns) and
+tests/kcheck.c (random products on awkward values, runs of panels, blocks
+of 32, 64 and a whole row).
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests import cases as C
+
+pytestmark = pytest.mark.gpu
+
+
+def same_bits(a: np.ndarray, b: np.ndarray) -> bool:
+    return a.tobytes() == b.tobytes()
+
+
+def first_diff(a: np.ndarray, b: np.ndarray) -> str:
+    av, bv = a.reshape(-1).view(np.uint32), b.reshape(-1).view(np.uint32)
+    i = int(np.nonzero(av != bv)[0][0])
+    return f"element {i}: {a.reshape(-1)[i]!r} vs oracle {b.reshape(-1)[i]!r} ({int((av != bv).sum())} differ)"
+
+
+# ------------------------------------------------------------- quantize --
+
+QUANT_SHAPES = [(1, 32, 32, 32), (5, 128, 32, 160), (20, 1024, 32, 1024), (7, 1024, 64, 1056),
+                (3, 640, 640, 640), (2, 96, 96, 96), (13, 4096, 32, 4096), (4, 16384, 16384, 16384),
+                (750, 1024, 32, 1024), (33, 256, 64, 257)]
+
+
+@pytest.mark.parametrize("T,n,qb,xs", QUANT_SHAPES)
+@pytest.mark.parametrize("rmode", [O.RN, O.RD, O.RU, O.RZ])
+def test_quantize_host(pkb, cuda_device, T, n, qb, xs, rmode):
+    rng = O.XorShift(0x1234 + T * 7 + n + qb + rmode)
+    scale = 1e4 if (T + n) % 3 == 0 else 1.0
+    x = C.awkward_array(rng, T * xs + n, scale)
+    if T > 1:
+        x[:qb] = 0.0  # a block of zeros: scale 0
+    x[min(5, x.size - 1)] = np.float32(1e-40)
+    q, d = pkb.quantize_host(x, n, qb, T=T, xs=xs, rmode=rmode)
+    qo, do = O.quantize(x, n, qb, T=T, xs=xs, rmode=rmode)
+    assert np.array_equal(q, qo)
+    assert same_bits(d, do), first_diff(d, do)
+    assert q.min() >= -127 or rmode in (O.RU, O.RD)
+
+
+def test_quantize_nonfinite_and_tiny(pkb, cuda_device):
+    # tests/kcheck.c:120-175: non-finite inputs and amax either side of 2^-121
+    T, n, qb = 2, 64, 32
+    x = np.array([O.XorShift(9).frand() for _ in range(T * n)], np.float32)
+    x[3], x[40], x[n + 5], x[n + 45] = np.nan, np.inf, -np.inf, np.nan
+    q, d = pkb.quantize_host(x, n, qb)
+    assert not q.any() and not d.any()
+    tops = np.array([2.0**-140, 2.0**-130, 2.0**-122, np.float32(float.fromhex('0x1.fffffep-122')), 2.0**-121, 2.0**-120,
+                     2.0**-100], np.float32)
+    n = 32 * len(tops)
+    rng = O.XorShift(77)
+    x = np.empty(2 * n, np.float32)
+    for t in range(2):
+        for b, top in enumerate(tops):
+            v = np.array([top * np.float32(rng.frand()) for _ in range(32)], np.float32)
+            v[rng.rnd() % 32] = -top if t else top
+            x[t * n + 32 * b: t * n + 32 * b + 32] = v
+    q, d = pkb.quantize_host(x, n, 32)
+    qo, do = O.quantize(x, n, 32)
+    assert np.array_equal(q, qo) and same_bits(d, do)
+    assert ((d.reshape(2, -1) == 0) == (tops < 2.0**-121)[None, :]).all()
+
+
+def test_quantize_dev_matches_host(pkb, cuda_device):
+    import torch
+    T, n, qb = 300, 4096, 32
+    x = O.seeded_normal(T * n, 5)
+    xd = torch.from_numpy(x).cuda()
+    q = torch.empty(T * n, dtype=torch.int8, device="cuda")
+    d = torch.empty(T * n // qb, dtype=torch.float32, device="cuda")
+    pkb.quantize_dev(q, d, xd, n, T, n, qb)
+    torch.cuda.synchronize()
+    qo, do = O.quantize(x, n, qb)
+    assert np.array_equal(q.cpu().numpy().reshape(T, n), qo)
+    assert same_bits(d.cpu().numpy().reshape(T, -1), do)
+
+
+# ---------------------------------------------------------------- gemm_q8 --
+
+def run_host_case(pkb, c, rmode=O.RN):
+    got = c["out"].copy()
+    pkb.gemm_q8_host(got, c["os"], c["w"], c["ws"], c["bias"], c["rows"], c["q"], c["d"], c["n"], c["qb"], c["T"],
+                     c["add"], rmode)
+    want = c["out"].copy()
+    O.gemm_q8(want, c["os"], c["w"], c["ws"], c["bias"], c["rows"], c["q"], c["d"], c["n"], c["qb"], c["T"],
+              c["add"], rmode)
+    return got, want
+
+
+@pytest.mark.parametrize("shape", C.q8check_shapes(), ids=lambda s: "n%d-qb%d-T%d-f%d" % s)
+def test_q8check_edges(pkb, cuda_device, shape):
+    got, want = run_host_case(pkb, C.q8check_case(*shape))
+    assert same_bits(got, want), first_diff(got, want)  # the floats between columns too
+
+
+@pytest.mark.parametrize("rmode", [O.RD, O.RU, O.RZ])
+@pytest.mark.parametrize("shape", C.q8check_mode_shapes(), ids=lambda s: "n%d-qb%d-T%d-f%d" % s)
+def test_q8check_rounding_modes(pkb, cuda_device, shape, rmode):
+    got, want = run_host_case(pkb, C.q8check_case(*shape), rmode)
+    assert same_bits(got, want), first_diff(got, want)
+
+
+def test_no_columns(pkb, cuda_device):
+    out = np.array([-0.0], np.float32)
+    lib = pkb.lib()
+    rc = lib.pkb_gemm_q8_host(out.ctypes.data, 16, None, None, None, 16, None, None, 32, 32, 0, 0, 0)
+    assert rc == 0 and out.tobytes() == np.array([-0.0], np.float32).tobytes()
+    rc = lib.pkb_quantize_host(None, None, 32, 32, 0, None, 32, 0)
+    assert rc == 0
+
+
+RANDOM = [(rows, n, T, qb, add, bias)
+          for i, (rows, n, T, qb) in enumerate([
+              (16, 32, 1, 32), (48, 64, 7, 32), (64, 96, 13, 96), (32, 256, 37, 32), (384, 640, 3, 640),
+              (64, 1024, 20, 32), (208, 1024, 1, 1024), (64, 4096, 9, 32), (16, 4096, 37, 4096),
+              (128, 1024, 129, 64), (256, 256, 200, 64), (48, 640, 31, 64), (64, 4096, 48, 64),
+              (32, 1024, 193, 32), (16, 4096, 101, 4096), (2048, 1024, 5, 32)])
+          for add in (0, 1) for bias in (0, 1) if (i + add + bias) % 2 == 0 or T == 1]
+
+
+@pytest.mark.parametrize("rows,n,T,qb,add,bias", RANDOM)
+def test_random_products(pkb, cuda_device, rows, n, T, qb, add, bias):
+    c = C.random_gemm_case(rows * 31 + n + T * 7 + qb + add * 3 + bias, rows, n, T, qb, bool(add), bool(bias))
+    r0, nr = c["r0"], rows - c["r0"]
+    got = c["out"].copy()
+    b = None if c["bias_full"] is None else c["bias_full"][r0:]
+    pkb.gemm_q8_host(got[r0:], c["os"], c["w_full"][r0 * n:], c["ws_full"][r0:], b, nr, c["q"], c["d"], n, qb, T,
+                     bool(add))
+    want = C.gemm_oracle(c)
+    assert same_bits(got, want), first_diff(got, want)
+
+
+def test_table_entry(pkb, cuda_device):
+    """pk_kernels_cuda_b200, called as the reference's passes call a backend."""
+    tab = pkb.Table()
+    assert tab.id == "cuda-b200"
+    T, n, qb, rows = 37, 1024, 32, 64
+    x = O.seeded_normal(T * n, 11)
+    q = np.zeros(T * n, np.int8)
+    d = np.zeros(T * n // qb, np.float32)
+    act = pkb.PkAct(q.ctypes.data, d.ctypes.data, n, qb, T)
+    tab.quantize(act, x, n)
+    qo, do = O.quantize(x, n, qb)
+    assert np.array_equal(q.reshape(T, n), qo) and same_bits(d.reshape(T, -1), do)
+    w = O.pack_q8(O.uniform_weights(rows, n, 3))
+    ws = np.linspace(1e-3, 1e-2, rows).astype(np.float32)
+    out = np.full(T * rows, 7.0, np.float32)
+    tab.gemm_q8(out, rows, w, ws, None, rows, act, True)
+    want = np.full(T * rows, 7.0, np.float32)
+    O.gemm_q8(want, rows, w, ws, None, rows, qo, do, n, qb, T, True)
+    assert same_bits(out, want), first_diff(out, want)
+
+
+def test_weights_changed_in_place(pkb, cuda_device):
+    """A matrix rewritten at the same host address is uploaded again."""
+    T, n, qb, rows = 9, 256, 32, 32
+    x = O.seeded_normal(T * n, 2)
+    q, d = O.quantize(x, n, qb)
+    w = O.pack_q8(O.uniform_weights(rows, n, 4))
+    ws = np.full(rows, 0.01, np.float32)
+    for seed in (4, 5):
+        w[:] = O.pack_q8(O.uniform_weights(rows, n, seed))
+        got = np.zeros(T * rows, np.float32)
+        pkb.gemm_q8_host(got, rows, w, ws, None, rows, q, d, n, qb, T, False)
+        want = np.zeros(T * rows, np.float32)
+        O.gemm_q8(want, rows, w, ws, None, rows, q, d, n, qb, T, False)
+        assert same_bits(got, want)
+    pkb.forget(w)
+
+
+@pytest.mark.parametrize("T,rows,n,qb", [(750, 4096, 1024, 32), (750, 1024, 4096, 64), (1499, 1024, 1024, 32),
+                                         (300, 640, 1024, 1024)])
+def test_device_path_full_layer_shapes(pkb, cuda_device, T, rows, n, qb):
+    """Encoder shapes at a minute of audio (T = 750, the position table's
+    1499), on device buffers, against the oracle."""
+    import torch
+    x = O.seeded_normal(T * n, T + rows)
+    q, d = O.quantize(x, n, qb)
+    w_pk = O.pack_q8(O.uniform_weights(rows, n, rows + n))
+    ws = (1e-3 + 9e-3 * np.random.default_rng(rows).random(rows)).astype(np.float32)
+    bias = np.random.default_rng(n).standard_normal(rows).astype(np.float32)
+    out0 = np.random.default_rng(T).standard_normal(T * rows).astype(np.float32)
+    add = qb != 32
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    wpack = torch.empty(rows * n, dtype=torch.int8, device="cuda")
+    pkb.repack_q8_dev(wpack, dev(w_pk), rows, n)
+    out = dev(out0)
+    pkb.gemm_q8_dev(out, rows, wpack, dev(ws), dev(bias), rows, dev(q), dev(d), n, qb, T, add)
+    torch.cuda.synchronize()
+    assert pkb.device_errors(0) == 0
+    got = out.cpu().numpy()
+    want = out0.copy()
+    O.gemm_q8(want, rows, w_pk, ws, bias, rows, q, d, n, qb, T, add)
+    assert same_bits(got, want), first_diff(got, want)

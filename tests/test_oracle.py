@@ -1,0 +1,135 @@
+"""The oracle pinned before it is trusted (CPU only).
+
+* Against the committed golden vectors (tests/golden/q8_golden.npz), which
+  the reference's own ref backend wrote (tests/golden/make_golden.py).
+* Against the reference's ref backend live, where oracle/_ref was built from
+  the reference's sources in this checkout.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests import cases as C
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "q8_golden.npz")
+
+
+@pytest.fixture(scope="module")
+def golden():
+    return np.load(GOLDEN)
+
+
+def keys(g, prefix):
+    return sorted({k.split("/")[1] for k in g.files if k.startswith(prefix + "/")}, key=lambda s: (len(s), s))
+
+
+def test_golden_quantize(golden):
+    for i in keys(golden, "qc"):
+        T, n, qb, xs = (int(v) for v in golden[f"qc/{i}/shape"])
+        q, d = O.quantize(golden[f"qc/{i}/x"], n, qb, T=T, xs=xs)
+        assert np.array_equal(q, golden[f"qc/{i}/q"]), i
+        assert d.tobytes() == golden[f"qc/{i}/d"].tobytes(), i
+    q, d = O.quantize(golden["qx/nonfinite/x"], 64, 32)
+    assert np.array_equal(q, golden["qx/nonfinite/q"]) and d.tobytes() == golden["qx/nonfinite/d"].tobytes()
+    assert not q.any() and not d.any()
+    n = golden["qx/tiny/x"].size // 2
+    q, d = O.quantize(golden["qx/tiny/x"], n, 32)
+    assert np.array_equal(q, golden["qx/tiny/q"]) and d.tobytes() == golden["qx/tiny/d"].tobytes()
+
+
+def test_golden_q8check_products(golden):
+    for j in keys(golden, "g8"):
+        shape = tuple(int(v) for v in golden[f"g8/{j}/shape"])
+        rmode = int(golden[f"g8/{j}/rmode"])
+        c = C.q8check_case(*shape)
+        o = c["out"].copy()
+        O.gemm_q8(o, c["os"], c["w"], c["ws"], c["bias"], c["rows"], c["q"], c["d"], c["n"], c["qb"], c["T"],
+                  c["add"], rmode)
+        assert o.tobytes() == golden[f"g8/{j}/out"].tobytes(), (shape, rmode)
+
+
+def test_golden_random_products(golden):
+    for i in keys(golden, "gr"):
+        p = f"gr/{i}/"
+        rows, n, T, qb, add, bias, r0, os_ = (int(v) for v in golden[p + "meta"])
+        o = golden[p + "out_in"].copy()
+        b = golden[p + "bias"][r0:] if bias else None
+        O.gemm_q8(o[r0:], os_, golden[p + "w"][r0 * n:], golden[p + "ws"][r0:], b, rows - r0, golden[p + "q"],
+                  golden[p + "d"], n, qb, T, bool(add))
+        assert o.tobytes() == golden[p + "out"].tobytes(), i
+
+
+def test_block_sums_exact():
+    """The integer sums equal an int64 definition (tests/kcheck.c:217-239)."""
+    rng = np.random.default_rng(3)
+    rows, n, T, qb = 32, 256, 5, 32
+    w_rm = rng.integers(-128, 128, (rows, n)).astype(np.int8)
+    q = rng.integers(-127, 128, (T, n)).astype(np.int8)
+    s = O.block_sums(O.pack_q8(w_rm), rows, q, n, qb, T)
+    want = np.einsum("tbk,rbk->trb", q.reshape(T, n // qb, qb).astype(np.int64),
+                     w_rm.reshape(rows, n // qb, qb).astype(np.int64))
+    assert np.array_equal(s, want)
+
+
+def test_pack_roundtrip():
+    w = O.uniform_weights(48, 640, 1)
+    assert np.array_equal(O.unpack_q8(O.pack_q8(w), 48, 640), w)
+
+
+needs_ref = pytest.mark.skipif(not O.have_ref(), reason="oracle/_ref not built (reference sources absent)")
+
+
+@needs_ref
+@pytest.mark.parametrize("rmode", [O.RN, O.RD, O.RU, O.RZ])
+def test_live_reference_products(rmode):
+    """The oracle's product equals the reference's ref in every rounding mode."""
+    for seed, (rows, n, T, qb) in enumerate([(32, 128, 5, 32), (48, 1024, 7, 64), (16, 640, 3, 640),
+                                             (64, 4096, 9, 32), (32, 96, 2, 96), (16, 16384, 3, 32)]):
+        g = np.random.default_rng(seed)
+        x = (g.standard_normal(T * n) * g.choice([1.0, 1e4, 1e-38], T * n)).astype(np.float32)
+        q, d = O.ref_quantize(x, n, qb)
+        w = O.pack_q8(g.integers(-128, 128, (rows, n)).astype(np.int8))
+        ws = (g.random(rows) - 0.3).astype(np.float32)
+        b = g.standard_normal(rows).astype(np.float32)
+        for add in (False, True):
+            o1 = g.standard_normal(T * (rows + 3)).astype(np.float32)
+            o2 = o1.copy()
+            O.gemm_q8(o1, rows + 3, w, ws, b, rows, q, d, n, qb, T, add, rmode)
+            O.ref_gemm_q8(o2, rows + 3, w, ws, b, rows, q, d, n, qb, T, add, rmode)
+            assert o1.tobytes() == o2.tobytes(), (seed, add)
+
+
+@needs_ref
+def test_live_reference_quantize_rn():
+    for seed, (T, n, qb, xs) in enumerate([(5, 128, 32, 160), (7, 1024, 64, 1024), (3, 640, 640, 672),
+                                           (9, 4096, 32, 4096), (13, 16384, 32, 16384)]):
+        g = np.random.default_rng(100 + seed)
+        x = (g.standard_normal(T * xs + n) * g.choice([1.0, 1e4, 1e-38], T * xs + n)).astype(np.float32)
+        x[g.integers(0, x.size, 4)] = np.float32(1e-40)
+        q1, d1 = O.quantize(x, n, qb, T=T, xs=xs)
+        q2, d2 = O.ref_quantize(x, n, qb, T=T, xs=xs)
+        assert np.array_equal(q1, q2) and d1.tobytes() == d2.tobytes()
+
+
+@needs_ref
+def test_reference_quantize_directed_modes_differs_only_in_rint():
+    """Under RD/RU the reference's ref, as gcc compiles it for baseline
+    x86-64, rounds |v * id| and restores the sign (its inline rintf), so a
+    negative value rounds toward zero under RD and away from it under RU,
+    where IEEE rint (the contract's rint, backend/kernels.h:52, which the
+    oracle and the CUDA path follow) rounds down and up. The reference's own
+    checks never quantize in a directed mode. This pins that the two differ
+    there and nowhere else: the scales agree, every byte of a non-negative
+    input agrees, and a negative input's bytes are at most one step apart."""
+    n, qb, T = 1024, 32, 8
+    x = np.random.default_rng(7).standard_normal(T * n).astype(np.float32) * 100
+    neg = x.reshape(T, n) < 0
+    for rmode in (O.RD, O.RU):
+        q1, d1 = O.quantize(x, n, qb, rmode=rmode)
+        q2, d2 = O.ref_quantize(x, n, qb, rmode=rmode)
+        assert d1.tobytes() == d2.tobytes()
+        assert np.array_equal(q1[~neg], q2[~neg])
+        diff = q2[neg].astype(np.int32) - q1[neg].astype(np.int32)
+        assert np.all(np.abs(diff) <= 1) and np.any(diff != 0)
