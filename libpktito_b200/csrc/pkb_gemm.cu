@@ -62,14 +62,22 @@ constexpr int B_BYTES = BN * BK;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int EPI_PITCH = 33;      // floats a row of an epilogue warp's transpose tile
 constexpr int EPI_BYTES = EPI_WARPS * 32 * EPI_PITCH * 4;
-constexpr int BAR_BYTES = 256;
-constexpr int SMEM_BYTES = NSTAGE * STAGE_BYTES + EPI_BYTES + BAR_BYTES + 1024;  // + alignment slack
+constexpr int DCHUNK = 4;          // blocks of scales a TMA box of d carries (16 bytes a frame)
+constexpr int NDS = 8;             // slots of the scales ring
+constexpr int DS_BYTES = BM * DCHUNK * 4;
+constexpr int BAR_BYTES = 512;
+constexpr int SMEM_BYTES = NSTAGE * STAGE_BYTES + EPI_BYTES + NDS * DS_BYTES + BAR_BYTES + 1024;  // + alignment slack
 
 static_assert(TMEM_COLS == 512, "TMEM ring must fit the SM's 512 columns");
-static_assert((2 * NSTAGE + 2 * NTMEM + 1) * 8 + 8 <= BAR_BYTES, "barrier area");
+static_assert((2 * NSTAGE + 2 * NTMEM + 2 * NDS + 1) * 8 + 8 <= BAR_BYTES, "barrier area");
 
 // acc[8*half + i] (two output rows each) = fma(float(s), d, acc), for the
 // 16 block sums of one TMEM load, two rows an instruction.
+// The int32 each block accumulator starts from when block sums convert
+// exactly (|s| < 2^22): its bits are the float 1.5 * 2^23, so the MMA's
+// integer sum added to it is, read as a float, 1.5 * 2^23 + s.
+constexpr uint32_t SUM_BIAS = 0x4B400000u;
+
 template <int RM, bool EXACT_SUM>
 __device__ __forceinline__ void chain16(uint64_t (&acc)[16], const uint32_t (&s)[16], int half, float dv) {
     const uint64_t d2 = pack2(dv, dv);
@@ -77,9 +85,10 @@ __device__ __forceinline__ void chain16(uint64_t (&acc)[16], const uint32_t (&s)
     for (int i = 0; i < 8; i++) {
         uint64_t f;
         if constexpr (EXACT_SUM) {
-            // the sums plus 0x4B400000 are the floats 1.5 * 2^23 + s; less
-            // 1.5 * 2^23, rounded to nearest, they are exactly s
-            f = add2_rn(pack2(__uint_as_float(s[2 * i] + 0x4B400000u), __uint_as_float(s[2 * i + 1] + 0x4B400000u)),
+            // the accumulators started at 0x4B400000 (SUM_BIAS), so each word
+            // is the float 1.5 * 2^23 + s; less 1.5 * 2^23, rounded to nearest,
+            // it is exactly s (and +0 for a zero sum)
+            f = add2_rn(pack2(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])),
                         pack2(-12582912.0f, -12582912.0f));
         } else {
             f = pack2(i2f_r<RM>(static_cast<int>(s[2 * i])), i2f_r<RM>(static_cast<int>(s[2 * i + 1])));
@@ -88,18 +97,21 @@ __device__ __forceinline__ void chain16(uint64_t (&acc)[16], const uint32_t (&s)
     }
 }
 
-template <int RM, bool EXACT_SUM>
+template <int RM, bool EXACT_SUM, int G, bool DTMA>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_q8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                   const GemmArgs g) {
+                   const __grid_constant__ CUtensorMap map_d, const GemmArgs g) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float* epi = reinterpret_cast<float*>(smem + NSTAGE * STAGE_BYTES);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + NSTAGE * STAGE_BYTES + EPI_BYTES);
+    float* dring = reinterpret_cast<float*>(smem + NSTAGE * STAGE_BYTES + EPI_BYTES);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + NSTAGE * STAGE_BYTES + EPI_BYTES + NDS * DS_BYTES);
     uint64_t* empty = full + NSTAGE;
     uint64_t* tfull = empty + NSTAGE;
     uint64_t* tempty = tfull + NTMEM;
-    uint64_t* drain = tempty + NTMEM;
+    uint64_t* dfull = tempty + NTMEM;
+    uint64_t* dempty = dfull + NDS;
+    uint64_t* drain = dempty + NDS;
     uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
 
@@ -115,6 +127,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&tfull[i], 1);
             mbar_init(&tempty[i], EPI_WARPS);
         }
+        for (int i = 0; i < NDS; i++) {
+            mbar_init(&dfull[i], 1);
+            mbar_init(&dempty[i], EPI_WARPS);
+        }
         mbar_init(drain, 1);
         *abort = 0;
         fence_mbar_init();
@@ -126,11 +142,28 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (warp == TMA_WARP && lane == 0) {
         tma_prefetch_map(&map_a);
         tma_prefetch_map(&map_b);
+        if constexpr (DTMA) tma_prefetch_map(&map_d);
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *tslot;
+    if constexpr (EXACT_SUM) {
+        // every accumulator starts at SUM_BIAS: each epilogue warp fills its
+        // lane quarter of its 32 columns in every TMEM slot
+        if (warp < EPI_WARPS) {
+            const uint32_t ta = tbase + ((32 * (warp & 3)) << 16) + 32 * (warp >> 2);
+#pragma unroll
+            for (int k = 0; k < NTMEM; k++) {
+                tmem_st_32x32b_x16_fill(ta + k * BN, SUM_BIAS);
+                tmem_st_32x32b_x16_fill(ta + k * BN + 16, SUM_BIAS);
+            }
+            tmem_st_wait();
+        }
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    }
 
     const uint32_t nk = g.n / KSTEP;            // K steps of a tile
     const uint32_t nc = (g.n + BK - 1) / BK;     // shared-memory stages of a tile
@@ -141,12 +174,32 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     if (warp == TMA_WARP) {
         if (lane == 0) {
-            uint32_t it = 0;
+            uint32_t it = 0, dcnt = 0;
+            const uint32_t nchunks = (nb + DCHUNK - 1) / DCHUNK;
             bool ok = true;
             for (uint32_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
                 const int m0 = static_cast<int>((tile / g.tiles_n) * BM);
                 const int n0 = static_cast<int>((tile % g.tiles_n) * BN);
-                for (uint32_t c = 0; c < nc; c++, it++) {
+                uint32_t dk = 0;  // the tile's next chunk of scales
+                for (uint32_t c = 0; ok && c < nc; c++, it++) {
+                    if constexpr (DTMA) {
+                        // the scales of every chunk of blocks starting in this
+                        // stage's K range, into the scales ring (the box's x,
+                        // a multiple of 4 floats, is 16-byte aligned)
+                        while (dk < nchunks && DCHUNK * dk * g.qb < (c + 1) * BK) {
+                            const uint32_t ds = dcnt % NDS;
+                            if (!mbar_wait(&dempty[ds], ((dcnt / NDS) & 1) ^ 1, abort, limit)) {
+                                ok = false;
+                                break;
+                            }
+                            mbar_arrive_expect_tx(&dfull[ds], DS_BYTES);
+                            tma_load_2d(&map_d, reinterpret_cast<uint8_t*>(dring) + ds * DS_BYTES, &dfull[ds],
+                                        static_cast<int>(DCHUNK * dk), m0);
+                            dk++;
+                            dcnt++;
+                        }
+                        if (!ok) break;
+                    }
                     const uint32_t s = it % NSTAGE, ph = (it / NSTAGE) & 1;
                     if (!mbar_wait(&empty[s], ph ^ 1, abort, limit)) {
                         ok = false;
@@ -165,42 +218,62 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const uint32_t back = it < NSTAGE ? it : NSTAGE;
                 for (uint32_t i = it - back; i < it; i++)
                     mbar_drain(&full[i % NSTAGE], (i / NSTAGE) & 1, limit);
+                const uint32_t dback = dcnt < NDS ? dcnt : NDS;
+                for (uint32_t i = dcnt - dback; i < dcnt; i++)
+                    mbar_drain(&dfull[i % NDS], (i / NDS) & 1, limit);
             }
         }
     } else if (warp == MMA_WARP) {
         if (lane == 0) {
+            // G consecutive blocks share one TMEM-full commit (a commit blocks
+            // its thread for about a hundred cycles, and at blocks of 32 this
+            // one thread would otherwise issue five a stage); NTMEM / G groups
+            // of G accumulators ring through TMEM. Every count is stepped, none
+            // divided, and the descriptors are stepped by adding offsets.
             constexpr uint32_t idesc = i8_instr_desc(BM, BN);
-            uint32_t it = 0, tb = 0;
+            constexpr uint32_t NGROUP = NTMEM / G;
+            const uint64_t desc0 = sw128_kmajor_desc(smem_u32(smem));
+            uint32_t s = 0, sph = 0, gc = 0, gs = 0;
             bool ok = true;
             for (uint32_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
-                for (uint32_t c = 0; c < nc && ok; c++, it++) {
-                    const uint32_t s = it % NSTAGE, ph = (it / NSTAGE) & 1;
-                    if (!mbar_wait(&full[s], ph, abort, limit)) {
+                uint32_t kpos = 0, block = 0, kin = 0;  // K step in its block, block, block in its group
+                uint32_t left = nk;                     // K steps of the tile still to issue
+                for (uint32_t c = 0; c < nc && ok; c++) {
+                    if (!mbar_wait(&full[s], sph, abort, limit)) {
                         ok = false;
                         break;
                     }
-                    tc_fence_after();
-                    const uint32_t a_addr = smem_u32(smem + s * STAGE_BYTES);
-                    const uint32_t b_addr = a_addr + A_BYTES;
-                    const uint32_t jn = nk - 4 * c < 4 ? nk - 4 * c : 4;
+                    const uint64_t adesc = desc0 + ((s * STAGE_BYTES) >> 4);
+                    const uint64_t bdesc = adesc + (A_BYTES >> 4);
+                    const uint32_t jn = left < 4 ? left : 4;
+                    left -= jn;
                     for (uint32_t j = 0; j < jn; j++) {
-                        const uint32_t pos = (4 * c + j) % spb;
-                        const uint32_t ts = tb % NTMEM;
-                        if (pos == 0) {
-                            if (!mbar_wait(&tempty[ts], ((tb / NTMEM) & 1) ^ 1, abort, limit)) {
+                        if (kpos == 0 && kin == 0) {
+                            if (!mbar_wait(&tempty[gs], ((gc / NGROUP) & 1) ^ 1, abort, limit)) {
                                 ok = false;
                                 break;
                             }
                             tc_fence_after();
                         }
-                        umma_i8(tbase + ts * BN, sw128_kmajor_desc(a_addr + j * KSTEP),
-                                sw128_kmajor_desc(b_addr + j * KSTEP), idesc, pos != 0);
-                        if (pos == spb - 1) {
-                            umma_commit(&tfull[ts]);
-                            tb++;
+                        // onto the bias when sums convert exactly, else from zero
+                        umma_i8(tbase + (gs * G + kin) * BN, adesc + 2 * j, bdesc + 2 * j, idesc,
+                                EXACT_SUM ? 1u : kpos);
+                        if (++kpos == spb) {
+                            kpos = 0;
+                            block++;
+                            if (++kin == G || block == nb) {
+                                umma_commit(&tfull[gs]);
+                                kin = 0;
+                                gc++;
+                                gs = gc % NGROUP;
+                            }
                         }
                     }
                     umma_commit(&empty[s]);
+                    if (++s == NSTAGE) {
+                        s = 0;
+                        sph ^= 1;
+                    }
                 }
             }
             if (!ok) {
@@ -216,7 +289,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t quarter = warp & 3, cgroup = warp >> 2;
         const uint32_t lane_base = 32 * quarter;
         float* tw = epi + warp * (32 * EPI_PITCH);  // this warp's 32 x 32 transpose tile
-        uint32_t tb = 0;
+        constexpr uint32_t NGROUP = NTMEM / G;
+        uint32_t gc = 0, gs = 0, dcnt = 0;
         bool ok = true;
         for (uint32_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
             const uint32_t m0 = (tile / g.tiles_n) * BM;
@@ -229,45 +303,68 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int j = 0; j < 16; j++) acc[j] = 0;  // +0, +0
 
-            // the frame's block scales, four blocks at a time, fetched one
-            // chunk of four ahead of their use
-            float dc[4];
-#pragma unroll
-            for (int j = 0; j < 4; j++) dc[j] = (tvalid && static_cast<uint32_t>(j) < nb) ? __ldg(drow + j) : 0.0f;
-            for (uint32_t b0 = 0; ok && b0 < nb; b0 += 4) {
-                float dn[4];
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const uint32_t bb = b0 + 4 + j;
-                    dn[j] = (tvalid && bb < nb) ? __ldg(drow + bb) : 0.0f;
+            // without the scales ring: the frame's scales from global memory,
+            // one block ahead
+            float dnext = (!DTMA && tvalid) ? __ldg(drow) : 0.0f;
+            for (uint32_t b = 0; b < nb; b++) {
+                float dv;
+                if constexpr (DTMA) {
+                    const uint32_t ds = dcnt % NDS;
+                    if ((b & (DCHUNK - 1)) == 0) {
+                        uint32_t seen = 1;
+                        if (lane == 0) seen = mbar_wait(&dfull[ds], (dcnt / NDS) & 1, abort, limit) ? 1u : 0u;
+                        if (!__shfl_sync(0xffffffffu, seen, 0)) {
+                            ok = false;
+                            break;
+                        }
+                    }
+                    dv = dring[ds * (DS_BYTES / 4) + (lane_base + lane) * DCHUNK + (b & (DCHUNK - 1))];
+                } else {
+                    dv = dnext;
+                    dnext = (tvalid && b + 1 < nb) ? __ldg(drow + b + 1) : 0.0f;
                 }
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    if (b0 + j >= nb) break;
-                    const uint32_t ts = tb % NTMEM;
-                    // every lane waits, and the warp goes on only if all saw
-                    // the phase: the TMEM loads are whole-warp instructions
-                    const bool seen = mbar_wait(&tfull[ts], (tb / NTMEM) & 1, abort, limit);
-                    if (!__all_sync(0xffffffffu, seen)) {
+                const uint32_t kin = b & (G - 1);  // block in its group
+                if (kin == 0) {
+                    // lane 0 waits and tells the warp: the TMEM loads below
+                    // are whole-warp instructions
+                    uint32_t seen = 1;
+                    if (lane == 0) seen = mbar_wait(&tfull[gs], (gc / NGROUP) & 1, abort, limit) ? 1u : 0u;
+                    if (!__shfl_sync(0xffffffffu, seen, 0)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t ta = tbase + (lane_base << 16) + ts * BN + 32 * cgroup;
-                    uint32_t s0[16], s1[16];
-                    tmem_ld_32x32b_x16(ta, s0);
-                    tmem_ld_wait(s0);
-                    tmem_ld_32x32b_x16(ta + 16, s1);  // in flight under the first half's chain
-                    chain16<RM, EXACT_SUM>(acc, s0, 0, dc[j]);
-                    tmem_ld_wait(s1);
+                }
+                const uint32_t ta = tbase + (lane_base << 16) + (gs * G + kin) * BN + 32 * cgroup;
+                // the two halves of the warp's 32 columns in turn (a TMEM
+                // load's round trip is a few tens of cycles)
+                uint32_t sv[16];
+                tmem_ld_32x32b_x16(ta, sv);
+                tmem_ld_wait(sv);
+                chain16<RM, EXACT_SUM>(acc, sv, 0, dv);
+                tmem_ld_32x32b_x16(ta + 16, sv);
+                tmem_ld_wait(sv);
+                if constexpr (EXACT_SUM) {
+                    // the slot back to SUM_BIAS for the block that takes it next
+                    tmem_st_32x32b_x16_fill(ta, SUM_BIAS);
+                    tmem_st_32x32b_x16_fill(ta + 16, SUM_BIAS);
+                    tmem_st_wait();
+                }
+                if (kin == G - 1 || b == nb - 1) {
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&tempty[ts]);
-                    chain16<RM, EXACT_SUM>(acc, s1, 1, dc[j]);
-                    tb++;
+                    if (lane == 0) mbar_arrive(&tempty[gs]);
+                    gc++;
+                    gs = gc % NGROUP;
                 }
-#pragma unroll
-                for (int j = 0; j < 4; j++) dc[j] = dn[j];
+                chain16<RM, EXACT_SUM>(acc, sv, 1, dv);
+                if constexpr (DTMA) {
+                    if ((b & (DCHUNK - 1)) == DCHUNK - 1 || b == nb - 1) {
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&dempty[dcnt % NDS]);
+                        dcnt++;
+                    }
+                }
             }
             if (!ok) break;
 
@@ -324,12 +421,18 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 template <int RM, bool EXACT_SUM>
-static cudaError_t launch_rm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, int grid,
-                             cudaStream_t stream) {
-    auto kern = gemm_q8_kernel<RM, EXACT_SUM>;
+static cudaError_t launch_rm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap* md, const GemmArgs& g,
+                             int grid, cudaStream_t stream) {
+    // blocks of up to 64 inputs (two or more a stage) commit in pairs; the
+    // scales go through the TMA ring when they have a tensor map
+    void (*kern)(CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs);
+    if (md)
+        kern = g.qb <= 64 ? gemm_q8_kernel<RM, EXACT_SUM, 2, true> : gemm_q8_kernel<RM, EXACT_SUM, 1, true>;
+    else
+        kern = g.qb <= 64 ? gemm_q8_kernel<RM, EXACT_SUM, 2, false> : gemm_q8_kernel<RM, EXACT_SUM, 1, false>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    kern<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, g);
+    kern<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, md ? *md : ma, g);
     return cudaGetLastError();
 }
 
@@ -339,8 +442,10 @@ int gemm_tile_rows() { return gemm::BM; }
 int gemm_tile_cols() { return gemm::BN; }
 int gemm_box_k() { return gemm::BK; }
 
-cudaError_t launch_gemm_q8(const CUtensorMap& map_a, const CUtensorMap& map_b, const GemmArgs& g, int num_sms,
-                           int rmode, cudaStream_t stream) {
+int gemm_scale_chunk() { return gemm::DCHUNK; }
+
+cudaError_t launch_gemm_q8(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap* map_d,
+                           const GemmArgs& g, int num_sms, int rmode, cudaStream_t stream) {
     const uint32_t ntiles = g.tiles_m * g.tiles_n;
     const int grid = static_cast<int>(ntiles < static_cast<uint32_t>(num_sms) ? ntiles : num_sms);
     // block sums convert to float exactly through the bias trick while
@@ -348,14 +453,14 @@ cudaError_t launch_gemm_q8(const CUtensorMap& map_a, const CUtensorMap& map_b, c
     // the conversion in the mode, as the reference's (float)s does
     const bool exact = g.qb <= 256;
     switch (rmode * 2 + (exact ? 1 : 0)) {
-    case 0: return gemm::launch_rm<0, false>(map_a, map_b, g, grid, stream);
-    case 1: return gemm::launch_rm<0, true>(map_a, map_b, g, grid, stream);
-    case 2: return gemm::launch_rm<1, false>(map_a, map_b, g, grid, stream);
-    case 3: return gemm::launch_rm<1, true>(map_a, map_b, g, grid, stream);
-    case 4: return gemm::launch_rm<2, false>(map_a, map_b, g, grid, stream);
-    case 5: return gemm::launch_rm<2, true>(map_a, map_b, g, grid, stream);
-    case 6: return gemm::launch_rm<3, false>(map_a, map_b, g, grid, stream);
-    default: return gemm::launch_rm<3, true>(map_a, map_b, g, grid, stream);
+    case 0: return gemm::launch_rm<0, false>(map_a, map_b, map_d, g, grid, stream);
+    case 1: return gemm::launch_rm<0, true>(map_a, map_b, map_d, g, grid, stream);
+    case 2: return gemm::launch_rm<1, false>(map_a, map_b, map_d, g, grid, stream);
+    case 3: return gemm::launch_rm<1, true>(map_a, map_b, map_d, g, grid, stream);
+    case 4: return gemm::launch_rm<2, false>(map_a, map_b, map_d, g, grid, stream);
+    case 5: return gemm::launch_rm<2, true>(map_a, map_b, map_d, g, grid, stream);
+    case 6: return gemm::launch_rm<3, false>(map_a, map_b, map_d, g, grid, stream);
+    default: return gemm::launch_rm<3, true>(map_a, map_b, map_d, g, grid, stream);
     }
 }
 

@@ -24,9 +24,13 @@ struct GemmArgs {
 int gemm_tile_rows();   // frames a tile (TMA box of the activations)
 int gemm_tile_cols();   // output rows a tile (TMA box of the weights)
 int gemm_box_k();       // inputs of K a TMA box
+int gemm_scale_chunk(); // blocks of scales a TMA box of the scales carries
 
-cudaError_t launch_gemm_q8(const CUtensorMap& map_a, const CUtensorMap& map_b, const GemmArgs& g, int num_sms,
-                           int rmode, cudaStream_t stream);
+// map_d: a tensor map of the block scales d [T][n/qb] (float32, boxes of
+// gemm_scale_chunk() blocks by gemm_tile_rows() frames), or null to read
+// them from global memory directly
+cudaError_t launch_gemm_q8(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap* map_d,
+                           const GemmArgs& g, int num_sms, int rmode, cudaStream_t stream);
 
 cudaError_t launch_quantize(int8_t* q, float* d, const float* x, size_t xs, uint32_t T, uint32_t n, uint32_t qb,
                             int rmode, int num_sms, cudaStream_t stream);
