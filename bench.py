@@ -1,0 +1,532 @@
+#!/usr/bin/env python3
+"""libpktito's int8 path on B200: the batched encoder benchmark.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload ("batched encoder"): 64 independent
+segments of seeded lengths uniform in 2-30 s (25-375 encoder frames each),
+through the int8 GEMM path of a 24-layer, d_model 1024 Parakeet-shaped
+encoder with random int8 weights: per layer its eleven products (feed-forward
+up/down twice, q/k/v, the position projection over 2T-1 rows, attention out,
+pointwise convolutions 1024->2048 and 1024->1024, core/encoder.c:329-368),
+plus the subsampling's three (core/encoder.c:218-251, 463-465); every
+product's float32 input quantized (blocks of 32) and multiplied. The
+segments' frames are concatenated into one M per product, which is
+bit-identical per frame to running them one by one (a product's columns are
+independent). The float parts between products (norms, attention, GLU,
+depthwise convolution) are outside the int8 path and not timed; each
+product's input is a resident float32 activation ~N(0,1).
+
+A step is one pass over the batch: 24 x 11 + 3 quantize+product pairs. value
+is whole-job int8 TOPS (2*M*N*K summed over the products, over every rank);
+audio-seconds per second is reported beside it. Multi-GPU: one process per
+GPU (torchrun), each with its own 64 segments (weak scaling), no collective
+on the data path; the time is the max over ranks.
+
+`--impl reference` times the reference's own CPU backend (the one its picker
+chooses on this host, built from its sources into oracle/_ref) on a bounded
+sample of the same products, on all host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "int8 GEMM TOPS (% of B200 int8 peak); encoder audio-s/s at 1/2/4/8 GPUs"
+SEGMENTS = 64
+LAYERS = 24
+D, F, C = 1024, 4096, 256
+QB = 32
+SEED = 20261201
+
+
+# ---------------------------------------------------------------- workload --
+
+def segments(rank: int) -> list[tuple[float, int, int, int]]:
+    """(seconds, T0, T2, T3) of the rank's 64 segments: mel frames at 100/s,
+    each 2x subsampling stage ceil-halving (core/encoder.c:430)."""
+    rng = np.random.default_rng(SEED + rank)
+    out = []
+    for sec in rng.uniform(2.0, 30.0, SEGMENTS):
+        t0 = int(sec * 100)
+        t1 = (t0 + 1) // 2
+        t2 = (t1 + 1) // 2
+        t3 = (t2 + 1) // 2
+        out.append((float(sec), t0, t2, t3))
+    return out
+
+
+def products(segs) -> list[dict]:
+    """The step's products: name, rows (N), n (K), M, add, bias, layer."""
+    t3 = sum(s[3] for s in segs)
+    r = sum(2 * s[3] - 1 for s in segs)
+    t2 = sum(s[2] for s in segs)
+    prods = [dict(name="sub_pw1", rows=C, n=C, M=t2 * 32, add=0, bias=1, layer=-1),
+             dict(name="sub_pw2", rows=C, n=C, M=t3 * 16, add=0, bias=1, layer=-1),
+             dict(name="sub_out", rows=D, n=F, M=t3, add=0, bias=1, layer=-1)]
+    for l in range(LAYERS):
+        prods += [dict(name="ff1_up", rows=F, n=D, M=t3, add=0, bias=0, layer=l),
+                  dict(name="ff1_down", rows=D, n=F, M=t3, add=1, bias=0, layer=l),
+                  dict(name="q", rows=D, n=D, M=t3, add=0, bias=0, layer=l),
+                  dict(name="k", rows=D, n=D, M=t3, add=0, bias=0, layer=l),
+                  dict(name="v", rows=D, n=D, M=t3, add=0, bias=0, layer=l),
+                  dict(name="pos", rows=D, n=D, M=r, add=0, bias=0, layer=l),
+                  dict(name="o", rows=D, n=D, M=t3, add=1, bias=0, layer=l),
+                  dict(name="pw1", rows=2 * D, n=D, M=t3, add=0, bias=0, layer=l),
+                  dict(name="pw2", rows=D, n=D, M=t3, add=1, bias=0, layer=l),
+                  dict(name="ff2_up", rows=F, n=D, M=t3, add=0, bias=0, layer=l),
+                  dict(name="ff2_down", rows=D, n=F, M=t3, add=1, bias=0, layer=l)]
+    return prods
+
+
+def step_ops(prods) -> float:
+    return float(sum(2.0 * p["M"] * p["rows"] * p["n"] for p in prods))
+
+
+def audio_seconds(segs) -> float:
+    return float(sum(s[0] for s in segs))
+
+
+# ------------------------------------------------------------------ clocks --
+
+class ClockSampler:
+    """nvidia-smi's clocks and throttle reasons, sampled every 200 ms while
+    the timed region runs."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------ CPU baseline --
+
+CPU_SAMPLE_M = 4096
+
+
+def cpu_baseline(prods, budget_s: float = 15.0) -> dict:
+    """The reference's own CPU backend (its picker's choice, oracle/_ref) on a
+    bounded sample: the subsampling's three products and one layer's eleven,
+    each at min(M, 4096) frames (the CPU's tiles stream frames, so its rate
+    per MAC does not depend on M past a few hundred), on every host core."""
+    import ctypes
+    so = os.path.join(ROOT, "oracle", "_ref", "libcpubench.so")
+    if not os.path.exists(so):
+        return {"value": None, "unit": "TOPS", "cores": None, "kind": "reference",
+                "sample": "unavailable: oracle/_ref/libcpubench.so not built"}
+    lib = ctypes.CDLL(so)
+    lib.cpub_backend.restype = ctypes.c_char_p
+    lib.cpub_backend.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
+    lib.cpub_time.restype = ctypes.c_double
+    lib.cpub_time.argtypes = [ctypes.c_uint32] * 5 + [ctypes.c_int, ctypes.c_int, ctypes.c_uint64,
+                                                      ctypes.POINTER(ctypes.c_double)]
+    picks = ctypes.create_string_buffer(512)
+    backend = lib.cpub_backend(picks, 512).decode()
+    cores = os.cpu_count() or 1
+    sample = [p for p in prods if p["layer"] in (-1, 0)]
+    ops = t = 0.0
+    qs = ctypes.c_double()
+    t_start = time.time()
+    reps = max(1, int(os.environ.get("PKB_CPU_REPS", "3")))
+    for p in sample:
+        m = min(p["M"], CPU_SAMPLE_M)
+        sec = lib.cpub_time(p["rows"], p["n"], m, QB, p["add"], cores, reps, 1, ctypes.byref(qs))
+        if sec <= 0:
+            continue
+        ops += 2.0 * m * p["rows"] * p["n"]
+        t += sec
+        if time.time() - t_start > budget_s:
+            break
+    value = ops / t / 1e12 if t > 0 else None
+    return {"value": value, "unit": "TOPS", "cores": cores, "kind": "reference",
+            "backend": backend, "picks": picks.value.decode(),
+            "sample": f"{len(sample)} products (subsampling + layer 0) at min(M, {CPU_SAMPLE_M}) frames, "
+                      f"quantize + product, best of {reps} timed runs after a warm one each; "
+                      f"{time.time() - t_start:.1f} s of CPU work, {t:.2f} s in the best runs"}
+
+
+# ------------------------------------------------------------ our GPU arm --
+
+class Model:
+    """Device-resident weights (PK_Q8 bytes repacked once, as at load time),
+    activations and outputs for one rank's workload."""
+
+    def __init__(self, prods, dev, seed):
+        import torch
+        import libpktito_b200 as P
+        self.P, self.torch = P, torch
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.w, self.ws, self.bias = {}, {}, {}
+        for p in prods:
+            key = (p["layer"], p["name"])
+            if key in self.w:
+                continue
+            rows, n = p["rows"], p["n"]
+            # random weights uniform in [-127, 127]: in the model file's PK_Q8
+            # panel order they are random bytes too; repacked on the device
+            # as at load time
+            w_pk = torch.randint(-127, 128, (rows * n,), dtype=torch.int8, device=dev, generator=g)
+            wpack = torch.empty(rows * n, dtype=torch.int8, device=dev)
+            P.repack_q8_dev(wpack, w_pk, rows, n)
+            self.w[key] = wpack
+            self.ws[key] = (1e-3 + 9e-3 * torch.rand(rows, device=dev, generator=g)).float()
+            self.bias[key] = torch.randn(rows, device=dev, generator=g) if p["bias"] else None
+        self.x, self.q, self.d, self.out = {}, {}, {}, {}
+        for p in prods:
+            xk = (p["M"], p["n"])
+            if xk not in self.x:
+                self.x[xk] = torch.randn(p["M"] * p["n"], device=dev, generator=g)
+                self.q[xk] = torch.empty(p["M"] * p["n"], dtype=torch.int8, device=dev)
+                self.d[xk] = torch.empty(p["M"] * p["n"] // QB, dtype=torch.float32, device=dev)
+            ok = (p["M"], p["rows"])
+            if ok not in self.out:
+                self.out[ok] = torch.zeros(p["M"] * p["rows"], device=dev)
+        self.prods = prods
+        torch.cuda.synchronize()
+
+    def step(self, stream=None):
+        P = self.P
+        for p in self.prods:
+            key, xk, ok = (p["layer"], p["name"]), (p["M"], p["n"]), (p["M"], p["rows"])
+            P.quantize_dev(self.q[xk], self.d[xk], self.x[xk], p["n"], p["M"], p["n"], QB, stream=stream)
+            P.gemm_q8_dev(self.out[ok], p["rows"], self.w[key], self.ws[key], self.bias[key], p["rows"],
+                          self.q[xk], self.d[xk], p["n"], QB, p["M"], bool(p["add"]), stream=stream)
+
+
+def kernel_roofline(model, prods) -> dict:
+    """The dominant kernel (the product) timed alone on its most frequent
+    shape, with CUDA events on its stream: achieved int8 TOPS over the
+    measured peak."""
+    torch, P = model.torch, model.P
+    p = next(x for x in prods if x["name"] == "ff1_up")
+    key, xk, ok = (p["layer"], p["name"]), (p["M"], p["n"]), (p["M"], p["rows"])
+    s = torch.cuda.current_stream()
+    for _ in range(3):
+        P.gemm_q8_dev(model.out[ok], p["rows"], model.w[key], model.ws[key], None, p["rows"], model.q[xk],
+                      model.d[xk], p["n"], QB, p["M"], False)
+    reps = 20
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.synchronize()
+    e0.record(s)
+    for _ in range(reps):
+        P.gemm_q8_dev(model.out[ok], p["rows"], model.w[key], model.ws[key], None, p["rows"], model.q[xk],
+                      model.d[xk], p["n"], QB, p["M"], False)
+    e1.record(s)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    achieved = 2.0 * p["M"] * p["rows"] * p["n"] / (ms * 1e-3) / 1e12
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        peaks = json.load(open(peaks_path))
+        peak, src = 2.0 * float(peaks["bf16_tflops"]), "of measured: 2 x bf16_tflops (burst) of MEASURED_PEAKS.json"
+    except (OSError, KeyError, ValueError):
+        peak, src = 2.0 * 1590.0, "of fallback: 2 x 1.59 PFLOP/s bf16"
+    traffic = None
+    prof = os.path.join(ROOT, "profiles", "gemm_q8_traffic.json")
+    if os.path.exists(prof):
+        try:
+            t = json.load(open(prof))
+            if (t.get("M"), t.get("rows"), t.get("n")) == (p["M"], p["rows"], p["n"]):
+                traffic = t.get("bytes_per_launch")
+        except (OSError, ValueError):
+            traffic = None
+    # the epilogue's own bound: one fp32 FMA (and a packed subtract) per
+    # output per block of 32 on the CUDA cores
+    return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "traffic": traffic, "kernel": "pkb::gemm::gemm_q8_kernel",
+            "shape": f"M {p['M']} x N {p['rows']} x K {p['n']}, qb {QB}", "ms_per_launch": ms,
+            "peak_note": src + "; int8 dense is twice bf16 dense on B200 (4.5 vs 2.25 PFLOP/s nominal)",
+            "algorithmic_ops_per_launch": 2.0 * p["M"] * p["rows"] * p["n"]}
+
+
+def e2e_host(prods, steps: int, seed: int) -> dict:
+    """The same step through the reference-facing table (pk_kernels_cuda_b200:
+    quantize and gemm_q8 on HOST buffers, copies inside each call), as the
+    reference's passes would call the backend, whole matrices a call."""
+    import libpktito_b200 as P
+    tab = P.Table()
+    rng = np.random.default_rng(seed)
+    w, ws, bias = {}, {}, {}
+    xs, qs, ds, outs = {}, {}, {}, {}
+    for p in prods:
+        key = (p["layer"], p["name"])
+        if key not in w:
+            w[key] = rng.integers(-127, 128, p["rows"] * p["n"], dtype=np.int8)  # PK_Q8 bytes, random
+            ws[key] = (1e-3 + 9e-3 * rng.random(p["rows"])).astype(np.float32)
+            bias[key] = rng.standard_normal(p["rows"]).astype(np.float32) if p["bias"] else None
+        xk, ok = (p["M"], p["n"]), (p["M"], p["rows"])
+        if xk not in xs:
+            xs[xk] = rng.standard_normal(p["M"] * p["n"], dtype=np.float32)
+            qs[xk] = np.empty(p["M"] * p["n"], np.int8)
+            ds[xk] = np.empty(p["M"] * p["n"] // QB, np.float32)
+        if ok not in outs:
+            outs[ok] = np.zeros(p["M"] * p["rows"], np.float32)
+    h2d = d2h = 0
+    for p in prods:
+        nb = p["n"] // QB
+        h2d += p["M"] * p["n"] * 4 + p["M"] * (p["n"] + 4 * nb) + 8 * p["rows"] + (p["M"] * p["rows"] * 4 if p["add"] else 0)
+        d2h += p["M"] * (p["n"] + 4 * nb) + p["M"] * p["rows"] * 4
+
+    def one():
+        for p in prods:
+            key, xk, ok = (p["layer"], p["name"]), (p["M"], p["n"]), (p["M"], p["rows"])
+            act = P.PkAct(qs[xk].ctypes.data, ds[xk].ctypes.data, p["n"], QB, p["M"])
+            tab.quantize(act, xs[xk], p["n"])
+            tab.gemm_q8(outs[ok], p["rows"], w[key], ws[key], bias[key], p["rows"], act, bool(p["add"]))
+
+    one()  # uploads and caches the weights, grows the staging buffers
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one()
+    sec = (time.perf_counter() - t0) / steps
+    return {"seconds_per_step": sec, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+
+# -------------------------------------------------------------- the arms --
+
+def dist_setup(gpus: int):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    pg = None
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+    return rank, world, local, pg
+
+
+def run_ours(args) -> None:
+    import torch
+    rank, world, local, dist = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    import libpktito_b200 as P
+    P.set_thread_device(local)
+    dev = torch.device("cuda", local)
+    segs = segments(rank)
+    prods = products(segs)
+    ops = step_ops(prods)
+    model = Model(prods, dev, SEED + 1000 * rank)
+
+    def barrier():
+        if dist:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        model.step()
+    l0 = P.launch_count()
+    model.step()
+    launches_per_step = P.launch_count() - l0
+    graph = None
+    if not args.no_graph:
+        # the step captured once and replayed: no host work between launches
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            model.step()
+        graph.replay()
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_wall = time.perf_counter()
+    e0.record(stream)
+    for _ in range(args.steps):
+        if graph:
+            graph.replay()
+        else:
+            model.step()
+    e1.record(stream)
+    barrier()
+    wall = time.perf_counter() - t_wall
+    ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    if P.device_errors(local):
+        raise RuntimeError("a kernel reported a timeout during the timed steps")
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    used_graph = graph is not None
+    del graph  # released before the process group goes (it holds no collective, but keep the order safe)
+    roof = kernel_roofline(model, prods) if rank == 0 else None
+    e2e = None
+    if rank == 0 and not args.no_e2e:
+        e = e2e_host(prods, args.e2e_steps, SEED + 7)
+        e2e = {"value": ops / e["seconds_per_step"] / 1e12, "unit": "TOPS",
+               "h2d_bytes_per_step": e["h2d_bytes_per_step"], "d2h_bytes_per_step": e["d2h_bytes_per_step"],
+               "audio_s_per_s": audio_seconds(segs) / e["seconds_per_step"],
+               "path": "pk_kernels_cuda_b200 table (quantize + gemm_q8 on host buffers), whole matrices a call",
+               "steps": args.e2e_steps}
+    cpu = cpu_baseline(prods) if (rank == 0 and world == 1 and not args.no_cpu) else None
+    if dist:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    ms_step = ms / args.steps
+    value = ops * world / (ms_step * 1e-3) / 1e12
+    t3 = sum(s[3] for s in segs)
+    line = {
+        "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded segments, random int8 weights, N(0,1) activations)",
+        "config": {"workload": "configs[3] batched encoder: 64 segments of 2-30 s per GPU, 24 layers x 11 products "
+                               "+ 3 subsampling products, quantize + product each, qb 32",
+                   "segments_per_gpu": SEGMENTS, "encoder_frames_per_gpu": t3, "layers": LAYERS, "d_model": D,
+                   "ff_dim": F, "qb": QB, "global_batch": SEGMENTS * world, "seq_len": t3 // SEGMENTS,
+                   "parallelism": f"dp{world}", "l2": "no flush: each step streams 576 MiB of weights and "
+                                                       "~1.4 GB of activations, well over the 126 MB L2",
+                   "cuda_graph": used_graph},
+        "audio_s_per_s": audio_seconds(segs) * world / (ms_step * 1e-3),
+        "ops_per_step": ops * world, "wall_s": wall,
+        "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "clocks": clk,
+        "roofline": roof, "cpu_baseline": cpu,
+    }
+    print(json.dumps(line))
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    segs = segments(0)
+    prods = products(segs)
+    ops = step_ops(prods)
+    cpu = None
+    times = []
+    for i in range(args.warmup + args.steps):
+        c = cpu_baseline(prods, budget_s=20.0)
+        if c["value"] is None:
+            print(json.dumps({"impl": "reference", "unavailable": c["sample"]}))
+            return
+        if i >= args.warmup:
+            times.append(c["value"])
+        cpu = c
+    value = float(np.median(times))
+    step_s = ops / (value * 1e12)
+    cpu["value"] = value
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (seeded segments, random int8 weights, N(0,1) activations)",
+            "config": {"workload": "configs[3] batched encoder (as the GPU arm); each step times the reference's "
+                                   "CPU backend on a sample (subsampling + one layer's products at the batch's M) "
+                                   "and scales to the step", "segments": SEGMENTS, "layers": LAYERS, "qb": QB},
+            "audio_s_per_s": audio_seconds(segs) / step_s,
+            "cpu_baseline": cpu,
+            "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def run_kernel_only() -> None:
+    """The dominant product alone: quantize once, then three launches of the
+    product kernel on the FF-up shape at the batch's M (11521 x 4096 x 1024,
+    qb 32; 12 MB of activations, 4 MB of weights, 189 MB of output, which
+    is more than the 126 MB L2)."""
+    import torch
+    import libpktito_b200 as P
+    segs = segments(0)
+    p = next(x for x in products(segs) if x["name"] == "ff1_up")
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(SEED)
+    M, rows, n = p["M"], p["rows"], p["n"]
+    x = torch.randn(M * n, device=dev, generator=g)
+    q = torch.empty(M * n, dtype=torch.int8, device=dev)
+    d = torch.empty(M * n // QB, device=dev)
+    w_pk = torch.randint(-127, 128, (rows * n,), dtype=torch.int8, device=dev, generator=g)
+    wpack = torch.empty_like(w_pk)
+    ws = 1e-3 + 9e-3 * torch.rand(rows, device=dev, generator=g)
+    out = torch.zeros(M * rows, device=dev)
+    P.quantize_dev(q, d, x, n, M, n, QB)
+    P.repack_q8_dev(wpack, w_pk, rows, n)
+    for _ in range(3):
+        P.gemm_q8_dev(out, rows, wpack, ws, None, rows, q, d, n, QB, M, False)
+    torch.cuda.synchronize()
+    print(json.dumps({"kernel_only": f"M {M} x N {rows} x K {n} qb {QB}", "launches": P.launch_count(),
+                      "device_errors": P.device_errors(0)}))
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=1)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="only the dominant product (FF up at the batch's M), 3 launches: the ncu capture's case")
+    args = ap.parse_args()
+    if args.kernel_only:
+        run_kernel_only()
+    elif args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

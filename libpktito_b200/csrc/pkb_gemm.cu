@@ -430,10 +430,21 @@ static cudaError_t launch_rm(const CUtensorMap& ma, const CUtensorMap& mb, const
         kern = g.qb <= 64 ? gemm_q8_kernel<RM, EXACT_SUM, 2, true> : gemm_q8_kernel<RM, EXACT_SUM, 1, true>;
     else
         kern = g.qb <= 64 ? gemm_q8_kernel<RM, EXACT_SUM, 2, false> : gemm_q8_kernel<RM, EXACT_SUM, 1, false>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (e != cudaSuccess) return e;
     kern<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, md ? *md : ma, g);
     return cudaGetLastError();
+}
+
+// Every instance's dynamic shared memory allowance, on the current device.
+template <int RM, bool EXACT_SUM>
+static cudaError_t prepare_rm() {
+    void (*k[4])(CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs) = {
+        gemm_q8_kernel<RM, EXACT_SUM, 1, false>, gemm_q8_kernel<RM, EXACT_SUM, 2, false>,
+        gemm_q8_kernel<RM, EXACT_SUM, 1, true>, gemm_q8_kernel<RM, EXACT_SUM, 2, true>};
+    for (auto f : k) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 }  // namespace gemm
@@ -443,6 +454,18 @@ int gemm_tile_cols() { return gemm::BN; }
 int gemm_box_k() { return gemm::BK; }
 
 int gemm_scale_chunk() { return gemm::DCHUNK; }
+
+cudaError_t prepare_gemm_q8() {
+    cudaError_t e;
+    if ((e = gemm::prepare_rm<0, false>()) != cudaSuccess) return e;
+    if ((e = gemm::prepare_rm<0, true>()) != cudaSuccess) return e;
+    if ((e = gemm::prepare_rm<1, false>()) != cudaSuccess) return e;
+    if ((e = gemm::prepare_rm<1, true>()) != cudaSuccess) return e;
+    if ((e = gemm::prepare_rm<2, false>()) != cudaSuccess) return e;
+    if ((e = gemm::prepare_rm<2, true>()) != cudaSuccess) return e;
+    if ((e = gemm::prepare_rm<3, false>()) != cudaSuccess) return e;
+    return gemm::prepare_rm<3, true>();
+}
 
 cudaError_t launch_gemm_q8(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap* map_d,
                            const GemmArgs& g, int num_sms, int rmode, cudaStream_t stream) {

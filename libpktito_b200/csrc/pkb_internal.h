@@ -26,6 +26,10 @@ int gemm_tile_cols();   // output rows a tile (TMA box of the weights)
 int gemm_box_k();       // inputs of K a TMA box
 int gemm_scale_chunk(); // blocks of scales a TMA box of the scales carries
 
+// Sets the product kernels' launch attributes on the current device (once,
+// at the device's set-up, outside any stream capture).
+cudaError_t prepare_gemm_q8();
+
 // map_d: a tensor map of the block scales d [T][n/qb] (float32, boxes of
 // gemm_scale_chunk() blocks by gemm_tile_rows() frames), or null to read
 // them from global memory directly
