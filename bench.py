@@ -3,7 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload ("batched encoder"): 64 independent
+Workload (the benchmark configuration "batched encoder"): 64 independent
 segments of seeded lengths uniform in 2-30 s (25-375 encoder frames each),
 through the int8 GEMM path of a 24-layer, d_model 1024 Parakeet-shaped
 encoder with random int8 weights: per layer its eleven products (feed-forward

@@ -126,7 +126,7 @@ static void k_resample(float *y, const float *x, uint32_t nb, uint32_t orig, uin
 /* The CPU features it needs. The reference's picker (backend/kernels.c:
  * 227-236) takes the first backend whose needs the CPU meets, so inside
  * the reference's tree this names "cuda", which core/os.c's cpu_has answers
- * from pkb_device_count(); built alone, nothing, and a
+ * from pkb_device_count() (a one-line addition there); built alone, nothing, and a
  * caller selects it by name (PKTITO_KERNELS=cuda-b200) or by its place in
  * a list. */
 #ifdef PK_CUDA_B200_NEEDS_CUDA
