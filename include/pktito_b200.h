@@ -116,6 +116,29 @@ int pkb_gemm_q8_dev(void *stream, float *out, size_t os, const int8_t *wpack, co
  * device: the evidence a benchmark reports for its own kernels' work. */
 uint64_t pkb_launch_count(void);
 
+/* ------------------------------------------------- without allocating -- */
+
+/* Bytes of the fixed device staging pkb_quantize_host_noalloc works in. */
+#define PKB_NOALLOC_BYTES (8u << 20)
+
+/* pkb_quantize_host's result, for callers that cannot allocate memory when
+ * they quantize: an application that gives all of a GPU's memory to its own
+ * pool at start-up, or a real-time audio callback in which an allocation (it
+ * can synchronize the whole device) is not allowed. It calls no cudaMalloc,
+ * cudaMallocHost or cudaFree: the device staging is one array of
+ * PKB_NOALLOC_BYTES compiled into the library, which every GPU that loads the
+ * library holds until the process exits; the columns are copied straight from
+ * the caller's memory. T * n * (5 + 4/qb) bytes (each of the three parts
+ * rounded up to 256) must fit in it, or the call fails with PKB_EINVAL and
+ * does nothing. The first call on a device asks the runtime for the array's
+ * address on that device; make it before starting any stream capture. Calls
+ * share the array: calls in one process are serialized and each waits for
+ * its GPU work before returning, because two calls whose GPU work overlapped
+ * would race on it.
+ * No counterpart in the reference: its backends never allocate per call. */
+int pkb_quantize_host_noalloc(int8_t *q, float *d, uint32_t n, uint32_t qb, uint32_t T, const float *x,
+                              size_t xs, int rmode);
+
 #ifdef __cplusplus
 }
 #endif

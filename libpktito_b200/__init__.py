@@ -83,6 +83,8 @@ _SIGS = {
                                        ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
                                        ctypes.c_int, ctypes.c_int]),
     "pkb_launch_count": (ctypes.c_uint64, []),
+    "pkb_quantize_host_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,
+                                                 ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]),
 }
 
 

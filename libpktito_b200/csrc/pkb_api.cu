@@ -385,6 +385,15 @@ int weights_for(HostCtx* c, Device* dev, const int8_t* w, uint32_t rows, uint32_
 }
 
 }  // namespace
+
+int set_error(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(tl_err, sizeof tl_err, fmt, ap);
+    va_end(ap);
+    return code;
+}
+
 }  // namespace pkb
 
 using namespace pkb;

@@ -8,6 +8,10 @@
 
 namespace pkb {
 
+// Records the calling thread's error message (what pkb_last_error returns)
+// and returns code.
+int set_error(int code, const char* fmt, ...);
+
 // Arguments of the product kernel (pkb_gemm.cu) besides its two tensor maps.
 struct GemmArgs {
     float* out;            // out[t*os + r]
