@@ -292,42 +292,63 @@ def kernel_roofline(model, prods) -> dict:
             "algorithmic_ops_per_launch": 2.0 * p["M"] * p["rows"] * p["n"]}
 
 
-def e2e_host(prods, steps: int, seed: int) -> dict:
+def e2e_host(prods, steps: int, seed: int, lanes: int) -> dict:
     """The same step through the reference-facing table (pk_kernels_cuda_b200:
-    quantize and gemm_q8 on HOST buffers, copies inside each call), as the
-    reference's passes would call the backend, whole matrices a call."""
+    quantize and gemm_q8 on HOST buffers, copies inside each call), called
+    as the reference engine calls a backend: whole matrices a call, from
+    `lanes` threads at once, each lane its own products' outputs and
+    activations (the reference runs independent chunks in lanes the same
+    way, core/asr.c:346-572; every call is synchronous, and ctypes releases
+    the interpreter while it runs)."""
+    import threading
     import libpktito_b200 as P
     tab = P.Table()
     rng = np.random.default_rng(seed)
-    w, ws, bias = {}, {}, {}
-    xs, qs, ds, outs = {}, {}, {}, {}
+    w, ws, bias, xs = {}, {}, {}, {}
     for p in prods:
-        key = (p["layer"], p["name"])
+        key, xk = (p["layer"], p["name"]), (p["M"], p["n"])
         if key not in w:
             w[key] = rng.integers(-127, 128, p["rows"] * p["n"], dtype=np.int8)  # PK_Q8 bytes, random
             ws[key] = (1e-3 + 9e-3 * rng.random(p["rows"])).astype(np.float32)
             bias[key] = rng.standard_normal(p["rows"]).astype(np.float32) if p["bias"] else None
-        xk, ok = (p["M"], p["n"]), (p["M"], p["rows"])
         if xk not in xs:
             xs[xk] = rng.standard_normal(p["M"] * p["n"], dtype=np.float32)
-            qs[xk] = np.empty(p["M"] * p["n"], np.int8)
-            ds[xk] = np.empty(p["M"] * p["n"] // QB, np.float32)
-        if ok not in outs:
-            outs[ok] = np.zeros(p["M"] * p["rows"], np.float32)
+    lane_prods = [prods[i::lanes] for i in range(lanes)]
+    bufs = []
+    for lp in lane_prods:
+        qs, ds, outs = {}, {}, {}
+        for p in lp:
+            xk, ok = (p["M"], p["n"]), (p["M"], p["rows"])
+            if xk not in qs:
+                qs[xk] = np.empty(p["M"] * p["n"], np.int8)
+                ds[xk] = np.empty(p["M"] * p["n"] // QB, np.float32)
+            if ok not in outs:
+                outs[ok] = np.zeros(p["M"] * p["rows"], np.float32)
+        bufs.append((qs, ds, outs))
     h2d = d2h = 0
     for p in prods:
         nb = p["n"] // QB
         h2d += p["M"] * p["n"] * 4 + p["M"] * (p["n"] + 4 * nb) + 8 * p["rows"] + (p["M"] * p["rows"] * 4 if p["add"] else 0)
         d2h += p["M"] * (p["n"] + 4 * nb) + p["M"] * p["rows"] * 4
+    device = __import__("torch").cuda.current_device()
 
-    def one():
-        for p in prods:
+    def lane(i: int):
+        P.set_thread_device(device)
+        qs, ds, outs = bufs[i]
+        for p in lane_prods[i]:
             key, xk, ok = (p["layer"], p["name"]), (p["M"], p["n"]), (p["M"], p["rows"])
             act = P.PkAct(qs[xk].ctypes.data, ds[xk].ctypes.data, p["n"], QB, p["M"])
             tab.quantize(act, xs[xk], p["n"])
             tab.gemm_q8(outs[ok], p["rows"], w[key], ws[key], bias[key], p["rows"], act, bool(p["add"]))
 
-    one()  # uploads and caches the weights, grows the staging buffers
+    def one():
+        ts = [threading.Thread(target=lane, args=(i,)) for i in range(lanes)]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+
+    one()  # uploads and caches the weights, grows each lane's staging
     t0 = time.perf_counter()
     for _ in range(steps):
         one()
@@ -412,12 +433,12 @@ def run_ours(args) -> None:
     roof = kernel_roofline(model, prods) if rank == 0 else None
     e2e = None
     if rank == 0 and not args.no_e2e:
-        e = e2e_host(prods, args.e2e_steps, SEED + 7)
+        e = e2e_host(prods, args.e2e_steps, SEED + 7, args.e2e_lanes)
         e2e = {"value": ops / e["seconds_per_step"] / 1e12, "unit": "TOPS",
                "h2d_bytes_per_step": e["h2d_bytes_per_step"], "d2h_bytes_per_step": e["d2h_bytes_per_step"],
                "audio_s_per_s": audio_seconds(segs) / e["seconds_per_step"],
-               "path": "pk_kernels_cuda_b200 table (quantize + gemm_q8 on host buffers), whole matrices a call",
-               "steps": args.e2e_steps}
+               "path": "pk_kernels_cuda_b200 table (quantize + gemm_q8 on host buffers), whole matrices a call, "
+                       f"{args.e2e_lanes} lanes of calls at once", "steps": args.e2e_steps, "lanes": args.e2e_lanes}
     cpu = cpu_baseline(prods) if (rank == 0 and world == 1 and not args.no_cpu) else None
     if dist:
         dist.barrier(device_ids=[local])
@@ -514,6 +535,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=1)
+    ap.add_argument("--e2e-lanes", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-graph", action="store_true")

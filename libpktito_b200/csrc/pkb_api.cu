@@ -1,12 +1,7 @@
-// The C ABI of libpktito_b200 (include/pktito_b200.h): argument checks,
-// tensor maps, launches, and the host-pointer contract of the reference's
-// backend table (backend/kernels.h:47-78) on top of the device kernels.
+// The device side of the C ABI of libpktito_b200 (include/pktito_b200.h):
+// argument checks, device set-up, tensor maps and launches.
 //
-// Host-pointer calls arrive synchronously, from any number of the caller's
-// threads at once (the reference's pool calls a backend's gemm_q8 from every
-// worker, core/pool.c:115-122, on disjoint outputs). Each calling thread
-// gets its own CUDA stream and its own device and pinned host scratch, grown
-// as needed and kept; matrices are uploaded once per device and shared.
+// The host-pointer entry points are in pkb_host.cu.
 
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -230,161 +225,18 @@ int repack_dev(cudaStream_t stream, int8_t* wpack, const int8_t* w_pk, uint32_t 
     return PKB_OK;
 }
 
-// ----------------------------------------------------- host-pointer path --
-
-size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
-
-// One calling thread's stream and scratch on its device.
-struct HostCtx {
-    int dev = -1;
-    cudaStream_t stream = nullptr;
-    uint8_t* dbuf = nullptr;  // device scratch
-    size_t dcap = 0;
-    uint8_t* hbuf = nullptr;  // pinned host scratch
-    size_t hcap = 0;
-    uint32_t* herr = nullptr;  // pinned copy of the error word
-    ~HostCtx() { release(); }
-    void release() {
-        if (dev < 0) return;
-        int cur = -1;
-        if (cudaGetDevice(&cur) == cudaSuccess) {
-            cudaSetDevice(dev);
-            if (stream) cudaStreamDestroy(stream);
-            if (dbuf) cudaFree(dbuf);
-            if (hbuf) cudaFreeHost(hbuf);
-            if (herr) cudaFreeHost(herr);
-            if (cur >= 0) cudaSetDevice(cur);
-        }
-        stream = nullptr;
-        dbuf = nullptr;
-        hbuf = nullptr;
-        herr = nullptr;
-        dcap = hcap = 0;
-        dev = -1;
-    }
-};
-
-thread_local int tl_device = 0;
-thread_local HostCtx tl_ctx;
-
-int host_ctx(HostCtx** out, size_t dbytes, size_t hbytes) {
-    HostCtx& c = tl_ctx;
-    if (c.dev != tl_device) c.release();
-    PKB_CUDA(cudaSetDevice(tl_device), "cudaSetDevice");
-    Device* dev;
-    int rc = current_device(&dev);
-    if (rc) return rc;
-    if (c.dev < 0) {
-        c.dev = tl_device;
-        PKB_CUDA(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking), "cudaStreamCreate");
-        PKB_CUDA(cudaMallocHost(&c.herr, sizeof(uint32_t)), "cudaMallocHost");
-    }
-    if (dbytes > c.dcap) {
-        if (c.dbuf) cudaFree(c.dbuf);
-        c.dbuf = nullptr;
-        c.dcap = 0;
-        const size_t want = up256(dbytes + dbytes / 4);
-        PKB_CUDA(cudaMalloc(&c.dbuf, want), "cudaMalloc (scratch)");
-        c.dcap = want;
-    }
-    if (hbytes > c.hcap) {
-        if (c.hbuf) cudaFreeHost(c.hbuf);
-        c.hbuf = nullptr;
-        c.hcap = 0;
-        const size_t want = up256(hbytes + hbytes / 4);
-        PKB_CUDA(cudaMallocHost(&c.hbuf, want), "cudaMallocHost (staging)");
-        c.hcap = want;
-    }
-    *out = &c;
-    return PKB_OK;
-}
-
-// Waits for this thread's stream, then reads and clears the device error
-// word; a kernel that gave up makes the call fail.
-int finish(HostCtx* c, Device* dev) {
-    PKB_CUDA(cudaMemcpyFromSymbolAsync(c->herr, g_device_error, sizeof(uint32_t), 0, cudaMemcpyDeviceToHost,
-                                       c->stream),
-             "error word read");
-    PKB_CUDA(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
-    if (*c->herr) {
-        const uint32_t w = *c->herr;
-        const uint32_t zero = 0;
-        cudaMemcpyToSymbol(g_device_error, &zero, sizeof zero);
-        (void)dev;
-        return fail(PKB_ETIMEOUT, "a kernel gave up waiting (device error word 0x%x)", w);
-    }
-    return PKB_OK;
-}
-
-// A matrix uploaded to one device: the host bytes it came from, a copy of
-// them to tell whether they still are what was uploaded, and its repacked
-// rows on the device.
-struct Matrix {
-    const int8_t* host;
-    uint32_t rows, n;
-    int dev;
-    std::vector<int8_t> shadow;
-    int8_t* wpack;
-};
-
-std::mutex g_mat_mu;
-std::vector<Matrix*> g_mats;
-std::vector<Matrix*> g_stale;  // replaced while maybe in use elsewhere: freed by pkb_forget
-
-// The device rows for `rows` rows of the PK_Q8 matrix at host address w (a
-// run of whole panels, possibly from inside a matrix uploaded before).
-int weights_for(HostCtx* c, Device* dev, const int8_t* w, uint32_t rows, uint32_t n, const int8_t** wpack) {
-    const size_t bytes = static_cast<size_t>(rows) * n;
-    Matrix* hit = nullptr;
-    size_t row0 = 0;
-    {
-        std::lock_guard<std::mutex> lock(g_mat_mu);
-        for (Matrix* m : g_mats) {
-            if (m->dev != c->dev || m->n != n) continue;
-            const uintptr_t lo = reinterpret_cast<uintptr_t>(m->host);
-            const uintptr_t p = reinterpret_cast<uintptr_t>(w);
-            if (p < lo || p + bytes > lo + static_cast<size_t>(m->rows) * n) continue;
-            if ((p - lo) % (16 * static_cast<size_t>(n))) continue;  // not on a panel boundary
-            hit = m;
-            row0 = (p - lo) / n;
-            break;
-        }
-    }
-    if (hit && memcmp(hit->shadow.data() + row0 * n, w, bytes) == 0) {
-        *wpack = hit->wpack + row0 * n;
-        return PKB_OK;
-    }
-    if (hit) {  // the bytes at that address changed: retire the old upload
-        std::lock_guard<std::mutex> lock(g_mat_mu);
-        for (size_t i = 0; i < g_mats.size(); i++)
-            if (g_mats[i] == hit) {
-                g_mats.erase(g_mats.begin() + static_cast<long>(i));
-                g_stale.push_back(hit);
-                break;
-            }
-    }
-    Matrix* m = new Matrix{w, rows, n, c->dev, std::vector<int8_t>(w, w + bytes), nullptr};
-    cudaError_t e = cudaMalloc(&m->wpack, bytes);
-    if (e != cudaSuccess) {
-        delete m;
-        return cuda_fail(e, "cudaMalloc (weights)");
-    }
-    // the panels through this thread's scratch, repacked into place
-    memcpy(c->hbuf, w, bytes);
-    PKB_CUDA(cudaMemcpyAsync(c->dbuf, c->hbuf, bytes, cudaMemcpyHostToDevice, c->stream), "weights upload");
-    PKB_CUDA(launch_repack_q8(m->wpack, reinterpret_cast<int8_t*>(c->dbuf), rows, n, dev->sms, c->stream),
-             "repack launch");
-    g_launches.fetch_add(1, std::memory_order_relaxed);
-    PKB_CUDA(cudaStreamSynchronize(c->stream), "weights upload");
-    {
-        std::lock_guard<std::mutex> lock(g_mat_mu);
-        g_mats.push_back(m);
-    }
-    *wpack = m->wpack;
-    return PKB_OK;
-}
-
 }  // namespace
+
+int current_device_info(int* sms, uint32_t** err_word) {
+    Device* d;
+    const int rc = current_device(&d);
+    if (rc) return rc;
+    *sms = d->sms;
+    *err_word = d->err;
+    return PKB_OK;
+}
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int set_error(int code, const char* fmt, ...) {
     va_list ap;
@@ -414,14 +266,6 @@ int pkb_device_count(void) {
         if (cudaGetDeviceProperties(&prop, i) == cudaSuccess && prop.major == 10) ok++;
     }
     return ok;
-}
-
-int pkb_set_thread_device(int device) {
-    int n = 0;
-    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n || device >= MAX_DEV)
-        return fail(PKB_ENODEV, "device %d is not present", device);
-    tl_device = device;
-    return PKB_OK;
 }
 
 int pkb_device_errors(int device, uint32_t* word) {
@@ -455,116 +299,6 @@ int pkb_gemm_q8_dev(void* stream, float* out, size_t os, const int8_t* wpack, co
                     uint32_t rows, const int8_t* q, const float* d, uint32_t n, uint32_t qb, uint32_t T, int add,
                     int rmode) {
     return gemm_dev(static_cast<cudaStream_t>(stream), out, os, wpack, ws, bias, rows, q, d, n, qb, T, add, rmode);
-}
-
-int pkb_quantize_host(int8_t* q, float* d, uint32_t n, uint32_t qb, uint32_t T, const float* x, size_t xs,
-                      int rmode) {
-    int rc = check_act_shape(n, qb);
-    if (rc) return rc;
-    if ((rc = check_rmode(rmode))) return rc;
-    if (!T) return PKB_OK;
-    if (!q || !d || !x) return fail(PKB_EINVAL, "quantize: null pointer");
-    if (xs < n) return fail(PKB_EINVAL, "quantize: column stride %zu below n = %u", xs, n);
-    const uint32_t nb = n / qb;
-    const size_t xbytes = static_cast<size_t>(T) * n * 4;
-    const size_t qbytes = static_cast<size_t>(T) * n, dbytes = static_cast<size_t>(T) * nb * 4;
-    const size_t off_q = up256(xbytes), off_d = off_q + up256(qbytes), total = off_d + up256(dbytes);
-    HostCtx* c;
-    if ((rc = host_ctx(&c, total, total))) return rc;
-    Device* dev;
-    if ((rc = current_device(&dev))) return rc;
-    // the columns, packed (n floats each) into the staging buffer
-    float* hx = reinterpret_cast<float*>(c->hbuf);
-    if (xs == n)
-        memcpy(hx, x, xbytes);
-    else
-        for (uint32_t t = 0; t < T; t++) memcpy(hx + static_cast<size_t>(t) * n, x + t * xs, static_cast<size_t>(n) * 4);
-    PKB_CUDA(cudaMemcpyAsync(c->dbuf, c->hbuf, xbytes, cudaMemcpyHostToDevice, c->stream), "quantize upload");
-    if ((rc = quantize_dev(c->stream, reinterpret_cast<int8_t*>(c->dbuf + off_q), reinterpret_cast<float*>(c->dbuf + off_d),
-                           reinterpret_cast<const float*>(c->dbuf), n, T, n, qb, rmode)))
-        return rc;
-    PKB_CUDA(cudaMemcpyAsync(c->hbuf + off_q, c->dbuf + off_q, off_d + dbytes - off_q, cudaMemcpyDeviceToHost,
-                             c->stream),
-             "quantize download");
-    if ((rc = finish(c, dev))) return rc;
-    memcpy(q, c->hbuf + off_q, qbytes);
-    memcpy(d, c->hbuf + off_d, dbytes);
-    return PKB_OK;
-}
-
-int pkb_gemm_q8_host(float* out, size_t os, const int8_t* w, const float* ws, const float* bias, uint32_t rows,
-                     const int8_t* q, const float* d, uint32_t n, uint32_t qb, uint32_t T, int add, int rmode) {
-    int rc = check_act_shape(n, qb);
-    if (rc) return rc;
-    if ((rc = check_rmode(rmode))) return rc;
-    if (rows % 16) return fail(PKB_EINVAL, "rows = %u: a multiple of 16", rows);
-    if (os < rows) return fail(PKB_EINVAL, "output stride %zu below rows = %u", os, rows);
-    if (!T || !rows) return PKB_OK;
-    if (!out || !w || !ws || !q || !d) return fail(PKB_EINVAL, "gemm_q8: null pointer");
-    const uint32_t nb = n / qb;
-    const size_t qbytes = static_cast<size_t>(T) * n, dbytes = static_cast<size_t>(T) * nb * 4;
-    const size_t vbytes = static_cast<size_t>(rows) * 4, obytes = static_cast<size_t>(T) * rows * 4;
-    const size_t off_d = up256(qbytes), off_ws = off_d + up256(dbytes), off_b = off_ws + up256(vbytes);
-    const size_t off_o = off_b + up256(vbytes), total = off_o + up256(obytes);
-    const size_t wbytes = static_cast<size_t>(rows) * n;
-    HostCtx* c;
-    if ((rc = host_ctx(&c, total > wbytes ? total : wbytes, total > wbytes ? total : wbytes))) return rc;
-    Device* dev;
-    if ((rc = current_device(&dev))) return rc;
-    const int8_t* wpack;
-    if ((rc = weights_for(c, dev, w, rows, n, &wpack))) return rc;
-
-    uint8_t* h = c->hbuf;
-    memcpy(h, q, qbytes);
-    memcpy(h + off_d, d, dbytes);
-    memcpy(h + off_ws, ws, vbytes);
-    if (bias) memcpy(h + off_b, bias, vbytes);
-    float* ho = reinterpret_cast<float*>(h + off_o);
-    if (add)
-        for (uint32_t t = 0; t < T; t++) memcpy(ho + static_cast<size_t>(t) * rows, out + t * os, vbytes);
-    const size_t up = add ? off_o + obytes : off_o;
-    PKB_CUDA(cudaMemcpyAsync(c->dbuf, h, up, cudaMemcpyHostToDevice, c->stream), "gemm_q8 upload");
-    uint8_t* db = c->dbuf;
-    if ((rc = gemm_dev(c->stream, reinterpret_cast<float*>(db + off_o), rows, wpack,
-                       reinterpret_cast<const float*>(db + off_ws), bias ? reinterpret_cast<const float*>(db + off_b) : nullptr,
-                       rows, reinterpret_cast<const int8_t*>(db), reinterpret_cast<const float*>(db + off_d), n, qb, T,
-                       add, rmode)))
-        return rc;
-    PKB_CUDA(cudaMemcpyAsync(ho, db + off_o, obytes, cudaMemcpyDeviceToHost, c->stream), "gemm_q8 download");
-    if ((rc = finish(c, dev))) return rc;
-    for (uint32_t t = 0; t < T; t++) memcpy(out + t * os, ho + static_cast<size_t>(t) * rows, vbytes);
-    return PKB_OK;
-}
-
-int pkb_forget(const void* p, size_t bytes) {
-    const uintptr_t lo = reinterpret_cast<uintptr_t>(p), hi = lo + bytes;
-    std::vector<Matrix*> drop;
-    {
-        std::lock_guard<std::mutex> lock(g_mat_mu);
-        for (size_t i = 0; i < g_mats.size();) {
-            Matrix* m = g_mats[i];
-            const uintptr_t mlo = reinterpret_cast<uintptr_t>(m->host);
-            const uintptr_t mhi = mlo + static_cast<size_t>(m->rows) * m->n;
-            if (mlo < hi && lo < mhi) {
-                drop.push_back(m);
-                g_mats.erase(g_mats.begin() + static_cast<long>(i));
-            } else {
-                i++;
-            }
-        }
-        drop.insert(drop.end(), g_stale.begin(), g_stale.end());
-        g_stale.clear();
-    }
-    int cur = -1;
-    cudaGetDevice(&cur);
-    for (Matrix* m : drop) {
-        cudaSetDevice(m->dev);
-        cudaDeviceSynchronize();
-        cudaFree(m->wpack);
-        delete m;
-    }
-    if (cur >= 0) cudaSetDevice(cur);
-    return PKB_OK;
 }
 
 }  // extern "C"

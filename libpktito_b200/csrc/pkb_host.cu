@@ -1,0 +1,591 @@
+// The host-pointer contract of libpktito's backend table
+// (backend/kernels.h:47-78): pkb_quantize_host, pkb_gemm_q8_host,
+// pkb_forget, pkb_set_thread_device.
+//
+// A call gets host pointers and returns when its results are in host memory,
+// so its cost is mostly copies: the inputs up over PCIe, the results back. A
+// call is cut into chunks of frames and run as a pipeline over two slots of
+// pinned and device staging: while chunk c's inputs go up (one stream) and
+// chunk c-1's results come down (another), the kernels of the chunk between
+// run on a third, and the host copies the next chunk's inputs into pinned
+// memory and the last chunk's results out of it. The host copies are split
+// over a pool of worker threads (one thread's memcpy reaches about a fifth of
+// what a B200 host's memory and PCIe can move).
+//
+// Calls arrive synchronously from any number of the caller's threads at once
+// (the reference's pool calls a backend from every worker, core/pool.c:
+// 115-122, on disjoint outputs): each calling thread has its own streams and
+// staging, grown as needed and kept; matrices are uploaded once per device
+// and shared, keyed by host address and checked against a host copy of their
+// bytes on every call.
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <condition_variable>
+#include <cstdlib>
+#include <cstring>
+#include <deque>
+#include <functional>
+#include <memory>
+#include <mutex>
+#include <thread>
+#include <vector>
+
+#include "../../include/pktito_b200.h"
+#include "pkb_internal.h"
+
+namespace pkb {
+namespace {
+
+constexpr int MAX_DEV = 16;
+
+int cuda_err(cudaError_t e, const char* what) {
+    return set_error(e == cudaErrorMemoryAllocation ? PKB_ENOMEM : PKB_ECUDA, "%s: %s", what,
+                     cudaGetErrorString(e));
+}
+
+#define HOST_CUDA(call, what)                                \
+    do {                                                     \
+        cudaError_t e_ = (call);                             \
+        if (e_ != cudaSuccess) return cuda_err(e_, what);    \
+    } while (0)
+
+size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// ------------------------------------------------------------- copy pool --
+
+// Worker threads that split a large host copy (or comparison) between them
+// and the calling thread. Jobs from several calling threads queue up.
+class CopyPool {
+  public:
+    static CopyPool& get() {
+        static CopyPool pool;
+        return pool;
+    }
+
+    // rows of `bytes` each from src (pitch spitch) to dst (pitch dpitch)
+    void copy2d(void* dst, size_t dpitch, const void* src, size_t spitch, size_t bytes, size_t rows) {
+        const size_t total = bytes * rows;
+        if (!rows || !bytes) return;
+        if (dpitch == bytes && spitch == bytes) {  // one run
+            copy(dst, src, total);
+            return;
+        }
+        const int parts = split(total, rows);
+        run(parts, [=](int p) {
+            const size_t r0 = rows * p / parts, r1 = rows * (p + 1) / parts;
+            for (size_t r = r0; r < r1; r++)
+                memcpy(static_cast<char*>(dst) + r * dpitch, static_cast<const char*>(src) + r * spitch, bytes);
+        });
+    }
+
+    void copy(void* dst, const void* src, size_t bytes) {
+        const int parts = split(bytes, bytes / 4096 + 1);
+        run(parts, [=](int p) {
+            const size_t b0 = (bytes * p / parts) & ~size_t(63), b1 = p + 1 == parts ? bytes : (bytes * (p + 1) / parts) & ~size_t(63);
+            memcpy(static_cast<char*>(dst) + b0, static_cast<const char*>(src) + b0, b1 - b0);
+        });
+    }
+
+    bool equal(const void* a, const void* b, size_t bytes) {
+        std::atomic<bool> same{true};
+        const int parts = split(bytes, bytes / 4096 + 1);
+        run(parts, [&](int p) {
+            const size_t b0 = (bytes * p / parts) & ~size_t(63), b1 = p + 1 == parts ? bytes : (bytes * (p + 1) / parts) & ~size_t(63);
+            if (same.load(std::memory_order_relaxed) &&
+                memcmp(static_cast<const char*>(a) + b0, static_cast<const char*>(b) + b0, b1 - b0))
+                same = false;
+        });
+        return same;
+    }
+
+  private:
+    struct Job {
+        std::function<void(int)> fn;
+        int parts;
+        std::atomic<int> next{0}, done{0};
+    };
+
+    std::vector<std::thread> workers_;
+    std::mutex mu_;
+    std::condition_variable cv_;
+    std::deque<std::shared_ptr<Job>> queue_;
+    int nthreads_ = 0;
+
+    CopyPool() {
+        unsigned hw = std::thread::hardware_concurrency();
+        int n = hw ? static_cast<int>(hw) : 4;
+        if (n > 16) n = 16;
+        if (const char* e = getenv("PKB_HOST_THREADS")) n = atoi(e);
+        if (n < 1) n = 1;
+        nthreads_ = n;
+        for (int i = 1; i < n; i++) workers_.emplace_back([this] { work(); });  // the caller is the n-th
+    }
+    ~CopyPool() {
+        {
+            std::lock_guard<std::mutex> lock(mu_);
+            queue_.push_back(nullptr);  // stop
+        }
+        cv_.notify_all();
+        for (auto& t : workers_) t.join();
+    }
+
+    // parts worth splitting into: about 1 MB each, at most one per thread
+    int split(size_t bytes, size_t units) const {
+        size_t parts = bytes / (1u << 20);
+        if (parts > static_cast<size_t>(nthreads_)) parts = nthreads_;
+        if (parts > units) parts = units;
+        return parts < 1 ? 1 : static_cast<int>(parts);
+    }
+
+    static void take(Job& j) {
+        for (int p; (p = j.next.fetch_add(1)) < j.parts;) {
+            j.fn(p);
+            j.done.fetch_add(1, std::memory_order_acq_rel);
+        }
+    }
+
+    void run(int parts, std::function<void(int)> fn) {
+        if (parts <= 1 || workers_.empty()) {
+            fn(0);
+            return;
+        }
+        auto job = std::make_shared<Job>();
+        job->fn = std::move(fn);
+        job->parts = parts;
+        {
+            std::lock_guard<std::mutex> lock(mu_);
+            queue_.push_back(job);
+        }
+        cv_.notify_all();
+        take(*job);
+        while (job->done.load(std::memory_order_acquire) < parts) std::this_thread::yield();
+        std::lock_guard<std::mutex> lock(mu_);
+        for (auto it = queue_.begin(); it != queue_.end(); ++it)
+            if (*it == job) {
+                queue_.erase(it);
+                break;
+            }
+    }
+
+    void work() {
+        for (;;) {
+            std::shared_ptr<Job> job;
+            {
+                std::unique_lock<std::mutex> lock(mu_);
+                cv_.wait(lock, [this] {
+                    if (!queue_.empty() && !queue_.front()) return true;
+                    for (auto& j : queue_)
+                        if (j && j->next.load() < j->parts) return true;
+                    return false;
+                });
+                if (!queue_.front()) return;
+                for (auto& j : queue_)
+                    if (j && j->next.load() < j->parts) {
+                        job = j;
+                        break;
+                    }
+            }
+            if (job) take(*job);
+        }
+    }
+};
+
+// ------------------------------------------------------------- staging --
+
+// One calling thread's pipeline on its device: three streams, two slots of
+// pinned and device staging each way, and the events that order them.
+struct Pipe {
+    int dev = -1;
+    cudaStream_t s_in = nullptr, s_comp = nullptr, s_out = nullptr;
+    cudaEvent_t ev_in[2] = {}, ev_comp[2] = {}, ev_out[2] = {};
+    uint8_t* pin_in[2] = {};
+    uint8_t* pin_out[2] = {};
+    uint8_t* dev_in[2] = {};
+    uint8_t* dev_out[2] = {};
+    size_t in_cap = 0, out_cap = 0;
+    uint8_t* pin_vec = nullptr;  // row scales and biases going up
+    uint8_t* dev_vec = nullptr;
+    size_t vec_cap = 0;
+    uint32_t* herr = nullptr;    // the device error word, read back
+
+    ~Pipe() { release(); }
+
+    void release() {
+        if (dev < 0) return;
+        int cur = -1;
+        if (cudaGetDevice(&cur) != cudaSuccess) return;  // the runtime is gone at exit
+        cudaSetDevice(dev);
+        for (cudaStream_t s : {s_in, s_comp, s_out})
+            if (s) cudaStreamDestroy(s);
+        for (int i = 0; i < 2; i++) {
+            for (cudaEvent_t e : {ev_in[i], ev_comp[i], ev_out[i]})
+                if (e) cudaEventDestroy(e);
+            if (pin_in[i]) cudaFreeHost(pin_in[i]);
+            if (pin_out[i]) cudaFreeHost(pin_out[i]);
+            if (dev_in[i]) cudaFree(dev_in[i]);
+            if (dev_out[i]) cudaFree(dev_out[i]);
+        }
+        if (pin_vec) cudaFreeHost(pin_vec);
+        if (dev_vec) cudaFree(dev_vec);
+        if (herr) cudaFreeHost(herr);
+        *this = Pipe();
+        if (cur >= 0) cudaSetDevice(cur);
+    }
+
+    int open(int device) {
+        if (dev == device) return PKB_OK;
+        release();
+        HOST_CUDA(cudaSetDevice(device), "cudaSetDevice");
+        dev = device;
+        for (cudaStream_t* s : {&s_in, &s_comp, &s_out})
+            HOST_CUDA(cudaStreamCreateWithFlags(s, cudaStreamNonBlocking), "cudaStreamCreate");
+        for (int i = 0; i < 2; i++)
+            for (cudaEvent_t* e : {&ev_in[i], &ev_comp[i], &ev_out[i]})
+                HOST_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "cudaEventCreate");
+        HOST_CUDA(cudaMallocHost(&herr, sizeof(uint32_t)), "cudaMallocHost");
+        return PKB_OK;
+    }
+
+    // slots of at least in_bytes / out_bytes each way, and vec_bytes of vectors
+    int reserve(size_t in_bytes, size_t out_bytes, size_t vec_bytes) {
+        if (in_bytes > in_cap) {
+            const size_t want = up256(in_bytes + in_bytes / 4);
+            for (int i = 0; i < 2; i++) {
+                if (pin_in[i]) cudaFreeHost(pin_in[i]);
+                if (dev_in[i]) cudaFree(dev_in[i]);
+                pin_in[i] = dev_in[i] = nullptr;
+            }
+            in_cap = 0;
+            for (int i = 0; i < 2; i++) {
+                HOST_CUDA(cudaMallocHost(&pin_in[i], want), "cudaMallocHost (staging)");
+                HOST_CUDA(cudaMalloc(&dev_in[i], want), "cudaMalloc (staging)");
+            }
+            in_cap = want;
+        }
+        if (out_bytes > out_cap) {
+            const size_t want = up256(out_bytes + out_bytes / 4);
+            for (int i = 0; i < 2; i++) {
+                if (pin_out[i]) cudaFreeHost(pin_out[i]);
+                if (dev_out[i]) cudaFree(dev_out[i]);
+                pin_out[i] = dev_out[i] = nullptr;
+            }
+            out_cap = 0;
+            for (int i = 0; i < 2; i++) {
+                HOST_CUDA(cudaMallocHost(&pin_out[i], want), "cudaMallocHost (staging)");
+                HOST_CUDA(cudaMalloc(&dev_out[i], want), "cudaMalloc (staging)");
+            }
+            out_cap = want;
+        }
+        if (vec_bytes > vec_cap) {
+            const size_t want = up256(vec_bytes + vec_bytes / 4);
+            if (pin_vec) cudaFreeHost(pin_vec);
+            if (dev_vec) cudaFree(dev_vec);
+            pin_vec = dev_vec = nullptr;
+            vec_cap = 0;
+            HOST_CUDA(cudaMallocHost(&pin_vec, want), "cudaMallocHost (staging)");
+            HOST_CUDA(cudaMalloc(&dev_vec, want), "cudaMalloc (staging)");
+            vec_cap = want;
+        }
+        return PKB_OK;
+    }
+
+    // All three streams drained; the device error word read and cleared.
+    int finish(uint32_t* err_word) {
+        HOST_CUDA(cudaMemcpyAsync(herr, err_word, sizeof(uint32_t), cudaMemcpyDeviceToHost, s_out), "error word read");
+        HOST_CUDA(cudaStreamSynchronize(s_in), "cudaStreamSynchronize");
+        HOST_CUDA(cudaStreamSynchronize(s_comp), "cudaStreamSynchronize");
+        HOST_CUDA(cudaStreamSynchronize(s_out), "cudaStreamSynchronize");
+        if (*herr) {
+            const uint32_t w = *herr;
+            cudaMemsetAsync(err_word, 0, sizeof(uint32_t), s_out);
+            cudaStreamSynchronize(s_out);
+            return set_error(PKB_ETIMEOUT, "a kernel gave up waiting (device error word 0x%x)", w);
+        }
+        return PKB_OK;
+    }
+};
+
+thread_local int tl_device = 0;
+thread_local Pipe tl_pipe;
+
+// A chunk's frames: its input and output bytes per frame kept near these
+// sizes, in whole tiles of 128 frames where the call has that many.
+constexpr size_t CHUNK_IN = 16u << 20, CHUNK_OUT = 32u << 20;
+
+uint32_t chunk_frames(uint32_t T, size_t in_per_frame, size_t out_per_frame) {
+    size_t tc = CHUNK_IN / (in_per_frame ? in_per_frame : 1);
+    const size_t to = CHUNK_OUT / (out_per_frame ? out_per_frame : 1);
+    if (to < tc) tc = to;
+    tc = tc / 128 * 128;
+    if (tc < 128) tc = 128;
+    return tc >= T ? T : static_cast<uint32_t>(tc);
+}
+
+// ------------------------------------------------------------- matrices --
+
+// A matrix uploaded to one device: the host bytes it came from, a copy of
+// them to tell whether they still are what was uploaded, and its repacked
+// rows on the device.
+struct Matrix {
+    const int8_t* host;
+    uint32_t rows, n;
+    int dev;
+    std::vector<int8_t> shadow;
+    int8_t* wpack;
+};
+
+std::mutex g_mat_mu;
+std::vector<Matrix*> g_mats;
+std::vector<Matrix*> g_stale;  // replaced while maybe in use elsewhere: freed by pkb_forget
+
+// The device rows for `rows` rows of the PK_Q8 matrix at host address w (a
+// run of whole panels, possibly from inside a matrix uploaded before).
+int weights_for(Pipe& p, const int8_t* w, uint32_t rows, uint32_t n, const int8_t** wpack) {
+    const size_t bytes = static_cast<size_t>(rows) * n;
+    Matrix* hit = nullptr;
+    size_t row0 = 0;
+    {
+        std::lock_guard<std::mutex> lock(g_mat_mu);
+        for (Matrix* m : g_mats) {
+            if (m->dev != p.dev || m->n != n) continue;
+            const uintptr_t lo = reinterpret_cast<uintptr_t>(m->host);
+            const uintptr_t a = reinterpret_cast<uintptr_t>(w);
+            if (a < lo || a + bytes > lo + static_cast<size_t>(m->rows) * n) continue;
+            if ((a - lo) % (16 * static_cast<size_t>(n))) continue;  // not on a panel boundary
+            hit = m;
+            row0 = (a - lo) / n;
+            break;
+        }
+    }
+    if (hit && CopyPool::get().equal(hit->shadow.data() + row0 * n, w, bytes)) {
+        *wpack = hit->wpack + row0 * n;
+        return PKB_OK;
+    }
+    if (hit) {  // the bytes at that address changed: retire the old upload
+        std::lock_guard<std::mutex> lock(g_mat_mu);
+        for (size_t i = 0; i < g_mats.size(); i++)
+            if (g_mats[i] == hit) {
+                g_mats.erase(g_mats.begin() + static_cast<long>(i));
+                g_stale.push_back(hit);
+                break;
+            }
+    }
+    Matrix* m = new Matrix{w, rows, n, p.dev, std::vector<int8_t>(bytes), nullptr};
+    CopyPool::get().copy(m->shadow.data(), w, bytes);
+    cudaError_t e = cudaMalloc(&m->wpack, bytes);
+    if (e != cudaSuccess) {
+        delete m;
+        return cuda_err(e, "cudaMalloc (weights)");
+    }
+    // the panels through slot 0's staging, repacked into place
+    int rc = p.reserve(bytes, 0, 0);
+    if (rc) return rc;
+    HOST_CUDA(cudaStreamSynchronize(p.s_in), "cudaStreamSynchronize");
+    HOST_CUDA(cudaStreamSynchronize(p.s_comp), "cudaStreamSynchronize");
+    CopyPool::get().copy(p.pin_in[0], w, bytes);
+    HOST_CUDA(cudaMemcpyAsync(p.dev_in[0], p.pin_in[0], bytes, cudaMemcpyHostToDevice, p.s_comp), "weights upload");
+    if ((rc = pkb_repack_q8_dev(p.s_comp, m->wpack, reinterpret_cast<int8_t*>(p.dev_in[0]), rows, n))) return rc;
+    HOST_CUDA(cudaStreamSynchronize(p.s_comp), "weights upload");
+    {
+        std::lock_guard<std::mutex> lock(g_mat_mu);
+        g_mats.push_back(m);
+    }
+    *wpack = m->wpack;
+    return PKB_OK;
+}
+
+int open_pipe(Pipe** out, uint32_t** err_word) {
+    Pipe& p = tl_pipe;
+    int rc = p.open(tl_device);
+    if (rc) return rc;
+    HOST_CUDA(cudaSetDevice(p.dev), "cudaSetDevice");
+    int sms;
+    if ((rc = current_device_info(&sms, err_word))) return rc;
+    *out = &p;
+    return PKB_OK;
+}
+
+int check_shape(uint32_t n, uint32_t qb, int rmode) {
+    if (n == 0 || n % 32 || n > PKB_MAX_N) return set_error(PKB_EINVAL, "n = %u: a multiple of 32 up to %u", n, PKB_MAX_N);
+    if (qb == 0 || qb % 32 || n % qb) return set_error(PKB_EINVAL, "qb = %u: a multiple of 32 dividing n = %u", qb, n);
+    if (rmode < PKB_RN || rmode > PKB_RZ) return set_error(PKB_EINVAL, "rounding mode %d", rmode);
+    return PKB_OK;
+}
+
+}  // namespace
+}  // namespace pkb
+
+using namespace pkb;
+
+extern "C" {
+
+int pkb_set_thread_device(int device) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n || device >= MAX_DEV)
+        return set_error(PKB_ENODEV, "device %d is not present", device);
+    tl_device = device;
+    return PKB_OK;
+}
+
+int pkb_quantize_host(int8_t* q, float* d, uint32_t n, uint32_t qb, uint32_t T, const float* x, size_t xs,
+                      int rmode) {
+    int rc = check_shape(n, qb, rmode);
+    if (rc) return rc;
+    if (!T) return PKB_OK;
+    if (!q || !d || !x) return set_error(PKB_EINVAL, "quantize: null pointer");
+    if (xs < n) return set_error(PKB_EINVAL, "quantize: column stride %zu below n = %u", xs, n);
+    Pipe* p;
+    uint32_t* err;
+    if ((rc = open_pipe(&p, &err))) return rc;
+    const uint32_t nb = n / qb;
+    const size_t xrow = static_cast<size_t>(n) * 4, qrow = n, drow = static_cast<size_t>(nb) * 4;
+    const uint32_t TC = chunk_frames(T, xrow, qrow + drow);
+    const size_t off_d = up256(static_cast<size_t>(TC) * qrow);
+    if ((rc = p->reserve(static_cast<size_t>(TC) * xrow, off_d + static_cast<size_t>(TC) * drow, 0))) return rc;
+    CopyPool& pool = CopyPool::get();
+    const uint32_t nchunks = (T + TC - 1) / TC;
+    auto frames = [&](uint32_t c) { return std::min(TC, T - c * TC); };
+    auto take_out = [&](uint32_t c) -> int {  // chunk c's bytes and scales to the caller
+        const int s = c & 1;
+        HOST_CUDA(cudaEventSynchronize(p->ev_out[s]), "cudaEventSynchronize");
+        pool.copy(q + static_cast<size_t>(c) * TC * qrow, p->pin_out[s], frames(c) * qrow);
+        pool.copy(d + static_cast<size_t>(c) * TC * nb, p->pin_out[s] + off_d, frames(c) * drow);
+        return PKB_OK;
+    };
+    for (uint32_t c = 0; c < nchunks; c++) {
+        const int s = c & 1;
+        const uint32_t tc = frames(c);
+        if (c >= 2) HOST_CUDA(cudaEventSynchronize(p->ev_in[s]), "cudaEventSynchronize");
+        pool.copy2d(p->pin_in[s], xrow, x + static_cast<size_t>(c) * TC * xs, xs * 4, xrow, tc);
+        if (c >= 2) HOST_CUDA(cudaStreamWaitEvent(p->s_in, p->ev_comp[s], 0), "cudaStreamWaitEvent");
+        HOST_CUDA(cudaMemcpyAsync(p->dev_in[s], p->pin_in[s], tc * xrow, cudaMemcpyHostToDevice, p->s_in), "upload");
+        HOST_CUDA(cudaEventRecord(p->ev_in[s], p->s_in), "cudaEventRecord");
+        HOST_CUDA(cudaStreamWaitEvent(p->s_comp, p->ev_in[s], 0), "cudaStreamWaitEvent");
+        if (c >= 2) HOST_CUDA(cudaStreamWaitEvent(p->s_comp, p->ev_out[s], 0), "cudaStreamWaitEvent");
+        if ((rc = pkb_quantize_dev(p->s_comp, reinterpret_cast<int8_t*>(p->dev_out[s]),
+                                   reinterpret_cast<float*>(p->dev_out[s] + off_d),
+                                   reinterpret_cast<const float*>(p->dev_in[s]), n, tc, n, qb, rmode)))
+            return rc;
+        HOST_CUDA(cudaEventRecord(p->ev_comp[s], p->s_comp), "cudaEventRecord");
+        HOST_CUDA(cudaStreamWaitEvent(p->s_out, p->ev_comp[s], 0), "cudaStreamWaitEvent");
+        HOST_CUDA(cudaMemcpyAsync(p->pin_out[s], p->dev_out[s], tc * qrow, cudaMemcpyDeviceToHost, p->s_out),
+                  "download");
+        HOST_CUDA(cudaMemcpyAsync(p->pin_out[s] + off_d, p->dev_out[s] + off_d, tc * drow, cudaMemcpyDeviceToHost,
+                                  p->s_out),
+                  "download");
+        HOST_CUDA(cudaEventRecord(p->ev_out[s], p->s_out), "cudaEventRecord");
+        if (c >= 1 && (rc = take_out(c - 1))) return rc;
+    }
+    if ((rc = p->finish(err))) return rc;
+    return take_out(nchunks - 1);
+}
+
+int pkb_gemm_q8_host(float* out, size_t os, const int8_t* w, const float* ws, const float* bias, uint32_t rows,
+                     const int8_t* q, const float* d, uint32_t n, uint32_t qb, uint32_t T, int add, int rmode) {
+    int rc = check_shape(n, qb, rmode);
+    if (rc) return rc;
+    if (rows % 16) return set_error(PKB_EINVAL, "rows = %u: a multiple of 16", rows);
+    if (os < rows) return set_error(PKB_EINVAL, "output stride %zu below rows = %u", os, rows);
+    if (!T || !rows) return PKB_OK;
+    if (!out || !w || !ws || !q || !d) return set_error(PKB_EINVAL, "gemm_q8: null pointer");
+    Pipe* p;
+    uint32_t* err;
+    if ((rc = open_pipe(&p, &err))) return rc;
+    const int8_t* wpack;
+    if ((rc = weights_for(*p, w, rows, n, &wpack))) return rc;
+    const uint32_t nb = n / qb;
+    const size_t qrow = n, drow = static_cast<size_t>(nb) * 4, orow = static_cast<size_t>(rows) * 4;
+    const uint32_t TC = chunk_frames(T, qrow + drow + (add ? orow : 0), orow);
+    const size_t off_d = up256(static_cast<size_t>(TC) * qrow);
+    const size_t in_bytes = off_d + static_cast<size_t>(TC) * drow;
+    if ((rc = p->reserve(in_bytes, static_cast<size_t>(TC) * orow, 2 * up256(orow)))) return rc;
+    CopyPool& pool = CopyPool::get();
+    // the row scales and biases, once a call
+    memcpy(p->pin_vec, ws, orow);
+    if (bias) memcpy(p->pin_vec + up256(orow), bias, orow);
+    HOST_CUDA(cudaMemcpyAsync(p->dev_vec, p->pin_vec, up256(orow) + orow, cudaMemcpyHostToDevice, p->s_comp),
+              "upload");
+    const float* dws = reinterpret_cast<const float*>(p->dev_vec);
+    const float* dbias = bias ? reinterpret_cast<const float*>(p->dev_vec + up256(orow)) : nullptr;
+    const uint32_t nchunks = (T + TC - 1) / TC;
+    auto frames = [&](uint32_t c) { return std::min(TC, T - c * TC); };
+    auto take_out = [&](uint32_t c) -> int {  // chunk c's rows of out, at the caller's stride
+        const int s = c & 1;
+        HOST_CUDA(cudaEventSynchronize(p->ev_out[s]), "cudaEventSynchronize");
+        pool.copy2d(out + static_cast<size_t>(c) * TC * os, os * 4, p->pin_out[s], orow, orow, frames(c));
+        return PKB_OK;
+    };
+    for (uint32_t c = 0; c < nchunks; c++) {
+        const int s = c & 1;
+        const uint32_t tc = frames(c);
+        const size_t t0 = static_cast<size_t>(c) * TC;
+        if (c >= 2) HOST_CUDA(cudaEventSynchronize(p->ev_in[s]), "cudaEventSynchronize");
+        pool.copy(p->pin_in[s], q + t0 * qrow, tc * qrow);
+        pool.copy(p->pin_in[s] + off_d, d + t0 * nb, tc * drow);
+        if (add) {
+            // the residual the product adds to: its rows, packed, into the
+            // output slot (its previous chunk there was taken out already)
+            pool.copy2d(p->pin_out[s], orow, out + t0 * os, os * 4, orow, tc);
+        }
+        if (c >= 2) {
+            HOST_CUDA(cudaStreamWaitEvent(p->s_in, p->ev_comp[s], 0), "cudaStreamWaitEvent");
+            HOST_CUDA(cudaStreamWaitEvent(p->s_in, p->ev_out[s], 0), "cudaStreamWaitEvent");
+        }
+        HOST_CUDA(cudaMemcpyAsync(p->dev_in[s], p->pin_in[s], off_d + tc * drow, cudaMemcpyHostToDevice, p->s_in),
+                  "upload");
+        if (add)
+            HOST_CUDA(cudaMemcpyAsync(p->dev_out[s], p->pin_out[s], tc * orow, cudaMemcpyHostToDevice, p->s_in),
+                      "upload");
+        HOST_CUDA(cudaEventRecord(p->ev_in[s], p->s_in), "cudaEventRecord");
+        HOST_CUDA(cudaStreamWaitEvent(p->s_comp, p->ev_in[s], 0), "cudaStreamWaitEvent");
+        if (c >= 2) HOST_CUDA(cudaStreamWaitEvent(p->s_comp, p->ev_out[s], 0), "cudaStreamWaitEvent");
+        if ((rc = pkb_gemm_q8_dev(p->s_comp, reinterpret_cast<float*>(p->dev_out[s]), rows, wpack, dws, dbias, rows,
+                                  reinterpret_cast<const int8_t*>(p->dev_in[s]),
+                                  reinterpret_cast<const float*>(p->dev_in[s] + off_d), n, qb, tc, add, rmode)))
+            return rc;
+        HOST_CUDA(cudaEventRecord(p->ev_comp[s], p->s_comp), "cudaEventRecord");
+        HOST_CUDA(cudaStreamWaitEvent(p->s_out, p->ev_comp[s], 0), "cudaStreamWaitEvent");
+        HOST_CUDA(cudaMemcpyAsync(p->pin_out[s], p->dev_out[s], tc * orow, cudaMemcpyDeviceToHost, p->s_out),
+                  "download");
+        HOST_CUDA(cudaEventRecord(p->ev_out[s], p->s_out), "cudaEventRecord");
+        if (c >= 1 && (rc = take_out(c - 1))) return rc;
+    }
+    if ((rc = p->finish(err))) return rc;
+    return take_out(nchunks - 1);
+}
+
+int pkb_forget(const void* ptr, size_t bytes) {
+    const uintptr_t lo = reinterpret_cast<uintptr_t>(ptr), hi = lo + bytes;
+    std::vector<Matrix*> drop;
+    {
+        std::lock_guard<std::mutex> lock(g_mat_mu);
+        for (size_t i = 0; i < g_mats.size();) {
+            Matrix* m = g_mats[i];
+            const uintptr_t mlo = reinterpret_cast<uintptr_t>(m->host);
+            const uintptr_t mhi = mlo + static_cast<size_t>(m->rows) * m->n;
+            if (mlo < hi && lo < mhi) {
+                drop.push_back(m);
+                g_mats.erase(g_mats.begin() + static_cast<long>(i));
+            } else {
+                i++;
+            }
+        }
+        drop.insert(drop.end(), g_stale.begin(), g_stale.end());
+        g_stale.clear();
+    }
+    int cur = -1;
+    cudaGetDevice(&cur);
+    for (Matrix* m : drop) {
+        cudaSetDevice(m->dev);
+        cudaDeviceSynchronize();
+        cudaFree(m->wpack);
+        delete m;
+    }
+    if (cur >= 0) cudaSetDevice(cur);
+    return PKB_OK;
+}
+
+}  // extern "C"

@@ -12,6 +12,13 @@ namespace pkb {
 // and returns code.
 int set_error(int code, const char* fmt, ...);
 
+// The current device, checked to be an sm_100 one and set up: its SM count
+// and the device address of its error word.
+int current_device_info(int* sms, uint32_t** err_word);
+
+// One more kernel launched (pkb_launch_count).
+void count_launch();
+
 // Arguments of the product kernel (pkb_gemm.cu) besides its two tensor maps.
 struct GemmArgs {
     float* out;            // out[t*os + r]
