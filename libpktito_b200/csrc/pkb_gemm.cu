@@ -78,23 +78,80 @@ static_assert((2 * NSTAGE + 2 * NTMEM + 2 * NDS + 1) * 8 + 8 <= BAR_BYTES, "barr
 // integer sum added to it is, read as a float, 1.5 * 2^23 + s.
 constexpr uint32_t SUM_BIAS = 0x4B400000u;
 
+#ifndef PKB_PACKED_CHAIN
+#define PKB_PACKED_CHAIN 0
+#endif
+
+// The 32 running sums of a thread (its frame x the warp's 32 output rows).
+#if PKB_PACKED_CHAIN
+using Acc = uint64_t[16];  // two rows a 64-bit register, for the f32x2 instructions
+#else
+using Acc = float[32];
+#endif
+
+// acc[16*half + i] = fma(float(s[i]), dv, acc[16*half + i]) for the 16 block
+// sums of one TMEM load, each rounded once in the mode RM.
 template <int RM, bool EXACT_SUM>
-__device__ __forceinline__ void chain16(uint64_t (&acc)[16], const uint32_t (&s)[16], int half, float dv) {
+__device__ __forceinline__ void chain16(Acc& acc, const uint32_t (&s)[16], int half, float dv) {
+#if PKB_PACKED_CHAIN
     const uint64_t d2 = pack2(dv, dv);
 #pragma unroll
     for (int i = 0; i < 8; i++) {
         uint64_t f;
-        if constexpr (EXACT_SUM) {
-            // the accumulators started at 0x4B400000 (SUM_BIAS), so each word
-            // is the float 1.5 * 2^23 + s; less 1.5 * 2^23, rounded to nearest,
-            // it is exactly s (and +0 for a zero sum)
+        if constexpr (EXACT_SUM)
             f = add2_rn(pack2(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])),
                         pack2(-12582912.0f, -12582912.0f));
-        } else {
+        else
             f = pack2(i2f_r<RM>(static_cast<int>(s[2 * i])), i2f_r<RM>(static_cast<int>(s[2 * i + 1])));
-        }
         acc[8 * half + i] = fma2_r<RM>(f, d2, acc[8 * half + i]);
     }
+#else
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+        // the accumulators started at SUM_BIAS, so each word is the float
+        // 1.5 * 2^23 + s; less 1.5 * 2^23, rounded to nearest, it is exactly
+        // s (+0 for a zero sum); wider blocks convert in the mode
+        const float f = EXACT_SUM ? __fsub_rn(__uint_as_float(s[i]), 12582912.0f) : i2f_r<RM>(static_cast<int>(s[i]));
+        acc[16 * half + i] = fma_r<RM>(f, dv, acc[16 * half + i]);
+    }
+#endif
+}
+
+__device__ __forceinline__ float acc_at(const Acc& acc, int j) {
+#if PKB_PACKED_CHAIN
+    float lo, hi;
+    unpack2(acc[j / 2], lo, hi);
+    return (j & 1) ? hi : lo;
+#else
+    return acc[j];
+#endif
+}
+
+// One block's accumulator (the warp's 32 columns at ta) into the chain, and
+// the slot set back to SUM_BIAS for the block that takes it next (its wait
+// is the caller's, before it releases the slot).
+template <int RM, bool EXACT_SUM>
+__device__ __forceinline__ void epi_block(Acc& acc, uint32_t ta, float dv) {
+    uint32_t sv[16];
+    tmem_ld_32x32b_x16(ta, sv);
+    tmem_ld_wait(sv);
+    chain16<RM, EXACT_SUM>(acc, sv, 0, dv);
+    tmem_ld_32x32b_x16(ta + 16, sv);
+    tmem_ld_wait(sv);
+    if constexpr (EXACT_SUM) {
+        tmem_st_32x32b_x16_fill(ta, SUM_BIAS);
+        tmem_st_32x32b_x16_fill(ta + 16, SUM_BIAS);
+    }
+    chain16<RM, EXACT_SUM>(acc, sv, 1, dv);
+}
+
+// Lane 0 waits for `bar`'s phase and tells the warp (the TMEM loads that
+// follow are whole-warp instructions); false if the wait gave up.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int lane, volatile int* abort,
+                                          long long limit) {
+    uint32_t seen = 1;
+    if (lane == 0) seen = mbar_wait(bar, parity, abort, limit) ? 1u : 0u;
+    return __shfl_sync(0xffffffffu, seen, 0) != 0;
 }
 
 template <int RM, bool EXACT_SUM, int G, bool DTMA>
@@ -299,24 +356,57 @@ __global__ void __launch_bounds__(THREADS, 1)
             const bool tvalid = t < g.T;
             const float* drow = g.d + static_cast<size_t>(tvalid ? t : 0) * nb;
 
-            uint64_t acc[16];
+            Acc acc;
 #pragma unroll
-            for (int j = 0; j < 16; j++) acc[j] = 0;  // +0, +0
+            for (int j = 0; j < static_cast<int>(sizeof(Acc) / sizeof(acc[0])); j++) acc[j] = 0;  // +0
 
-            // without the scales ring: the frame's scales from global memory,
-            // one block ahead
-            float dnext = (!DTMA && tvalid) ? __ldg(drow) : 0.0f;
-            for (uint32_t b = 0; b < nb; b++) {
-                float dv;
-                if constexpr (DTMA) {
+            uint32_t b = 0;
+            if constexpr (DTMA) {
+                // four blocks an iteration, the blocks of one chunk of scales:
+                // one wait for the scales, one for each group of G blocks, all
+                // of it unrolled
+                const uint32_t tl = tbase + (lane_base << 16) + 32 * cgroup;
+                for (; b + DCHUNK <= nb; b += DCHUNK) {
                     const uint32_t ds = dcnt % NDS;
-                    if ((b & (DCHUNK - 1)) == 0) {
-                        uint32_t seen = 1;
-                        if (lane == 0) seen = mbar_wait(&dfull[ds], (dcnt / NDS) & 1, abort, limit) ? 1u : 0u;
-                        if (!__shfl_sync(0xffffffffu, seen, 0)) {
+                    if (!warp_wait(&dfull[ds], (dcnt / NDS) & 1, lane, abort, limit)) {
+                        ok = false;
+                        break;
+                    }
+                    const float4 dq = *reinterpret_cast<const float4*>(dring + ds * (DS_BYTES / 4) + (lane_base + lane) * DCHUNK);
+                    const float dd[4] = {dq.x, dq.y, dq.z, dq.w};
+#pragma unroll
+                    for (int g2 = 0; g2 < DCHUNK / G; g2++) {
+                        if (!warp_wait(&tfull[gs], (gc / NGROUP) & 1, lane, abort, limit)) {
                             ok = false;
                             break;
                         }
+                        tc_fence_after();
+#pragma unroll
+                        for (int k = 0; k < G; k++) epi_block<RM, EXACT_SUM>(acc, tl + (gs * G + k) * BN, dd[g2 * G + k]);
+                        if constexpr (EXACT_SUM) tmem_st_wait();
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&tempty[gs]);
+                        gc++;
+                        gs = gc % NGROUP;
+                    }
+                    if (!ok) break;
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&dempty[ds]);
+                    dcnt++;
+                }
+            }
+            // the blocks left (every block, without the scales ring), one at a
+            // time; without the ring the frame's scales come from global
+            // memory, one block ahead
+            float dnext = (!DTMA && tvalid && b < nb) ? __ldg(drow + b) : 0.0f;
+            for (; ok && b < nb; b++) {
+                float dv;
+                if constexpr (DTMA) {
+                    const uint32_t ds = dcnt % NDS;
+                    if ((b & (DCHUNK - 1)) == 0 && !warp_wait(&dfull[ds], (dcnt / NDS) & 1, lane, abort, limit)) {
+                        ok = false;
+                        break;
                     }
                     dv = dring[ds * (DS_BYTES / 4) + (lane_base + lane) * DCHUNK + (b & (DCHUNK - 1))];
                 } else {
@@ -325,39 +415,21 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 const uint32_t kin = b & (G - 1);  // block in its group
                 if (kin == 0) {
-                    // lane 0 waits and tells the warp: the TMEM loads below
-                    // are whole-warp instructions
-                    uint32_t seen = 1;
-                    if (lane == 0) seen = mbar_wait(&tfull[gs], (gc / NGROUP) & 1, abort, limit) ? 1u : 0u;
-                    if (!__shfl_sync(0xffffffffu, seen, 0)) {
+                    if (!warp_wait(&tfull[gs], (gc / NGROUP) & 1, lane, abort, limit)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                 }
-                const uint32_t ta = tbase + (lane_base << 16) + (gs * G + kin) * BN + 32 * cgroup;
-                // the two halves of the warp's 32 columns in turn (a TMEM
-                // load's round trip is a few tens of cycles)
-                uint32_t sv[16];
-                tmem_ld_32x32b_x16(ta, sv);
-                tmem_ld_wait(sv);
-                chain16<RM, EXACT_SUM>(acc, sv, 0, dv);
-                tmem_ld_32x32b_x16(ta + 16, sv);
-                tmem_ld_wait(sv);
-                if constexpr (EXACT_SUM) {
-                    // the slot back to SUM_BIAS for the block that takes it next
-                    tmem_st_32x32b_x16_fill(ta, SUM_BIAS);
-                    tmem_st_32x32b_x16_fill(ta + 16, SUM_BIAS);
-                    tmem_st_wait();
-                }
+                epi_block<RM, EXACT_SUM>(acc, tbase + (lane_base << 16) + (gs * G + kin) * BN + 32 * cgroup, dv);
                 if (kin == G - 1 || b == nb - 1) {
+                    if constexpr (EXACT_SUM) tmem_st_wait();
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&tempty[gs]);
                     gc++;
                     gs = gc % NGROUP;
                 }
-                chain16<RM, EXACT_SUM>(acc, sv, 1, dv);
                 if constexpr (DTMA) {
                     if ((b & (DCHUNK - 1)) == DCHUNK - 1 || b == nb - 1) {
                         __syncwarp();
@@ -371,12 +443,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             // through shared memory, so that a lane owns one output row (a
             // column of the tile) and each store is 32 consecutive floats
 #pragma unroll
-            for (int j = 0; j < 16; j++) {
-                float lo, hi;
-                unpack2(acc[j], lo, hi);
-                tw[lane * EPI_PITCH + 2 * j] = lo;
-                tw[lane * EPI_PITCH + 2 * j + 1] = hi;
-            }
+            for (int j = 0; j < 32; j++) tw[lane * EPI_PITCH + j] = acc_at(acc, j);
             __syncwarp();
             const uint32_t col = n0 + 32 * cgroup + lane;
             const bool cvalid = col < g.rows;
