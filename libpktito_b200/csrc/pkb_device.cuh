@@ -219,6 +219,28 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
     return d;
 }
 
+// Shared-memory matrix descriptor for a K-major operand tile without
+// swizzle: 8-row x 16-byte core matrices, `lbo` bytes apart along K and
+// `sbo` bytes apart along the rows, version 1 (sm_100), layout SWIZZLE_NONE.
+__device__ __forceinline__ uint64_t plain_kmajor_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);   // start address >> 4, bits 0-13
+    d |= static_cast<uint64_t>(lbo >> 4) << 16;             // leading byte offset: K neighbours
+    d |= static_cast<uint64_t>(sbo >> 4) << 32;             // stride byte offset: 8-row groups
+    d |= static_cast<uint64_t>(1) << 46;                    // descriptor version for sm_100
+    return d;                                               // layout bits 61-63 = 0: no swizzle
+}
+
+// Instruction descriptor of tcgen05.mma.kind::f16 with bf16 A and B and a
+// float32 accumulator, both operands K-major, M x N.
+__host__ __device__ constexpr uint32_t bf16_instr_desc(uint32_t M, uint32_t N) {
+    return (1u << 4)            // D format: F32
+           | (1u << 7)          // A: bf16
+           | (1u << 10)         // B: bf16
+           | ((N >> 3) << 17)   // N / 8
+           | ((M >> 4) << 24);  // M / 16
+}
+
 // Instruction descriptor of tcgen05.mma.kind::i8: signed A and B, int32
 // accumulator, both operands K-major, M x N.
 __host__ __device__ constexpr uint32_t i8_instr_desc(uint32_t M, uint32_t N) {
@@ -236,6 +258,18 @@ __device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T for bf16 A and B, one K=16 step, float32
+// accumulator, issued by one thread.
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
@@ -291,6 +325,18 @@ __device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[16]) {
                  : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
                    "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
                    "+r"(r[15])
+                 :
+                 : "memory");
+}
+
+// The same for the 32 registers two x16 loads filled.
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                   "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                   "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
                  :
                  : "memory");
 }

@@ -20,20 +20,32 @@
 // tile is 128 frames (TMEM lanes, the MMA's M) by 128 output rows (TMEM
 // columns, the MMA's N).
 //
-// Warp roles in a 576-thread CTA, one CTA per SM (its 194 KB of shared
+// The int -> float conversion of a sum costs the chain no extra pass: before
+// a block's i8 MMAs, one kind::f16 MMA of constant bf16 tiles (16 products
+// 1536 x 512 a cell, all exact) writes the float 1.5 * 2^23 = 12582912,
+// bits 0x4B400000, into every cell of the block's accumulator; the i8 MMAs
+// add the integer sum to those bits, so each word read back is the float
+// 1.5 * 2^23 + s, and one exact subtraction gives (float)s (|s| < 2^22,
+// i.e. qb <= 256; wider blocks start from zero and convert in the mode).
+//
+// Warp roles in a 576-thread CTA, one CTA per SM (its 219 KB of shared
 // memory keeps a second off), persistent over the tiles:
 //   warp 16    TMA producer: 128-byte-swizzled 128x128 tiles of activations
-//              and weights into a 6-stage shared-memory ring
+//              and weights into a 4-stage shared-memory ring, and the
+//              activation scales into their own ring
 //   warp 17    allocates TMEM; one thread issues the MMAs and commits
 //   warps 0-15 the epilogue: warp w reads TMEM lanes 32*(w%4).. (the
 //              quarter its hardware warp slot may access) and columns
-//              32*(w/4)..+31 of each block's accumulator; each thread is one
-//              frame and runs the float chain of 32 output rows in registers,
-//              then scales, biases, adds and stores them.
+//              32*(w/4)..+31 of each block's accumulator, hands the slot back
+//              as soon as its loads have landed, and runs the float chain of
+//              its frame's 32 output rows in registers, two rows a packed
+//              f32x2 instruction; after the tile's last block it scales,
+//              biases, adds and stores them.
 //
-// The fp32 chain (one FMA per output and block, plus the int->float of the
-// sum) is the bound at 32-input blocks, not the tensor core: the MMAs of a
-// block take a quarter of the time the epilogue's CUDA cores need for it.
+// The fp32 chain is the bound at 32-input blocks, not the tensor core: per
+// block and output it is one subtraction and one FMA on the CUDA cores
+// (128 lanes a cycle per SM), against 64 tensor-core cycles for the whole
+// 128 x 128 x 32 block.
 //
 // Every wait is bounded: a role that waits past the limit sets the device
 // error word and an abort flag the other roles see, waits (bounded) for its
@@ -65,84 +77,51 @@ constexpr int EPI_BYTES = EPI_WARPS * 32 * EPI_PITCH * 4;
 constexpr int DCHUNK = 4;          // blocks of scales a TMA box of d carries (16 bytes a frame)
 constexpr int NDS = 8;             // slots of the scales ring
 constexpr int DS_BYTES = BM * DCHUNK * 4;
+constexpr int SEED_K = 16;         // K of the bf16 MMA that writes the accumulator's start value
+constexpr int SEED_BYTES = 128 * SEED_K * 2;  // one 128-row bf16 operand tile of it
 constexpr int BAR_BYTES = 512;
-constexpr int SMEM_BYTES = NSTAGE * STAGE_BYTES + EPI_BYTES + NDS * DS_BYTES + BAR_BYTES + 1024;  // + alignment slack
+constexpr int SMEM_BYTES =
+    NSTAGE * STAGE_BYTES + EPI_BYTES + NDS * DS_BYTES + 2 * SEED_BYTES + BAR_BYTES + 1024;  // + alignment slack
 
 static_assert(TMEM_COLS == 512, "TMEM ring must fit the SM's 512 columns");
 static_assert((2 * NSTAGE + 2 * NTMEM + 2 * NDS + 1) * 8 + 8 <= BAR_BYTES, "barrier area");
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory of one CTA");
 
-// acc[8*half + i] (two output rows each) = fma(float(s), d, acc), for the
-// 16 block sums of one TMEM load, two rows an instruction.
-// The int32 each block accumulator starts from when block sums convert
-// exactly (|s| < 2^22): its bits are the float 1.5 * 2^23, so the MMA's
-// integer sum added to it is, read as a float, 1.5 * 2^23 + s.
-constexpr uint32_t SUM_BIAS = 0x4B400000u;
+// The float 1.5 * 2^23, whose bits 0x4B400000 plus an int32 |s| < 2^22 are
+// the float 1.5 * 2^23 + s. The start-value MMA writes it as the sum of
+// SEED_K products SEED_A * SEED_B, every partial sum an exact integer.
+constexpr float SUM_BIAS_F = 12582912.0f;
+constexpr uint16_t SEED_A = 0x44C0;  // bf16 1536
+constexpr uint16_t SEED_B = 0x4400;  // bf16 512
+static_assert(1536.0 * 512.0 * SEED_K == 12582912.0, "start value");
 
-#ifndef PKB_PACKED_CHAIN
-#define PKB_PACKED_CHAIN 0
-#endif
+// The 32 running sums of a thread (its frame x the warp's 32 output rows),
+// two rows a 64-bit register, for the f32x2 instructions.
+using Acc = uint64_t[16];
 
-// The 32 running sums of a thread (its frame x the warp's 32 output rows).
-#if PKB_PACKED_CHAIN
-using Acc = uint64_t[16];  // two rows a 64-bit register, for the f32x2 instructions
-#else
-using Acc = float[32];
-#endif
-
-// acc[16*half + i] = fma(float(s[i]), dv, acc[16*half + i]) for the 16 block
-// sums of one TMEM load, each rounded once in the mode RM.
+// acc[i] = fma(float(s), d, acc[i]) for the 32 block sums of the warp's
+// columns, two an instruction, each rounded once in the mode RM.
 template <int RM, bool EXACT_SUM>
-__device__ __forceinline__ void chain16(Acc& acc, const uint32_t (&s)[16], int half, float dv) {
-#if PKB_PACKED_CHAIN
+__device__ __forceinline__ void chain32(Acc& acc, const uint32_t (&s)[32], float dv) {
     const uint64_t d2 = pack2(dv, dv);
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        uint64_t f;
-        if constexpr (EXACT_SUM)
-            f = add2_rn(pack2(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])),
-                        pack2(-12582912.0f, -12582912.0f));
-        else
-            f = pack2(i2f_r<RM>(static_cast<int>(s[2 * i])), i2f_r<RM>(static_cast<int>(s[2 * i + 1])));
-        acc[8 * half + i] = fma2_r<RM>(f, d2, acc[8 * half + i]);
-    }
-#else
+    const uint64_t bias2 = pack2(-SUM_BIAS_F, -SUM_BIAS_F);
 #pragma unroll
     for (int i = 0; i < 16; i++) {
-        // the accumulators started at SUM_BIAS, so each word is the float
-        // 1.5 * 2^23 + s; less 1.5 * 2^23, rounded to nearest, it is exactly
-        // s (+0 for a zero sum); wider blocks convert in the mode
-        const float f = EXACT_SUM ? __fsub_rn(__uint_as_float(s[i]), 12582912.0f) : i2f_r<RM>(static_cast<int>(s[i]));
-        acc[16 * half + i] = fma_r<RM>(f, dv, acc[16 * half + i]);
+        uint64_t f;
+        if constexpr (EXACT_SUM)
+            // each word is the float 1.5 * 2^23 + s; less 1.5 * 2^23, rounded
+            // to nearest, it is exactly s (+0 for a zero sum)
+            f = add2_rn(pack2(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), bias2);
+        else
+            f = pack2(i2f_r<RM>(static_cast<int>(s[2 * i])), i2f_r<RM>(static_cast<int>(s[2 * i + 1])));
+        acc[i] = fma2_r<RM>(f, d2, acc[i]);
     }
-#endif
 }
 
 __device__ __forceinline__ float acc_at(const Acc& acc, int j) {
-#if PKB_PACKED_CHAIN
     float lo, hi;
     unpack2(acc[j / 2], lo, hi);
     return (j & 1) ? hi : lo;
-#else
-    return acc[j];
-#endif
-}
-
-// One block's accumulator (the warp's 32 columns at ta) into the chain, and
-// the slot set back to SUM_BIAS for the block that takes it next (its wait
-// is the caller's, before it releases the slot).
-template <int RM, bool EXACT_SUM>
-__device__ __forceinline__ void epi_block(Acc& acc, uint32_t ta, float dv) {
-    uint32_t sv[16];
-    tmem_ld_32x32b_x16(ta, sv);
-    tmem_ld_wait(sv);
-    chain16<RM, EXACT_SUM>(acc, sv, 0, dv);
-    tmem_ld_32x32b_x16(ta + 16, sv);
-    tmem_ld_wait(sv);
-    if constexpr (EXACT_SUM) {
-        tmem_st_32x32b_x16_fill(ta, SUM_BIAS);
-        tmem_st_32x32b_x16_fill(ta + 16, SUM_BIAS);
-    }
-    chain16<RM, EXACT_SUM>(acc, sv, 1, dv);
 }
 
 // Lane 0 waits for `bar`'s phase and tells the warp (the TMEM loads that
@@ -154,7 +133,26 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int la
     return __shfl_sync(0xffffffffu, seen, 0) != 0;
 }
 
-template <int RM, bool EXACT_SUM, int G, bool DTMA>
+// One block's accumulator (the warp's 32 columns at ta) out of TMEM: waits
+// for the MMAs, loads, hands the slot back to the MMA thread and runs the
+// chain. False if the wait gave up.
+template <int RM, bool EXACT_SUM>
+__device__ __forceinline__ bool epi_block(Acc& acc, uint32_t ta, float dv, uint64_t* tfull, uint64_t* tempty,
+                                          uint32_t parity, int lane, volatile int* abort, long long limit) {
+    if (!warp_wait(tfull, parity, lane, abort, limit)) return false;
+    tc_fence_after();
+    uint32_t sv[32];
+    tmem_ld_32x32b_x16(ta, *reinterpret_cast<uint32_t(*)[16]>(&sv[0]));
+    tmem_ld_32x32b_x16(ta + 16, *reinterpret_cast<uint32_t(*)[16]>(&sv[16]));
+    tmem_ld_wait(sv);
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(tempty);
+    chain32<RM, EXACT_SUM>(acc, sv, dv);
+    return true;
+}
+
+template <int RM, bool EXACT_SUM, bool DTMA>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_q8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    const __grid_constant__ CUtensorMap map_d, const GemmArgs g) {
@@ -162,7 +160,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float* epi = reinterpret_cast<float*>(smem + NSTAGE * STAGE_BYTES);
     float* dring = reinterpret_cast<float*>(smem + NSTAGE * STAGE_BYTES + EPI_BYTES);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + NSTAGE * STAGE_BYTES + EPI_BYTES + NDS * DS_BYTES);
+    uint8_t* seed = smem + NSTAGE * STAGE_BYTES + EPI_BYTES + NDS * DS_BYTES;  // A tile, then B tile
+    uint64_t* full = reinterpret_cast<uint64_t*>(seed + 2 * SEED_BYTES);
     uint64_t* empty = full + NSTAGE;
     uint64_t* tfull = empty + NSTAGE;
     uint64_t* tempty = tfull + NTMEM;
@@ -192,6 +191,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         *abort = 0;
         fence_mbar_init();
     }
+    if (EXACT_SUM && warp < EPI_WARPS) {
+        // the start-value MMA's operand tiles: every bf16 of A 1536, of B 512
+        uint32_t* sw = reinterpret_cast<uint32_t*>(seed);
+        for (int i = threadIdx.x; i < SEED_BYTES / 4; i += EPI_WARPS * 32) {
+            sw[i] = (uint32_t(SEED_A) << 16) | SEED_A;
+            sw[SEED_BYTES / 4 + i] = (uint32_t(SEED_B) << 16) | SEED_B;
+        }
+        // written through the generic proxy, read by the tensor core
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
     if (warp == MMA_WARP) {
         tmem_alloc(tslot, TMEM_COLS);
         tmem_relinquish();
@@ -205,22 +214,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *tslot;
-    if constexpr (EXACT_SUM) {
-        // every accumulator starts at SUM_BIAS: each epilogue warp fills its
-        // lane quarter of its 32 columns in every TMEM slot
-        if (warp < EPI_WARPS) {
-            const uint32_t ta = tbase + ((32 * (warp & 3)) << 16) + 32 * (warp >> 2);
-#pragma unroll
-            for (int k = 0; k < NTMEM; k++) {
-                tmem_st_32x32b_x16_fill(ta + k * BN, SUM_BIAS);
-                tmem_st_32x32b_x16_fill(ta + k * BN + 16, SUM_BIAS);
-            }
-            tmem_st_wait();
-        }
-        tc_fence_before();
-        __syncthreads();
-        tc_fence_after();
-    }
 
     const uint32_t nk = g.n / KSTEP;            // K steps of a tile
     const uint32_t nc = (g.n + BK - 1) / BK;     // shared-memory stages of a tile
@@ -282,19 +275,23 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     } else if (warp == MMA_WARP) {
         if (lane == 0) {
-            // G consecutive blocks share one TMEM-full commit (a commit blocks
-            // its thread for about a hundred cycles, and at blocks of 32 this
-            // one thread would otherwise issue five a stage); NTMEM / G groups
-            // of G accumulators ring through TMEM. Every count is stepped, none
-            // divided, and the descriptors are stepped by adding offsets.
+            // one TMEM-full commit a block (a commit costs this thread next to
+            // nothing while the MMAs run); block accumulators ring through
+            // the NTMEM slots. Every count is stepped, none divided, and the
+            // descriptors are stepped by adding offsets.
             constexpr uint32_t idesc = i8_instr_desc(BM, BN);
-            constexpr uint32_t NGROUP = NTMEM / G;
+            constexpr uint32_t sdesc_i = bf16_instr_desc(BM, BN);
             const uint64_t desc0 = sw128_kmajor_desc(smem_u32(smem));
-            uint32_t s = 0, sph = 0, gc = 0, gs = 0;
+            // the start-value tiles: K-major without swizzle, core matrices
+            // 128 bytes apart along K and 256 bytes apart along the rows
+            const uint64_t seed_a = plain_kmajor_desc(smem_u32(seed), 128, 256);
+            const uint64_t seed_b = plain_kmajor_desc(smem_u32(seed + SEED_BYTES), 128, 256);
+            uint32_t s = 0, sph = 0;      // stage, its phase
+            uint32_t slot = 0, tph = 0;   // TMEM slot, the phase of its release
             bool ok = true;
             for (uint32_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
-                uint32_t kpos = 0, block = 0, kin = 0;  // K step in its block, block, block in its group
-                uint32_t left = nk;                     // K steps of the tile still to issue
+                uint32_t kpos = 0;        // K step in its block
+                uint32_t left = nk;       // K steps of the tile still to issue
                 for (uint32_t c = 0; c < nc && ok; c++) {
                     if (!mbar_wait(&full[s], sph, abort, limit)) {
                         ok = false;
@@ -305,24 +302,24 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const uint32_t jn = left < 4 ? left : 4;
                     left -= jn;
                     for (uint32_t j = 0; j < jn; j++) {
-                        if (kpos == 0 && kin == 0) {
-                            if (!mbar_wait(&tempty[gs], ((gc / NGROUP) & 1) ^ 1, abort, limit)) {
+                        const uint32_t ta = tbase + slot * BN;
+                        if (kpos == 0) {
+                            // the slot's previous block has been read out
+                            if (!mbar_wait(&tempty[slot], tph ^ 1, abort, limit)) {
                                 ok = false;
                                 break;
                             }
                             tc_fence_after();
+                            if constexpr (EXACT_SUM) umma_bf16(ta, seed_a, seed_b, sdesc_i, 0u);
                         }
-                        // onto the bias when sums convert exactly, else from zero
-                        umma_i8(tbase + (gs * G + kin) * BN, adesc + 2 * j, bdesc + 2 * j, idesc,
-                                EXACT_SUM ? 1u : kpos);
+                        // onto the start value when sums convert exactly, else from zero
+                        umma_i8(ta, adesc + 2 * j, bdesc + 2 * j, idesc, EXACT_SUM ? 1u : kpos);
                         if (++kpos == spb) {
                             kpos = 0;
-                            block++;
-                            if (++kin == G || block == nb) {
-                                umma_commit(&tfull[gs]);
-                                kin = 0;
-                                gc++;
-                                gs = gc % NGROUP;
+                            umma_commit(&tfull[slot]);
+                            if (++slot == NTMEM) {
+                                slot = 0;
+                                tph ^= 1;
                             }
                         }
                     }
@@ -345,9 +342,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         // epilogue: frame t of the tile is this thread's TMEM lane
         const uint32_t quarter = warp & 3, cgroup = warp >> 2;
         const uint32_t lane_base = 32 * quarter;
+        const uint32_t tl = tbase + (lane_base << 16) + 32 * cgroup;
         float* tw = epi + warp * (32 * EPI_PITCH);  // this warp's 32 x 32 transpose tile
-        constexpr uint32_t NGROUP = NTMEM / G;
-        uint32_t gc = 0, gs = 0, dcnt = 0;
+        uint32_t slot = 0, tph = 0, dcnt = 0;
         bool ok = true;
         for (uint32_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
             const uint32_t m0 = (tile / g.tiles_n) * BM;
@@ -358,83 +355,51 @@ __global__ void __launch_bounds__(THREADS, 1)
 
             Acc acc;
 #pragma unroll
-            for (int j = 0; j < static_cast<int>(sizeof(Acc) / sizeof(acc[0])); j++) acc[j] = 0;  // +0
+            for (int j = 0; j < 16; j++) acc[j] = 0;  // +0, +0
 
             uint32_t b = 0;
             if constexpr (DTMA) {
-                // four blocks an iteration, the blocks of one chunk of scales:
-                // one wait for the scales, one for each group of G blocks, all
-                // of it unrolled
-                const uint32_t tl = tbase + (lane_base << 16) + 32 * cgroup;
-                for (; b + DCHUNK <= nb; b += DCHUNK) {
+                // four blocks an iteration, the blocks of one chunk of scales
+                // and one turn of the TMEM ring (the slot counter is a
+                // multiple of four here, every tile having a multiple of four
+                // blocks on this path)
+                for (; b < nb; b += DCHUNK) {
                     const uint32_t ds = dcnt % NDS;
                     if (!warp_wait(&dfull[ds], (dcnt / NDS) & 1, lane, abort, limit)) {
                         ok = false;
                         break;
                     }
-                    const float4 dq = *reinterpret_cast<const float4*>(dring + ds * (DS_BYTES / 4) + (lane_base + lane) * DCHUNK);
-                    const float dd[4] = {dq.x, dq.y, dq.z, dq.w};
-#pragma unroll
-                    for (int g2 = 0; g2 < DCHUNK / G; g2++) {
-                        if (!warp_wait(&tfull[gs], (gc / NGROUP) & 1, lane, abort, limit)) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-#pragma unroll
-                        for (int k = 0; k < G; k++) epi_block<RM, EXACT_SUM>(acc, tl + (gs * G + k) * BN, dd[g2 * G + k]);
-                        if constexpr (EXACT_SUM) tmem_st_wait();
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&tempty[gs]);
-                        gc++;
-                        gs = gc % NGROUP;
-                    }
-                    if (!ok) break;
+                    const float4 dq =
+                        *reinterpret_cast<const float4*>(dring + ds * (DS_BYTES / 4) + (lane_base + lane) * DCHUNK);
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&dempty[ds]);
                     dcnt++;
-                }
-            }
-            // the blocks left (every block, without the scales ring), one at a
-            // time; without the ring the frame's scales come from global
-            // memory, one block ahead
-            float dnext = (!DTMA && tvalid && b < nb) ? __ldg(drow + b) : 0.0f;
-            for (; ok && b < nb; b++) {
-                float dv;
-                if constexpr (DTMA) {
-                    const uint32_t ds = dcnt % NDS;
-                    if ((b & (DCHUNK - 1)) == 0 && !warp_wait(&dfull[ds], (dcnt / NDS) & 1, lane, abort, limit)) {
+                    if (!epi_block<RM, EXACT_SUM>(acc, tl, dq.x, &tfull[0], &tempty[0], tph, lane, abort, limit) ||
+                        !epi_block<RM, EXACT_SUM>(acc, tl + BN, dq.y, &tfull[1], &tempty[1], tph, lane, abort, limit) ||
+                        !epi_block<RM, EXACT_SUM>(acc, tl + 2 * BN, dq.z, &tfull[2], &tempty[2], tph, lane, abort,
+                                                  limit) ||
+                        !epi_block<RM, EXACT_SUM>(acc, tl + 3 * BN, dq.w, &tfull[3], &tempty[3], tph, lane, abort,
+                                                  limit)) {
                         ok = false;
                         break;
                     }
-                    dv = dring[ds * (DS_BYTES / 4) + (lane_base + lane) * DCHUNK + (b & (DCHUNK - 1))];
-                } else {
-                    dv = dnext;
+                    tph ^= 1;
+                }
+            } else {
+                // one block at a time, the frame's scales from global memory,
+                // one block ahead
+                float dnext = (tvalid && nb > 0) ? __ldg(drow) : 0.0f;
+                for (; b < nb; b++) {
+                    const float dv = dnext;
                     dnext = (tvalid && b + 1 < nb) ? __ldg(drow + b + 1) : 0.0f;
-                }
-                const uint32_t kin = b & (G - 1);  // block in its group
-                if (kin == 0) {
-                    if (!warp_wait(&tfull[gs], (gc / NGROUP) & 1, lane, abort, limit)) {
+                    if (!epi_block<RM, EXACT_SUM>(acc, tl + slot * BN, dv, &tfull[slot], &tempty[slot], tph, lane,
+                                                  abort, limit)) {
                         ok = false;
                         break;
                     }
-                    tc_fence_after();
-                }
-                epi_block<RM, EXACT_SUM>(acc, tbase + (lane_base << 16) + (gs * G + kin) * BN + 32 * cgroup, dv);
-                if (kin == G - 1 || b == nb - 1) {
-                    if constexpr (EXACT_SUM) tmem_st_wait();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&tempty[gs]);
-                    gc++;
-                    gs = gc % NGROUP;
-                }
-                if constexpr (DTMA) {
-                    if ((b & (DCHUNK - 1)) == DCHUNK - 1 || b == nb - 1) {
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&dempty[dcnt % NDS]);
-                        dcnt++;
+                    if (++slot == NTMEM) {
+                        slot = 0;
+                        tph ^= 1;
                     }
                 }
             }
@@ -487,16 +452,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
+using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs);
+
 template <int RM, bool EXACT_SUM>
 static cudaError_t launch_rm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap* md, const GemmArgs& g,
                              int grid, cudaStream_t stream) {
-    // blocks of up to 64 inputs (two or more a stage) commit in pairs; the
-    // scales go through the TMA ring when they have a tensor map
-    void (*kern)(CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs);
-    if (md)
-        kern = g.qb <= 64 ? gemm_q8_kernel<RM, EXACT_SUM, 2, true> : gemm_q8_kernel<RM, EXACT_SUM, 1, true>;
-    else
-        kern = g.qb <= 64 ? gemm_q8_kernel<RM, EXACT_SUM, 2, false> : gemm_q8_kernel<RM, EXACT_SUM, 1, false>;
+    // the scales go through the TMA ring when they have a tensor map
+    const KernelFn kern = md ? gemm_q8_kernel<RM, EXACT_SUM, true> : gemm_q8_kernel<RM, EXACT_SUM, false>;
     kern<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, md ? *md : ma, g);
     return cudaGetLastError();
 }
@@ -504,9 +466,7 @@ static cudaError_t launch_rm(const CUtensorMap& ma, const CUtensorMap& mb, const
 // Every instance's dynamic shared memory allowance, on the current device.
 template <int RM, bool EXACT_SUM>
 static cudaError_t prepare_rm() {
-    void (*k[4])(CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs) = {
-        gemm_q8_kernel<RM, EXACT_SUM, 1, false>, gemm_q8_kernel<RM, EXACT_SUM, 2, false>,
-        gemm_q8_kernel<RM, EXACT_SUM, 1, true>, gemm_q8_kernel<RM, EXACT_SUM, 2, true>};
+    const KernelFn k[2] = {gemm_q8_kernel<RM, EXACT_SUM, false>, gemm_q8_kernel<RM, EXACT_SUM, true>};
     for (auto f : k) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
         if (e != cudaSuccess) return e;
@@ -538,7 +498,7 @@ cudaError_t launch_gemm_q8(const CUtensorMap& map_a, const CUtensorMap& map_b, c
                            const GemmArgs& g, int num_sms, int rmode, cudaStream_t stream) {
     const uint32_t ntiles = g.tiles_m * g.tiles_n;
     const int grid = static_cast<int>(ntiles < static_cast<uint32_t>(num_sms) ? ntiles : num_sms);
-    // block sums convert to float exactly through the bias trick while
+    // block sums convert to float exactly through the start-value trick while
     // |s| <= 128 * 127 * qb < 2^22, i.e. qb <= 256; wider blocks round
     // the conversion in the mode, as the reference's (float)s does
     const bool exact = g.qb <= 256;
