@@ -28,12 +28,14 @@
 // 1.5 * 2^23 + s, and one exact subtraction gives (float)s (|s| < 2^22,
 // i.e. qb <= 256; wider blocks start from zero and convert in the mode).
 //
-// Warp roles in a 576-thread CTA, one CTA per SM (its 219 KB of shared
+// Warp roles in a 608-thread CTA, one CTA per SM (its 219 KB of shared
 // memory keeps a second off), persistent over the tiles:
 //   warp 16    TMA producer: 128-byte-swizzled 128x128 tiles of activations
 //              and weights into a 4-stage shared-memory ring, and the
 //              activation scales into their own ring
-//   warp 17    allocates TMEM; one thread issues the MMAs and commits
+//   warps 17, 18  one thread each issues the MMAs and commits of alternate
+//              blocks (warp 17 alone where a stage does not hold whole
+//              blocks); warp 17 allocates TMEM
 //   warps 0-15 the epilogue: warp w reads TMEM lanes 32*(w%4).. (the
 //              quarter its hardware warp slot may access) and columns
 //              32*(w/4)..+31 of each block's accumulator, hands the slot back
@@ -67,8 +69,9 @@ constexpr int NTMEM = 4;          // block accumulators in TMEM
 constexpr int TMEM_COLS = NTMEM * BN;  // 512
 constexpr int EPI_WARPS = 16;
 constexpr int TMA_WARP = 16;
-constexpr int MMA_WARP = 17;
-constexpr int THREADS = 18 * 32;
+constexpr int MMA_WARP = 17;      // allocates TMEM; its lane 0 issues the even blocks' MMAs
+constexpr int MMA_WARP2 = 18;     // lane 0 issues the odd blocks' MMAs (the staged paths)
+constexpr int THREADS = 19 * 32;
 constexpr int A_BYTES = BM * BK;
 constexpr int B_BYTES = BN * BK;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -84,7 +87,7 @@ constexpr int SMEM_BYTES =
     NSTAGE * STAGE_BYTES + EPI_BYTES + NDS * DS_BYTES + 2 * SEED_BYTES + BAR_BYTES + 1024;  // + alignment slack
 
 static_assert(TMEM_COLS == 512, "TMEM ring must fit the SM's 512 columns");
-static_assert((2 * NSTAGE + 2 * NTMEM + 2 * NDS + 1) * 8 + 8 <= BAR_BYTES, "barrier area");
+static_assert((2 * NSTAGE + 2 * NTMEM + 2 * NDS + 2) * 8 + 8 <= BAR_BYTES, "barrier area");
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory of one CTA");
 
 // The float 1.5 * 2^23, whose bits 0x4B400000 plus an int32 |s| < 2^22 are
@@ -152,7 +155,9 @@ __device__ __forceinline__ bool epi_block(Acc& acc, uint32_t ta, float dv, uint6
     return true;
 }
 
-template <int RM, bool EXACT_SUM, bool DTMA>
+// SPB: K steps a block (1, 2 or 4, with n a multiple of BK: every stage
+// starts a block and holds four K steps), or 0 for any qb and n.
+template <int RM, bool EXACT_SUM, bool DTMA, int SPB>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_q8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    const __grid_constant__ CUtensorMap map_d, const GemmArgs g) {
@@ -167,8 +172,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t* tempty = tfull + NTMEM;
     uint64_t* dfull = tempty + NTMEM;
     uint64_t* dempty = dfull + NDS;
-    uint64_t* drain = dempty + NDS;
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* drain = dempty + NDS;  // one for each MMA thread
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 2);
     volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -177,7 +182,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < NSTAGE; i++) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 1);
+            mbar_init(&empty[i], SPB ? 2 : 1);  // both MMA threads release a stage on the staged paths
         }
         for (int i = 0; i < NTMEM; i++) {
             mbar_init(&tfull[i], 1);
@@ -187,7 +192,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&dfull[i], 1);
             mbar_init(&dempty[i], EPI_WARPS);
         }
-        mbar_init(drain, 1);
+        mbar_init(&drain[0], 1);
+        mbar_init(&drain[1], 1);
         *abort = 0;
         fence_mbar_init();
     }
@@ -273,12 +279,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                     mbar_drain(&dfull[i % NDS], (i / NDS) & 1, limit);
             }
         }
-    } else if (warp == MMA_WARP) {
-        if (lane == 0) {
-            // one TMEM-full commit a block (a commit costs this thread next to
-            // nothing while the MMAs run); block accumulators ring through
-            // the NTMEM slots. Every count is stepped, none divided, and the
-            // descriptors are stepped by adding offsets.
+    } else if (warp == MMA_WARP || warp == MMA_WARP2) {
+        // one TMEM-full commit a block; block accumulators ring through the
+        // NTMEM slots. Every count is stepped, none divided, and the
+        // descriptors are stepped by adding offsets.
+        const uint32_t me = warp == MMA_WARP ? 0u : 1u;
+        if (lane == 0 && (SPB != 0 || me == 0)) {
             constexpr uint32_t idesc = i8_instr_desc(BM, BN);
             constexpr uint32_t sdesc_i = bf16_instr_desc(BM, BN);
             const uint64_t desc0 = sw128_kmajor_desc(smem_u32(smem));
@@ -286,47 +292,96 @@ __global__ void __launch_bounds__(THREADS, 1)
             // 128 bytes apart along K and 256 bytes apart along the rows
             const uint64_t seed_a = plain_kmajor_desc(smem_u32(seed), 128, 256);
             const uint64_t seed_b = plain_kmajor_desc(smem_u32(seed + SEED_BYTES), 128, 256);
-            uint32_t s = 0, sph = 0;      // stage, its phase
-            uint32_t slot = 0, tph = 0;   // TMEM slot, the phase of its release
+            uint32_t s = 0, sph = 0;  // stage, its phase
             bool ok = true;
-            for (uint32_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
-                uint32_t kpos = 0;        // K step in its block
-                uint32_t left = nk;       // K steps of the tile still to issue
-                for (uint32_t c = 0; c < nc && ok; c++) {
-                    if (!mbar_wait(&full[s], sph, abort, limit)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint64_t adesc = desc0 + ((s * STAGE_BYTES) >> 4);
-                    const uint64_t bdesc = adesc + (A_BYTES >> 4);
-                    const uint32_t jn = left < 4 ? left : 4;
-                    left -= jn;
-                    for (uint32_t j = 0; j < jn; j++) {
-                        const uint32_t ta = tbase + slot * BN;
-                        if (kpos == 0) {
+            if constexpr (SPB != 0) {
+                // Staged: every stage starts a block and holds 4 / SPB whole
+                // blocks. Block b (counted over all tiles, both threads
+                // stepping the count alike) goes to thread b & 1 and TMEM slot
+                // b % 4, so each thread issues into two slots of its own and
+                // the two threads' MMAs, commits and waits overlap: the
+                // issuing thread, not the tensor core, paces a lone thread at
+                // 32-input blocks. The stage's K steps are unrolled.
+                constexpr uint32_t BPS = 4 / SPB;  // blocks a stage
+                uint32_t blk = 0;
+                for (uint32_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+                    for (uint32_t c = 0; c < nc && ok; c++) {
+                        if (!mbar_wait(&full[s], sph, abort, limit)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint64_t adesc = desc0 + ((s * STAGE_BYTES) >> 4);
+                        const uint64_t bdesc = adesc + (A_BYTES >> 4);
+#pragma unroll
+                        for (uint32_t k = 0; k < BPS; k++) {
+                            const uint32_t b = blk + k;
+                            if ((b & 1) != me) continue;
+                            const uint32_t slot = b & (NTMEM - 1);
+                            const uint32_t ta = tbase + slot * BN;
                             // the slot's previous block has been read out
-                            if (!mbar_wait(&tempty[slot], tph ^ 1, abort, limit)) {
+                            if (!mbar_wait(&tempty[slot], ((b / NTMEM) & 1) ^ 1, abort, limit)) {
                                 ok = false;
                                 break;
                             }
                             tc_fence_after();
                             if constexpr (EXACT_SUM) umma_bf16(ta, seed_a, seed_b, sdesc_i, 0u);
-                        }
-                        // onto the start value when sums convert exactly, else from zero
-                        umma_i8(ta, adesc + 2 * j, bdesc + 2 * j, idesc, EXACT_SUM ? 1u : kpos);
-                        if (++kpos == spb) {
-                            kpos = 0;
+#pragma unroll
+                            for (uint32_t j = 0; j < SPB; j++)
+                                umma_i8(ta, adesc + 2 * (k * SPB + j), bdesc + 2 * (k * SPB + j), idesc,
+                                        EXACT_SUM ? 1u : j);
                             umma_commit(&tfull[slot]);
-                            if (++slot == NTMEM) {
-                                slot = 0;
-                                tph ^= 1;
-                            }
+                        }
+                        if (!ok) break;
+                        umma_commit(&empty[s]);
+                        blk += BPS;
+                        if (++s == NSTAGE) {
+                            s = 0;
+                            sph ^= 1;
                         }
                     }
-                    umma_commit(&empty[s]);
-                    if (++s == NSTAGE) {
-                        s = 0;
-                        sph ^= 1;
+                }
+            } else {
+                // any qb and n, one thread
+                uint32_t slot = 0, tph = 0;  // TMEM slot, the phase of its release
+                for (uint32_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+                    uint32_t kpos = 0;   // K step in its block
+                    uint32_t left = nk;  // K steps of the tile still to issue
+                    for (uint32_t c = 0; c < nc && ok; c++) {
+                        if (!mbar_wait(&full[s], sph, abort, limit)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint64_t adesc = desc0 + ((s * STAGE_BYTES) >> 4);
+                        const uint64_t bdesc = adesc + (A_BYTES >> 4);
+                        const uint32_t jn = left < 4 ? left : 4;
+                        left -= jn;
+                        for (uint32_t j = 0; j < jn; j++) {
+                            const uint32_t ta = tbase + slot * BN;
+                            if (kpos == 0) {
+                                // the slot's previous block has been read out
+                                if (!mbar_wait(&tempty[slot], tph ^ 1, abort, limit)) {
+                                    ok = false;
+                                    break;
+                                }
+                                tc_fence_after();
+                                if constexpr (EXACT_SUM) umma_bf16(ta, seed_a, seed_b, sdesc_i, 0u);
+                            }
+                            // onto the start value when sums convert exactly, else from zero
+                            umma_i8(ta, adesc + 2 * j, bdesc + 2 * j, idesc, EXACT_SUM ? 1u : kpos);
+                            if (++kpos == spb) {
+                                kpos = 0;
+                                umma_commit(&tfull[slot]);
+                                if (++slot == NTMEM) {
+                                    slot = 0;
+                                    tph ^= 1;
+                                }
+                            }
+                        }
+                        umma_commit(&empty[s]);
+                        if (++s == NSTAGE) {
+                            s = 0;
+                            sph ^= 1;
+                        }
                     }
                 }
             }
@@ -334,8 +389,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 *abort = 1;
                 atomicOr(g.err, PKB_DEVERR_TIMEOUT);
                 // the MMAs this thread issued: let them finish before TMEM is freed
-                umma_commit(drain);
-                mbar_drain(drain, 0, limit);
+                umma_commit(&drain[me]);
+                mbar_drain(&drain[me], 0, limit);
             }
         }
     } else {
@@ -454,11 +509,24 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs);
 
+// The instance for these arguments: the staged MMA paths where qb is 32, 64
+// or 128 and n a multiple of BK, the scales through the TMA ring where they
+// have a tensor map.
+template <int RM, bool EXACT_SUM>
+static KernelFn pick(uint32_t n, uint32_t qb, bool dtma) {
+    if constexpr (EXACT_SUM) {
+        const uint32_t spb = qb / KSTEP;
+        if (n % BK == 0 && spb == 1) return dtma ? gemm_q8_kernel<RM, true, true, 1> : gemm_q8_kernel<RM, true, false, 1>;
+        if (n % BK == 0 && spb == 2) return dtma ? gemm_q8_kernel<RM, true, true, 2> : gemm_q8_kernel<RM, true, false, 2>;
+        if (n % BK == 0 && spb == 4) return dtma ? gemm_q8_kernel<RM, true, true, 4> : gemm_q8_kernel<RM, true, false, 4>;
+    }
+    return dtma ? gemm_q8_kernel<RM, EXACT_SUM, true, 0> : gemm_q8_kernel<RM, EXACT_SUM, false, 0>;
+}
+
 template <int RM, bool EXACT_SUM>
 static cudaError_t launch_rm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap* md, const GemmArgs& g,
                              int grid, cudaStream_t stream) {
-    // the scales go through the TMA ring when they have a tensor map
-    const KernelFn kern = md ? gemm_q8_kernel<RM, EXACT_SUM, true> : gemm_q8_kernel<RM, EXACT_SUM, false>;
+    const KernelFn kern = pick<RM, EXACT_SUM>(g.n, g.qb, md != nullptr);
     kern<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, md ? *md : ma, g);
     return cudaGetLastError();
 }
@@ -466,7 +534,10 @@ static cudaError_t launch_rm(const CUtensorMap& ma, const CUtensorMap& mb, const
 // Every instance's dynamic shared memory allowance, on the current device.
 template <int RM, bool EXACT_SUM>
 static cudaError_t prepare_rm() {
-    const KernelFn k[2] = {gemm_q8_kernel<RM, EXACT_SUM, false>, gemm_q8_kernel<RM, EXACT_SUM, true>};
+    const KernelFn k[8] = {gemm_q8_kernel<RM, EXACT_SUM, false, 0>, gemm_q8_kernel<RM, EXACT_SUM, true, 0>,
+                           pick<RM, EXACT_SUM>(BK, 32, false),       pick<RM, EXACT_SUM>(BK, 32, true),
+                           pick<RM, EXACT_SUM>(BK, 64, false),       pick<RM, EXACT_SUM>(BK, 64, true),
+                           pick<RM, EXACT_SUM>(BK, 128, false),      pick<RM, EXACT_SUM>(BK, 128, true)};
     for (auto f : k) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
         if (e != cudaSuccess) return e;
