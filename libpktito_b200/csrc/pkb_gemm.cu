@@ -127,23 +127,27 @@ __device__ __forceinline__ float acc_at(const Acc& acc, int j) {
     return (j & 1) ? hi : lo;
 }
 
-// Lane 0 waits for `bar`'s phase and tells the warp (the TMEM loads that
-// follow are whole-warp instructions); false if the wait gave up.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int lane, volatile int* abort,
-                                          long long limit) {
-    uint32_t seen = 1;
-    if (lane == 0) seen = mbar_wait(bar, parity, abort, limit) ? 1u : 0u;
-    return __shfl_sync(0xffffffffu, seen, 0) != 0;
+// The whole warp waits for `bar`'s phase: every lane polls the barrier, so
+// the warp stays converged for the whole-warp TMEM loads that follow, with
+// no branch around one lane's wait and no shuffle (measured on B200: a
+// lane-0 wait and a shuffle cost the epilogue a third of its time at
+// 32-input blocks). False if the wait gave up.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort, long long limit) {
+    const bool ok = mbar_wait(bar, parity, abort, limit);
+    __syncwarp();
+    return ok;
 }
 
-// One block's accumulator (the warp's 32 columns at ta) out of TMEM: waits
-// for the MMAs, loads, hands the slot back to the MMA thread and runs the
-// chain. False if the wait gave up.
+// Block accumulators are handed over in pairs: block B (counted over all of
+// a CTA's tiles) lives in TMEM slot B % 4, and its pair B / 2 is announced
+// by one commit on tfull[(B / 2) % 2]. The epilogue waits once a pair and
+// releases each slot on its own as soon as it has been loaded.
+//
+// One block's accumulator (the warp's 32 columns at ta) out of TMEM, after
+// its pair's wait: loads, hands the slot back to the MMA threads and runs
+// the chain.
 template <int RM, bool EXACT_SUM>
-__device__ __forceinline__ bool epi_block(Acc& acc, uint32_t ta, float dv, uint64_t* tfull, uint64_t* tempty,
-                                          uint32_t parity, int lane, volatile int* abort, long long limit) {
-    if (!warp_wait(tfull, parity, lane, abort, limit)) return false;
-    tc_fence_after();
+__device__ __forceinline__ void epi_block(Acc& acc, uint32_t ta, float dv, uint64_t* tempty, int lane) {
     uint32_t sv[32];
     tmem_ld_32x32b_x16(ta, *reinterpret_cast<uint32_t(*)[16]>(&sv[0]));
     tmem_ld_32x32b_x16(ta + 16, *reinterpret_cast<uint32_t(*)[16]>(&sv[16]));
@@ -152,7 +156,6 @@ __device__ __forceinline__ bool epi_block(Acc& acc, uint32_t ta, float dv, uint6
     __syncwarp();
     if (lane == 0) mbar_arrive(tempty);
     chain32<RM, EXACT_SUM>(acc, sv, dv);
-    return true;
 }
 
 // SPB: K steps a block (1, 2 or 4, with n a multiple of BK: every stage
@@ -294,16 +297,20 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint64_t seed_b = plain_kmajor_desc(smem_u32(seed + SEED_BYTES), 128, 256);
             uint32_t s = 0, sph = 0;  // stage, its phase
             bool ok = true;
+            // Block B (counted over all tiles) goes to TMEM slot B % 4; the
+            // slot's previous block B - 4 must have been read out first
+            // (phase ((B / 4) & 1) ^ 1 of tempty[B % 4]). Pair B / 2 is
+            // committed on tfull[(B / 2) & 1] after its second block (or
+            // after the CTA's last block when that one is alone).
+            uint32_t blk = 0;  // blocks issued or passed (all tiles)
             if constexpr (SPB != 0) {
                 // Staged: every stage starts a block and holds 4 / SPB whole
-                // blocks. Block b (counted over all tiles, both threads
-                // stepping the count alike) goes to thread b & 1 and TMEM slot
-                // b % 4, so each thread issues into two slots of its own and
-                // the two threads' MMAs, commits and waits overlap: the
-                // issuing thread, not the tensor core, paces a lone thread at
-                // 32-input blocks. The stage's K steps are unrolled.
+                // blocks; pair P goes to thread P & 1, so each thread issues
+                // into two slots of its own and the two threads' MMAs,
+                // commits and waits overlap (the issuing thread, not the
+                // tensor core, paces a lone thread at 32-input blocks). The
+                // stage's K steps are unrolled.
                 constexpr uint32_t BPS = 4 / SPB;  // blocks a stage
-                uint32_t blk = 0;
                 for (uint32_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
                     for (uint32_t c = 0; c < nc && ok; c++) {
                         if (!mbar_wait(&full[s], sph, abort, limit)) {
@@ -315,11 +322,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                         for (uint32_t k = 0; k < BPS; k++) {
                             const uint32_t b = blk + k;
-                            if ((b & 1) != me) continue;
+                            if (((b >> 1) & 1) != me) continue;
                             const uint32_t slot = b & (NTMEM - 1);
                             const uint32_t ta = tbase + slot * BN;
-                            // the slot's previous block has been read out
-                            if (!mbar_wait(&tempty[slot], ((b / NTMEM) & 1) ^ 1, abort, limit)) {
+                            if (!mbar_wait(&tempty[slot], ((b >> 2) & 1) ^ 1, abort, limit)) {
                                 ok = false;
                                 break;
                             }
@@ -329,7 +335,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                             for (uint32_t j = 0; j < SPB; j++)
                                 umma_i8(ta, adesc + 2 * (k * SPB + j), bdesc + 2 * (k * SPB + j), idesc,
                                         EXACT_SUM ? 1u : j);
-                            umma_commit(&tfull[slot]);
+                            if (b & 1) umma_commit(&tfull[(b >> 1) & 1]);
                         }
                         if (!ok) break;
                         umma_commit(&empty[s]);
@@ -340,9 +346,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                         }
                     }
                 }
+                // a last pair of one block is committed by its thread
+                if (ok && (blk & 1) && (((blk - 1) >> 1) & 1) == me) umma_commit(&tfull[((blk - 1) >> 1) & 1]);
             } else {
                 // any qb and n, one thread
-                uint32_t slot = 0, tph = 0;  // TMEM slot, the phase of its release
                 for (uint32_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
                     uint32_t kpos = 0;   // K step in its block
                     uint32_t left = nk;  // K steps of the tile still to issue
@@ -356,10 +363,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const uint32_t jn = left < 4 ? left : 4;
                         left -= jn;
                         for (uint32_t j = 0; j < jn; j++) {
+                            const uint32_t slot = blk & (NTMEM - 1);
                             const uint32_t ta = tbase + slot * BN;
                             if (kpos == 0) {
-                                // the slot's previous block has been read out
-                                if (!mbar_wait(&tempty[slot], tph ^ 1, abort, limit)) {
+                                if (!mbar_wait(&tempty[slot], ((blk >> 2) & 1) ^ 1, abort, limit)) {
                                     ok = false;
                                     break;
                                 }
@@ -370,11 +377,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                             umma_i8(ta, adesc + 2 * j, bdesc + 2 * j, idesc, EXACT_SUM ? 1u : kpos);
                             if (++kpos == spb) {
                                 kpos = 0;
-                                umma_commit(&tfull[slot]);
-                                if (++slot == NTMEM) {
-                                    slot = 0;
-                                    tph ^= 1;
-                                }
+                                if (blk & 1) umma_commit(&tfull[(blk >> 1) & 1]);
+                                blk++;
                             }
                         }
                         umma_commit(&empty[s]);
@@ -384,6 +388,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         }
                     }
                 }
+                if (ok && (blk & 1)) umma_commit(&tfull[((blk - 1) >> 1) & 1]);
             }
             if (!ok) {
                 *abort = 1;
@@ -399,7 +404,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t lane_base = 32 * quarter;
         const uint32_t tl = tbase + (lane_base << 16) + 32 * cgroup;
         float* tw = epi + warp * (32 * EPI_PITCH);  // this warp's 32 x 32 transpose tile
-        uint32_t slot = 0, tph = 0, dcnt = 0;
+        uint32_t gb = 0, dcnt = 0;  // blocks consumed (all tiles), scale chunks consumed
         bool ok = true;
         for (uint32_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
             const uint32_t m0 = (tile / g.tiles_n) * BM;
@@ -412,15 +417,13 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int j = 0; j < 16; j++) acc[j] = 0;  // +0, +0
 
-            uint32_t b = 0;
             if constexpr (DTMA) {
-                // four blocks an iteration, the blocks of one chunk of scales
-                // and one turn of the TMEM ring (the slot counter is a
-                // multiple of four here, every tile having a multiple of four
-                // blocks on this path)
-                for (; b < nb; b += DCHUNK) {
+                // four blocks an iteration: one chunk of scales, two pairs,
+                // one turn of the TMEM ring (every tile has a multiple of
+                // four blocks on this path, so gb is one here too)
+                for (uint32_t b = 0; b < nb; b += DCHUNK) {
                     const uint32_t ds = dcnt % NDS;
-                    if (!warp_wait(&dfull[ds], (dcnt / NDS) & 1, lane, abort, limit)) {
+                    if (!warp_wait(&dfull[ds], (dcnt / NDS) & 1, abort, limit)) {
                         ok = false;
                         break;
                     }
@@ -429,33 +432,39 @@ __global__ void __launch_bounds__(THREADS, 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&dempty[ds]);
                     dcnt++;
-                    if (!epi_block<RM, EXACT_SUM>(acc, tl, dq.x, &tfull[0], &tempty[0], tph, lane, abort, limit) ||
-                        !epi_block<RM, EXACT_SUM>(acc, tl + BN, dq.y, &tfull[1], &tempty[1], tph, lane, abort, limit) ||
-                        !epi_block<RM, EXACT_SUM>(acc, tl + 2 * BN, dq.z, &tfull[2], &tempty[2], tph, lane, abort,
-                                                  limit) ||
-                        !epi_block<RM, EXACT_SUM>(acc, tl + 3 * BN, dq.w, &tfull[3], &tempty[3], tph, lane, abort,
-                                                  limit)) {
+                    const uint32_t tph = (gb >> 2) & 1;
+                    if (!warp_wait(&tfull[0], tph, abort, limit)) {
                         ok = false;
                         break;
                     }
-                    tph ^= 1;
+                    tc_fence_after();
+                    epi_block<RM, EXACT_SUM>(acc, tl, dq.x, &tempty[0], lane);
+                    epi_block<RM, EXACT_SUM>(acc, tl + BN, dq.y, &tempty[1], lane);
+                    if (!warp_wait(&tfull[1], tph, abort, limit)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    epi_block<RM, EXACT_SUM>(acc, tl + 2 * BN, dq.z, &tempty[2], lane);
+                    epi_block<RM, EXACT_SUM>(acc, tl + 3 * BN, dq.w, &tempty[3], lane);
+                    gb += 4;
                 }
             } else {
                 // one block at a time, the frame's scales from global memory,
-                // one block ahead
+                // one block ahead; a pair may straddle two tiles
                 float dnext = (tvalid && nb > 0) ? __ldg(drow) : 0.0f;
-                for (; b < nb; b++) {
+                for (uint32_t b = 0; b < nb; b++, gb++) {
                     const float dv = dnext;
                     dnext = (tvalid && b + 1 < nb) ? __ldg(drow + b + 1) : 0.0f;
-                    if (!epi_block<RM, EXACT_SUM>(acc, tl + slot * BN, dv, &tfull[slot], &tempty[slot], tph, lane,
-                                                  abort, limit)) {
-                        ok = false;
-                        break;
+                    if ((gb & 1) == 0) {
+                        if (!warp_wait(&tfull[(gb >> 1) & 1], (gb >> 2) & 1, abort, limit)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
                     }
-                    if (++slot == NTMEM) {
-                        slot = 0;
-                        tph ^= 1;
-                    }
+                    const uint32_t slot = gb & (NTMEM - 1);
+                    epi_block<RM, EXACT_SUM>(acc, tl + slot * BN, dv, &tempty[slot], lane);
                 }
             }
             if (!ok) break;
