@@ -192,22 +192,33 @@ int gemm_dev(cudaStream_t stream, float* out, size_t os, const int8_t* wpack, co
     g.tiles_m = (T + gemm_tile_rows() - 1) / gemm_tile_rows();
     g.tiles_n = (rows + gemm_tile_cols() - 1) / gemm_tile_cols();
     g.timeout = wait_limit();
-    // the scales through TMA where their rows are whole 16-byte units
-    CUtensorMap md;
+    // scales, row scales, biases and results through TMA where their rows
+    // are whole 16-byte units
+    CUtensorMap md, mo;
     const CUtensorMap* mdp = nullptr;
+    const CUtensorMap* mop = nullptr;
     const uint32_t nb = n / qb;
-    if (nb % 4 == 0 && aligned(d, 16)) {
-        cuuint64_t dims[2] = {nb, T};
-        cuuint64_t strides[1] = {static_cast<cuuint64_t>(nb) * 4};
-        cuuint32_t box[2] = {static_cast<cuuint32_t>(gemm_scale_chunk()), static_cast<cuuint32_t>(gemm_tile_rows())};
+    if (nb % 4 == 0 && aligned(d, 16) && os % 4 == 0 && aligned(out, 16) && aligned(ws, 16) &&
+        (!bias || aligned(bias, 16))) {
         cuuint32_t estr[2] = {1, 1};
-        CUresult r = g_encode(&md, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(d), dims, strides, box, estr,
-                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+        cuuint64_t ddims[2] = {nb, T};
+        cuuint64_t dstrides[1] = {static_cast<cuuint64_t>(nb) * 4};
+        cuuint32_t dbox[2] = {static_cast<cuuint32_t>(gemm_scale_box()), static_cast<cuuint32_t>(gemm_tile_rows())};
+        CUresult r = g_encode(&md, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(d), ddims, dstrides, dbox,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                               CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) return fail(PKB_ECUDA, "cuTensorMapEncodeTiled (scales) failed (%d)", static_cast<int>(r));
+        cuuint64_t odims[2] = {rows, T};
+        cuuint64_t ostrides[1] = {static_cast<cuuint64_t>(os) * 4};
+        cuuint32_t obox[2] = {static_cast<cuuint32_t>(gemm_out_box()), static_cast<cuuint32_t>(gemm_out_box())};
+        r = g_encode(&mo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, out, odims, ostrides, obox, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return fail(PKB_ECUDA, "cuTensorMapEncodeTiled (results) failed (%d)", static_cast<int>(r));
         mdp = &md;
+        mop = &mo;
     }
-    PKB_CUDA(launch_gemm_q8(ma, mb, mdp, g, dev->sms, rmode, stream), "gemm_q8 launch");
+    PKB_CUDA(launch_gemm_q8(ma, mb, mdp, mop, g, dev->sms, rmode, stream), "gemm_q8 launch");
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return PKB_OK;
 }

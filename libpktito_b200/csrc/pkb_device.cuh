@@ -189,6 +189,41 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, void* dst, u
         : "memory");
 }
 
+// `bytes` (a multiple of 16) from global `src` into this CTA's shared memory
+// `dst` (both 16-byte aligned), completing as bytes on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// A 2-D tile of this CTA's shared memory into `map` at element coordinates
+// (x inner, y outer), asynchronously, in the thread's current bulk group;
+// elements outside the tensor are not written. x * element size is a
+// multiple of 16 bytes and both coordinates are non-negative at every call
+// site.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_u32(src)), "r"(x), "r"(y)
+                 : "memory");
+}
+
+// Closes the thread's current bulk group of TMA stores.
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Waits until the thread's bulk groups have finished reading their shared
+// memory (the source may be written again).
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
+// Waits until the thread's bulk groups have completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy (TMA, tensor core) reads of them.
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // ------------------------------------------------------------------- tcgen05 --
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {

@@ -75,19 +75,25 @@ constexpr int THREADS = 19 * 32;
 constexpr int A_BYTES = BM * BK;
 constexpr int B_BYTES = BN * BK;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int EPI_PITCH = 33;      // floats a row of an epilogue warp's transpose tile
+constexpr int EPI_PITCH = 33;      // floats a row of an epilogue warp's transpose tile (plain stores)
 constexpr int EPI_BYTES = EPI_WARPS * 32 * EPI_PITCH * 4;
-constexpr int DCHUNK = 4;          // blocks of scales a TMA box of d carries (16 bytes a frame)
-constexpr int NDS = 8;             // slots of the scales ring
-constexpr int DS_BYTES = BM * DCHUNK * 4;
+constexpr int STG_BYTES = 32 * 32 * 4;  // an epilogue warp's 128-byte-swizzled staging box (TMA stores)
+static_assert(EPI_WARPS * STG_BYTES <= EPI_BYTES, "staging boxes share the transpose area");
+constexpr int CHUNK = 4;           // blocks a turn of the TMEM ring
+constexpr int DBLK = 8;            // blocks of scales a TMA box of d carries (32 bytes a frame)
+constexpr int NDS = 4;             // slots of the scales ring (24 blocks ahead)
+constexpr int DS_BYTES = BM * DBLK * 4;
+constexpr int WS_BYTES = 2 * BN * 4;  // a tile's row scales, then its biases
+constexpr int NWS = 2;             // slots of their ring (a tile each)
 constexpr int SEED_K = 16;         // K of the bf16 MMA that writes the accumulator's start value
 constexpr int SEED_BYTES = 128 * SEED_K * 2;  // one 128-row bf16 operand tile of it
 constexpr int BAR_BYTES = 512;
 constexpr int SMEM_BYTES =
-    NSTAGE * STAGE_BYTES + EPI_BYTES + NDS * DS_BYTES + 2 * SEED_BYTES + BAR_BYTES + 1024;  // + alignment slack
+    NSTAGE * STAGE_BYTES + EPI_BYTES + NDS * DS_BYTES + NWS * WS_BYTES + 2 * SEED_BYTES + BAR_BYTES +
+    1024;  // + alignment slack
 
 static_assert(TMEM_COLS == 512, "TMEM ring must fit the SM's 512 columns");
-static_assert((2 * NSTAGE + 2 * NTMEM + 2 * NDS + 2) * 8 + 8 <= BAR_BYTES, "barrier area");
+static_assert((2 * NSTAGE + 2 + NTMEM + 2 + EPI_WARPS + 2 * NDS + 2 * NWS) * 8 + 8 <= BAR_BYTES, "barrier area");
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory of one CTA");
 
 // The float 1.5 * 2^23, whose bits 0x4B400000 plus an int32 |s| < 2^22 are
@@ -141,7 +147,9 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
 // Block accumulators are handed over in pairs: block B (counted over all of
 // a CTA's tiles) lives in TMEM slot B % 4, and its pair B / 2 is announced
 // by one commit on tfull[(B / 2) % 2]. The epilogue waits once a pair and
-// releases each slot on its own as soon as it has been loaded.
+// releases each slot on its own as soon as it has been loaded (waiting for
+// whole turns of the ring instead, measured on B200, leaves the MMAs of a
+// turn's last pair too little time).
 //
 // One block's accumulator (the warp's 32 columns at ta) out of TMEM, after
 // its pair's wait: loads, hands the slot back to the MMA threads and runs
@@ -160,23 +168,35 @@ __device__ __forceinline__ void epi_block(Acc& acc, uint32_t ta, float dv, uint6
 
 // SPB: K steps a block (1, 2 or 4, with n a multiple of BK: every stage
 // starts a block and holds four K steps), or 0 for any qb and n.
-template <int RM, bool EXACT_SUM, bool DTMA, int SPB>
+// TIO (a multiple of four blocks a tile; the scales' rows, the results' rows
+// and the row scales and biases whole 16-byte units): the block scales come
+// through a TMA ring (map_d), the row scales and biases through a bulk-copy
+// ring, the results leave through TMA stores (map_o), so the epilogue's
+// loop holds no global load (on B200 a global load in flight there costs
+// the chain as much as one waited for at once); otherwise plain loads and
+// stores.
+template <int RM, bool EXACT_SUM, bool TIO, int SPB>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_q8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                   const __grid_constant__ CUtensorMap map_d, const GemmArgs g) {
+                   const __grid_constant__ CUtensorMap map_d, const __grid_constant__ CUtensorMap map_o,
+                   const GemmArgs g) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float* epi = reinterpret_cast<float*>(smem + NSTAGE * STAGE_BYTES);
     float* dring = reinterpret_cast<float*>(smem + NSTAGE * STAGE_BYTES + EPI_BYTES);
-    uint8_t* seed = smem + NSTAGE * STAGE_BYTES + EPI_BYTES + NDS * DS_BYTES;  // A tile, then B tile
+    float* wsring = reinterpret_cast<float*>(smem + NSTAGE * STAGE_BYTES + EPI_BYTES + NDS * DS_BYTES);
+    uint8_t* seed = smem + NSTAGE * STAGE_BYTES + EPI_BYTES + NDS * DS_BYTES + NWS * WS_BYTES;  // A tile, B tile
     uint64_t* full = reinterpret_cast<uint64_t*>(seed + 2 * SEED_BYTES);
     uint64_t* empty = full + NSTAGE;
-    uint64_t* tfull = empty + NSTAGE;
-    uint64_t* tempty = tfull + NTMEM;
-    uint64_t* dfull = tempty + NTMEM;
+    uint64_t* tfull = empty + NSTAGE;  // [2]: pairs announced
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + NTMEM;  // one for each MMA thread
+    uint64_t* obar = drain + 2;      // an epilogue warp's load of the results it adds to
+    uint64_t* dfull = obar + EPI_WARPS;
     uint64_t* dempty = dfull + NDS;
-    uint64_t* drain = dempty + NDS;  // one for each MMA thread
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 2);
+    uint64_t* wsfull = dempty + NDS;
+    uint64_t* wsempty = wsfull + NWS;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(wsempty + NWS);
     volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -187,16 +207,20 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], SPB ? 2 : 1);  // both MMA threads release a stage on the staged paths
         }
-        for (int i = 0; i < NTMEM; i++) {
-            mbar_init(&tfull[i], 1);
-            mbar_init(&tempty[i], EPI_WARPS);
-        }
+        mbar_init(&tfull[0], 1);
+        mbar_init(&tfull[1], 1);
+        for (int i = 0; i < NTMEM; i++) mbar_init(&tempty[i], EPI_WARPS);
+        mbar_init(&drain[0], 1);
+        mbar_init(&drain[1], 1);
+        for (int i = 0; i < EPI_WARPS; i++) mbar_init(&obar[i], 1);
         for (int i = 0; i < NDS; i++) {
             mbar_init(&dfull[i], 1);
             mbar_init(&dempty[i], EPI_WARPS);
         }
-        mbar_init(&drain[0], 1);
-        mbar_init(&drain[1], 1);
+        for (int i = 0; i < NWS; i++) {
+            mbar_init(&wsfull[i], 1);
+            mbar_init(&wsempty[i], EPI_WARPS);
+        }
         *abort = 0;
         fence_mbar_init();
     }
@@ -217,7 +241,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (warp == TMA_WARP && lane == 0) {
         tma_prefetch_map(&map_a);
         tma_prefetch_map(&map_b);
-        if constexpr (DTMA) tma_prefetch_map(&map_d);
+        if constexpr (TIO) {
+            tma_prefetch_map(&map_d);
+            tma_prefetch_map(&map_o);
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -233,19 +260,35 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     if (warp == TMA_WARP) {
         if (lane == 0) {
-            uint32_t it = 0, dcnt = 0;
-            const uint32_t nchunks = (nb + DCHUNK - 1) / DCHUNK;
+            uint32_t it = 0, dcnt = 0, wcnt = 0;
+            const uint32_t nchunks = (nb + DBLK - 1) / DBLK;
             bool ok = true;
             for (uint32_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
                 const int m0 = static_cast<int>((tile / g.tiles_n) * BM);
                 const int n0 = static_cast<int>((tile % g.tiles_n) * BN);
+                if constexpr (TIO) {
+                    // the tile's row scales and biases (rows a multiple of 16,
+                    // so every copy is whole 64-byte units)
+                    const uint32_t wsl = wcnt % NWS;
+                    if (!mbar_wait(&wsempty[wsl], ((wcnt / NWS) & 1) ^ 1, abort, limit)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t ncol = g.rows - n0 < static_cast<uint32_t>(BN) ? g.rows - n0 : BN;
+                    mbar_arrive_expect_tx(&wsfull[wsl], (g.bias ? 2 : 1) * ncol * 4);
+                    float* wd = wsring + wsl * (WS_BYTES / 4);
+                    bulk_load(wd, g.ws + n0, ncol * 4, &wsfull[wsl]);
+                    if (g.bias) bulk_load(wd + BN, g.bias + n0, ncol * 4, &wsfull[wsl]);
+                    wcnt++;
+                }
                 uint32_t dk = 0;  // the tile's next chunk of scales
                 for (uint32_t c = 0; ok && c < nc; c++, it++) {
-                    if constexpr (DTMA) {
+                    if constexpr (TIO) {
                         // the scales of every chunk of blocks starting in this
                         // stage's K range, into the scales ring (the box's x,
-                        // a multiple of 4 floats, is 16-byte aligned)
-                        while (dk < nchunks && DCHUNK * dk * g.qb < (c + 1) * BK) {
+                        // a multiple of 8 floats, is 16-byte aligned; blocks
+                        // past n / qb read as zeros)
+                        while (dk < nchunks && DBLK * dk * g.qb < (c + 1) * BK) {
                             const uint32_t ds = dcnt % NDS;
                             if (!mbar_wait(&dempty[ds], ((dcnt / NDS) & 1) ^ 1, abort, limit)) {
                                 ok = false;
@@ -253,7 +296,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                             }
                             mbar_arrive_expect_tx(&dfull[ds], DS_BYTES);
                             tma_load_2d(&map_d, reinterpret_cast<uint8_t*>(dring) + ds * DS_BYTES, &dfull[ds],
-                                        static_cast<int>(DCHUNK * dk), m0);
+                                        static_cast<int>(DBLK * dk), m0);
                             dk++;
                             dcnt++;
                         }
@@ -280,6 +323,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const uint32_t dback = dcnt < NDS ? dcnt : NDS;
                 for (uint32_t i = dcnt - dback; i < dcnt; i++)
                     mbar_drain(&dfull[i % NDS], (i / NDS) & 1, limit);
+                const uint32_t wback = wcnt < NWS ? wcnt : NWS;
+                for (uint32_t i = wcnt - wback; i < wcnt; i++)
+                    mbar_drain(&wsfull[i % NWS], (i / NWS) & 1, limit);
             }
         }
     } else if (warp == MMA_WARP || warp == MMA_WARP2) {
@@ -303,6 +349,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             // committed on tfull[(B / 2) & 1] after its second block (or
             // after the CTA's last block when that one is alone).
             uint32_t blk = 0;  // blocks issued or passed (all tiles)
+            auto pair_bar = [&](uint32_t b) { return &tfull[(b >> 1) & 1]; };
             if constexpr (SPB != 0) {
                 // Staged: every stage starts a block and holds 4 / SPB whole
                 // blocks; pair P goes to thread P & 1, so each thread issues
@@ -335,7 +382,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                             for (uint32_t j = 0; j < SPB; j++)
                                 umma_i8(ta, adesc + 2 * (k * SPB + j), bdesc + 2 * (k * SPB + j), idesc,
                                         EXACT_SUM ? 1u : j);
-                            if (b & 1) umma_commit(&tfull[(b >> 1) & 1]);
+                            if (b & 1) umma_commit(pair_bar(b));
                         }
                         if (!ok) break;
                         umma_commit(&empty[s]);
@@ -347,7 +394,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                 }
                 // a last pair of one block is committed by its thread
-                if (ok && (blk & 1) && (((blk - 1) >> 1) & 1) == me) umma_commit(&tfull[((blk - 1) >> 1) & 1]);
+                if (ok && (blk & 1) && (((blk - 1) >> 1) & 1) == me) umma_commit(pair_bar(blk - 1));
             } else {
                 // any qb and n, one thread
                 for (uint32_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
@@ -377,7 +424,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                             umma_i8(ta, adesc + 2 * j, bdesc + 2 * j, idesc, EXACT_SUM ? 1u : kpos);
                             if (++kpos == spb) {
                                 kpos = 0;
-                                if (blk & 1) umma_commit(&tfull[(blk >> 1) & 1]);
+                                if (blk & 1) umma_commit(pair_bar(blk));
                                 blk++;
                             }
                         }
@@ -388,7 +435,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         }
                     }
                 }
-                if (ok && (blk & 1)) umma_commit(&tfull[((blk - 1) >> 1) & 1]);
+                if (ok && (blk & 1)) umma_commit(pair_bar(blk - 1));
             }
             if (!ok) {
                 *abort = 1;
@@ -404,7 +451,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t lane_base = 32 * quarter;
         const uint32_t tl = tbase + (lane_base << 16) + 32 * cgroup;
         float* tw = epi + warp * (32 * EPI_PITCH);  // this warp's 32 x 32 transpose tile
-        uint32_t gb = 0, dcnt = 0;  // blocks consumed (all tiles), scale chunks consumed
+        uint8_t* stg = reinterpret_cast<uint8_t*>(epi) + warp * STG_BYTES;  // its staging box (1024-aligned)
+        uint32_t gb = 0;            // blocks consumed (all tiles)
+        uint32_t dcnt = 0, wcnt = 0;  // scale chunks, row-scale slots consumed
+        uint32_t ocnt = 0;          // loads of results to add to
         bool ok = true;
         for (uint32_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
             const uint32_t m0 = (tile / g.tiles_n) * BM;
@@ -417,21 +467,38 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int j = 0; j < 16; j++) acc[j] = 0;  // +0, +0
 
-            if constexpr (DTMA) {
-                // four blocks an iteration: one chunk of scales, two pairs,
-                // one turn of the TMEM ring (every tile has a multiple of
-                // four blocks on this path, so gb is one here too)
-                for (uint32_t b = 0; b < nb; b += DCHUNK) {
+            // the warp's box of the results: 32 output rows from col0 by 32
+            // frames from frame0
+            const uint32_t col0 = n0 + 32 * cgroup, frame0 = m0 + lane_base;
+            const bool live = col0 < g.rows && frame0 < g.T;
+            if constexpr (TIO) {
+                if (g.add && live && lane == 0) {
+                    // the results added to, into the staging box once the
+                    // previous tile's store has read it
+                    bulk_wait_read();
+                    mbar_arrive_expect_tx(&obar[warp], STG_BYTES);
+                    tma_load_2d(&map_o, stg, &obar[warp], static_cast<int>(col0), static_cast<int>(frame0));
+                }
+            }
+
+            if constexpr (TIO) {
+                // four blocks an iteration, two pairs; the frame's four scales
+                // one 16-byte shared load out of the chunk of eight blocks
+                // the scales ring holds (one wait a chunk)
+                for (uint32_t b = 0; b < nb; b += CHUNK) {
                     const uint32_t ds = dcnt % NDS;
-                    if (!warp_wait(&dfull[ds], (dcnt / NDS) & 1, abort, limit)) {
+                    if ((b & (DBLK - 1)) == 0 && !warp_wait(&dfull[ds], (dcnt / NDS) & 1, abort, limit)) {
                         ok = false;
                         break;
                     }
-                    const float4 dq =
-                        *reinterpret_cast<const float4*>(dring + ds * (DS_BYTES / 4) + (lane_base + lane) * DCHUNK);
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&dempty[ds]);
-                    dcnt++;
+                    const float4 dq = *reinterpret_cast<const float4*>(dring + ds * (DS_BYTES / 4) +
+                                                                       (lane_base + lane) * DBLK + (b & (DBLK - 1)));
+                    if ((b & (DBLK - 1)) == DBLK - CHUNK || b + CHUNK >= nb) {
+                        // the chunk's last use (or the tile's): the slot goes back
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&dempty[ds]);
+                        dcnt++;
+                    }
                     const uint32_t tph = (gb >> 2) & 1;
                     if (!warp_wait(&tfull[0], tph, abort, limit)) {
                         ok = false;
@@ -447,7 +514,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     tc_fence_after();
                     epi_block<RM, EXACT_SUM>(acc, tl + 2 * BN, dq.z, &tempty[2], lane);
                     epi_block<RM, EXACT_SUM>(acc, tl + 3 * BN, dq.w, &tempty[3], lane);
-                    gb += 4;
+                    gb += CHUNK;
                 }
             } else {
                 // one block at a time, the frame's scales from global memory,
@@ -469,43 +536,107 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             if (!ok) break;
 
-            // through shared memory, so that a lane owns one output row (a
-            // column of the tile) and each store is 32 consecutive floats
+            if constexpr (TIO) {
+                // Lane i holds frame frame0 + i, i.e. row i of the box, 128
+                // bytes of results: into the staging box (its 16-byte chunks
+                // swizzled by the row, as the tensor map's 128-byte swizzle
+                // lays them out, so the 16-byte stores of a quarter-warp hit
+                // distinct banks), then one TMA store of the box while the
+                // warp goes on with the next tile.
+                // the tile's row scales and biases, one a lane
+                const uint32_t wsl = wcnt % NWS;
+                if (!warp_wait(&wsfull[wsl], (wcnt / NWS) & 1, abort, limit)) {
+                    ok = false;
+                    break;
+                }
+                const float* wsv = wsring + wsl * (WS_BYTES / 4) + 32 * cgroup;
+                const float ws_l = col0 + lane < g.rows ? wsv[lane] : 0.0f;
+                const float b_l = (g.bias && col0 + lane < g.rows) ? wsv[BN + lane] : 0.0f;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&wsempty[wsl]);
+                wcnt++;
+                if (live) {
+                    if (g.add) {
+                        if (!warp_wait(&obar[warp], ocnt & 1, abort, limit)) {
+                            ok = false;
+                            break;
+                        }
+                        ocnt++;
+                    } else {
+                        if (lane == 0) bulk_wait_read();
+                        __syncwarp();
+                    }
+                    uint8_t* row = stg + lane * 128;
 #pragma unroll
-            for (int j = 0; j < 32; j++) tw[lane * EPI_PITCH + j] = acc_at(acc, j);
-            __syncwarp();
-            const uint32_t col = n0 + 32 * cgroup + lane;
-            const bool cvalid = col < g.rows;
-            const float wsv = cvalid ? __ldg(g.ws + col) : 0.0f;
-            const float bv = (g.bias && cvalid) ? __ldg(g.bias + col) : 0.0f;
-            const uint32_t tr0 = m0 + lane_base;
+                    for (int k = 0; k < 8; k++) {
+                        float4* c4 = reinterpret_cast<float4*>(row + ((k ^ (lane & 7)) << 4));
+                        float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                        if (g.add) {
+                            const float4 ov = *c4;
+                            o[0] = ov.x;
+                            o[1] = ov.y;
+                            o[2] = ov.z;
+                            o[3] = ov.w;
+                        }
+                        float v[4];
 #pragma unroll
-            for (int i0 = 0; i0 < 32; i0 += 8) {
-                float old[8];
-                if (g.add) {
+                        for (int e = 0; e < 4; e++) {
+                            const int j = 4 * k + e;
+                            v[e] = mul_r<RM>(acc_at(acc, j), __shfl_sync(0xffffffffu, ws_l, j));
+                            if (g.bias) v[e] = add_r<RM>(v[e], __shfl_sync(0xffffffffu, b_l, j));
+                            if (g.add) v[e] = add_r<RM>(o[e], v[e]);
+                        }
+                        *c4 = make_float4(v[0], v[1], v[2], v[3]);
+                    }
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&map_o, stg, static_cast<int>(col0), static_cast<int>(frame0));
+                        bulk_commit();
+                    }
+                }
+            } else {
+                // through shared memory, so that a lane owns one output row (a
+                // column of the tile) and each store is 32 consecutive floats
+#pragma unroll
+                for (int j = 0; j < 32; j++) tw[lane * EPI_PITCH + j] = acc_at(acc, j);
+                __syncwarp();
+                const uint32_t col = n0 + 32 * cgroup + lane;
+                const bool cvalid = col < g.rows;
+                const float wsv = cvalid ? __ldg(g.ws + col) : 0.0f;
+                const float bv = (g.bias && cvalid) ? __ldg(g.bias + col) : 0.0f;
+                const uint32_t tr0 = m0 + lane_base;
+#pragma unroll
+                for (int i0 = 0; i0 < 32; i0 += 8) {
+                    float old[8];
+                    if (g.add) {
+#pragma unroll
+                        for (int i = 0; i < 8; i++) {
+                            const uint32_t tt = tr0 + i0 + i;
+                            old[i] = (cvalid && tt < g.T) ? g.out[static_cast<size_t>(tt) * g.os + col] : 0.0f;
+                        }
+                    }
 #pragma unroll
                     for (int i = 0; i < 8; i++) {
                         const uint32_t tt = tr0 + i0 + i;
-                        old[i] = (cvalid && tt < g.T) ? g.out[static_cast<size_t>(tt) * g.os + col] : 0.0f;
+                        if (cvalid && tt < g.T) {
+                            float v = mul_r<RM>(tw[(i0 + i) * EPI_PITCH + lane], wsv);
+                            if (g.bias) v = add_r<RM>(v, bv);
+                            if (g.add) v = add_r<RM>(old[i], v);
+                            g.out[static_cast<size_t>(tt) * g.os + col] = v;
+                        }
                     }
                 }
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    const uint32_t tt = tr0 + i0 + i;
-                    if (cvalid && tt < g.T) {
-                        float v = mul_r<RM>(tw[(i0 + i) * EPI_PITCH + lane], wsv);
-                        if (g.bias) v = add_r<RM>(v, bv);
-                        if (g.add) v = add_r<RM>(old[i], v);
-                        g.out[static_cast<size_t>(tt) * g.os + col] = v;
-                    }
-                }
+                __syncwarp();
             }
-            __syncwarp();
         }
         if (!ok) {
             *abort = 1;
             atomicOr(g.err, PKB_DEVERR_TIMEOUT);
         }
+        // the warp's TMA stores complete before the CTA (and its shared
+        // memory) goes
+        if (TIO && lane == 0) bulk_wait_all();
     }
 
     tc_fence_before();
@@ -516,11 +647,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
-using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs);
+using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs);
 
 // The instance for these arguments: the staged MMA paths where qb is 32, 64
-// or 128 and n a multiple of BK, the scales through the TMA ring where they
-// have a tensor map.
+// or 128 and n a multiple of BK, the TMA path where the results have a
+// tensor map.
 template <int RM, bool EXACT_SUM>
 static KernelFn pick(uint32_t n, uint32_t qb, bool dtma) {
     if constexpr (EXACT_SUM) {
@@ -533,10 +664,11 @@ static KernelFn pick(uint32_t n, uint32_t qb, bool dtma) {
 }
 
 template <int RM, bool EXACT_SUM>
-static cudaError_t launch_rm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap* md, const GemmArgs& g,
-                             int grid, cudaStream_t stream) {
-    const KernelFn kern = pick<RM, EXACT_SUM>(g.n, g.qb, md != nullptr);
-    kern<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, md ? *md : ma, g);
+static cudaError_t launch_rm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap* md,
+                             const CUtensorMap* mo, const GemmArgs& g, int grid, cudaStream_t stream) {
+    const bool tio = md != nullptr && mo != nullptr;
+    const KernelFn kern = pick<RM, EXACT_SUM>(g.n, g.qb, tio);
+    kern<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, tio ? *md : ma, tio ? *mo : ma, g);
     return cudaGetLastError();
 }
 
@@ -560,7 +692,8 @@ int gemm_tile_rows() { return gemm::BM; }
 int gemm_tile_cols() { return gemm::BN; }
 int gemm_box_k() { return gemm::BK; }
 
-int gemm_scale_chunk() { return gemm::DCHUNK; }
+int gemm_out_box() { return 32; }
+int gemm_scale_box() { return gemm::DBLK; }
 
 cudaError_t prepare_gemm_q8() {
     cudaError_t e;
@@ -575,7 +708,7 @@ cudaError_t prepare_gemm_q8() {
 }
 
 cudaError_t launch_gemm_q8(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap* map_d,
-                           const GemmArgs& g, int num_sms, int rmode, cudaStream_t stream) {
+                           const CUtensorMap* map_o, const GemmArgs& g, int num_sms, int rmode, cudaStream_t stream) {
     const uint32_t ntiles = g.tiles_m * g.tiles_n;
     const int grid = static_cast<int>(ntiles < static_cast<uint32_t>(num_sms) ? ntiles : num_sms);
     // block sums convert to float exactly through the start-value trick while
@@ -583,14 +716,14 @@ cudaError_t launch_gemm_q8(const CUtensorMap& map_a, const CUtensorMap& map_b, c
     // the conversion in the mode, as the reference's (float)s does
     const bool exact = g.qb <= 256;
     switch (rmode * 2 + (exact ? 1 : 0)) {
-    case 0: return gemm::launch_rm<0, false>(map_a, map_b, map_d, g, grid, stream);
-    case 1: return gemm::launch_rm<0, true>(map_a, map_b, map_d, g, grid, stream);
-    case 2: return gemm::launch_rm<1, false>(map_a, map_b, map_d, g, grid, stream);
-    case 3: return gemm::launch_rm<1, true>(map_a, map_b, map_d, g, grid, stream);
-    case 4: return gemm::launch_rm<2, false>(map_a, map_b, map_d, g, grid, stream);
-    case 5: return gemm::launch_rm<2, true>(map_a, map_b, map_d, g, grid, stream);
-    case 6: return gemm::launch_rm<3, false>(map_a, map_b, map_d, g, grid, stream);
-    default: return gemm::launch_rm<3, true>(map_a, map_b, map_d, g, grid, stream);
+    case 0: return gemm::launch_rm<0, false>(map_a, map_b, map_d, map_o, g, grid, stream);
+    case 1: return gemm::launch_rm<0, true>(map_a, map_b, map_d, map_o, g, grid, stream);
+    case 2: return gemm::launch_rm<1, false>(map_a, map_b, map_d, map_o, g, grid, stream);
+    case 3: return gemm::launch_rm<1, true>(map_a, map_b, map_d, map_o, g, grid, stream);
+    case 4: return gemm::launch_rm<2, false>(map_a, map_b, map_d, map_o, g, grid, stream);
+    case 5: return gemm::launch_rm<2, true>(map_a, map_b, map_d, map_o, g, grid, stream);
+    case 6: return gemm::launch_rm<3, false>(map_a, map_b, map_d, map_o, g, grid, stream);
+    default: return gemm::launch_rm<3, true>(map_a, map_b, map_d, map_o, g, grid, stream);
     }
 }
 

@@ -35,17 +35,22 @@ struct GemmArgs {
 int gemm_tile_rows();   // frames a tile (TMA box of the activations)
 int gemm_tile_cols();   // output rows a tile (TMA box of the weights)
 int gemm_box_k();       // inputs of K a TMA box
-int gemm_scale_chunk(); // blocks of scales a TMA box of the scales carries
 
 // Sets the product kernels' launch attributes on the current device (once,
 // at the device's set-up, outside any stream capture).
 cudaError_t prepare_gemm_q8();
 
 // map_d: a tensor map of the block scales d [T][n/qb] (float32, boxes of
-// gemm_scale_chunk() blocks by gemm_tile_rows() frames), or null to read
-// them from global memory directly
+// gemm_scale_box() blocks by gemm_tile_rows() frames); map_o: one of the
+// results out [T][rows] (float32, row stride os, boxes of gemm_out_box() by
+// gemm_out_box(), 128-byte swizzle). Both are given only where n / qb is a
+// multiple of 4 and d, out, ws and bias are 16-byte aligned, os a multiple
+// of 4; the kernel then moves scales, row scales, biases and results with
+// TMA. Null: plain loads and stores.
 cudaError_t launch_gemm_q8(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap* map_d,
-                           const GemmArgs& g, int num_sms, int rmode, cudaStream_t stream);
+                           const CUtensorMap* map_o, const GemmArgs& g, int num_sms, int rmode, cudaStream_t stream);
+int gemm_out_box();     // frames and output rows of a TMA box of the results
+int gemm_scale_box();   // blocks of scales a TMA box of them carries
 
 cudaError_t launch_quantize(int8_t* q, float* d, const float* x, size_t xs, uint32_t T, uint32_t n, uint32_t qb,
                             int rmode, int num_sms, cudaStream_t stream);
