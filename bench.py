@@ -154,14 +154,14 @@ class ClockSampler:
 
 # ------------------------------------------------------------ CPU baseline --
 
-CPU_SAMPLE_M = 4096
 
 
-def cpu_baseline(prods, budget_s: float = 15.0) -> dict:
+def cpu_baseline(prods, min_s: float = 10.0) -> dict:
     """The reference's own CPU backend (its picker's choice, oracle/_ref) on a
     bounded sample: the subsampling's three products and one layer's eleven,
-    each at min(M, 4096) frames (the CPU's tiles stream frames, so its rate
-    per MAC does not depend on M past a few hundred), on every host core."""
+    each at the batch's M, on every host core. Passes over the sample repeat
+    until at least `min_s` seconds of CPU work have run (at most 8); the rate
+    is the median pass's."""
     import ctypes
     so = os.path.join(ROOT, "oracle", "_ref", "libcpubench.so")
     if not os.path.exists(so):
@@ -177,25 +177,27 @@ def cpu_baseline(prods, budget_s: float = 15.0) -> dict:
     backend = lib.cpub_backend(picks, 512).decode()
     cores = os.cpu_count() or 1
     sample = [p for p in prods if p["layer"] in (-1, 0)]
-    ops = t = 0.0
     qs = ctypes.c_double()
     t_start = time.time()
     reps = max(1, int(os.environ.get("PKB_CPU_REPS", "3")))
-    for p in sample:
-        m = min(p["M"], CPU_SAMPLE_M)
-        sec = lib.cpub_time(p["rows"], p["n"], m, QB, p["add"], cores, reps, 1, ctypes.byref(qs))
-        if sec <= 0:
-            continue
-        ops += 2.0 * m * p["rows"] * p["n"]
-        t += sec
-        if time.time() - t_start > budget_s:
+    rates = []
+    while len(rates) < 8 and (not rates or time.time() - t_start < min_s):
+        ops = t = 0.0
+        for p in sample:
+            sec = lib.cpub_time(p["rows"], p["n"], p["M"], QB, p["add"], cores, reps, 1, ctypes.byref(qs))
+            if sec > 0:
+                ops += 2.0 * p["M"] * p["rows"] * p["n"]
+                t += sec
+        if t > 0:
+            rates.append(ops / t / 1e12)
+        else:
             break
-    value = ops / t / 1e12 if t > 0 else None
+    value = float(np.median(rates)) if rates else None
     return {"value": value, "unit": "TOPS", "cores": cores, "kind": "reference",
             "backend": backend, "picks": picks.value.decode(),
-            "sample": f"{len(sample)} products (subsampling + layer 0) at min(M, {CPU_SAMPLE_M}) frames, "
-                      f"quantize + product, best of {reps} timed runs after a warm one each; "
-                      f"{time.time() - t_start:.1f} s of CPU work, {t:.2f} s in the best runs"}
+            "sample": f"{len(sample)} products (subsampling + layer 0) at the batch's M, quantize + product, "
+                      f"best of {reps} timed runs after a warm one each; {len(rates)} passes, median pass rate; "
+                      f"{time.time() - t_start:.1f} s of CPU work"}
 
 
 # ------------------------------------------------------------ our GPU arm --
@@ -495,7 +497,7 @@ def run_reference(args) -> None:
     cpu = None
     times = []
     for i in range(args.warmup + args.steps):
-        c = cpu_baseline(prods, budget_s=20.0)
+        c = cpu_baseline(prods, min_s=8.0)
         if c["value"] is None:
             print(json.dumps({"impl": "reference", "unavailable": c["sample"]}))
             return
@@ -552,7 +554,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--e2e-steps", type=int, default=1)
+    ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--e2e-lanes", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
