@@ -137,11 +137,12 @@ __device__ __forceinline__ float acc_at(const Acc& acc, int j) {
 // the warp stays converged for the whole-warp TMEM loads that follow, with
 // no branch around one lane's wait and no shuffle (measured on B200: a
 // lane-0 wait and a shuffle cost the epilogue a third of its time at
-// 32-input blocks). False if the wait gave up.
+// 32-input blocks). Every lane runs the same polls on the same barrier, abort
+// flag and clock, so all take the loop's exit together and no further
+// warp-wide synchronisation is needed (one cost 2-3 %). False if the wait
+// gave up.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort, long long limit) {
-    const bool ok = mbar_wait(bar, parity, abort, limit);
-    __syncwarp();
-    return ok;
+    return mbar_wait(bar, parity, abort, limit);
 }
 
 // Block accumulators are handed over in pairs: block B (counted over all of
@@ -155,14 +156,14 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
 // its pair's wait: loads, hands the slot back to the MMA threads and runs
 // the chain.
 template <int RM, bool EXACT_SUM>
-__device__ __forceinline__ void epi_block(Acc& acc, uint32_t ta, float dv, uint64_t* tempty, int lane) {
+__device__ __forceinline__ void epi_block(Acc& acc, uint32_t ta, float dv, uint64_t* tempty) {
     uint32_t sv[32];
-    tmem_ld_32x32b_x16(ta, *reinterpret_cast<uint32_t(*)[16]>(&sv[0]));
-    tmem_ld_32x32b_x16(ta + 16, *reinterpret_cast<uint32_t(*)[16]>(&sv[16]));
+    tmem_ld_32x32b_x32(ta, sv);  // one load of the 32 columns (two of 16 cost 2 % more)
     tmem_ld_wait(sv);
+    // every thread orders its own loads before its own arrival (the slot's
+    // barrier counts all the epilogue's threads): no warp-wide step between
     tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(tempty);
+    mbar_arrive(tempty);
     chain32<RM, EXACT_SUM>(acc, sv, dv);
 }
 
@@ -209,7 +210,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         mbar_init(&tfull[0], 1);
         mbar_init(&tfull[1], 1);
-        for (int i = 0; i < NTMEM; i++) mbar_init(&tempty[i], EPI_WARPS);
+        for (int i = 0; i < NTMEM; i++) mbar_init(&tempty[i], EPI_WARPS * 32);
         mbar_init(&drain[0], 1);
         mbar_init(&drain[1], 1);
         for (int i = 0; i < EPI_WARPS; i++) mbar_init(&obar[i], 1);
@@ -505,15 +506,15 @@ __global__ void __launch_bounds__(THREADS, 1)
                         break;
                     }
                     tc_fence_after();
-                    epi_block<RM, EXACT_SUM>(acc, tl, dq.x, &tempty[0], lane);
-                    epi_block<RM, EXACT_SUM>(acc, tl + BN, dq.y, &tempty[1], lane);
+                    epi_block<RM, EXACT_SUM>(acc, tl, dq.x, &tempty[0]);
+                    epi_block<RM, EXACT_SUM>(acc, tl + BN, dq.y, &tempty[1]);
                     if (!warp_wait(&tfull[1], tph, abort, limit)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    epi_block<RM, EXACT_SUM>(acc, tl + 2 * BN, dq.z, &tempty[2], lane);
-                    epi_block<RM, EXACT_SUM>(acc, tl + 3 * BN, dq.w, &tempty[3], lane);
+                    epi_block<RM, EXACT_SUM>(acc, tl + 2 * BN, dq.z, &tempty[2]);
+                    epi_block<RM, EXACT_SUM>(acc, tl + 3 * BN, dq.w, &tempty[3]);
                     gb += CHUNK;
                 }
             } else {
@@ -531,7 +532,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         tc_fence_after();
                     }
                     const uint32_t slot = gb & (NTMEM - 1);
-                    epi_block<RM, EXACT_SUM>(acc, tl + slot * BN, dv, &tempty[slot], lane);
+                    epi_block<RM, EXACT_SUM>(acc, tl + slot * BN, dv, &tempty[slot]);
                 }
             }
             if (!ok) break;
