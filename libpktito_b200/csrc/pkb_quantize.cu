@@ -14,9 +14,10 @@
 //
 // Layout of the work: a block of 32 is 8 threads of 4 inputs (one 16-byte
 // load each), a block of 64 is 16 threads, so a warp takes 4 or 2 blocks at
-// once and reduces each within its thread group by shuffles; wider blocks
-// (qb = n, up to 16384) take a warp each, in two passes over the block.
-// Warps stride over the blocks, grid sized to the SMs.
+// once (and four such chunks a pass, their loads in flight together) and
+// reduces each within its thread group by shuffles; wider blocks (qb = n, up
+// to 16384) take a warp each, in two passes over the block. Warps stride over
+// the blocks, grid sized to the SMs.
 //
 // repack: PK_Q8 panels (core/pkf.h:28-41: 16 rows by 4 inputs in 64-byte
 // groups) to plain rows of n bytes, which the product's TMA tiles read.
@@ -51,40 +52,68 @@ __device__ __forceinline__ uint32_t quant4(float4 v, float id) {
     return b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
 }
 
-// Blocks of G*4 inputs (G = 8 or 16 threads a block).
+// Blocks of G*4 inputs (G = 8 or 16 threads a block). A warp takes 32 / G
+// blocks a chunk and U chunks a pass, loading all U before reducing any:
+// U 16-byte loads in flight a thread keep HBM busy where one at a time left
+// it waiting on latency (measured on B200: 2.7 TB/s with one). IDX is the
+// index type, 32-bit wherever T * n / qb fits.
+template <int RM, int G, int U, typename IDX>
+__device__ __forceinline__ void quantize_narrow_body(int8_t* __restrict__ q, float* __restrict__ d,
+                                                     const float* __restrict__ x, size_t xs, IDX nb, IDX total,
+                                                     bool vec) {
+    constexpr uint32_t QB = 4 * G;
+    constexpr uint32_t PER_WARP = 32 / G;
+    const uint32_t lane = threadIdx.x & 31, lg = lane % G;
+    const IDX nwarps = static_cast<IDX>(gridDim.x) * (blockDim.x / 32);
+    const IDX warp0 = static_cast<IDX>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+    const IDX chunks = (total + PER_WARP - 1) / PER_WARP;
+    for (IDX c0 = warp0; c0 < chunks; c0 += nwarps * U) {  // warp-uniform
+        float4 v[U];
+        IDX t[U], b[U];
+        bool valid[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const IDX blk = (c0 + u * nwarps) * PER_WARP + lane / G;
+            valid[u] = blk < total;
+            t[u] = valid[u] ? blk / nb : 0;
+            b[u] = valid[u] ? blk - t[u] * nb : 0;
+            v[u] = valid[u] ? load4(x + static_cast<size_t>(t[u]) * xs + static_cast<size_t>(b[u]) * QB + 4 * lg, vec)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            float amax = amax4(v[u]);
+            uint32_t bad = finite4(v[u]) ? 0u : 1u;
+#pragma unroll
+            for (int off = G / 2; off >= 1; off >>= 1) {
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+                bad |= __shfl_xor_sync(0xffffffffu, bad, off);
+            }
+            if (!valid[u]) continue;
+            uint32_t packed = 0;
+            float scale = 0.0f;
+            if (!bad && amax >= 0x1p-121f) {
+                scale = div_r<RM>(amax, 127.0f);
+                packed = quant4<RM>(v[u], div_r<RM>(127.0f, amax));
+            }
+            const size_t row = static_cast<size_t>(t[u]);
+            *reinterpret_cast<uint32_t*>(q + row * (nb * QB) + static_cast<size_t>(b[u]) * QB + 4 * lg) = packed;
+            if (lg == 0) d[row * nb + b[u]] = scale;
+        }
+    }
+}
+
 template <int RM, int G>
 __global__ void __launch_bounds__(256) quantize_narrow(int8_t* __restrict__ q, float* __restrict__ d,
                                                        const float* __restrict__ x, size_t xs, uint32_t T,
                                                        uint32_t n, bool vec) {
-    constexpr uint32_t QB = 4 * G;
-    constexpr uint32_t PER_WARP = 32 / G;
-    const uint32_t nb = n / QB;
-    const size_t total = static_cast<size_t>(T) * nb;
-    const uint32_t lane = threadIdx.x & 31, lg = lane % G;
-    const size_t warp0 = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32;
-    const size_t nwarps = static_cast<size_t>(gridDim.x) * blockDim.x / 32;
-    for (size_t wb = warp0 * PER_WARP; wb < total; wb += nwarps * PER_WARP) {  // warp-uniform
-        const size_t blk = wb + lane / G;
-        const bool valid = blk < total;
-        const size_t t = valid ? blk / nb : 0, b = valid ? blk % nb : 0;
-        const float4 v = valid ? load4(x + t * xs + b * QB + 4 * lg, vec) : make_float4(0.f, 0.f, 0.f, 0.f);
-        float amax = amax4(v);
-        uint32_t bad = finite4(v) ? 0u : 1u;
-#pragma unroll
-        for (int off = G / 2; off >= 1; off >>= 1) {
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-            bad |= __shfl_xor_sync(0xffffffffu, bad, off);
-        }
-        if (!valid) continue;
-        uint32_t packed = 0;
-        float scale = 0.0f;
-        if (!bad && amax >= 0x1p-121f) {
-            scale = div_r<RM>(amax, 127.0f);
-            packed = quant4<RM>(v, div_r<RM>(127.0f, amax));
-        }
-        *reinterpret_cast<uint32_t*>(q + t * n + b * QB + 4 * lg) = packed;
-        if (lg == 0) d[t * nb + b] = scale;
-    }
+    constexpr int U = 4;
+    const uint32_t nb = n / (4 * G);
+    const uint64_t total = static_cast<uint64_t>(T) * nb;
+    if (total <= 0xFFFFFFF0ull)
+        quantize_narrow_body<RM, G, U, uint32_t>(q, d, x, xs, nb, static_cast<uint32_t>(total), vec);
+    else
+        quantize_narrow_body<RM, G, U, uint64_t>(q, d, x, xs, nb, total, vec);
 }
 
 // Blocks of any multiple of 32 inputs, a warp each.
@@ -126,7 +155,7 @@ cudaError_t quantize_rm(int8_t* q, float* d, const float* x, size_t xs, uint32_t
                         int num_sms, cudaStream_t stream) {
     const bool vec = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (xs % 4 == 0);
     const size_t blocks = static_cast<size_t>(T) * (n / qb);
-    const size_t per_cta = qb == 32 ? 8 * 4 : qb == 64 ? 8 * 2 : 8;  // blocks a 256-thread CTA takes per pass
+    const size_t per_cta = qb == 32 ? 8 * 4 * 4 : qb == 64 ? 8 * 2 * 4 : 8;  // blocks a 256-thread CTA takes per pass
     size_t grid = (blocks + per_cta - 1) / per_cta;
     const size_t cap = static_cast<size_t>(num_sms) * 8;
     if (grid > cap) grid = cap;
