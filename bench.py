@@ -20,8 +20,11 @@ product's input is a resident float32 activation ~N(0,1).
 A step is one pass over the batch: 24 x 11 + 3 quantize+product pairs. value
 is whole-job int8 TOPS (2*M*N*K summed over the products, over every rank);
 audio-seconds per second is reported beside it. Multi-GPU: one process per
-GPU (torchrun), each with its own 64 segments (weak scaling), no collective
-on the data path; the time is the max over ranks.
+GPU (torchrun); the batch of 64 segments is dealt across the GPUs longest
+first (strong scaling, the configuration's "data-partitioned across 1/2/4/8
+GPUs"; `--scaling weak` gives every GPU 64 segments of its own instead), no
+collective on the data path; the time is the max over ranks, the work the
+sum.
 
 `--impl reference` times the reference's own CPU backend (the one its picker
 chooses on this host, built from its sources into oracle/_ref) on a bounded
@@ -53,10 +56,10 @@ SEED = 20261201
 
 # ---------------------------------------------------------------- workload --
 
-def segments(rank: int) -> list[tuple[float, int, int, int]]:
-    """(seconds, T0, T2, T3) of the rank's 64 segments: mel frames at 100/s,
-    each 2x subsampling stage ceil-halving (core/encoder.c:430)."""
-    rng = np.random.default_rng(SEED + rank)
+def draw_segments(seed: int) -> list[tuple[float, int, int, int]]:
+    """(seconds, T0, T2, T3) of 64 segments of seeded lengths: mel frames at
+    100/s, each 2x subsampling stage ceil-halving (core/encoder.c:430)."""
+    rng = np.random.default_rng(seed)
     out = []
     for sec in rng.uniform(2.0, 30.0, SEGMENTS):
         t0 = int(sec * 100)
@@ -65,6 +68,30 @@ def segments(rank: int) -> list[tuple[float, int, int, int]]:
         t3 = (t2 + 1) // 2
         out.append((float(sec), t0, t2, t3))
     return out
+
+
+def partition(segs, world: int) -> list[list[int]]:
+    """The segments dealt to `world` GPUs longest first, each to the GPU with
+    the fewest encoder frames so far (ties to the lower rank), as the
+    reference deals chunks to lanes (core/asr.c:373-398)."""
+    order = sorted(range(len(segs)), key=lambda i: (-segs[i][3], i))
+    load = [0] * world
+    share: list[list[int]] = [[] for _ in range(world)]
+    for i in order:
+        r = min(range(world), key=lambda k: (load[k], k))
+        share[r].append(i)
+        load[r] += segs[i][3]
+    return [sorted(s) for s in share]
+
+
+def segments(rank: int, world: int = 1, scaling: str = "strong") -> list[tuple[float, int, int, int]]:
+    """The rank's segments. Strong scaling (configs[3]: one batch of 64
+    segments partitioned across the GPUs): the rank's share of the one draw.
+    Weak scaling: a draw of 64 of its own."""
+    if scaling == "weak":
+        return draw_segments(SEED + rank)
+    segs = draw_segments(SEED)
+    return [segs[i] for i in partition(segs, world)[rank]]
 
 
 def products(segs) -> list[dict]:
@@ -248,10 +275,11 @@ class Model:
                           self.q[xk], self.d[xk], p["n"], QB, p["M"], bool(p["add"]), stream=stream)
 
 
-def kernel_roofline(model, prods) -> dict:
+def kernel_roofline(model, prods, sm_mhz: float | None) -> dict:
     """The dominant kernel (the product) timed alone on its most frequent
     shape, with CUDA events on its stream: achieved int8 TOPS over the
-    measured peak."""
+    measured peak; beside it the fraction of the fp32 bound its epilogue
+    chain has at this qb, and the quantizer's HBM rate on the same input."""
     torch, P = model.torch, model.P
     p = next(x for x in prods if x["name"] == "ff1_up")
     key, xk, ok = (p["layer"], p["name"]), (p["M"], p["n"]), (p["M"], p["rows"])
@@ -285,13 +313,40 @@ def kernel_roofline(model, prods) -> dict:
                 traffic = t.get("bytes_per_launch")
         except (OSError, ValueError):
             traffic = None
-    # the epilogue's own bound: one fp32 FMA (and a packed subtract) per
-    # output per block of 32 on the CUDA cores
+    # the epilogue's own bound: per output and block one exact subtract and
+    # one FMA, two fp32 lane-operations, on 128 FP32 lanes a cycle per SM
+    mhz = sm_mhz or 1965.0
+    lane_ops = 2.0 * p["M"] * p["rows"] * (p["n"] // QB)
+    fp32_peak = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count * 128 * mhz * 1e6
+    epi = {"lane_ops_per_launch": lane_ops, "achieved_lane_ops_per_s": lane_ops / (ms * 1e-3),
+           "peak_lane_ops_per_s": fp32_peak, "frac": lane_ops / (ms * 1e-3) / fp32_peak,
+           "note": f"one subtract + one FMA per output per block of {QB}; 128 fp32 lanes/clk/SM at {mhz:.0f} MHz"}
+    # the quantizer on the same product's input
+    qd = model.q[xk]
+    x = model.x[xk]
+    for _ in range(3):
+        P.quantize_dev(qd, model.d[xk], x, p["n"], p["M"], p["n"], QB)
+    s.synchronize()
+    e0.record(s)
+    for _ in range(reps):
+        P.quantize_dev(qd, model.d[xk], x, p["n"], p["M"], p["n"], QB)
+    e1.record(s)
+    e1.synchronize()
+    qms = e0.elapsed_time(e1) / reps
+    qbytes = p["M"] * p["n"] * (4 + 1 + 4.0 / QB)
+    try:
+        hbm = float(json.load(open(peaks_path))["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        hbm = 6650.0
+    quant = {"ms_per_launch": qms, "gbs": qbytes / (qms * 1e-3) / 1e9, "peak_gbs": hbm,
+             "frac": qbytes / (qms * 1e-3) / 1e9 / hbm, "bytes_per_launch": qbytes,
+             "shape": f"T {p['M']} x n {p['n']}, qb {QB}"}
     return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
             "traffic": traffic, "kernel": "pkb::gemm::gemm_q8_kernel",
             "shape": f"M {p['M']} x N {p['rows']} x K {p['n']}, qb {QB}", "ms_per_launch": ms,
             "peak_note": src + "; int8 dense is twice bf16 dense on B200 (4.5 vs 2.25 PFLOP/s nominal)",
-            "algorithmic_ops_per_launch": 2.0 * p["M"] * p["rows"] * p["n"]}
+            "algorithmic_ops_per_launch": 2.0 * p["M"] * p["rows"] * p["n"],
+            "epilogue_fp32": epi, "quantize": quant}
 
 
 def e2e_host(prods, steps: int, seed: int, lanes: int) -> dict:
@@ -397,10 +452,10 @@ def run_ours(args) -> None:
     import libpktito_b200 as P
     P.set_thread_device(local)
     dev = torch.device("cuda", local)
-    segs = segments(rank)
+    segs = segments(rank, world, args.scaling)
     prods = products(segs)
     ops = step_ops(prods)
-    model = Model(prods, dev, SEED + 1000 * rank)
+    model = Model(prods, dev, SEED + 1000)  # one model, replicated on every GPU
 
     def barrier():
         if dist:
@@ -443,7 +498,7 @@ def run_ours(args) -> None:
     ms, ops_job, audio_job = job_totals(dist, dev, ms, ops, audio_seconds(segs))
     used_graph = graph is not None
     del graph  # released before the process group goes (it holds no collective, but keep the order safe)
-    roof = kernel_roofline(model, prods) if rank == 0 else None
+    roof = kernel_roofline(model, prods, clk.get("sm_mhz")) if rank == 0 else None
     e2e = None
     if not args.no_e2e:
         # every rank at once through the host table, each on its own
@@ -468,14 +523,17 @@ def run_ours(args) -> None:
     ms_step = ms / args.steps
     value = ops_job / (ms_step * 1e-3) / 1e12
     t3 = sum(s[3] for s in segs)
+    nseg = SEGMENTS if args.scaling == "strong" else SEGMENTS * world
     line = {
         "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": args.scaling,
         "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded segments, random int8 weights, N(0,1) activations)",
-        "config": {"workload": "configs[3] batched encoder: 64 segments of 2-30 s per GPU, 24 layers x 11 products "
-                               "+ 3 subsampling products, quantize + product each, qb 32",
-                   "segments_per_gpu": SEGMENTS, "encoder_frames_per_gpu": t3, "layers": LAYERS, "d_model": D,
-                   "ff_dim": F, "qb": QB, "global_batch": SEGMENTS * world, "seq_len": t3 // SEGMENTS,
+        "config": {"workload": ("configs[3] batched encoder: one batch of 64 segments of 2-30 s dealt across the "
+                                "GPUs longest first" if args.scaling == "strong" else
+                                "configs[3] batched encoder, weak scaling: 64 segments of 2-30 s per GPU") +
+                               ", 24 layers x 11 products + 3 subsampling products, quantize + product each, qb 32",
+                   "segments_rank0": len(segs), "encoder_frames_rank0": t3, "layers": LAYERS, "d_model": D,
+                   "ff_dim": F, "qb": QB, "global_batch": nseg, "seq_len": t3 // max(1, len(segs)),
                    "parallelism": f"dp{world}", "l2": "no flush: each step streams 576 MiB of weights and "
                                                        "~1.4 GB of activations, well over the 126 MB L2",
                    "cuda_graph": used_graph},
@@ -559,6 +617,9 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                    help="strong: the one batch of 64 segments split across the GPUs (configs[3]); "
+                         "weak: 64 segments per GPU")
     ap.add_argument("--kernel-only", action="store_true",
                     help="only the dominant product (FF up at the batch's M), 3 launches: the ncu capture's case")
     args = ap.parse_args()

@@ -1,11 +1,13 @@
 """The multi-GPU host logic on CPU, two `gloo` ranks in spawned processes.
 
 The benchmark partitions the batched encoder by rank with no collective on
-the data path: every rank draws its own 64 segments (seed + rank) and runs
-them on its own GPU; the job's figures come from one reduction at the end,
-the time as the max over ranks and the work (int8 ops, audio seconds) as the
-sum. These tests run exactly that host code (bench.segments, bench.products,
-bench.job_totals) with the gloo backend on 127.0.0.1.
+the data path: the batch of 64 segments is dealt across the ranks longest
+first (strong scaling; with weak scaling every rank draws 64 of its own) and
+each rank runs its share on its own GPU; the job's figures come from one
+reduction at the end, the time as the max over ranks and the work (int8
+ops, audio seconds) as the sum. These tests run exactly that host code
+(bench.segments, bench.partition, bench.products, bench.job_totals) with
+the gloo backend on 127.0.0.1.
 """
 from __future__ import annotations
 
@@ -28,7 +30,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank_main(rank: int, world: int, port: int, queue) -> None:
+def _rank_main(rank: int, world: int, port: int, queue, scaling: str = "strong") -> None:
     import torch
     import torch.distributed as dist
 
@@ -36,7 +38,7 @@ def _rank_main(rank: int, world: int, port: int, queue) -> None:
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
-        segs = bench.segments(rank)
+        segs = bench.segments(rank, world, scaling)
         prods = bench.products(segs)
         ops = bench.step_ops(prods)
         audio = bench.audio_seconds(segs)
@@ -48,13 +50,13 @@ def _rank_main(rank: int, world: int, port: int, queue) -> None:
         dist.destroy_process_group()
 
 
-def _run(world: int) -> list[dict]:
+def _run(world: int, scaling: str = "strong") -> list[dict]:
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, queue)) for r in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, queue, scaling)) for r in range(world)]
     for p in procs:
         p.start()
     out = [queue.get(timeout=180) for _ in range(world)]
@@ -69,14 +71,38 @@ def two_ranks() -> list[dict]:
     return _run(2)
 
 
-def test_each_rank_its_own_segments(two_ranks):
+@pytest.fixture(scope="module")
+def two_ranks_weak() -> list[dict]:
+    return _run(2, "weak")
+
+
+def test_strong_scaling_deals_the_one_batch(two_ranks):
     a, b = two_ranks
+    whole = [s[3] for s in bench.draw_segments(bench.SEED)]
+    # the two shares together are the batch, each segment once
+    assert sorted(a["frames"] + b["frames"]) == sorted(whole)
+    assert len(a["frames"]) + len(b["frames"]) == bench.SEGMENTS
+    # longest first to the lighter rank: the loads differ by at most one segment
+    assert abs(sum(a["frames"]) - sum(b["frames"])) <= max(whole)
+    # encoder frames 25..375 a segment (2..30 s at 80 ms)
+    assert all(25 <= f <= 376 for f in whole)
+
+
+def test_partition_at_every_width():
+    segs = bench.draw_segments(bench.SEED)
+    for world in (1, 2, 4, 8):
+        shares = bench.partition(segs, world)
+        assert sorted(i for s in shares for i in s) == list(range(bench.SEGMENTS))
+        loads = [sum(segs[i][3] for i in s) for s in shares]
+        assert max(loads) - min(loads) <= max(s[3] for s in segs)
+
+
+def test_weak_scaling_each_rank_its_own_segments(two_ranks_weak):
+    a, b = two_ranks_weak
     assert len(a["frames"]) == bench.SEGMENTS and len(b["frames"]) == bench.SEGMENTS
     assert a["frames"] != b["frames"]
     # the draw is the rank's alone: the same rank draws the same segments again
-    assert [s[3] for s in bench.segments(1)] == b["frames"]
-    # encoder frames 25..375 a segment (2..30 s at 80 ms)
-    assert all(25 <= f <= 376 for f in a["frames"] + b["frames"])
+    assert [s[3] for s in bench.segments(1, 2, "weak")] == b["frames"]
 
 
 def test_job_totals_max_time_sum_work(two_ranks):
@@ -89,6 +115,9 @@ def test_job_totals_max_time_sum_work(two_ranks):
         assert audio == pytest.approx(want[2], rel=1e-12)
     # the per-rank work differs, so rank 0's times the world size is not the job's
     assert a["ops"] != b["ops"]
+    # strong scaling: the job's work is the whole batch's
+    whole = bench.step_ops(bench.products(bench.draw_segments(bench.SEED)))
+    assert a["totals"][1] == pytest.approx(whole, rel=1e-12)
 
 
 def test_job_totals_alone():
