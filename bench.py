@@ -10,14 +10,16 @@ encoder with random int8 weights: per layer its eleven products (feed-forward
 up/down twice, q/k/v, the position projection over 2T-1 rows, attention out,
 pointwise convolutions 1024->2048 and 1024->1024, core/encoder.c:329-368),
 plus the subsampling's three (core/encoder.c:218-251, 463-465); every
-product's float32 input quantized (blocks of 32) and multiplied. The
+product's float32 input quantized (blocks of 32) and multiplied, each input
+once as the reference does (q, k and v share the layer's normed input; the
+position input is quantized once a forward pass). The
 segments' frames are concatenated into one M per product, which is
 bit-identical per frame to running them one by one (a product's columns are
 independent). The float parts between products (norms, attention, GLU,
 depthwise convolution) are outside the int8 path and not timed; each
 product's input is a resident float32 activation ~N(0,1).
 
-A step is one pass over the batch: 24 x 11 + 3 quantize+product pairs. value
+A step is one pass over the batch: 267 products and 196 quantizations. value
 is whole-job int8 TOPS (2*M*N*K summed over the products, over every rank);
 audio-seconds per second is reported beside it. Multi-GPU: one process per
 GPU (torchrun); the batch of 64 segments is dealt across the GPUs longest
@@ -52,6 +54,7 @@ LAYERS = 24
 D, F, C = 1024, 4096, 256
 QB = 32
 SEED = 20261201
+CONCURRENT = ("q", "k", "v", "pos")  # a layer's products that read no other's results
 
 
 # ---------------------------------------------------------------- workload --
@@ -95,7 +98,11 @@ def segments(rank: int, world: int = 1, scaling: str = "strong") -> list[tuple[f
 
 
 def products(segs) -> list[dict]:
-    """The step's products: name, rows (N), n (K), M, add, bias, layer."""
+    """The step's products: name, rows (N), n (K), M, add, bias, layer, and
+    inp, the quantized activation the product reads: q, k and v read one
+    (the layer's normed input, core/encoder.c:345-350), every layer's
+    position product reads the one quantized once a forward pass
+    (core/encoder.c:469); every other product has its own."""
     t3 = sum(s[3] for s in segs)
     r = sum(2 * s[3] - 1 for s in segs)
     t2 = sum(s[2] for s in segs)
@@ -114,6 +121,9 @@ def products(segs) -> list[dict]:
                   dict(name="pw2", rows=D, n=D, M=t3, add=1, bias=0, layer=l),
                   dict(name="ff2_up", rows=F, n=D, M=t3, add=0, bias=0, layer=l),
                   dict(name="ff2_down", rows=D, n=F, M=t3, add=1, bias=0, layer=l)]
+    for p in prods:
+        p["inp"] = ("ape" if p["name"] == "pos" else f"{p['layer']}:att" if p["name"] in ("q", "k", "v")
+                    else f"{p['layer']}:{p['name']}")
     return prods
 
 
@@ -260,19 +270,55 @@ class Model:
                 self.x[xk] = torch.randn(p["M"] * p["n"], device=dev, generator=g)
                 self.q[xk] = torch.empty(p["M"] * p["n"], dtype=torch.int8, device=dev)
                 self.d[xk] = torch.empty(p["M"] * p["n"] // QB, dtype=torch.float32, device=dev)
-            ok = (p["M"], p["rows"])
+            ok = self.out_key(p)
             if ok not in self.out:
                 self.out[ok] = torch.zeros(p["M"] * p["rows"], device=dev)
         self.prods = prods
+        # q, k, v and the position product of a layer depend on no one of
+        # them (core/encoder.c:347-352): they run side by side on streams of
+        # their own, each into its own output
+        self.side = [torch.cuda.Stream(dev) for _ in range(len(CONCURRENT))]
         torch.cuda.synchronize()
 
-    def step(self, stream=None):
-        P = self.P
-        for p in self.prods:
-            key, xk, ok = (p["layer"], p["name"]), (p["M"], p["n"]), (p["M"], p["rows"])
-            P.quantize_dev(self.q[xk], self.d[xk], self.x[xk], p["n"], p["M"], p["n"], QB, stream=stream)
-            P.gemm_q8_dev(self.out[ok], p["rows"], self.w[key], self.ws[key], self.bias[key], p["rows"],
-                          self.q[xk], self.d[xk], p["n"], QB, p["M"], bool(p["add"]), stream=stream)
+    @staticmethod
+    def out_key(p):
+        return (p["M"], p["rows"], p["name"] if p["name"] in CONCURRENT else "")
+
+    def step(self):
+        P, torch = self.P, self.torch
+        s0 = torch.cuda.current_stream()
+        held = {}  # the input each activation buffer holds, quantized
+
+        def quantize(p, s):
+            xk = (p["M"], p["n"])
+            if held.get(xk) != p["inp"]:
+                P.quantize_dev(self.q[xk], self.d[xk], self.x[xk], p["n"], p["M"], p["n"], QB, stream=s.cuda_stream)
+                held[xk] = p["inp"]
+
+        def gemm(p, s):
+            key, xk = (p["layer"], p["name"]), (p["M"], p["n"])
+            P.gemm_q8_dev(self.out[self.out_key(p)], p["rows"], self.w[key], self.ws[key], self.bias[key], p["rows"],
+                          self.q[xk], self.d[xk], p["n"], QB, p["M"], bool(p["add"]), stream=s.cuda_stream)
+
+        prods = self.prods
+        i = 0
+        while i < len(prods):
+            p = prods[i]
+            if p["name"] != CONCURRENT[0]:
+                quantize(p, s0)
+                gemm(p, s0)
+                i += 1
+                continue
+            group = prods[i:i + len(CONCURRENT)]
+            assert [g["name"] for g in group] == list(CONCURRENT)
+            for g in group:  # their inputs, once, before the fork
+                quantize(g, s0)
+            for g, s in zip(group, self.side):
+                s.wait_stream(s0)
+                gemm(g, s)
+            for s in self.side:
+                s0.wait_stream(s)
+            i += len(CONCURRENT)
 
 
 def kernel_roofline(model, prods, sm_mhz: float | None) -> dict:
@@ -282,7 +328,7 @@ def kernel_roofline(model, prods, sm_mhz: float | None) -> dict:
     chain has at this qb, and the quantizer's HBM rate on the same input."""
     torch, P = model.torch, model.P
     p = next(x for x in prods if x["name"] == "ff1_up")
-    key, xk, ok = (p["layer"], p["name"]), (p["M"], p["n"]), (p["M"], p["rows"])
+    key, xk, ok = (p["layer"], p["name"]), (p["M"], p["n"]), model.out_key(p)
     s = torch.cuda.current_stream()
     for _ in range(3):
         P.gemm_q8_dev(model.out[ok], p["rows"], model.w[key], model.ws[key], None, p["rows"], model.q[xk],
@@ -382,20 +428,32 @@ def e2e_host(prods, steps: int, seed: int, lanes: int) -> dict:
             if ok not in outs:
                 outs[ok] = np.zeros(p["M"] * p["rows"], np.float32)
         bufs.append((qs, ds, outs))
+    # the bytes each call copies: a quantize takes x in and gives q, d back;
+    # a product takes q, d, row scales, biases (and the results it adds to)
+    # in and gives its results back
     h2d = d2h = 0
-    for p in prods:
-        nb = p["n"] // QB
-        h2d += p["M"] * p["n"] * 4 + p["M"] * (p["n"] + 4 * nb) + 8 * p["rows"] + (p["M"] * p["rows"] * 4 if p["add"] else 0)
-        d2h += p["M"] * (p["n"] + 4 * nb) + p["M"] * p["rows"] * 4
+    for lp in lane_prods:
+        held = {}
+        for p in lp:
+            nb, xk = p["n"] // QB, (p["M"], p["n"])
+            if held.get(xk) != p["inp"]:
+                h2d += p["M"] * p["n"] * 4
+                d2h += p["M"] * (p["n"] + 4 * nb)
+                held[xk] = p["inp"]
+            h2d += p["M"] * (p["n"] + 4 * nb) + 8 * p["rows"] + (p["M"] * p["rows"] * 4 if p["add"] else 0)
+            d2h += p["M"] * p["rows"] * 4
     device = __import__("torch").cuda.current_device()
 
     def lane(i: int):
         P.set_thread_device(device)
         qs, ds, outs = bufs[i]
+        held = {}
         for p in lane_prods[i]:
             key, xk, ok = (p["layer"], p["name"]), (p["M"], p["n"]), (p["M"], p["rows"])
             act = P.PkAct(qs[xk].ctypes.data, ds[xk].ctypes.data, p["n"], QB, p["M"])
-            tab.quantize(act, xs[xk], p["n"])
+            if held.get(xk) != p["inp"]:  # a lane quantizes what it has not got
+                tab.quantize(act, xs[xk], p["n"])
+                held[xk] = p["inp"]
             tab.gemm_q8(outs[ok], p["rows"], w[key], ws[key], bias[key], p["rows"], act, bool(p["add"]))
 
     def one():
@@ -531,7 +589,8 @@ def run_ours(args) -> None:
         "config": {"workload": ("configs[3] batched encoder: one batch of 64 segments of 2-30 s dealt across the "
                                 "GPUs longest first" if args.scaling == "strong" else
                                 "configs[3] batched encoder, weak scaling: 64 segments of 2-30 s per GPU") +
-                               ", 24 layers x 11 products + 3 subsampling products, quantize + product each, qb 32",
+                               ", 24 layers x 11 products + 3 subsampling products, 196 quantizations (q, k, v share "
+                               "one input; the position input is quantized once), qb 32",
                    "segments_rank0": len(segs), "encoder_frames_rank0": t3, "layers": LAYERS, "d_model": D,
                    "ff_dim": F, "qb": QB, "global_batch": nseg, "seq_len": t3 // max(1, len(segs)),
                    "parallelism": f"dp{world}", "l2": "no flush: each step streams 576 MiB of weights and "

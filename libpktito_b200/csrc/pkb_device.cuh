@@ -224,6 +224,19 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 // async-proxy (TMA, tensor core) reads of them.
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// ----------------------------------------------- programmatic dependent launch --
+//
+// Kernels of this library are launched with programmatic stream
+// serialization: the next kernel in the stream may start as soon as every
+// CTA of the current one has called pdl_trigger(), and its CTAs take SMs as
+// the current kernel's last CTAs leave. Before it touches global memory a
+// kernel calls pdl_wait(), which returns once the preceding kernel has
+// completed and its memory operations are visible (at once where there is
+// no preceding kernel or the launch did not allow the overlap).
+
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ------------------------------------------------------------------- tcgen05 --
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {

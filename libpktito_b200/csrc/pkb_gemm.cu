@@ -251,6 +251,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *tslot;
+    // set up: the next kernel may launch now; this one reads and writes
+    // global memory only once the one before has completed
+    pdl_trigger();
+    pdl_wait();
 
     const uint32_t nk = g.n / KSTEP;            // K steps of a tile
     const uint32_t nc = (g.n + BK - 1) / BK;     // shared-memory stages of a tile
@@ -669,8 +673,8 @@ static cudaError_t launch_rm(const CUtensorMap& ma, const CUtensorMap& mb, const
                              const CUtensorMap* mo, const GemmArgs& g, int grid, cudaStream_t stream) {
     const bool tio = md != nullptr && mo != nullptr;
     const KernelFn kern = pick<RM, EXACT_SUM>(g.n, g.qb, tio);
-    kern<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, tio ? *md : ma, tio ? *mo : ma, g);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3(grid), dim3(THREADS), SMEM_BYTES, stream, ma, mb, tio ? *md : ma,
+                      tio ? *mo : ma, g);
 }
 
 // Every instance's dynamic shared memory allowance, on the current device.

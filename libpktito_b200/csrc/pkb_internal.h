@@ -52,6 +52,24 @@ cudaError_t launch_gemm_q8(const CUtensorMap& map_a, const CUtensorMap& map_b, c
 int gemm_out_box();     // frames and output rows of a TMA box of the results
 int gemm_scale_box();   // blocks of scales a TMA box of them carries
 
+// Launches `kern` on `stream` with programmatic stream serialization allowed
+// (the kernel calls pdl_trigger / pdl_wait, pkb_device.cuh).
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<Params>(args)...);
+}
+
 cudaError_t launch_quantize(int8_t* q, float* d, const float* x, size_t xs, uint32_t T, uint32_t n, uint32_t qb,
                             int rmode, int num_sms, cudaStream_t stream);
 

@@ -107,6 +107,8 @@ template <int RM, int G>
 __global__ void __launch_bounds__(256) quantize_narrow(int8_t* __restrict__ q, float* __restrict__ d,
                                                        const float* __restrict__ x, size_t xs, uint32_t T,
                                                        uint32_t n, bool vec) {
+    pdl_trigger();
+    pdl_wait();
     constexpr int U = 4;
     const uint32_t nb = n / (4 * G);
     const uint64_t total = static_cast<uint64_t>(T) * nb;
@@ -121,6 +123,8 @@ template <int RM>
 __global__ void __launch_bounds__(256) quantize_wide(int8_t* __restrict__ q, float* __restrict__ d,
                                                      const float* __restrict__ x, size_t xs, uint32_t T,
                                                      uint32_t n, uint32_t qb, bool vec) {
+    pdl_trigger();
+    pdl_wait();
     const uint32_t nb = n / qb;
     const size_t total = static_cast<size_t>(T) * nb;
     const uint32_t lane = threadIdx.x & 31;
@@ -161,16 +165,20 @@ cudaError_t quantize_rm(int8_t* q, float* d, const float* x, size_t xs, uint32_t
     if (grid > cap) grid = cap;
     if (grid == 0) grid = 1;
     if (qb == 32)
-        quantize_narrow<RM, 8><<<static_cast<unsigned>(grid), 256, 0, stream>>>(q, d, x, xs, T, n, vec);
+        return launch_pdl(quantize_narrow<RM, 8>, dim3(static_cast<unsigned>(grid)), dim3(256), 0, stream, q, d, x, xs,
+                          T, n, vec);
     else if (qb == 64)
-        quantize_narrow<RM, 16><<<static_cast<unsigned>(grid), 256, 0, stream>>>(q, d, x, xs, T, n, vec);
+        return launch_pdl(quantize_narrow<RM, 16>, dim3(static_cast<unsigned>(grid)), dim3(256), 0, stream, q, d, x,
+                          xs, T, n, vec);
     else
-        quantize_wide<RM><<<static_cast<unsigned>(grid), 256, 0, stream>>>(q, d, x, xs, T, n, qb, vec);
-    return cudaGetLastError();
+        return launch_pdl(quantize_wide<RM>, dim3(static_cast<unsigned>(grid)), dim3(256), 0, stream, q, d, x, xs, T,
+                          n, qb, vec);
 }
 
 __global__ void __launch_bounds__(256) repack_q8(uint32_t* __restrict__ dst, const uint32_t* __restrict__ src,
                                                  uint32_t rows, uint32_t n) {
+    pdl_trigger();
+    pdl_wait();
     // word (r, k/4) of the plain rows from word ((r/16)*(n/4) + k/4)*16 + r%16
     // of the panels
     const uint32_t n4 = n / 4;
@@ -201,9 +209,8 @@ cudaError_t launch_repack_q8(int8_t* wpack, const int8_t* w_pk, uint32_t rows, u
     const size_t cap = static_cast<size_t>(num_sms) * 16;
     if (grid > cap) grid = cap;
     if (grid == 0) grid = 1;
-    repack_q8<<<static_cast<unsigned>(grid), 256, 0, stream>>>(reinterpret_cast<uint32_t*>(wpack),
-                                                              reinterpret_cast<const uint32_t*>(w_pk), rows, n);
-    return cudaGetLastError();
+    return launch_pdl(repack_q8, dim3(static_cast<unsigned>(grid)), dim3(256), 0, stream,
+                      reinterpret_cast<uint32_t*>(wpack), reinterpret_cast<const uint32_t*>(w_pk), rows, n);
 }
 
 }  // namespace pkb
