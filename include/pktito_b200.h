@@ -66,6 +66,13 @@ int pkb_set_thread_device(int device);
  * after synchronising. */
 int pkb_device_errors(int device, uint32_t *word);
 
+/* A self-test of that failure path (no counterpart in the reference): on the
+ * calling thread's current device, one small kernel waits on a barrier that
+ * nothing completes, gives up after limit_cycles SM clock cycles (1000 to
+ * 2^31), sets the error word's timeout bit and returns. *gave_up is 1 when
+ * it did; the device stays usable. For tests and health checks. */
+int pkb_wait_selftest(uint64_t limit_cycles, int *gave_up);
+
 /* ---------------------------------------------- host-pointer contract -- */
 
 /* pk_k_quantize (backend/kernels.h:47-58; ref backend/ref/kernels.c:24-58):

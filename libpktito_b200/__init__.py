@@ -65,6 +65,7 @@ _SIGS = {
     "pkb_device_count": (ctypes.c_int, []),
     "pkb_set_thread_device": (ctypes.c_int, [ctypes.c_int]),
     "pkb_device_errors": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)]),
+    "pkb_wait_selftest": (ctypes.c_int, [ctypes.c_uint64, ctypes.POINTER(ctypes.c_int)]),
     "pkb_quantize_host": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,
                                          ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]),
     "pkb_gemm_q8_host": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p,
@@ -118,6 +119,15 @@ def device_count() -> int:
 
 def set_thread_device(dev: int) -> None:
     _check(lib().pkb_set_thread_device(dev))
+
+
+def wait_selftest(limit_cycles: int = 2_000_000) -> bool:
+    """Runs the bounded-wait self-test on the current device (a wait that
+    nothing completes gives up, sets the error word's timeout bit); True if
+    the wait gave up as it should."""
+    g = ctypes.c_int(0)
+    _check(lib().pkb_wait_selftest(limit_cycles, ctypes.byref(g)))
+    return bool(g.value)
 
 
 def device_errors(dev: int = 0) -> int:
