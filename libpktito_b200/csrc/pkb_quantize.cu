@@ -12,9 +12,9 @@
 // that mode). The maximum is exact in any order, so the reduction's shape
 // is free. HBM-bound: 4 bytes read and 1 + 4/qb written an input.
 //
-// Layout of the work: a block of 32 is 8 threads of 4 inputs (one 16-byte
-// load each), a block of 64 is 16 threads, so a warp takes 4 or 2 blocks at
-// once (and four such chunks a pass, their loads in flight together) and
+// Layout of the work: a block of 32 is 4 threads of 8 inputs (two 16-byte
+// loads each), a block of 64 8 threads of 8, so a warp takes 8 or 4 blocks
+// at once (and four such chunks a pass, their loads in flight together) and
 // reduces each within its thread group by shuffles; wider blocks (qb = n, up
 // to 16384) take a warp each, in two passes over the block. Warps stride over
 // the blocks, grid sized to the SMs.
@@ -52,23 +52,25 @@ __device__ __forceinline__ uint32_t quant4(float4 v, float id) {
     return b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
 }
 
-// Blocks of G*4 inputs (G = 8 or 16 threads a block). A warp takes 32 / G
-// blocks a chunk and U chunks a pass, loading all U before reducing any:
-// U 16-byte loads in flight a thread keep HBM busy where one at a time left
-// it waiting on latency (measured on B200: 2.7 TB/s with one). IDX is the
-// index type, 32-bit wherever T * n / qb fits.
-template <int RM, int G, int U, typename IDX>
+// Blocks of QB = 32 or 64 inputs, E inputs (E / 4 16-byte loads) a thread,
+// QB / E threads a block. A warp takes 32 / (QB / E) blocks a chunk and U
+// chunks a pass, loading all of them before reducing any: many 16-byte
+// loads in flight a thread keep HBM busy (measured on B200 at qb 32: one a
+// thread 2.7 TB/s, four 3.6-4.0, eight 4.4-5.1). IDX is the index type,
+// 32-bit wherever T * n / qb fits.
+template <int RM, int QB, int E, int U, typename IDX>
 __device__ __forceinline__ void quantize_narrow_body(int8_t* __restrict__ q, float* __restrict__ d,
                                                      const float* __restrict__ x, size_t xs, IDX nb, IDX total,
                                                      bool vec) {
-    constexpr uint32_t QB = 4 * G;
-    constexpr uint32_t PER_WARP = 32 / G;
+    constexpr uint32_t G = QB / E;         // threads a block
+    constexpr uint32_t PER_WARP = 32 / G;  // blocks a warp chunk
+    constexpr int V = E / 4;               // 16-byte loads a thread and block
     const uint32_t lane = threadIdx.x & 31, lg = lane % G;
     const IDX nwarps = static_cast<IDX>(gridDim.x) * (blockDim.x / 32);
     const IDX warp0 = static_cast<IDX>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
     const IDX chunks = (total + PER_WARP - 1) / PER_WARP;
     for (IDX c0 = warp0; c0 < chunks; c0 += nwarps * U) {  // warp-uniform
-        float4 v[U];
+        float4 v[U][V];
         IDX t[U], b[U];
         bool valid[U];
 #pragma unroll
@@ -77,46 +79,64 @@ __device__ __forceinline__ void quantize_narrow_body(int8_t* __restrict__ q, flo
             valid[u] = blk < total;
             t[u] = valid[u] ? blk / nb : 0;
             b[u] = valid[u] ? blk - t[u] * nb : 0;
-            v[u] = valid[u] ? load4(x + static_cast<size_t>(t[u]) * xs + static_cast<size_t>(b[u]) * QB + 4 * lg, vec)
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float* xp = x + static_cast<size_t>(t[u]) * xs + static_cast<size_t>(b[u]) * QB + E * lg;
+#pragma unroll
+            for (int e = 0; e < V; e++) v[u][e] = valid[u] ? load4(xp + 4 * e, vec) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int u = 0; u < U; u++) {
-            float amax = amax4(v[u]);
-            uint32_t bad = finite4(v[u]) ? 0u : 1u;
+            float amax = amax4(v[u][0]);
+            uint32_t bad = finite4(v[u][0]) ? 0u : 1u;
+#pragma unroll
+            for (int e = 1; e < V; e++) {
+                amax = fmaxf(amax, amax4(v[u][e]));
+                bad |= finite4(v[u][e]) ? 0u : 1u;
+            }
 #pragma unroll
             for (int off = G / 2; off >= 1; off >>= 1) {
                 amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
                 bad |= __shfl_xor_sync(0xffffffffu, bad, off);
             }
             if (!valid[u]) continue;
-            uint32_t packed = 0;
+            uint32_t packed[V];
+#pragma unroll
+            for (int e = 0; e < V; e++) packed[e] = 0;
             float scale = 0.0f;
             if (!bad && amax >= 0x1p-121f) {
                 scale = div_r<RM>(amax, 127.0f);
-                packed = quant4<RM>(v[u], div_r<RM>(127.0f, amax));
+                const float id = div_r<RM>(127.0f, amax);
+#pragma unroll
+                for (int e = 0; e < V; e++) packed[e] = quant4<RM>(v[u][e], id);
             }
             const size_t row = static_cast<size_t>(t[u]);
-            *reinterpret_cast<uint32_t*>(q + row * (nb * QB) + static_cast<size_t>(b[u]) * QB + 4 * lg) = packed;
+            int8_t* qo = q + row * (nb * QB) + static_cast<size_t>(b[u]) * QB + E * lg;  // E-byte aligned
+#pragma unroll
+            for (int e = 0; e + 1 < V; e += 2)
+                *reinterpret_cast<uint2*>(qo + 4 * e) = make_uint2(packed[e], packed[e + 1]);
+            if constexpr (V & 1) *reinterpret_cast<uint32_t*>(qo + 4 * (V - 1)) = packed[V - 1];
             if (lg == 0) d[row * nb + b[u]] = scale;
         }
     }
 }
 
-template <int RM, int G>
+template <int RM, int QB, int E>
 __global__ void __launch_bounds__(256) quantize_narrow(int8_t* __restrict__ q, float* __restrict__ d,
                                                        const float* __restrict__ x, size_t xs, uint32_t T,
                                                        uint32_t n, bool vec) {
     pdl_trigger();
     pdl_wait();
     constexpr int U = 4;
-    const uint32_t nb = n / (4 * G);
+    const uint32_t nb = n / QB;
     const uint64_t total = static_cast<uint64_t>(T) * nb;
     if (total <= 0xFFFFFFF0ull)
-        quantize_narrow_body<RM, G, U, uint32_t>(q, d, x, xs, nb, static_cast<uint32_t>(total), vec);
+        quantize_narrow_body<RM, QB, E, U, uint32_t>(q, d, x, xs, nb, static_cast<uint32_t>(total), vec);
     else
-        quantize_narrow_body<RM, G, U, uint64_t>(q, d, x, xs, nb, total, vec);
+        quantize_narrow_body<RM, QB, E, U, uint64_t>(q, d, x, xs, nb, total, vec);
 }
+
+#ifndef PKB_Q64_E
+#define PKB_Q64_E 8
+#endif
 
 // Blocks of any multiple of 32 inputs, a warp each.
 template <int RM>
@@ -159,20 +179,25 @@ cudaError_t quantize_rm(int8_t* q, float* d, const float* x, size_t xs, uint32_t
                         int num_sms, cudaStream_t stream) {
     const bool vec = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (xs % 4 == 0);
     const size_t blocks = static_cast<size_t>(T) * (n / qb);
-    const size_t per_cta = qb == 32 ? 8 * 4 * 4 : qb == 64 ? 8 * 2 * 4 : 8;  // blocks a 256-thread CTA takes per pass
+    // eight inputs a thread store 8 bytes of q at once: only where q is 8-byte
+    // aligned (the interface asks 4), else four inputs and 4-byte stores
+    const bool q8 = reinterpret_cast<uintptr_t>(q) % 8 == 0;
+    const int e = qb == 32 ? (q8 ? 8 : 4) : qb == 64 ? (q8 ? PKB_Q64_E : 4) : 0;
+    // blocks a 256-thread CTA takes a pass: 8 warps x U = 4 chunks x blocks a chunk
+    const size_t per_cta = e ? 8 * 4 * (32 / (qb / e)) : 8;
     size_t grid = (blocks + per_cta - 1) / per_cta;
     const size_t cap = static_cast<size_t>(num_sms) * 8;
     if (grid > cap) grid = cap;
     if (grid == 0) grid = 1;
+    const dim3 g(static_cast<unsigned>(grid)), b(256);
     if (qb == 32)
-        return launch_pdl(quantize_narrow<RM, 8>, dim3(static_cast<unsigned>(grid)), dim3(256), 0, stream, q, d, x, xs,
-                          T, n, vec);
+        return q8 ? launch_pdl(quantize_narrow<RM, 32, 8>, g, b, 0, stream, q, d, x, xs, T, n, vec)
+                  : launch_pdl(quantize_narrow<RM, 32, 4>, g, b, 0, stream, q, d, x, xs, T, n, vec);
     else if (qb == 64)
-        return launch_pdl(quantize_narrow<RM, 16>, dim3(static_cast<unsigned>(grid)), dim3(256), 0, stream, q, d, x,
-                          xs, T, n, vec);
+        return q8 ? launch_pdl(quantize_narrow<RM, 64, PKB_Q64_E>, g, b, 0, stream, q, d, x, xs, T, n, vec)
+                  : launch_pdl(quantize_narrow<RM, 64, 4>, g, b, 0, stream, q, d, x, xs, T, n, vec);
     else
-        return launch_pdl(quantize_wide<RM>, dim3(static_cast<unsigned>(grid)), dim3(256), 0, stream, q, d, x, xs, T,
-                          n, qb, vec);
+        return launch_pdl(quantize_wide<RM>, g, b, 0, stream, q, d, x, xs, T, n, qb, vec);
 }
 
 __global__ void __launch_bounds__(256) repack_q8(uint32_t* __restrict__ dst, const uint32_t* __restrict__ src,

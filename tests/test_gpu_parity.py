@@ -88,6 +88,26 @@ def test_quantize_dev_matches_host(pkb, cuda_device):
     assert same_bits(d.cpu().numpy().reshape(T, -1), do)
 
 
+@pytest.mark.parametrize("qoff", [0, 4, 8, 12])
+@pytest.mark.parametrize("qb", [32, 64])
+def test_quantize_dev_q_alignment(pkb, cuda_device, qoff, qb):
+    # the interface asks q to be 4-byte aligned; 8-byte stores of q are only
+    # taken where it is 8-byte aligned, so both forms must give ref's bytes
+    import torch
+    T, n = 37, 1024
+    x = O.seeded_normal(T * n, 11 + qoff + qb)
+    xd = torch.from_numpy(x).cuda()
+    qbuf = torch.full((T * n + 16,), 99, dtype=torch.int8, device="cuda")
+    d = torch.empty(T * n // qb, dtype=torch.float32, device="cuda")
+    pkb.quantize_dev(qbuf[qoff:], d, xd, n, T, n, qb, rmode=O.RD)
+    torch.cuda.synchronize()
+    qo, do = O.quantize(x, n, qb, rmode=O.RD)
+    got = qbuf.cpu().numpy()
+    assert np.array_equal(got[qoff:qoff + T * n].reshape(T, n), qo)
+    assert (got[:qoff] == 99).all() and (got[qoff + T * n:] == 99).all()
+    assert same_bits(d.cpu().numpy().reshape(T, -1), do)
+
+
 # ---------------------------------------------------------------- gemm_q8 --
 
 def run_host_case(pkb, c, rmode=O.RN):
