@@ -119,6 +119,48 @@ int pkb_gemm_q8_dev(void *stream, float *out, size_t os, const int8_t *wpack, co
                     const float *bias, uint32_t rows, const int8_t *q, const float *d, uint32_t n,
                     uint32_t qb, uint32_t T, int add, int rmode);
 
+/* ---------------------------------------- fused producers (device) -- */
+
+/* The producers of the product's int8 inputs in the reference's encoder,
+ * each one kernel on device buffers, enqueued on stream: the float step and
+ * the quantization of its result, bit for bit the reference's (each float
+ * operation its own, in its order, rounded in rmode; the quantization
+ * k_quantize's). Blocks qb of 32 or 64, the encoder's qb()
+ * (core/encoder.c:56). No counterpart in the backend table: the reference
+ * makes these in core/encoder.c from the table's float kernels and
+ * pk_quant_part (core/passes.c:114-118) on the host. */
+
+/* The largest row pkb_layernorm_quantize_dev takes. */
+#define PKB_LN_MAX_N 8192u
+
+/* normq (core/encoder.c:112-130): each of T rows of n floats (row t at
+ * x + t*xs) normalized by k_layernorm (backend/ref/kernels.c:115-131: its
+ * two sums in 16 lanes, folded 8, 4, 2, 1; w and b of n; eps) and quantized
+ * into q [T][n], d [T][n/qb]. n a multiple of qb, at most PKB_LN_MAX_N. */
+int pkb_layernorm_quantize_dev(void *stream, int8_t *q, float *d, const float *x, size_t xs, uint32_t T,
+                               uint32_t n, uint32_t qb, const float *w, const float *b, float eps, int rmode);
+
+/* siluq_tile (core/encoder.c:150-158): T rows of n floats (row t at
+ * u + t*us) through k_silu (backend/ref/kernels.c:149-151: x * pk_sigmoidf(x),
+ * core/vmath.h:134-151) and quantized into q [T][n], d [T][n/qb]. */
+int pkb_silu_quantize_dev(void *stream, int8_t *q, float *d, const float *u, size_t us, uint32_t T,
+                          uint32_t n, uint32_t qb, int rmode);
+
+/* glu_item + dw_item (core/encoder.c:160-183): the convolution module's
+ * depthwise convolution k_dwconv (backend/ref/kernels.c:163-177: C channels,
+ * K taps centred, the taps past either end skipped, + b, SiLU) over T
+ * frames, quantized a frame at a time into q [T][C], d [T][C/qb]. Its input:
+ * with glu 0, frame t's C floats at x + t*xs; with glu 1, pw1's output, 2C
+ * floats a frame at x + t*xs, made into k_glu's x[i] * pk_sigmoidf(x[C + i])
+ * (backend/ref/kernels.c:157-161) on the way in. w holds C rows of K taps.
+ * out, if not NULL, also receives the convolution's floats (frame t at
+ * out + t*os, os >= C), as k_dwconv writes them; it must not overlap x. C a
+ * multiple of qb, at most PKB_MAX_N; K odd, at most 63 (the model's bounds,
+ * core/model.c:480,500). */
+int pkb_dwconv_quantize_dev(void *stream, int8_t *q, float *d, float *out, size_t os, const float *x, size_t xs,
+                            uint32_t T, uint32_t C, const float *w, const float *b, uint32_t K, int glu,
+                            uint32_t qb, int rmode);
+
 /* Launches of libpktito_b200 kernels since the process started, on every
  * device: the evidence a benchmark reports for its own kernels' work. */
 uint64_t pkb_launch_count(void);

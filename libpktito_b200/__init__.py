@@ -83,6 +83,16 @@ _SIGS = {
                                        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p,
                                        ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
                                        ctypes.c_int, ctypes.c_int]),
+    "pkb_layernorm_quantize_dev": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                                  ctypes.c_size_t, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                                                  ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_int]),
+    "pkb_silu_quantize_dev": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                             ctypes.c_size_t, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                                             ctypes.c_int]),
+    "pkb_dwconv_quantize_dev": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                               ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint32,
+                                               ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32,
+                                               ctypes.c_int, ctypes.c_uint32, ctypes.c_int]),
     "pkb_launch_count": (ctypes.c_uint64, []),
     "pkb_quantize_host_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,
                                                  ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]),
@@ -208,6 +218,26 @@ def _stream(stream=None) -> int:
 
 def quantize_dev(q, d, x, xs: int, T: int, n: int, qb: int, rmode: int = RN, stream=None) -> None:
     _check(lib().pkb_quantize_dev(_stream(stream), _ptr(q), _ptr(d), _ptr(x), xs, T, n, qb, rmode))
+
+
+def layernorm_quantize_dev(q, d, x, xs: int, T: int, n: int, qb: int, w, b, eps: float, rmode: int = RN,
+                           stream=None) -> None:
+    """normq (core/encoder.c:112-130) on device buffers: rows layer-normalized
+    and quantized in one kernel."""
+    _check(lib().pkb_layernorm_quantize_dev(_stream(stream), _ptr(q), _ptr(d), _ptr(x), xs, T, n, qb, _ptr(w), _ptr(b),
+                                            eps, rmode))
+
+
+def silu_quantize_dev(q, d, u, us: int, T: int, n: int, qb: int, rmode: int = RN, stream=None) -> None:
+    """siluq_tile (core/encoder.c:150-158) on device buffers."""
+    _check(lib().pkb_silu_quantize_dev(_stream(stream), _ptr(q), _ptr(d), _ptr(u), us, T, n, qb, rmode))
+
+
+def dwconv_quantize_dev(q, d, out, os_: int, x, xs: int, T: int, C: int, w, b, K: int, glu: bool, qb: int,
+                        rmode: int = RN, stream=None) -> None:
+    """glu_item + dw_item (core/encoder.c:160-183) on device buffers; out may be None."""
+    _check(lib().pkb_dwconv_quantize_dev(_stream(stream), _ptr(q), _ptr(d), _ptr(out), os_, _ptr(x), xs, T, C, _ptr(w),
+                                         _ptr(b), K, int(glu), qb, rmode))
 
 
 def repack_q8_dev(wpack, w_pk, rows: int, n: int, stream=None) -> None:

@@ -223,6 +223,76 @@ int gemm_dev(cudaStream_t stream, float* out, size_t os, const int8_t* wpack, co
     return PKB_OK;
 }
 
+// ------------------------------------------------------ fused producers --
+
+int check_fused_qb(uint32_t qb) {
+    if (qb != 32 && qb != 64) return fail(PKB_EINVAL, "qb = %u: 32 or 64, the encoder's blocks", qb);
+    return PKB_OK;
+}
+
+int layernorm_quantize_dev(cudaStream_t stream, int8_t* q, float* d, const float* x, size_t xs, uint32_t T,
+                           uint32_t n, uint32_t qb, const float* w, const float* b, float eps, int rmode) {
+    int rc;
+    if ((rc = check_rmode(rmode)) || (rc = check_fused_qb(qb))) return rc;
+    if (n == 0 || n % qb || n > PKB_LN_MAX_N)
+        return fail(PKB_EINVAL, "layernorm_quantize: n = %u, a multiple of qb up to %u", n, PKB_LN_MAX_N);
+    if (!T) return PKB_OK;
+    if (!q || !d || !x || !w || !b) return fail(PKB_EINVAL, "layernorm_quantize: null pointer");
+    if (xs < n) return fail(PKB_EINVAL, "layernorm_quantize: row stride %zu below n = %u", xs, n);
+    if (!aligned(q, 4) || !aligned(d, 4) || !aligned(x, 4) || !aligned(w, 4) || !aligned(b, 4))
+        return fail(PKB_EINVAL, "layernorm_quantize: misaligned buffer");
+    Device* dev;
+    if ((rc = current_device(&dev))) return rc;
+    PKB_CUDA(launch_layernorm_quantize(q, d, x, xs, T, n, qb, w, b, eps, rmode, dev->sms, stream),
+             "layernorm_quantize launch");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return PKB_OK;
+}
+
+int silu_quantize_dev(cudaStream_t stream, int8_t* q, float* d, const float* u, size_t us, uint32_t T, uint32_t n,
+                      uint32_t qb, int rmode) {
+    int rc;
+    if ((rc = check_rmode(rmode)) || (rc = check_fused_qb(qb)) || (rc = check_act_shape(n, qb))) return rc;
+    if (!T) return PKB_OK;
+    if (!q || !d || !u) return fail(PKB_EINVAL, "silu_quantize: null pointer");
+    if (us < n) return fail(PKB_EINVAL, "silu_quantize: row stride %zu below n = %u", us, n);
+    if (!aligned(q, 4) || !aligned(d, 4) || !aligned(u, 4)) return fail(PKB_EINVAL, "silu_quantize: misaligned buffer");
+    Device* dev;
+    if ((rc = current_device(&dev))) return rc;
+    PKB_CUDA(launch_silu_quantize(q, d, u, us, T, n, qb, rmode, dev->sms, stream), "silu_quantize launch");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return PKB_OK;
+}
+
+int dwconv_quantize_dev(cudaStream_t stream, int8_t* q, float* d, float* out, size_t os, const float* x, size_t xs,
+                        uint32_t T, uint32_t C, const float* w, const float* b, uint32_t K, int glu, uint32_t qb,
+                        int rmode) {
+    int rc;
+    if ((rc = check_rmode(rmode)) || (rc = check_fused_qb(qb))) return rc;
+    if (C == 0 || C % qb || C > PKB_MAX_N)
+        return fail(PKB_EINVAL, "dwconv_quantize: C = %u, a multiple of qb up to %u", C, PKB_MAX_N);
+    if (K % 2 == 0 || K > 63) return fail(PKB_EINVAL, "dwconv_quantize: K = %u, odd and at most 63", K);
+    if (!T) return PKB_OK;
+    if (!q || !d || !x || !w || !b) return fail(PKB_EINVAL, "dwconv_quantize: null pointer");
+    const size_t width = glu ? 2 * static_cast<size_t>(C) : C;
+    if (xs < width) return fail(PKB_EINVAL, "dwconv_quantize: frame stride %zu below %zu", xs, width);
+    if (!aligned(q, 4) || !aligned(d, 4) || !aligned(x, 4) || !aligned(w, 4) || !aligned(b, 4) ||
+        (out && !aligned(out, 4)))
+        return fail(PKB_EINVAL, "dwconv_quantize: misaligned buffer");
+    if (out) {
+        if (os < C) return fail(PKB_EINVAL, "dwconv_quantize: out stride %zu below C = %u", os, C);
+        const uintptr_t x0 = reinterpret_cast<uintptr_t>(x), x1 = x0 + ((T - 1) * xs + width) * sizeof(float);
+        const uintptr_t o0 = reinterpret_cast<uintptr_t>(out), o1 = o0 + ((T - 1) * os + C) * sizeof(float);
+        if (o0 < x1 && x0 < o1) return fail(PKB_EINVAL, "dwconv_quantize: out overlaps x");
+    }
+    Device* dev;
+    if ((rc = current_device(&dev))) return rc;
+    PKB_CUDA(launch_dwconv_quantize(q, d, out, os, x, xs, T, C, w, b, K, glu != 0, qb, rmode, stream),
+             "dwconv_quantize launch");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return PKB_OK;
+}
+
 int repack_dev(cudaStream_t stream, int8_t* wpack, const int8_t* w_pk, uint32_t rows, uint32_t n) {
     if (rows % 16 || n % 32 || n == 0) return fail(PKB_EINVAL, "repack: rows %u (16s) by n %u (32s)", rows, n);
     if (!rows) return PKB_OK;
@@ -296,6 +366,23 @@ int pkb_device_errors(int device, uint32_t* word) {
 uint64_t pkb_launch_count(void) { return g_launches.load(); }
 
 size_t pkb_wpack_bytes(uint32_t rows, uint32_t n) { return static_cast<size_t>(rows) * n; }
+
+int pkb_layernorm_quantize_dev(void* stream, int8_t* q, float* d, const float* x, size_t xs, uint32_t T, uint32_t n,
+                               uint32_t qb, const float* w, const float* b, float eps, int rmode) {
+    return pkb::layernorm_quantize_dev(static_cast<cudaStream_t>(stream), q, d, x, xs, T, n, qb, w, b, eps, rmode);
+}
+
+int pkb_silu_quantize_dev(void* stream, int8_t* q, float* d, const float* u, size_t us, uint32_t T, uint32_t n,
+                          uint32_t qb, int rmode) {
+    return pkb::silu_quantize_dev(static_cast<cudaStream_t>(stream), q, d, u, us, T, n, qb, rmode);
+}
+
+int pkb_dwconv_quantize_dev(void* stream, int8_t* q, float* d, float* out, size_t os, const float* x, size_t xs,
+                            uint32_t T, uint32_t C, const float* w, const float* b, uint32_t K, int glu, uint32_t qb,
+                            int rmode) {
+    return pkb::dwconv_quantize_dev(static_cast<cudaStream_t>(stream), q, d, out, os, x, xs, T, C, w, b, K, glu, qb,
+                                    rmode);
+}
 
 int pkb_repack_q8_dev(void* stream, int8_t* wpack, const int8_t* w_pk, uint32_t rows, uint32_t n) {
     return repack_dev(static_cast<cudaStream_t>(stream), wpack, w_pk, rows, n);

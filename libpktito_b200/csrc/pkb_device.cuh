@@ -67,6 +67,32 @@ __device__ __forceinline__ float sum_to_float_exact(uint32_t s) {
     return __fsub_rn(__uint_as_float(s + 0x4B400000u), 12582912.0f);
 }
 
+// One quantized byte: (int8)rint(v * id), rint in the mode RM, through
+// int as the reference's (int8_t)rintf(...) (backend/ref/kernels.c:24-58)
+template <int RM>
+__device__ __forceinline__ uint32_t quant1(float v, float id) {
+    return static_cast<uint8_t>(static_cast<int8_t>(f2i_r<RM>(mul_r<RM>(v, id))));
+}
+
+// Four quantized bytes, packed little-endian in the inputs' order.
+template <int RM>
+__device__ __forceinline__ uint32_t quant4(float4 v, float id) {
+    return quant1<RM>(v.x, id) | (quant1<RM>(v.y, id) << 8) | (quant1<RM>(v.z, id) << 16) |
+           (quant1<RM>(v.w, id) << 24);
+}
+
+// |v|'s bits. For floats of one sign the bits order as the values, and
+// every infinity or NaN is above every finite value, so the largest of a
+// block's |v| bits is its amax, or at least 0x7F800000 where it holds a
+// non-finite value.
+__device__ __forceinline__ uint32_t abs_bits(float v) { return __float_as_uint(v) & 0x7FFFFFFFu; }
+
+// Whether a block whose largest |v| bits are m is quantized (finite, amax
+// at least 2^-121) or becomes zeros with scale 0.
+__device__ __forceinline__ bool block_scaled(uint32_t m) {
+    return m < 0x7F800000u && __uint_as_float(m) >= 0x1p-121f;
+}
+
 // Two floats in one 64-bit register, for the packed f32x2 instructions of
 // sm_100 (one instruction, two independent IEEE operations).
 __device__ __forceinline__ uint64_t pack2(float lo, float hi) {

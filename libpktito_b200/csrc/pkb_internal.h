@@ -73,6 +73,17 @@ cudaError_t launch_pdl(void (*kern)(Params...), dim3 grid, dim3 block, size_t sm
 cudaError_t launch_quantize(int8_t* q, float* d, const float* x, size_t xs, uint32_t T, uint32_t n, uint32_t qb,
                             int rmode, int num_sms, cudaStream_t stream);
 
+cudaError_t launch_silu_quantize(int8_t* q, float* d, const float* u, size_t us, uint32_t T, uint32_t n,
+                                 uint32_t qb, int rmode, int num_sms, cudaStream_t stream);
+
+cudaError_t launch_layernorm_quantize(int8_t* q, float* d, const float* x, size_t xs, uint32_t T, uint32_t n,
+                                      uint32_t qb, const float* w, const float* b, float eps, int rmode,
+                                      int num_sms, cudaStream_t stream);
+
+cudaError_t launch_dwconv_quantize(int8_t* q, float* d, float* out, size_t os, const float* x, size_t xs, uint32_t T,
+                                   uint32_t C, const float* w, const float* bias, uint32_t K, bool glu, uint32_t qb,
+                                   int rmode, cudaStream_t stream);
+
 cudaError_t launch_repack_q8(int8_t* wpack, const int8_t* w_pk, uint32_t rows, uint32_t n, int num_sms,
                              cudaStream_t stream);
 

@@ -24,6 +24,7 @@
 
 #include "pkb_device.cuh"
 #include "pkb_internal.h"
+#include "pkb_vmath.cuh"
 
 namespace pkb {
 
@@ -42,23 +43,15 @@ __device__ __forceinline__ float amax4(float4 v) {
     return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 }
 
-// Four quantized bytes, packed little-endian in the inputs' order.
-template <int RM>
-__device__ __forceinline__ uint32_t quant4(float4 v, float id) {
-    const uint32_t b0 = static_cast<uint8_t>(static_cast<int8_t>(f2i_r<RM>(mul_r<RM>(v.x, id))));
-    const uint32_t b1 = static_cast<uint8_t>(static_cast<int8_t>(f2i_r<RM>(mul_r<RM>(v.y, id))));
-    const uint32_t b2 = static_cast<uint8_t>(static_cast<int8_t>(f2i_r<RM>(mul_r<RM>(v.z, id))));
-    const uint32_t b3 = static_cast<uint8_t>(static_cast<int8_t>(f2i_r<RM>(mul_r<RM>(v.w, id))));
-    return b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
-}
-
 // Blocks of QB = 32 or 64 inputs, E inputs (E / 4 16-byte loads) a thread,
 // QB / E threads a block. A warp takes 32 / (QB / E) blocks a chunk and U
 // chunks a pass, loading all of them before reducing any: many 16-byte
 // loads in flight a thread keep HBM busy (measured on B200 at qb 32: one a
 // thread 2.7 TB/s, four 3.6-4.0, eight 4.4-5.1). IDX is the index type,
-// 32-bit wherever T * n / qb fits.
-template <int RM, int QB, int E, int U, typename IDX>
+// 32-bit wherever T * n / qb fits. SILU: each input goes through the
+// reference's SiLU first (siluq_tile, core/encoder.c:150-158: k_silu on the
+// row, then pk_quant_part).
+template <int RM, int QB, int E, int U, typename IDX, bool SILU>
 __device__ __forceinline__ void quantize_narrow_body(int8_t* __restrict__ q, float* __restrict__ d,
                                                      const float* __restrict__ x, size_t xs, IDX nb, IDX total,
                                                      bool vec) {
@@ -82,6 +75,14 @@ __device__ __forceinline__ void quantize_narrow_body(int8_t* __restrict__ q, flo
             const float* xp = x + static_cast<size_t>(t[u]) * xs + static_cast<size_t>(b[u]) * QB + E * lg;
 #pragma unroll
             for (int e = 0; e < V; e++) v[u][e] = valid[u] ? load4(xp + 4 * e, vec) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        if constexpr (SILU) {
+#pragma unroll
+            for (int u = 0; u < U; u++)
+#pragma unroll
+                for (int e = 0; e < V; e++)
+                    v[u][e] = make_float4(pk_silu<RM>(v[u][e].x), pk_silu<RM>(v[u][e].y), pk_silu<RM>(v[u][e].z),
+                                          pk_silu<RM>(v[u][e].w));
         }
 #pragma unroll
         for (int u = 0; u < U; u++) {
@@ -119,7 +120,7 @@ __device__ __forceinline__ void quantize_narrow_body(int8_t* __restrict__ q, flo
     }
 }
 
-template <int RM, int QB, int E>
+template <int RM, int QB, int E, bool SILU>
 __global__ void __launch_bounds__(256) quantize_narrow(int8_t* __restrict__ q, float* __restrict__ d,
                                                        const float* __restrict__ x, size_t xs, uint32_t T,
                                                        uint32_t n, bool vec) {
@@ -129,9 +130,9 @@ __global__ void __launch_bounds__(256) quantize_narrow(int8_t* __restrict__ q, f
     const uint32_t nb = n / QB;
     const uint64_t total = static_cast<uint64_t>(T) * nb;
     if (total <= 0xFFFFFFF0ull)
-        quantize_narrow_body<RM, QB, E, U, uint32_t>(q, d, x, xs, nb, static_cast<uint32_t>(total), vec);
+        quantize_narrow_body<RM, QB, E, U, uint32_t, SILU>(q, d, x, xs, nb, static_cast<uint32_t>(total), vec);
     else
-        quantize_narrow_body<RM, QB, E, U, uint64_t>(q, d, x, xs, nb, total, vec);
+        quantize_narrow_body<RM, QB, E, U, uint64_t, SILU>(q, d, x, xs, nb, total, vec);
 }
 
 #ifndef PKB_Q64_E
@@ -174,7 +175,7 @@ __global__ void __launch_bounds__(256) quantize_wide(int8_t* __restrict__ q, flo
     }
 }
 
-template <int RM>
+template <int RM, bool SILU>
 cudaError_t quantize_rm(int8_t* q, float* d, const float* x, size_t xs, uint32_t T, uint32_t n, uint32_t qb,
                         int num_sms, cudaStream_t stream) {
     const bool vec = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (xs % 4 == 0);
@@ -191,11 +192,13 @@ cudaError_t quantize_rm(int8_t* q, float* d, const float* x, size_t xs, uint32_t
     if (grid == 0) grid = 1;
     const dim3 g(static_cast<unsigned>(grid)), b(256);
     if (qb == 32)
-        return q8 ? launch_pdl(quantize_narrow<RM, 32, 8>, g, b, 0, stream, q, d, x, xs, T, n, vec)
-                  : launch_pdl(quantize_narrow<RM, 32, 4>, g, b, 0, stream, q, d, x, xs, T, n, vec);
+        return q8 ? launch_pdl(quantize_narrow<RM, 32, 8, SILU>, g, b, 0, stream, q, d, x, xs, T, n, vec)
+                  : launch_pdl(quantize_narrow<RM, 32, 4, SILU>, g, b, 0, stream, q, d, x, xs, T, n, vec);
     else if (qb == 64)
-        return q8 ? launch_pdl(quantize_narrow<RM, 64, PKB_Q64_E>, g, b, 0, stream, q, d, x, xs, T, n, vec)
-                  : launch_pdl(quantize_narrow<RM, 64, 4>, g, b, 0, stream, q, d, x, xs, T, n, vec);
+        return q8 ? launch_pdl(quantize_narrow<RM, 64, PKB_Q64_E, SILU>, g, b, 0, stream, q, d, x, xs, T, n, vec)
+                  : launch_pdl(quantize_narrow<RM, 64, 4, SILU>, g, b, 0, stream, q, d, x, xs, T, n, vec);
+    else if constexpr (SILU)
+        return cudaErrorInvalidValue;  // the encoder's blocks are 32 or 64 (qb(), core/encoder.c:56)
     else
         return launch_pdl(quantize_wide<RM>, g, b, 0, stream, q, d, x, xs, T, n, qb, vec);
 }
@@ -220,10 +223,20 @@ __global__ void __launch_bounds__(256) repack_q8(uint32_t* __restrict__ dst, con
 cudaError_t launch_quantize(int8_t* q, float* d, const float* x, size_t xs, uint32_t T, uint32_t n, uint32_t qb,
                             int rmode, int num_sms, cudaStream_t stream) {
     switch (rmode) {
-    case 1: return quantize_rm<1>(q, d, x, xs, T, n, qb, num_sms, stream);
-    case 2: return quantize_rm<2>(q, d, x, xs, T, n, qb, num_sms, stream);
-    case 3: return quantize_rm<3>(q, d, x, xs, T, n, qb, num_sms, stream);
-    default: return quantize_rm<0>(q, d, x, xs, T, n, qb, num_sms, stream);
+    case 1: return quantize_rm<1, false>(q, d, x, xs, T, n, qb, num_sms, stream);
+    case 2: return quantize_rm<2, false>(q, d, x, xs, T, n, qb, num_sms, stream);
+    case 3: return quantize_rm<3, false>(q, d, x, xs, T, n, qb, num_sms, stream);
+    default: return quantize_rm<0, false>(q, d, x, xs, T, n, qb, num_sms, stream);
+    }
+}
+
+cudaError_t launch_silu_quantize(int8_t* q, float* d, const float* u, size_t us, uint32_t T, uint32_t n,
+                                 uint32_t qb, int rmode, int num_sms, cudaStream_t stream) {
+    switch (rmode) {
+    case 1: return quantize_rm<1, true>(q, d, u, us, T, n, qb, num_sms, stream);
+    case 2: return quantize_rm<2, true>(q, d, u, us, T, n, qb, num_sms, stream);
+    case 3: return quantize_rm<3, true>(q, d, u, us, T, n, qb, num_sms, stream);
+    default: return quantize_rm<0, true>(q, d, u, us, T, n, qb, num_sms, stream);
     }
 }
 

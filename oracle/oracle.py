@@ -57,6 +57,17 @@ def olib() -> ctypes.CDLL:
         l.oracle_pack_q8.argtypes = [vp, vp, u32, u32]
         l.oracle_unpack_q8.argtypes = [vp, vp, u32, u32]
         l.oracle_block_sums.argtypes = [vp, vp, u32, vp, u32, u32, u32]
+        f32, i32 = ctypes.c_float, ctypes.c_int
+        l.oracle_set_rint_style.argtypes = [i32]
+        l.oracle_expf.argtypes = [vp, vp, sz, i32]
+        l.oracle_sigmoidf.argtypes = [vp, vp, sz, i32]
+        l.oracle_layernorm.argtypes = [vp, sz, vp, sz, u32, u32, vp, vp, f32, i32]
+        l.oracle_layernorm_quantize.argtypes = [vp, vp, vp, sz, u32, u32, u32, vp, vp, f32, i32]
+        l.oracle_silu_quantize.argtypes = [vp, vp, vp, sz, u32, u32, u32, i32]
+        l.oracle_dwconv_quantize.argtypes = [vp, vp, vp, sz, vp, sz, u32, u32, vp, vp, u32, i32, u32, i32]
+        for f in (l.oracle_set_rint_style, l.oracle_expf, l.oracle_sigmoidf, l.oracle_layernorm,
+                  l.oracle_layernorm_quantize, l.oracle_silu_quantize, l.oracle_dwconv_quantize):
+            f.restype = None
         for f in (l.oracle_quantize, l.oracle_gemm_q8, l.oracle_pack_q8, l.oracle_unpack_q8, l.oracle_block_sums):
             f.restype = None
         _or = l
@@ -77,9 +88,25 @@ _GF = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, 
                        ctypes.c_uint32, ctypes.POINTER(_Act), ctypes.c_int)
 
 
+_F32F = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,
+                         ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint32, ctypes.c_void_p,
+                         ctypes.c_size_t, ctypes.c_int)
+_LNF = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint32,
+                        ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float)
+_SMF = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_float)
+_ROWF = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_size_t)
+_GLUF = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint32,
+                         ctypes.c_uint32)
+_DWF = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint32,
+                        ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32)
+
+
 class _Table(ctypes.Structure):
+    """pk_kernels (backend/kernels.h:242-278) up to its dwconv entry."""
     _fields_ = [("id", ctypes.c_char_p), ("name", ctypes.c_char_p), ("needs", ctypes.c_void_p),
-                ("competes", ctypes.c_int), ("quantize", _QF), ("gemm_q8", _GF)]
+                ("competes", ctypes.c_int), ("quantize", _QF), ("gemm_q8", _GF), ("gemm_f32", _F32F),
+                ("layernorm", _LNF), ("softmax", _SMF), ("silu", _ROWF), ("gelu", _ROWF), ("glu", _GLUF),
+                ("dwconv", _DWF)]
 
 
 def rlib() -> ctypes.CDLL:
@@ -129,6 +156,76 @@ def block_sums(w: np.ndarray, rows: int, q: np.ndarray, n: int, qb: int, T: int)
     s = np.empty((T, rows, n // qb), np.int32)
     olib().oracle_block_sums(_p(s), _p(w), rows, _p(q), n, qb, T)
     return s
+
+
+class rint_style:
+    """Within the block, the oracle's rintf rounds as gcc compiles it for
+    baseline x86-64 (|x| in the mode, the sign put back: the reference's own
+    ref build) instead of IEEE's rint; for holding the oracle to that build
+    in the directed modes."""
+
+    def __enter__(self):
+        olib().oracle_set_rint_style(1)
+
+    def __exit__(self, *exc):
+        olib().oracle_set_rint_style(0)
+
+
+def expf(x: np.ndarray, rmode: int = RN) -> np.ndarray:
+    """pk_expf (core/vmath.h:134-147), elementwise."""
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    olib().oracle_expf(_p(y), _p(x), x.size, rmode)
+    return y
+
+
+def sigmoidf(x: np.ndarray, rmode: int = RN) -> np.ndarray:
+    """pk_sigmoidf (core/vmath.h:149-151), elementwise."""
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    olib().oracle_sigmoidf(_p(y), _p(x), x.size, rmode)
+    return y
+
+
+def layernorm_quantize(x: np.ndarray, xs: int, T: int, n: int, qb: int, w: np.ndarray, b: np.ndarray, eps: float,
+                       rmode: int = RN) -> tuple[np.ndarray, np.ndarray]:
+    """normq (core/encoder.c:112-130)."""
+    q = np.zeros((T, n), np.int8)
+    d = np.zeros((T, n // qb), np.float32)
+    olib().oracle_layernorm_quantize(_p(q), _p(d), _p(_f32(x)), xs, T, n, qb, _p(_f32(w)), _p(_f32(b)), eps, rmode)
+    return q, d
+
+
+def layernorm(x: np.ndarray, xs: int, T: int, n: int, w: np.ndarray, b: np.ndarray, eps: float,
+              rmode: int = RN) -> np.ndarray:
+    """k_layernorm (backend/ref/kernels.c:115-131)."""
+    out = np.zeros((T, n), np.float32)
+    olib().oracle_layernorm(_p(out), n, _p(_f32(x)), xs, T, n, _p(_f32(w)), _p(_f32(b)), eps, rmode)
+    return out
+
+
+def silu_quantize(u: np.ndarray, us: int, T: int, n: int, qb: int, rmode: int = RN) -> tuple[np.ndarray, np.ndarray]:
+    """siluq_tile (core/encoder.c:150-158)."""
+    q = np.zeros((T, n), np.int8)
+    d = np.zeros((T, n // qb), np.float32)
+    olib().oracle_silu_quantize(_p(q), _p(d), _p(_f32(u)), us, T, n, qb, rmode)
+    return q, d
+
+
+def dwconv_quantize(x: np.ndarray, xs: int, T: int, C: int, w: np.ndarray, b: np.ndarray, K: int, glu: bool, qb: int,
+                    rmode: int = RN) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """glu_item + dw_item (core/encoder.c:160-183): (q, d, the convolution's floats)."""
+    q = np.zeros((T, C), np.int8)
+    d = np.zeros((T, C // qb), np.float32)
+    out = np.zeros((T, C), np.float32)
+    olib().oracle_dwconv_quantize(_p(q), _p(d), _p(out), C, _p(_f32(x)), xs, T, C, _p(_f32(w)), _p(_f32(b)), K,
+                                  int(glu), qb, rmode)
+    return q, d, out
+
+
+def _f32(a: np.ndarray) -> np.ndarray:
+    a = np.ascontiguousarray(a, np.float32).reshape(-1)
+    return a
 
 
 # ------------------------------------------------- the reference's own ref --
@@ -214,3 +311,78 @@ def seeded_normal(shape, seed: int) -> np.ndarray:
 def uniform_weights(rows: int, n: int, seed: int) -> np.ndarray:
     rng = np.random.default_rng(seed)
     return rng.integers(-127, 128, size=(rows, n), dtype=np.int8)
+
+
+# ------------------------------- the reference's producers, as its encoder --
+
+def _part(q: np.ndarray, d: np.ndarray, t: int, k0: int, nn: int, n: int, qb: int) -> _Act:
+    """pk_quant_part's activation view (core/passes.c:114-118): nn inputs of
+    column t from input k0"""
+    at = t * n + k0
+    return _Act(q.ctypes.data + at, d.ctypes.data + 4 * (at // qb), nn, qb, 1)
+
+
+def ref_layernorm_quantize(x: np.ndarray, xs: int, T: int, n: int, qb: int, w: np.ndarray, b: np.ndarray, eps: float,
+                           rmode: int = RN) -> tuple[np.ndarray, np.ndarray]:
+    """normq_item (core/encoder.c:114-124) through the reference's ref table:
+    k_layernorm of a frame into a row, pk_quant_part of the row."""
+    x, w, b = _f32(x), _f32(w), _f32(b)
+    q = np.zeros((T, n), np.int8)
+    d = np.zeros((T, n // qb), np.float32)
+    row = np.zeros(n, np.float32)
+    k = _Table.in_dll(rlib(), "pk_kernels_ref")
+
+    def run():
+        for t in range(T):
+            k.layernorm(_p(row), n, x.ctypes.data + 4 * t * xs, n, 1, n, _p(w), _p(b), eps)
+            act = _part(q, d, t, 0, n, n, qb)
+            k.quantize(ctypes.byref(act), _p(row), n)
+    _with_mode(rmode, run)
+    return q, d
+
+
+def ref_silu_quantize(u: np.ndarray, us: int, T: int, n: int, qb: int, rmode: int = RN) -> tuple[np.ndarray, np.ndarray]:
+    """siluq_tile (core/encoder.c:150-158) through the ref table, the whole
+    row as one tile: copy, k_silu, pk_quant_part."""
+    u = _f32(u)
+    q = np.zeros((T, n), np.int8)
+    d = np.zeros((T, n // qb), np.float32)
+    k = _Table.in_dll(rlib(), "pk_kernels_ref")
+
+    def run():
+        for t in range(T):
+            row = u[t * us: t * us + n].copy()
+            k.silu(_p(row), n)
+            act = _part(q, d, t, 0, n, n, qb)
+            k.quantize(ctypes.byref(act), _p(row), n)
+    _with_mode(rmode, run)
+    return q, d
+
+
+def ref_dwconv_quantize(x: np.ndarray, xs: int, T: int, C: int, w: np.ndarray, b: np.ndarray, K: int, glu: bool,
+                        qb: int, rmode: int = RN) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """glu_item + dw_item (core/encoder.c:160-183) through the ref table:
+    k_glu over the frames where glu, then per chunk of 64 channels k_dwconv
+    and pk_quant_part of each frame's chunk."""
+    x, w, b = _f32(x), _f32(w), _f32(b)
+    q = np.zeros((T, C), np.int8)
+    d = np.zeros((T, C // qb), np.float32)
+    out = np.zeros((T, C), np.float32)
+    k = _Table.in_dll(rlib(), "pk_kernels_ref")
+
+    def run():
+        if glu:
+            h = np.zeros((T, C), np.float32)
+            k.glu(_p(h), C, _p(x), xs, T, C)
+            src, ss = h.reshape(-1), C
+        else:
+            src, ss = x, xs
+        for c0 in range(0, C, 64):
+            nc = min(64, C - c0)
+            k.dwconv(out.ctypes.data + 4 * c0, C, src.ctypes.data + 4 * c0, ss, T, nc, w.ctypes.data + 4 * c0 * K,
+                     b.ctypes.data + 4 * c0, K)
+            for t in range(T):
+                act = _part(q, d, t, c0, nc, C, qb)
+                k.quantize(ctypes.byref(act), out.ctypes.data + 4 * (t * C + c0), nc)
+    _with_mode(rmode, run)
+    return q, d, out

@@ -4,11 +4,21 @@
  * tests/, __graft_entry__.smoke() and bench.py's cpu_baseline leg load it;
  * the product (libpktito_b200) never links, calls or falls back to it.
  *
- * It restates two functions of the reference, in this file's own code:
+ * It restates these functions of the reference, in this file's own code:
  *
  *   oracle_quantize  backend/ref/kernels.c:24-58 (contract backend/kernels.h:47-58)
  *   oracle_gemm_q8   backend/ref/kernels.c:60-86 (contract backend/kernels.h:60-78),
  *                    with the PK_Q8 panel index of core/pkf.h:28-41
+ *   and the producers of the product's inputs in the encoder, with the float
+ *   kernels and the mathematics they use:
+ *   oracle_layernorm_quantize  normq, core/encoder.c:112-130 (k_layernorm,
+ *                    backend/ref/kernels.c:109-131, then pk_quant_part,
+ *                    core/passes.c:114-118)
+ *   oracle_silu_quantize       siluq_tile, core/encoder.c:150-158 (k_silu,
+ *                    backend/ref/kernels.c:149-151)
+ *   oracle_dwconv_quantize     glu_item + dw_item, core/encoder.c:160-183
+ *                    (k_glu :157-161, k_dwconv :163-177)
+ *   oracle_expf, oracle_sigmoidf  pk_expf, pk_sigmoidf, core/vmath.h:93-151
  *
  * Both take the rounding mode as an argument (PKB_RN/RD/RU/RZ, the codes of
  * include/pktito_b200.h) and run their float arithmetic under it, since the
@@ -34,6 +44,25 @@
 #pragma STDC FENV_ACCESS ON
 
 enum { OR_RN = 0, OR_RD = 1, OR_RU = 2, OR_RZ = 3 };
+
+/* How rintf rounds. 0: IEEE's roundToIntegral in the current mode, the
+ * contract's rint (backend/kernels.h:52). 1: as gcc compiles rintf for
+ * baseline x86-64 (the reference's own ref build): |x| rounded in the mode,
+ * the sign put back, so that under FE_DOWNWARD a negative value rounds
+ * toward zero and under FE_UPWARD away from it. The tests use 1 to hold this
+ * file to that compiled ref in every mode, and 0 for the CUDA path. */
+static int g_rint_style = 0;
+
+void oracle_set_rint_style(int style) { g_rint_style = style; }
+
+static float or_rintf(float x) {
+    if (!g_rint_style)
+        return rintf(x);
+    const float a = fabsf(x);
+    if (!(a < 0x1p23f))
+        return x;
+    return copysignf((a + 0x1p23f) - 0x1p23f, x);
+}
 
 static int fe_of(int rmode) {
     switch (rmode) {
@@ -70,7 +99,7 @@ static void quant_block(int8_t *q, float *d, const float *v, uint32_t qb) {
     for (uint32_t i = 0; i < qb; i++) {
         /* rintf rounds in the current mode; the conversion to int8 goes
          * through int, as the reference's (int8_t)rintf(...) does */
-        const float r = rintf(v[i] * inv);
+        const float r = or_rintf(v[i] * inv);
         q[i] = (int8_t)(int32_t)r;
     }
 }
@@ -173,4 +202,179 @@ void oracle_block_sums(int32_t *s, const int8_t *w, uint32_t rows, const int8_t 
                 s[((size_t)t * rows + r) * nb + b] =
                     block_sum(w_rm + (size_t)r * n + (size_t)b * qb, q + (size_t)t * n + (size_t)b * qb, qb);
     free(w_rm);
+}
+
+/* ------------------------------------------- the producers' float steps -- */
+
+/* pk_expf (core/vmath.h:134-147) with its constants (core/vmath.h:93-124):
+ * n = rint(x log2e) on the clamped x, r = x - n ln2 in two fused steps, a
+ * degree-6 polynomial by Horner in fused steps, times 2^n. */
+static float or_expf(float x) {
+    x = fminf(fmaxf(x, -87.0f), 88.0f);
+    const float n = or_rintf(x * 0x1.715476p+0f);
+    float r = fmaf(n, -0x1.62e430p-1f, x);
+    r = fmaf(n, 0x1.05c610p-29f, r);
+    float p = 0x1.6ab980p-10f;
+    p = fmaf(p, r, 0x1.126d0cp-7f);
+    p = fmaf(p, r, 0x1.55589ap-5f);
+    p = fmaf(p, r, 0x1.55540ap-3f);
+    p = fmaf(p, r, 0x1.fffffap-2f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    const uint32_t u = (uint32_t)((int32_t)n + 127) << 23;
+    float two_n;
+    memcpy(&two_n, &u, sizeof two_n);
+    return p * two_n;
+}
+
+/* pk_sigmoidf (core/vmath.h:149-151) */
+static float or_sigmoidf(float x) { return 1.0f / (1.0f + or_expf(-x)); }
+
+void oracle_expf(float *y, const float *x, size_t n, int rmode) {
+    const int was = fegetround();
+    fesetround(fe_of(rmode));
+    for (size_t i = 0; i < n; i++)
+        y[i] = or_expf(x[i]);
+    fesetround(was);
+}
+
+void oracle_sigmoidf(float *y, const float *x, size_t n, int rmode) {
+    const int was = fegetround();
+    fesetround(fe_of(rmode));
+    for (size_t i = 0; i < n; i++)
+        y[i] = or_sigmoidf(x[i]);
+    fesetround(was);
+}
+
+/* lanes_sum (backend/ref/kernels.c:109-113): 16 partial sums folded 8, 4, 2, 1 */
+static float or_fold16(float *acc) {
+    for (int h = 8; h > 0; h /= 2)
+        for (int i = 0; i < h; i++)
+            acc[i] = acc[i] + acc[i + h];
+    return acc[0];
+}
+
+/* k_layernorm (backend/ref/kernels.c:115-131) on one row: the sums in 16
+ * lanes, input i into lane i % 16, in order */
+static void or_layernorm_row(float *o, const float *v, uint32_t n, const float *w, const float *b, float eps) {
+    float acc[16] = { 0 };
+    for (uint32_t i = 0; i < n; i++)
+        acc[i % 16] = acc[i % 16] + v[i];
+    const float mean = or_fold16(acc) / (float)n;
+    memset(acc, 0, sizeof acc);
+    for (uint32_t i = 0; i < n; i++) {
+        const float c = v[i] - mean;
+        acc[i % 16] = acc[i % 16] + c * c;
+    }
+    const float var = or_fold16(acc) / (float)n;
+    const float r = 1.0f / sqrtf(var + eps);
+    for (uint32_t i = 0; i < n; i++)
+        o[i] = (v[i] - mean) * r * w[i] + b[i];
+}
+
+void oracle_layernorm(float *out, size_t os, const float *x, size_t xs, uint32_t T, uint32_t n, const float *w,
+                      const float *b, float eps, int rmode) {
+    const int was = fegetround();
+    fesetround(fe_of(rmode));
+    for (uint32_t t = 0; t < T; t++)
+        or_layernorm_row(out + (size_t)t * os, x + (size_t)t * xs, n, w, b, eps);
+    fesetround(was);
+}
+
+/* normq (core/encoder.c:112-130): each row normalized into scratch, then
+ * quantized whole (pk_quant_part with k0 = 0, core/passes.c:114-118) */
+void oracle_layernorm_quantize(int8_t *q, float *d, const float *x, size_t xs, uint32_t T, uint32_t n, uint32_t qb,
+                               const float *w, const float *b, float eps, int rmode) {
+    float *row = malloc((size_t)n * sizeof *row);
+    if (!row)
+        abort();
+    const int was = fegetround();
+    fesetround(fe_of(rmode));
+    const uint32_t nb = n / qb;
+    for (uint32_t t = 0; t < T; t++) {
+        or_layernorm_row(row, x + (size_t)t * xs, n, w, b, eps);
+        for (uint32_t k = 0; k < nb; k++)
+            quant_block(q + (size_t)t * n + (size_t)k * qb, d + (size_t)t * nb + k, row + (size_t)k * qb, qb);
+    }
+    fesetround(was);
+    free(row);
+}
+
+/* siluq_tile (core/encoder.c:150-158): a row copied to scratch, k_silu
+ * (backend/ref/kernels.c:149-151) on it, quantized */
+void oracle_silu_quantize(int8_t *q, float *d, const float *u, size_t us, uint32_t T, uint32_t n, uint32_t qb,
+                          int rmode) {
+    float *row = malloc((size_t)n * sizeof *row);
+    if (!row)
+        abort();
+    const int was = fegetround();
+    fesetround(fe_of(rmode));
+    const uint32_t nb = n / qb;
+    for (uint32_t t = 0; t < T; t++) {
+        for (uint32_t i = 0; i < n; i++) {
+            const float v = u[(size_t)t * us + i];
+            row[i] = v * or_sigmoidf(v);
+        }
+        for (uint32_t k = 0; k < nb; k++)
+            quant_block(q + (size_t)t * n + (size_t)k * qb, d + (size_t)t * nb + k, row + (size_t)k * qb, qb);
+    }
+    fesetround(was);
+    free(row);
+}
+
+/* k_glu (backend/ref/kernels.c:157-161): out[t][i] = a[i] * sigmoid(a[n + i]) */
+static void or_glu(float *out, size_t os, const float *x, size_t xs, uint32_t T, uint32_t n) {
+    for (uint32_t t = 0; t < T; t++)
+        for (uint32_t i = 0; i < n; i++)
+            out[(size_t)t * os + i] = x[(size_t)t * xs + i] * or_sigmoidf(x[(size_t)t * xs + n + i]);
+}
+
+/* k_dwconv (backend/ref/kernels.c:163-177): K taps centred, those reading
+ * past either end skipped, + bias, SiLU */
+static void or_dwconv(float *out, size_t os, const float *x, size_t xs, uint32_t T, uint32_t C, const float *w,
+                      const float *b, uint32_t K) {
+    for (uint32_t t = 0; t < T; t++)
+        for (uint32_t c = 0; c < C; c++) {
+            float acc = 0.0f;
+            for (uint32_t j = 0; j < K; j++) {
+                const int64_t s = (int64_t)t + j - K / 2;
+                if (s >= 0 && s < T)
+                    acc = fmaf(w[(size_t)c * K + j], x[(size_t)s * xs + c], acc);
+            }
+            const float v = acc + b[c];
+            out[(size_t)t * os + c] = v * or_sigmoidf(v);
+        }
+}
+
+/* glu_item + dw_item (core/encoder.c:160-183): with glu, x is pw1's output
+ * (2C a frame) made into k_glu's C first; the convolution into out (scratch
+ * when out is NULL), then each frame quantized (its chunks of 64 channels
+ * are whole blocks, so a frame's blocks are the same as the row's) */
+void oracle_dwconv_quantize(int8_t *q, float *d, float *out, size_t os, const float *x, size_t xs, uint32_t T,
+                            uint32_t C, const float *w, const float *b, uint32_t K, int glu, uint32_t qb, int rmode) {
+    float *h = NULL, *o = out;
+    if (glu && !(h = malloc((size_t)T * C * sizeof *h)))
+        abort();
+    if (!o) {
+        if (!(o = malloc((size_t)T * C * sizeof *o)))
+            abort();
+        os = C;
+    }
+    const int was = fegetround();
+    fesetround(fe_of(rmode));
+    if (glu) {
+        or_glu(h, C, x, xs, T, C);
+        or_dwconv(o, os, h, C, T, C, w, b, K);
+    } else {
+        or_dwconv(o, os, x, xs, T, C, w, b, K);
+    }
+    const uint32_t nb = C / qb;
+    for (uint32_t t = 0; t < T; t++)
+        for (uint32_t k = 0; k < nb; k++)
+            quant_block(q + (size_t)t * C + (size_t)k * qb, d + (size_t)t * nb + k, o + (size_t)t * os + (size_t)k * qb,
+                        qb);
+    fesetround(was);
+    if (o != out)
+        free(o);
+    free(h);
 }

@@ -133,3 +133,116 @@ def test_reference_quantize_directed_modes_differs_only_in_rint():
         assert np.array_equal(q1[~neg], q2[~neg])
         diff = q2[neg].astype(np.int32) - q1[neg].astype(np.int32)
         assert np.all(np.abs(diff) <= 1) and np.any(diff != 0)
+
+
+@needs_ref
+def test_reference_quantize_every_mode_with_its_rint():
+    """With the oracle's rintf rounding as the reference's baseline build
+    rounds it (|x| in the mode, the sign put back), the oracle's quantize is
+    the reference's ref byte for byte in every mode: rint is the whole
+    difference."""
+    n, qb, T = 1024, 32, 8
+    x = np.random.default_rng(8).standard_normal(T * n).astype(np.float32) * 100
+    for rmode in (O.RN, O.RD, O.RU, O.RZ):
+        with O.rint_style():
+            q1, d1 = O.quantize(x, n, qb, rmode=rmode)
+        q2, d2 = O.ref_quantize(x, n, qb, rmode=rmode)
+        assert np.array_equal(q1, q2) and d1.tobytes() == d2.tobytes()
+
+
+# ---------------------------------------------------- the fused producers --
+
+PRODUCERS = os.path.join(os.path.dirname(__file__), "golden", "producers_golden.npz")
+
+
+@pytest.fixture(scope="module")
+def producers():
+    return np.load(PRODUCERS)
+
+
+def producer_cases(g):
+    """(kind, prefix, meta, rounding modes stored) for every fixture case"""
+    for k in sorted(g.files):
+        if k.endswith("/meta"):
+            p = k[:-4]
+            modes = sorted(int(f[len(p) + 1:]) for f in g.files if f.startswith(p + "q"))
+            yield p.split("/")[0], p, [int(v) for v in g[k]], modes
+
+
+def run_producer(g, kind, p, meta, rmode):
+    """the oracle on a fixture case: (q, d, floats or None)"""
+    if kind == "ln":
+        T, n, qb, xs = meta
+        return (*O.layernorm_quantize(g[p + "x"], xs, T, n, qb, g[p + "w"], g[p + "b"], float(g[p + "eps"]), rmode),
+                None)
+    if kind == "si":
+        T, n, qb, us = meta
+        return (*O.silu_quantize(g[p + "u"], us, T, n, qb, rmode), None)
+    T, C, K, glu, qb, xs = meta
+    return O.dwconv_quantize(g[p + "x"], xs, T, C, g[p + "w"], g[p + "b"], K, bool(glu), qb, rmode)
+
+
+def same_as_fixture(g, p, rmode, q, d, o) -> bool:
+    return (np.array_equal(q, g[p + f"q{rmode}"]) and d.tobytes() == g[p + f"d{rmode}"].tobytes()
+            and (o is None or o.tobytes() == g[p + f"o{rmode}"].tobytes()))
+
+
+def test_golden_producers(producers):
+    """normq, siluq_tile and glu_item + dw_item as the reference's ref wrote
+    them (tests/golden/make_producers_golden.py): the oracle with the
+    reference's build of rintf matches every case in every mode, and with
+    IEEE's rint (what the CUDA path computes) every case in RN and RZ."""
+    n_cases = 0
+    for kind, p, meta, modes in producer_cases(producers):
+        for rmode in modes:
+            with O.rint_style():
+                assert same_as_fixture(producers, p, rmode, *run_producer(producers, kind, p, meta, rmode)), (p, rmode)
+            if rmode in (O.RN, O.RZ):
+                assert same_as_fixture(producers, p, rmode, *run_producer(producers, kind, p, meta, rmode)), (p, rmode)
+            n_cases += 1
+    assert n_cases >= 40
+
+
+@needs_ref
+@pytest.mark.parametrize("rmode", [O.RN, O.RD, O.RU, O.RZ])
+def test_live_reference_producers(rmode):
+    """The oracle's three producers against the reference's own, composed as
+    its encoder composes them, on fresh shapes in every mode."""
+    g = np.random.default_rng(50 + rmode)
+    for T, n, qb, xs in [(6, 256, 32, 272), (3, 2048, 64, 2048), (11, 160, 32, 160)]:
+        x = (g.standard_normal(T * xs + n) * 4 + 1).astype(np.float32)
+        w, b = g.standard_normal(n).astype(np.float32), g.standard_normal(n).astype(np.float32)
+        with O.rint_style():
+            q1, d1 = O.layernorm_quantize(x, xs, T, n, qb, w, b, 1e-5, rmode)
+        q2, d2 = O.ref_layernorm_quantize(x, xs, T, n, qb, w, b, 1e-5, rmode)
+        assert np.array_equal(q1, q2) and d1.tobytes() == d2.tobytes()
+        with O.rint_style():
+            q1, d1 = O.silu_quantize(x * 5, xs, T, n, qb, rmode)
+        q2, d2 = O.ref_silu_quantize(x * 5, xs, T, n, qb, rmode)
+        assert np.array_equal(q1, q2) and d1.tobytes() == d2.tobytes()
+    for T, C, K, glu, qb in [(13, 192, 9, 1, 64), (4, 96, 7, 0, 32), (30, 64, 15, 1, 32)]:
+        xs = 2 * C + 8
+        x = g.standard_normal(T * xs).astype(np.float32)
+        w, b = (g.standard_normal(C * K) * 0.5).astype(np.float32), g.standard_normal(C).astype(np.float32)
+        with O.rint_style():
+            r1 = O.dwconv_quantize(x, xs, T, C, w, b, K, bool(glu), qb, rmode)
+        r2 = O.ref_dwconv_quantize(x, xs, T, C, w, b, K, bool(glu), qb, rmode)
+        assert all(a.tobytes() == c.tobytes() for a, c in zip(r1, r2))
+
+
+def test_exp_and_sigmoid_properties():
+    """pk_expf and pk_sigmoidf as restated: exact at 0, within 1 and 2 ulp
+    of the double-precision functions on a sweep (the accuracy the reference
+    states, core/vmath.h:19-31), the clamp's ends, and a NaN taken to the
+    low end."""
+    x = np.linspace(-87, 88, 200001, dtype=np.float32)
+    e = O.expf(x)
+    ref = np.exp(x.astype(np.float64)).astype(np.float32)
+    ulp = np.abs(e.view(np.int32).astype(np.int64) - ref.view(np.int32).astype(np.int64))
+    assert ulp.max() <= 1
+    s = O.sigmoidf(x)
+    sref = (1.0 / (1.0 + np.exp(-x.astype(np.float64)))).astype(np.float32)
+    assert np.abs(s.view(np.int32).astype(np.int64) - sref.view(np.int32).astype(np.int64)).max() <= 2
+    special = np.array([0.0, np.nan, np.inf, -np.inf, 1000.0, -1000.0], np.float32)
+    e = O.expf(special)
+    assert e[0] == 1.0 and e[1] == e[5] == e[3] and e[2] == e[4] and np.isfinite(e).all()
