@@ -73,6 +73,14 @@ int pkb_device_errors(int device, uint32_t *word);
  * it did; the device stays usable. For tests and health checks. */
 int pkb_wait_selftest(uint64_t limit_cycles, int *gave_up);
 
+/* Checks the sigmoid's branch-free reciprocal (Markstein's method, used by
+ * the fused producers) against CUDA's correctly rounded reciprocal in the
+ * rounding mode rmode for every float whose bits lie in [lo_bits, hi_bits),
+ * within [1, 2^128): *mismatches = how many differ, *first_bad = the
+ * smallest such bits (0xFFFFFFFF if none). A test of this library's own
+ * arithmetic; no counterpart in the reference. */
+int pkb_rcp_selftest(int rmode, uint32_t lo_bits, uint32_t hi_bits, uint64_t *mismatches, uint32_t *first_bad);
+
 /* ---------------------------------------------- host-pointer contract -- */
 
 /* pk_k_quantize (backend/kernels.h:47-58; ref backend/ref/kernels.c:24-58):

@@ -66,6 +66,8 @@ _SIGS = {
     "pkb_set_thread_device": (ctypes.c_int, [ctypes.c_int]),
     "pkb_device_errors": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)]),
     "pkb_wait_selftest": (ctypes.c_int, [ctypes.c_uint64, ctypes.POINTER(ctypes.c_int)]),
+    "pkb_rcp_selftest": (ctypes.c_int, [ctypes.c_int, ctypes.c_uint32, ctypes.c_uint32,
+                                        ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint32)]),
     "pkb_quantize_host": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,
                                          ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]),
     "pkb_gemm_q8_host": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p,
@@ -138,6 +140,14 @@ def wait_selftest(limit_cycles: int = 2_000_000) -> bool:
     g = ctypes.c_int(0)
     _check(lib().pkb_wait_selftest(limit_cycles, ctypes.byref(g)))
     return bool(g.value)
+
+
+def rcp_selftest(rmode: int, lo_bits: int = 0x3F800000, hi_bits: int = 0x7F800000) -> tuple[int, int]:
+    """(mismatches, smallest mismatching bits) of the sigmoid's reciprocal
+    against the correctly rounded one over floats with bits in [lo, hi)."""
+    m, f = ctypes.c_uint64(0), ctypes.c_uint32(0)
+    _check(lib().pkb_rcp_selftest(rmode, lo_bits, hi_bits, ctypes.byref(m), ctypes.byref(f)))
+    return m.value, f.value
 
 
 def device_errors(dev: int = 0) -> int:

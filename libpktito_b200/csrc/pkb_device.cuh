@@ -67,18 +67,35 @@ __device__ __forceinline__ float sum_to_float_exact(uint32_t s) {
     return __fsub_rn(__uint_as_float(s + 0x4B400000u), 12582912.0f);
 }
 
-// One quantized byte: (int8)rint(v * id), rint in the mode RM, through
-// int as the reference's (int8_t)rintf(...) (backend/ref/kernels.c:24-58)
+// Rounding to an integer by adding 1.5 * 2^23 (RN, RD, RU): for |p| < 2^22
+// the sum lies in [2^23, 2^24), where floats are the integers, so the one
+// rounding of the addition is rint(p) in the mode (ties to even under RN:
+// 1.5 * 2^23 is even), and the sum's bits are 0x4B400000 + rint(p). Exact
+// and on the FP32 pipe, where a float-to-int conversion takes the
+// quarter-rate conversion pipe. Toward zero the sum would round a negative
+// p down, so RZ converts instead.
+constexpr float RINT_MAGIC = 12582912.0f;  // 1.5 * 2^23
+constexpr uint32_t RINT_MAGIC_BITS = 0x4B400000u;
+
+// One quantized byte, as the low byte of a word: (int8)rint(v * id), rint
+// in the mode RM, through int as the reference's (int8_t)rintf(...)
+// (backend/ref/kernels.c:24-58); |v * id| <= 127 rounded.
 template <int RM>
 __device__ __forceinline__ uint32_t quant1(float v, float id) {
-    return static_cast<uint8_t>(static_cast<int8_t>(f2i_r<RM>(mul_r<RM>(v, id))));
+    const float p = mul_r<RM>(v, id);
+    if constexpr (RM == 3) return static_cast<uint8_t>(static_cast<int8_t>(f2i_r<RM>(p)));
+    return __float_as_uint(add_r<RM>(p, RINT_MAGIC));  // low byte: 0x00 + rint(p), two's complement
+}
+
+// The low bytes of four words, packed little-endian in that order.
+__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
 // Four quantized bytes, packed little-endian in the inputs' order.
 template <int RM>
 __device__ __forceinline__ uint32_t quant4(float4 v, float id) {
-    return quant1<RM>(v.x, id) | (quant1<RM>(v.y, id) << 8) | (quant1<RM>(v.z, id) << 16) |
-           (quant1<RM>(v.w, id) << 24);
+    return pack_low_bytes(quant1<RM>(v.x, id), quant1<RM>(v.y, id), quant1<RM>(v.z, id), quant1<RM>(v.w, id));
 }
 
 // |v|'s bits. For floats of one sign the bits order as the values, and
@@ -133,6 +150,31 @@ __device__ __forceinline__ uint64_t add2_rn(uint64_t a, uint64_t b) {
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
     return r;
 }
+
+// a * b and a + b on both halves, each rounded once in the mode RM.
+// Measured on B200 (ptxas 12.9): a packed multiply whose result feeds a
+// packed add is fused into one packed FMA, explicit rounding and -fmad=false
+// notwithstanding, which rounds once where the reference rounds twice. So a
+// mul2_r result never goes into an add2_r (or fma2_r's addend); a multiply
+// that an add follows is the scalar mul_r (__fmul_rn and its kind are never
+// fused).
+template <int RM> __device__ __forceinline__ uint64_t mul2_r(uint64_t a, uint64_t b);
+template <int RM> __device__ __forceinline__ uint64_t add2_r(uint64_t a, uint64_t b);
+#define PKB_F32X2_OP(NAME, OP, RM, RND)                                                 \
+    template <> __device__ __forceinline__ uint64_t NAME<RM>(uint64_t a, uint64_t b) { \
+        uint64_t r;                                                                       \
+        asm(OP "." RND ".f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));                  \
+        return r;                                                                         \
+    }
+PKB_F32X2_OP(mul2_r, "mul", 0, "rn")
+PKB_F32X2_OP(mul2_r, "mul", 1, "rm")
+PKB_F32X2_OP(mul2_r, "mul", 2, "rp")
+PKB_F32X2_OP(mul2_r, "mul", 3, "rz")
+PKB_F32X2_OP(add2_r, "add", 0, "rn")
+PKB_F32X2_OP(add2_r, "add", 1, "rm")
+PKB_F32X2_OP(add2_r, "add", 2, "rp")
+PKB_F32X2_OP(add2_r, "add", 3, "rz")
+#undef PKB_F32X2_OP
 
 // --------------------------------------------------------------- smem / sync --
 
@@ -237,6 +279,20 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
 }
 
 // Closes the thread's current bulk group of TMA stores.
+// Per-thread asynchronous copies into shared memory (LDGSTS): 16 or 4
+// bytes, tracked in groups that the copying thread waits for itself (a
+// hardware wait, not a poll).
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// all but the newest N groups of this thread's copies have landed
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 // Waits until the thread's bulk groups have finished reading their shared

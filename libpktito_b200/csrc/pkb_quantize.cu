@@ -77,33 +77,44 @@ __device__ __forceinline__ void quantize_narrow_body(int8_t* __restrict__ q, flo
             for (int e = 0; e < V; e++) v[u][e] = valid[u] ? load4(xp + 4 * e, vec) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
         if constexpr (SILU) {
+            // the thread's U * V * 4 inputs through SiLU as one batch
+            float xs4[U * V * 4];
 #pragma unroll
             for (int u = 0; u < U; u++)
 #pragma unroll
-                for (int e = 0; e < V; e++)
-                    v[u][e] = make_float4(pk_silu<RM>(v[u][e].x), pk_silu<RM>(v[u][e].y), pk_silu<RM>(v[u][e].z),
-                                          pk_silu<RM>(v[u][e].w));
+                for (int e = 0; e < V; e++) {
+                    float* o = xs4 + 4 * (u * V + e);
+                    o[0] = v[u][e].x;
+                    o[1] = v[u][e].y;
+                    o[2] = v[u][e].z;
+                    o[3] = v[u][e].w;
+                }
+            silu_batch<RM, U * V * 4>(xs4);
+#pragma unroll
+            for (int u = 0; u < U; u++)
+#pragma unroll
+                for (int e = 0; e < V; e++) {
+                    const float* o = xs4 + 4 * (u * V + e);
+                    v[u][e] = make_float4(o[0], o[1], o[2], o[3]);
+                }
         }
 #pragma unroll
         for (int u = 0; u < U; u++) {
-            float amax = amax4(v[u][0]);
-            uint32_t bad = finite4(v[u][0]) ? 0u : 1u;
+            // the block's largest |x| bits: its amax, or a non-finite value
+            uint32_t m = 0;
 #pragma unroll
-            for (int e = 1; e < V; e++) {
-                amax = fmaxf(amax, amax4(v[u][e]));
-                bad |= finite4(v[u][e]) ? 0u : 1u;
-            }
+            for (int e = 0; e < V; e++)
+                m = max(m, max(max(abs_bits(v[u][e].x), abs_bits(v[u][e].y)),
+                               max(abs_bits(v[u][e].z), abs_bits(v[u][e].w))));
 #pragma unroll
-            for (int off = G / 2; off >= 1; off >>= 1) {
-                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-                bad |= __shfl_xor_sync(0xffffffffu, bad, off);
-            }
+            for (int off = G / 2; off >= 1; off >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, off));
             if (!valid[u]) continue;
             uint32_t packed[V];
 #pragma unroll
             for (int e = 0; e < V; e++) packed[e] = 0;
             float scale = 0.0f;
-            if (!bad && amax >= 0x1p-121f) {
+            if (block_scaled(m)) {
+                const float amax = __uint_as_float(m);
                 scale = div_r<RM>(amax, 127.0f);
                 const float id = div_r<RM>(127.0f, amax);
 #pragma unroll
@@ -120,13 +131,19 @@ __device__ __forceinline__ void quantize_narrow_body(int8_t* __restrict__ q, flo
     }
 }
 
+// chunks a pass for the SiLU form: fewer than the plain form's four, for
+// registers (its batch of values is live across the sigmoid)
+#ifndef PKB_SILU_U
+#define PKB_SILU_U 2
+#endif
+
 template <int RM, int QB, int E, bool SILU>
 __global__ void __launch_bounds__(256) quantize_narrow(int8_t* __restrict__ q, float* __restrict__ d,
                                                        const float* __restrict__ x, size_t xs, uint32_t T,
                                                        uint32_t n, bool vec) {
     pdl_trigger();
     pdl_wait();
-    constexpr int U = 4;
+    constexpr int U = SILU ? PKB_SILU_U : 4;
     const uint32_t nb = n / QB;
     const uint64_t total = static_cast<uint64_t>(T) * nb;
     if (total <= 0xFFFFFFF0ull)
@@ -184,8 +201,8 @@ cudaError_t quantize_rm(int8_t* q, float* d, const float* x, size_t xs, uint32_t
     // aligned (the interface asks 4), else four inputs and 4-byte stores
     const bool q8 = reinterpret_cast<uintptr_t>(q) % 8 == 0;
     const int e = qb == 32 ? (q8 ? 8 : 4) : qb == 64 ? (q8 ? PKB_Q64_E : 4) : 0;
-    // blocks a 256-thread CTA takes a pass: 8 warps x U = 4 chunks x blocks a chunk
-    const size_t per_cta = e ? 8 * 4 * (32 / (qb / e)) : 8;
+    // blocks a 256-thread CTA takes a pass: 8 warps x U chunks x blocks a chunk
+    const size_t per_cta = e ? 8 * (SILU ? PKB_SILU_U : 4) * (32 / (qb / e)) : 8;
     size_t grid = (blocks + per_cta - 1) / per_cta;
     const size_t cap = static_cast<size_t>(num_sms) * 8;
     if (grid > cap) grid = cap;

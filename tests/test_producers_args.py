@@ -72,3 +72,10 @@ def test_no_frames_is_a_no_op():
 def test_exported():
     for name in ("pkb_layernorm_quantize_dev", "pkb_silu_quantize_dev", "pkb_dwconv_quantize_dev"):
         assert isinstance(getattr(P.lib(), name), ctypes._CFuncPtr)
+
+
+@pytest.mark.parametrize("args", [(4, 0x3F800000, 0x40000000), (0, 0x3F000000, 0x40000000),
+                                  (0, 0x3F800000, 0x7F800001), (0, 0x40000000, 0x40000000)])
+def test_rcp_selftest_refuses(args):
+    m, f = ctypes.c_uint64(), ctypes.c_uint32()
+    assert P.lib().pkb_rcp_selftest(*args, ctypes.byref(m), ctypes.byref(f)) == EINVAL
