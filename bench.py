@@ -395,6 +395,74 @@ def kernel_roofline(model, prods, sm_mhz: float | None) -> dict:
             "epilogue_fp32": epi, "quantize": quant}
 
 
+def producers_roofline(model, T: int) -> dict:
+    """The fused producers of the product's inputs (the reference's normq,
+    siluq_tile and glu_item + dw_item, core/encoder.c:112-183) at this rank's
+    frame count, each timed alone with CUDA events on its stream, its inputs
+    rotated over buffers that together exceed the 126 MB L2: achieved bytes
+    (the input read once, q and d written, the small per-column operands)
+    over the measured HBM copy rate."""
+    torch, P = model.torch, model.P
+    s = torch.cuda.current_stream()
+    try:
+        hbm = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"])
+        src = "of measured: hbm_gbs of MEASURED_PEAKS.json"
+    except (OSError, KeyError, ValueError):
+        hbm, src = 6650.0, "of fallback: 6.65 TB/s"
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED + 99)
+    K = 9  # the FastConformer's depthwise kernel
+
+    def timed(fn, nbuf: int) -> float:
+        for i in range(3):
+            fn(i % nbuf)
+        s.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 12 * nbuf
+        e0.record(s)
+        for i in range(reps):
+            fn(i % nbuf)
+        e1.record(s)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    out = {}
+    q = torch.empty(T * F, dtype=torch.int8, device="cuda")
+    d = torch.empty(T * F // QB, dtype=torch.float32, device="cuda")
+    # LayerNorm -> quantize: 47 MB an input at T = 11521, three of them
+    xs = [torch.randn(T * D, device="cuda", generator=g) for _ in range(3)]
+    w, b = torch.randn(D, device="cuda", generator=g), torch.randn(D, device="cuda", generator=g)
+    ms = timed(lambda i: P.layernorm_quantize_dev(q, d, xs[i], D, T, D, QB, w, b, 1e-5), 3)
+    byt = T * D * (4 + 1 + 4.0 / QB) + 2 * D * 4
+    out["layernorm_quantize"] = {"us": ms * 1e3, "gbs": byt / (ms * 1e-3) / 1e9, "frac": byt / (ms * 1e-3) / 1e9 / hbm,
+                                 "bytes_per_launch": byt, "shape": f"T {T} x n {D}, qb {QB}",
+                                 "launches_per_step": 4 * LAYERS}
+    del xs
+    # SiLU -> quantize: the FF-up output, 189 MB
+    u = torch.randn(T * F, device="cuda", generator=g) * 4
+    ms = timed(lambda i: P.silu_quantize_dev(q, d, u, F, T, F, QB), 1)
+    byt = T * F * (4 + 1 + 4.0 / QB)
+    out["silu_quantize"] = {"us": ms * 1e3, "gbs": byt / (ms * 1e-3) / 1e9, "frac": byt / (ms * 1e-3) / 1e9 / hbm,
+                            "bytes_per_launch": byt, "shape": f"T {T} x n {F}, qb {QB}",
+                            "launches_per_step": 2 * LAYERS}
+    del u
+    # GLU + depthwise conv -> quantize from pw1's output: 94 MB, two of them
+    xg = [torch.randn(T * 2 * D, device="cuda", generator=g) for _ in range(2)]
+    wd, bd = torch.randn(D * K, device="cuda", generator=g) * 0.3, torch.randn(D, device="cuda", generator=g)
+    ms = timed(lambda i: P.dwconv_quantize_dev(q, d, None, D, xg[i], 2 * D, T, D, wd, bd, K, True, QB), 2)
+    byt = T * D * (8 + 1 + 4.0 / QB) + D * (K + 1) * 4
+    out["glu_dwconv_quantize"] = {"us": ms * 1e3, "gbs": byt / (ms * 1e-3) / 1e9,
+                                  "frac": byt / (ms * 1e-3) / 1e9 / hbm, "bytes_per_launch": byt,
+                                  "shape": f"T {T} x C {D}, K {K}, qb {QB}", "launches_per_step": LAYERS}
+    del xg
+    out["bound"] = "hbm"
+    out["peak_gbs"] = hbm
+    out["peak_note"] = src
+    out["note"] = ("bytes: the input read once, q and d written, w/b or taps; inputs rotated over buffers "
+                   "larger than L2; each producer bit-exact to the reference's float step + quantize")
+    return out
+
+
 def e2e_host(prods, steps: int, seed: int, lanes: int) -> dict:
     """The same step through the reference-facing table (pk_kernels_cuda_b200:
     quantize and gemm_q8 on HOST buffers, copies inside each call), called
@@ -557,6 +625,8 @@ def run_ours(args) -> None:
     used_graph = graph is not None
     del graph  # released before the process group goes (it holds no collective, but keep the order safe)
     roof = kernel_roofline(model, prods, clk.get("sm_mhz")) if rank == 0 else None
+    if roof is not None and not args.no_producers:
+        roof["producers"] = producers_roofline(model, sum(sg[3] for sg in segs))
     e2e = None
     if not args.no_e2e:
         # every rank at once through the host table, each on its own
@@ -675,6 +745,7 @@ def main() -> None:
     ap.add_argument("--e2e-lanes", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-producers", action="store_true", help="skip timing the fused producers (rank 0)")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
                     help="strong: the one batch of 64 segments split across the GPUs (configs[3]); "
