@@ -735,6 +735,31 @@ def run_kernel_only() -> None:
                       "device_errors": P.device_errors(0)}))
 
 
+def run_producers_only() -> None:
+    """The three fused producers at the batch's frame count, two launches
+    each in the order LayerNorm, SiLU, GLU + dwconv (the ncu capture's case:
+    inputs 47, 189 and 94 MB)."""
+    import torch
+    import libpktito_b200 as P
+    T = sum(s[3] for s in segments(0))
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(SEED)
+    q = torch.empty(T * F, dtype=torch.int8, device=dev)
+    d = torch.empty(T * F // QB, device=dev)
+    x = torch.randn(T * D, device=dev, generator=g)
+    w, b = torch.randn(D, device=dev, generator=g), torch.randn(D, device=dev, generator=g)
+    u = torch.randn(T * F, device=dev, generator=g) * 4
+    xg = torch.randn(T * 2 * D, device=dev, generator=g)
+    wd, bd = torch.randn(D * 9, device=dev, generator=g) * 0.3, torch.randn(D, device=dev, generator=g)
+    for _ in range(2):
+        P.layernorm_quantize_dev(q, d, x, D, T, D, QB, w, b, 1e-5)
+        P.silu_quantize_dev(q, d, u, F, T, F, QB)
+        P.dwconv_quantize_dev(q, d, None, D, xg, 2 * D, T, D, wd, bd, 9, True, QB)
+    torch.cuda.synchronize()
+    print(json.dumps({"producers_only": f"T {T}: layernorm n {D}, silu n {F}, glu+dwconv C {D} K 9, qb {QB}",
+                      "launches": P.launch_count(), "device_errors": P.device_errors(0)}))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -752,9 +777,13 @@ def main() -> None:
                          "weak: 64 segments per GPU")
     ap.add_argument("--kernel-only", action="store_true",
                     help="only the dominant product (FF up at the batch's M), 3 launches: the ncu capture's case")
+    ap.add_argument("--producers-only", action="store_true",
+                    help="only the fused producers at the batch's frame count, 2 launches each: the ncu capture's case")
     args = ap.parse_args()
     if args.kernel_only:
         run_kernel_only()
+    elif args.producers_only:
+        run_producers_only()
     elif args.impl == "reference":
         run_reference(args)
     else:

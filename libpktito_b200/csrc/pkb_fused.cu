@@ -48,7 +48,9 @@ __host__ __device__ constexpr uint32_t ln_padded(uint32_t n) { return n + 4 * (n
 // of a warp sit 16 banks apart
 __host__ __device__ constexpr uint32_t ln_pitch(uint32_t n) { return (ln_padded(n) + 31) / 32 * 32 + 16; }
 
-constexpr uint32_t LN_REG = 64;  // inputs a lane keeps in registers between the sums (n <= 1024)
+// NC: n / 16 where n is 1024 (the FastConformer's d_model), compiled with
+// the row's sums in registers; 0 for any other n, summed from shared memory
+constexpr uint32_t LN_NC = 64;
 
 // Block k of ROWS staged rows (the second pitch floats after the first, for
 // frames t0 and t0 + 1; the second only if live1): (x - mean) * r * w + b,
@@ -122,7 +124,7 @@ __device__ __forceinline__ void ln_block(int8_t* __restrict__ q, float* __restri
 // so that a block's maximum and its two divisions stay in one thread, the
 // arithmetic on pairs of inputs (f32x2, each half rounded as the scalar
 // operation), the bytes stored 16 at a time where q allows.
-template <int RM, int QB>
+template <int RM, int QB, uint32_t NC>
 __global__ void __launch_bounds__(256) layernorm_quantize(int8_t* __restrict__ q, float* __restrict__ d,
                                                           const float* __restrict__ x, size_t xs, uint32_t T,
                                                           uint32_t n, const float* __restrict__ w,
@@ -171,23 +173,22 @@ __global__ void __launch_bounds__(256) layernorm_quantize(int8_t* __restrict__ q
 
         // mean = sum / n; var = sum((x - mean)^2) / n; r = 1 / sqrt(var + eps)
         float acc = 0.0f, mean, var;
-        if (n <= 16 * LN_REG) {
-            // the lane's inputs held in registers between the two sums
-            float xv[LN_REG];
+        if (NC > 0) {
+            // n = 16 NC, known at compile time: the lane's NC inputs held in
+            // registers between the two sums
+            float xv[NC > 0 ? NC : 1];
 #pragma unroll
-            for (uint32_t k = 0; k < LN_REG; k++)
-                if (16 * k < n) {
-                    xv[k] = row[ln_at(16 * k + j)];
-                    acc = add_r<RM>(acc, xv[k]);
-                }
+            for (uint32_t k = 0; k < NC; k++) {
+                xv[k] = row[ln_at(16 * k + j)];
+                acc = add_r<RM>(acc, xv[k]);
+            }
             mean = div_r<RM>(fold16<RM>(acc), fn);
             acc = 0.0f;
 #pragma unroll
-            for (uint32_t k = 0; k < LN_REG; k++)
-                if (16 * k < n) {
-                    const float c = sub_r<RM>(xv[k], mean);
-                    acc = add_r<RM>(acc, mul_r<RM>(c, c));
-                }
+            for (uint32_t k = 0; k < NC; k++) {
+                const float c = sub_r<RM>(xv[k], mean);
+                acc = add_r<RM>(acc, mul_r<RM>(c, c));
+            }
         } else {
 #pragma unroll 8
             for (uint32_t i = j; i < n; i += 16) acc = add_r<RM>(acc, row[ln_at(i)]);
@@ -332,12 +333,20 @@ __global__ void __launch_bounds__(DW_THREADS) dwconv_quantize(int8_t* __restrict
         const uint32_t j1 = jend < K ? static_cast<uint32_t>(jend) : K;
         uint64_t acc = pack2(0.0f, 0.0f);
         if constexpr (KC > 0) {
+            if (j0 == 0 && j1 == KC) {  // an interior frame: every tap (warp-uniform)
 #pragma unroll
-            for (uint32_t jt = 0; jt < KC; jt++)
-                if (jt >= j0 && jt < j1) {
+                for (uint32_t jt = 0; jt < KC; jt++) {
                     const float2 xv = *reinterpret_cast<const float2*>(tile + (f + jt) * DW_CH + cl);
                     acc = fma2_r<RM>(pack2(wr[jt].x, wr[jt].y), pack2(xv.x, xv.y), acc);
                 }
+            } else {
+#pragma unroll
+                for (uint32_t jt = 0; jt < KC; jt++)
+                    if (jt >= j0 && jt < j1) {
+                        const float2 xv = *reinterpret_cast<const float2*>(tile + (f + jt) * DW_CH + cl);
+                        acc = fma2_r<RM>(pack2(wr[jt].x, wr[jt].y), pack2(xv.x, xv.y), acc);
+                    }
+            }
         } else {
             for (uint32_t jt = j0; jt < j1; jt++) {
                 const float2 xv = *reinterpret_cast<const float2*>(tile + (f + jt) * DW_CH + cl);
@@ -392,7 +401,7 @@ cudaError_t ln_launch(int8_t* q, float* d, const float* x, size_t xs, uint32_t T
     if (warps < 1) warps = 1;
     const size_t smem = wb + warps * per_warp;
     if (smem > LN_SMEM_MAX) return cudaErrorInvalidValue;  // n beyond the checked maximum
-    auto kern = layernorm_quantize<RM, QB>;
+    auto kern = n == 16 * LN_NC ? layernorm_quantize<RM, QB, LN_NC> : layernorm_quantize<RM, QB, 0>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     const size_t pairs = (static_cast<size_t>(T) + 1) / 2;

@@ -164,11 +164,13 @@ __device__ __forceinline__ void rcp_batch(const float (&den)[N], float (&rec)[N]
         for (int i = 0; i < N; i++) rec[i] = rcp_r<RM>(den[i]);
         return;
     }
+    // every value below 2^126: every reciprocal normal, so the approximation
+    // may flush subnormals (.ftz: none arise), which spares its scaling
 #pragma unroll
     for (int i = 0; i < N; i += 2) {
         float xa, xb;
-        asm("rcp.approx.f32 %0, %1;" : "=f"(xa) : "f"(den[i]));
-        asm("rcp.approx.f32 %0, %1;" : "=f"(xb) : "f"(den[i + 1]));
+        asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(xa) : "f"(den[i]));
+        asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(xb) : "f"(den[i + 1]));
         const uint64_t nd = pack2(-den[i], -den[i + 1]), one = pack2(1.0f, 1.0f);
         uint64_t r = pack2(xa, xb);
 #pragma unroll
