@@ -67,18 +67,27 @@ constexpr int KSTEP = 32;         // K of one kind::i8 MMA
 constexpr int NSTAGE = 4;         // shared-memory pipeline depth (16 blocks of 32 ahead)
 constexpr int NTMEM = 4;          // block accumulators in TMEM
 constexpr int TMEM_COLS = NTMEM * BN;  // 512
-constexpr int EPI_WARPS = 16;
-constexpr int TMA_WARP = 16;
-constexpr int MMA_WARP = 17;      // allocates TMEM; its lane 0 issues the even blocks' MMAs
-constexpr int MMA_WARP2 = 18;     // lane 0 issues the odd blocks' MMAs (the staged paths)
-constexpr int THREADS = 19 * 32;
+#ifndef PKB_EPI_COLS
+#define PKB_EPI_COLS 32
+#endif
+constexpr int EPI_COLS = PKB_EPI_COLS;   // output rows a thread of the epilogue holds (32 or 64)
+constexpr int EPI_HALVES = EPI_COLS / 32;  // its groups of 32: TMEM loads a block, staging boxes a tile
+constexpr int EPI_WARPS = 4 * (BN / EPI_COLS);  // a warp per lane quarter and column group
+constexpr int TMA_WARP = EPI_WARPS;
+constexpr int MMA_WARP = EPI_WARPS + 1;   // allocates TMEM; its lane 0 issues the even blocks' MMAs
+constexpr int MMA_WARP2 = EPI_WARPS + 2;  // lane 0 issues the odd blocks' MMAs (the staged paths)
+constexpr int THREADS = (EPI_WARPS + 3) * 32;
+static_assert(EPI_COLS == 32 || EPI_COLS == 64, "a thread's output rows");
 constexpr int A_BYTES = BM * BK;
 constexpr int B_BYTES = BN * BK;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int EPI_PITCH = 33;      // floats a row of an epilogue warp's transpose tile (plain stores)
-constexpr int EPI_BYTES = EPI_WARPS * 32 * EPI_PITCH * 4;
-constexpr int STG_BYTES = 32 * 32 * 4;  // an epilogue warp's 128-byte-swizzled staging box (TMA stores)
-static_assert(EPI_WARPS * STG_BYTES <= EPI_BYTES, "staging boxes share the transpose area");
+constexpr int STG_BYTES = 32 * 32 * 4;  // a 128-byte-swizzled staging box of 32 x 32 results (TMA stores)
+// the epilogue's area: each warp's transpose tile (plain stores, a group of
+// 32 at a time) or its EPI_HALVES staging boxes (TMA stores)
+constexpr int EPI_BYTES = EPI_WARPS * 32 * EPI_PITCH * 4 > EPI_WARPS * EPI_HALVES * STG_BYTES
+                              ? EPI_WARPS * 32 * EPI_PITCH * 4
+                              : EPI_WARPS * EPI_HALVES * STG_BYTES;
 constexpr int CHUNK = 4;           // blocks a turn of the TMEM ring
 constexpr int DBLK = 8;            // blocks of scales a TMA box of d carries (32 bytes a frame)
 constexpr int NDS = 4;             // slots of the scales ring (24 blocks ahead)
@@ -104,14 +113,15 @@ constexpr uint16_t SEED_A = 0x44C0;  // bf16 1536
 constexpr uint16_t SEED_B = 0x4400;  // bf16 512
 static_assert(1536.0 * 512.0 * SEED_K == 12582912.0, "start value");
 
-// The 32 running sums of a thread (its frame x the warp's 32 output rows),
-// two rows a 64-bit register, for the f32x2 instructions.
-using Acc = uint64_t[16];
+// The EPI_COLS running sums of a thread (its frame x the warp's output
+// rows), two rows a 64-bit register, for the f32x2 instructions.
+using Acc = uint64_t[EPI_COLS / 2];
 
-// acc[i] = fma(float(s), d, acc[i]) for the 32 block sums of the warp's
-// columns, two an instruction, each rounded once in the mode RM.
+// acc[16 h + i] = fma(float(s), d, acc[16 h + i]) for the 32 block sums of
+// the warp's column group h, two an instruction, each rounded once in the
+// mode RM.
 template <int RM, bool EXACT_SUM>
-__device__ __forceinline__ void chain32(Acc& acc, const uint32_t (&s)[32], float dv) {
+__device__ __forceinline__ void chain32(Acc& acc, const uint32_t (&s)[32], float dv, int h) {
     const uint64_t d2 = pack2(dv, dv);
     const uint64_t bias2 = pack2(-SUM_BIAS_F, -SUM_BIAS_F);
 #pragma unroll
@@ -123,7 +133,7 @@ __device__ __forceinline__ void chain32(Acc& acc, const uint32_t (&s)[32], float
             f = add2_rn(pack2(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), bias2);
         else
             f = pack2(i2f_r<RM>(static_cast<int>(s[2 * i])), i2f_r<RM>(static_cast<int>(s[2 * i + 1])));
-        acc[i] = fma2_r<RM>(f, d2, acc[i]);
+        acc[16 * h + i] = fma2_r<RM>(f, d2, acc[16 * h + i]);
     }
 }
 
@@ -157,14 +167,20 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
 // the chain.
 template <int RM, bool EXACT_SUM>
 __device__ __forceinline__ void epi_block(Acc& acc, uint32_t ta, float dv, uint64_t* tempty) {
-    uint32_t sv[32];
-    tmem_ld_32x32b_x32(ta, sv);  // one load of the 32 columns (two of 16 cost 2 % more)
-    tmem_ld_wait(sv);
+    uint32_t sv[EPI_HALVES][32];
+    // one load of each 32 columns (two of 16 cost 2 % more), all in flight
+    // before the one wait
+#pragma unroll
+    for (int h = 0; h < EPI_HALVES; h++) tmem_ld_32x32b_x32(ta + 32 * h, sv[h]);
+    tmem_ld_wait(sv[0]);
+#pragma unroll
+    for (int h = 1; h < EPI_HALVES; h++) tmem_ld_settled(sv[h]);
     // every thread orders its own loads before its own arrival (the slot's
     // barrier counts all the epilogue's threads): no warp-wide step between
     tc_fence_before();
     mbar_arrive(tempty);
-    chain32<RM, EXACT_SUM>(acc, sv, dv);
+#pragma unroll
+    for (int h = 0; h < EPI_HALVES; h++) chain32<RM, EXACT_SUM>(acc, sv[h], dv, h);
 }
 
 // SPB: K steps a block (1, 2 or 4, with n a multiple of BK: every stage
@@ -454,9 +470,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         // epilogue: frame t of the tile is this thread's TMEM lane
         const uint32_t quarter = warp & 3, cgroup = warp >> 2;
         const uint32_t lane_base = 32 * quarter;
-        const uint32_t tl = tbase + (lane_base << 16) + 32 * cgroup;
+        const uint32_t tl = tbase + (lane_base << 16) + EPI_COLS * cgroup;
         float* tw = epi + warp * (32 * EPI_PITCH);  // this warp's 32 x 32 transpose tile
-        uint8_t* stg = reinterpret_cast<uint8_t*>(epi) + warp * STG_BYTES;  // its staging box (1024-aligned)
+        // its staging boxes, one a group of 32 output rows (1024-aligned)
+        uint8_t* stg = reinterpret_cast<uint8_t*>(epi) + warp * EPI_HALVES * STG_BYTES;
         uint32_t gb = 0;            // blocks consumed (all tiles)
         uint32_t dcnt = 0, wcnt = 0;  // scale chunks, row-scale slots consumed
         uint32_t ocnt = 0;          // loads of results to add to
@@ -470,19 +487,25 @@ __global__ void __launch_bounds__(THREADS, 1)
 
             Acc acc;
 #pragma unroll
-            for (int j = 0; j < 16; j++) acc[j] = 0;  // +0, +0
+            for (int j = 0; j < EPI_COLS / 2; j++) acc[j] = 0;  // +0, +0
 
-            // the warp's box of the results: 32 output rows from col0 by 32
-            // frames from frame0
-            const uint32_t col0 = n0 + 32 * cgroup, frame0 = m0 + lane_base;
+            // the warp's boxes of the results: group h is 32 output rows from
+            // col0 + 32 h by 32 frames from frame0; a group past the last row
+            // is not stored (the groups that are live come first)
+            const uint32_t col0 = n0 + EPI_COLS * cgroup, frame0 = m0 + lane_base;
             const bool live = col0 < g.rows && frame0 < g.T;
+            uint32_t nlive = 0;
+#pragma unroll
+            for (int h = 0; h < EPI_HALVES; h++) nlive += (live && col0 + 32 * h < g.rows) ? 1u : 0u;
             if constexpr (TIO) {
                 if (g.add && live && lane == 0) {
-                    // the results added to, into the staging box once the
-                    // previous tile's store has read it
+                    // the results added to, into the staging boxes once the
+                    // previous tile's stores have read them
                     bulk_wait_read();
-                    mbar_arrive_expect_tx(&obar[warp], STG_BYTES);
-                    tma_load_2d(&map_o, stg, &obar[warp], static_cast<int>(col0), static_cast<int>(frame0));
+                    mbar_arrive_expect_tx(&obar[warp], nlive * STG_BYTES);
+                    for (uint32_t h = 0; h < nlive; h++)
+                        tma_load_2d(&map_o, stg + h * STG_BYTES, &obar[warp], static_cast<int>(col0 + 32 * h),
+                                    static_cast<int>(frame0));
                 }
             }
 
@@ -554,9 +577,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                     ok = false;
                     break;
                 }
-                const float* wsv = wsring + wsl * (WS_BYTES / 4) + 32 * cgroup;
-                const float ws_l = col0 + lane < g.rows ? wsv[lane] : 0.0f;
-                const float b_l = (g.bias && col0 + lane < g.rows) ? wsv[BN + lane] : 0.0f;
+                const float* wsv = wsring + wsl * (WS_BYTES / 4) + EPI_COLS * cgroup;
+                float ws_l[EPI_HALVES], b_l[EPI_HALVES];
+#pragma unroll
+                for (int h = 0; h < EPI_HALVES; h++) {
+                    const bool in = col0 + 32 * h + lane < g.rows;
+                    ws_l[h] = in ? wsv[32 * h + lane] : 0.0f;
+                    b_l[h] = (g.bias && in) ? wsv[BN + 32 * h + lane] : 0.0f;
+                }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&wsempty[wsl]);
                 wcnt++;
@@ -571,68 +599,78 @@ __global__ void __launch_bounds__(THREADS, 1)
                         if (lane == 0) bulk_wait_read();
                         __syncwarp();
                     }
-                    uint8_t* row = stg + lane * 128;
 #pragma unroll
-                    for (int k = 0; k < 8; k++) {
-                        float4* c4 = reinterpret_cast<float4*>(row + ((k ^ (lane & 7)) << 4));
-                        float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                        if (g.add) {
-                            const float4 ov = *c4;
-                            o[0] = ov.x;
-                            o[1] = ov.y;
-                            o[2] = ov.z;
-                            o[3] = ov.w;
-                        }
-                        float v[4];
+                    for (int h = 0; h < EPI_HALVES; h++) {
+                        if (h >= static_cast<int>(nlive)) break;  // warp-uniform
+                        uint8_t* row = stg + h * STG_BYTES + lane * 128;
 #pragma unroll
-                        for (int e = 0; e < 4; e++) {
-                            const int j = 4 * k + e;
-                            v[e] = mul_r<RM>(acc_at(acc, j), __shfl_sync(0xffffffffu, ws_l, j));
-                            if (g.bias) v[e] = add_r<RM>(v[e], __shfl_sync(0xffffffffu, b_l, j));
-                            if (g.add) v[e] = add_r<RM>(o[e], v[e]);
+                        for (int k = 0; k < 8; k++) {
+                            float4* c4 = reinterpret_cast<float4*>(row + ((k ^ (lane & 7)) << 4));
+                            float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                            if (g.add) {
+                                const float4 ov = *c4;
+                                o[0] = ov.x;
+                                o[1] = ov.y;
+                                o[2] = ov.z;
+                                o[3] = ov.w;
+                            }
+                            float v[4];
+#pragma unroll
+                            for (int e = 0; e < 4; e++) {
+                                const int j = 4 * k + e;
+                                v[e] = mul_r<RM>(acc_at(acc, 32 * h + j), __shfl_sync(0xffffffffu, ws_l[h], j));
+                                if (g.bias) v[e] = add_r<RM>(v[e], __shfl_sync(0xffffffffu, b_l[h], j));
+                                if (g.add) v[e] = add_r<RM>(o[e], v[e]);
+                            }
+                            *c4 = make_float4(v[0], v[1], v[2], v[3]);
                         }
-                        *c4 = make_float4(v[0], v[1], v[2], v[3]);
                     }
                     fence_async_smem();
                     __syncwarp();
                     if (lane == 0) {
-                        tma_store_2d(&map_o, stg, static_cast<int>(col0), static_cast<int>(frame0));
+                        for (uint32_t h = 0; h < nlive; h++)
+                            tma_store_2d(&map_o, stg + h * STG_BYTES, static_cast<int>(col0 + 32 * h),
+                                         static_cast<int>(frame0));
                         bulk_commit();
                     }
                 }
             } else {
-                // through shared memory, so that a lane owns one output row (a
-                // column of the tile) and each store is 32 consecutive floats
+                // through shared memory, a group of 32 output rows at a time, so
+                // that a lane owns one output row (a column of the tile) and
+                // each store is 32 consecutive floats
 #pragma unroll
-                for (int j = 0; j < 32; j++) tw[lane * EPI_PITCH + j] = acc_at(acc, j);
-                __syncwarp();
-                const uint32_t col = n0 + 32 * cgroup + lane;
-                const bool cvalid = col < g.rows;
-                const float wsv = cvalid ? __ldg(g.ws + col) : 0.0f;
-                const float bv = (g.bias && cvalid) ? __ldg(g.bias + col) : 0.0f;
-                const uint32_t tr0 = m0 + lane_base;
+                for (int h = 0; h < EPI_HALVES; h++) {
 #pragma unroll
-                for (int i0 = 0; i0 < 32; i0 += 8) {
-                    float old[8];
-                    if (g.add) {
+                    for (int j = 0; j < 32; j++) tw[lane * EPI_PITCH + j] = acc_at(acc, 32 * h + j);
+                    __syncwarp();
+                    const uint32_t col = col0 + 32 * h + lane;
+                    const bool cvalid = col < g.rows;
+                    const float wsv = cvalid ? __ldg(g.ws + col) : 0.0f;
+                    const float bv = (g.bias && cvalid) ? __ldg(g.bias + col) : 0.0f;
+                    const uint32_t tr0 = m0 + lane_base;
+#pragma unroll
+                    for (int i0 = 0; i0 < 32; i0 += 8) {
+                        float old[8];
+                        if (g.add) {
+#pragma unroll
+                            for (int i = 0; i < 8; i++) {
+                                const uint32_t tt = tr0 + i0 + i;
+                                old[i] = (cvalid && tt < g.T) ? g.out[static_cast<size_t>(tt) * g.os + col] : 0.0f;
+                            }
+                        }
 #pragma unroll
                         for (int i = 0; i < 8; i++) {
                             const uint32_t tt = tr0 + i0 + i;
-                            old[i] = (cvalid && tt < g.T) ? g.out[static_cast<size_t>(tt) * g.os + col] : 0.0f;
+                            if (cvalid && tt < g.T) {
+                                float v = mul_r<RM>(tw[(i0 + i) * EPI_PITCH + lane], wsv);
+                                if (g.bias) v = add_r<RM>(v, bv);
+                                if (g.add) v = add_r<RM>(old[i], v);
+                                g.out[static_cast<size_t>(tt) * g.os + col] = v;
+                            }
                         }
                     }
-#pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        const uint32_t tt = tr0 + i0 + i;
-                        if (cvalid && tt < g.T) {
-                            float v = mul_r<RM>(tw[(i0 + i) * EPI_PITCH + lane], wsv);
-                            if (g.bias) v = add_r<RM>(v, bv);
-                            if (g.add) v = add_r<RM>(old[i], v);
-                            g.out[static_cast<size_t>(tt) * g.os + col] = v;
-                        }
-                    }
+                    __syncwarp();
                 }
-                __syncwarp();
             }
         }
         if (!ok) {

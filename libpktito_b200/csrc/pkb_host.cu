@@ -12,6 +12,12 @@
 // over a pool of worker threads (one thread's memcpy reaches about a fifth of
 // what a B200 host's memory and PCIe can move).
 //
+// Where the caller's activations and results are page-locked (cudaMallocHost
+// or cudaHostRegister: an engine whose buffers live as long as it does can
+// pin them once), a call skips the host copies: each chunk is copied by DMA
+// straight from and into the caller's memory, and the call's only host-side
+// wait is the last.
+//
 // Calls arrive synchronously from any number of the caller's threads at once
 // (the reference's pool calls a backend from every worker, core/pool.c:
 // 115-122, on disjoint outputs): each calling thread has its own streams and
@@ -311,6 +317,22 @@ struct Pipe {
 thread_local int tl_device = 0;
 thread_local Pipe tl_pipe;
 
+// Whether [p, p + bytes) is page-locked host memory (both of its ends: a
+// range that is not wholly so is still copied correctly, only not at DMA
+// speed).
+bool pinned(const void* p, size_t bytes) {
+    if (!p || !bytes) return false;
+    for (const void* q : {p, static_cast<const void*>(static_cast<const char*>(p) + bytes - 1)}) {
+        cudaPointerAttributes a;
+        if (cudaPointerGetAttributes(&a, q) != cudaSuccess) {
+            cudaGetLastError();  // clears the error it may leave
+            return false;
+        }
+        if (a.type != cudaMemoryTypeHost) return false;
+    }
+    return true;
+}
+
 // A chunk's frames: its input and output bytes per frame kept near these
 // sizes, in whole tiles of 128 frames where the call has that many.
 constexpr size_t CHUNK_IN = 16u << 20, CHUNK_OUT = 32u << 20;
@@ -448,6 +470,33 @@ int pkb_quantize_host(int8_t* q, float* d, uint32_t n, uint32_t qb, uint32_t T, 
     CopyPool& pool = CopyPool::get();
     const uint32_t nchunks = (T + TC - 1) / TC;
     auto frames = [&](uint32_t c) { return std::min(TC, T - c * TC); };
+    if (pinned(x, ((T - 1) * xs + n) * 4) && pinned(q, T * qrow) && pinned(d, T * drow)) {
+        // page-locked: every chunk by DMA straight from x and into q and d
+        for (uint32_t c = 0; c < nchunks; c++) {
+            const int s = c & 1;
+            const uint32_t tc = frames(c);
+            const size_t t0 = static_cast<size_t>(c) * TC;
+            if (c >= 2) HOST_CUDA(cudaStreamWaitEvent(p->s_in, p->ev_comp[s], 0), "cudaStreamWaitEvent");
+            HOST_CUDA(cudaMemcpy2DAsync(p->dev_in[s], xrow, x + t0 * xs, xs * 4, xrow, tc, cudaMemcpyHostToDevice,
+                                        p->s_in),
+                      "upload");
+            HOST_CUDA(cudaEventRecord(p->ev_in[s], p->s_in), "cudaEventRecord");
+            HOST_CUDA(cudaStreamWaitEvent(p->s_comp, p->ev_in[s], 0), "cudaStreamWaitEvent");
+            if (c >= 2) HOST_CUDA(cudaStreamWaitEvent(p->s_comp, p->ev_out[s], 0), "cudaStreamWaitEvent");
+            if ((rc = pkb_quantize_dev(p->s_comp, reinterpret_cast<int8_t*>(p->dev_out[s]),
+                                       reinterpret_cast<float*>(p->dev_out[s] + off_d),
+                                       reinterpret_cast<const float*>(p->dev_in[s]), n, tc, n, qb, rmode)))
+                return rc;
+            HOST_CUDA(cudaEventRecord(p->ev_comp[s], p->s_comp), "cudaEventRecord");
+            HOST_CUDA(cudaStreamWaitEvent(p->s_out, p->ev_comp[s], 0), "cudaStreamWaitEvent");
+            HOST_CUDA(cudaMemcpyAsync(q + t0 * qrow, p->dev_out[s], tc * qrow, cudaMemcpyDeviceToHost, p->s_out),
+                      "download");
+            HOST_CUDA(cudaMemcpyAsync(d + t0 * nb, p->dev_out[s] + off_d, tc * drow, cudaMemcpyDeviceToHost, p->s_out),
+                      "download");
+            HOST_CUDA(cudaEventRecord(p->ev_out[s], p->s_out), "cudaEventRecord");
+        }
+        return p->finish(err);
+    }
     auto take_out = [&](uint32_t c) -> int {  // chunk c's bytes and scales to the caller
         const int s = c & 1;
         HOST_CUDA(cudaEventSynchronize(p->ev_out[s]), "cudaEventSynchronize");
@@ -512,6 +561,41 @@ int pkb_gemm_q8_host(float* out, size_t os, const int8_t* w, const float* ws, co
     const float* dbias = bias ? reinterpret_cast<const float*>(p->dev_vec + up256(orow)) : nullptr;
     const uint32_t nchunks = (T + TC - 1) / TC;
     auto frames = [&](uint32_t c) { return std::min(TC, T - c * TC); };
+    if (pinned(q, T * qrow) && pinned(d, T * drow) && pinned(out, ((T - 1) * os + rows) * 4)) {
+        // page-locked: every chunk by DMA straight from q, d (and the rows
+        // added to) and into out at its stride
+        for (uint32_t c = 0; c < nchunks; c++) {
+            const int s = c & 1;
+            const uint32_t tc = frames(c);
+            const size_t t0 = static_cast<size_t>(c) * TC;
+            if (c >= 2) {
+                HOST_CUDA(cudaStreamWaitEvent(p->s_in, p->ev_comp[s], 0), "cudaStreamWaitEvent");
+                HOST_CUDA(cudaStreamWaitEvent(p->s_in, p->ev_out[s], 0), "cudaStreamWaitEvent");
+            }
+            HOST_CUDA(cudaMemcpyAsync(p->dev_in[s], q + t0 * qrow, tc * qrow, cudaMemcpyHostToDevice, p->s_in),
+                      "upload");
+            HOST_CUDA(cudaMemcpyAsync(p->dev_in[s] + off_d, d + t0 * nb, tc * drow, cudaMemcpyHostToDevice, p->s_in),
+                      "upload");
+            if (add)
+                HOST_CUDA(cudaMemcpy2DAsync(p->dev_out[s], orow, out + t0 * os, os * 4, orow, tc,
+                                            cudaMemcpyHostToDevice, p->s_in),
+                          "upload");
+            HOST_CUDA(cudaEventRecord(p->ev_in[s], p->s_in), "cudaEventRecord");
+            HOST_CUDA(cudaStreamWaitEvent(p->s_comp, p->ev_in[s], 0), "cudaStreamWaitEvent");
+            if (c >= 2) HOST_CUDA(cudaStreamWaitEvent(p->s_comp, p->ev_out[s], 0), "cudaStreamWaitEvent");
+            if ((rc = pkb_gemm_q8_dev(p->s_comp, reinterpret_cast<float*>(p->dev_out[s]), rows, wpack, dws, dbias,
+                                      rows, reinterpret_cast<const int8_t*>(p->dev_in[s]),
+                                      reinterpret_cast<const float*>(p->dev_in[s] + off_d), n, qb, tc, add, rmode)))
+                return rc;
+            HOST_CUDA(cudaEventRecord(p->ev_comp[s], p->s_comp), "cudaEventRecord");
+            HOST_CUDA(cudaStreamWaitEvent(p->s_out, p->ev_comp[s], 0), "cudaStreamWaitEvent");
+            HOST_CUDA(cudaMemcpy2DAsync(out + t0 * os, os * 4, p->dev_out[s], orow, orow, tc, cudaMemcpyDeviceToHost,
+                                        p->s_out),
+                      "download");
+            HOST_CUDA(cudaEventRecord(p->ev_out[s], p->s_out), "cudaEventRecord");
+        }
+        return p->finish(err);
+    }
     auto take_out = [&](uint32_t c) -> int {  // chunk c's rows of out, at the caller's stride
         const int s = c & 1;
         HOST_CUDA(cudaEventSynchronize(p->ev_out[s]), "cudaEventSynchronize");

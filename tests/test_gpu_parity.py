@@ -225,3 +225,45 @@ def test_device_path_full_layer_shapes(pkb, cuda_device, T, rows, n, qb):
     want = out0.copy()
     O.gemm_q8(want, rows, w_pk, ws, bias, rows, q, d, n, qb, T, add)
     assert same_bits(got, want), first_diff(got, want)
+
+
+# ------------------------------------------------ page-locked host buffers --
+
+def pinned_like(a: np.ndarray) -> tuple[object, np.ndarray]:
+    """a copy of a in page-locked host memory (the tensor keeps it alive)"""
+    import torch
+    t = torch.empty(a.size, dtype={np.dtype(np.float32): torch.float32, np.dtype(np.int8): torch.int8}[a.dtype],
+                    pin_memory=True)
+    v = t.numpy()
+    v[:] = a.reshape(-1)
+    return t, v
+
+
+@pytest.mark.parametrize("rmode", [O.RN, O.RU])
+def test_host_calls_on_page_locked_buffers(pkb, cuda_device, rmode):
+    """Page-locked activations and results take the direct-DMA path (no
+    host staging): several chunks, a strided output with the floats between
+    rows untouched, a product that adds to its output, with bias; the same
+    bytes as the oracle."""
+    lib = pkb.lib()
+    T, n, qb, xs, rows, os_ = 40000, 1024, 32, 1040, 256, 272
+    g = np.random.default_rng(17 + rmode)
+    x = g.standard_normal(T * xs).astype(np.float32)
+    keep_x, xp = pinned_like(x)
+    keep_q, qp = pinned_like(np.zeros(T * n, np.int8))
+    keep_d, dp = pinned_like(np.zeros(T * n // qb, np.float32))
+    assert lib.pkb_quantize_host(qp.ctypes.data, dp.ctypes.data, n, qb, T, xp.ctypes.data, xs, rmode) == 0
+    qo, do = O.quantize(x, n, qb, T=T, xs=xs, rmode=rmode)
+    assert np.array_equal(qp.reshape(T, n), qo) and same_bits(dp.reshape(T, -1), do)
+    w_rm = g.integers(-127, 128, (rows, n), dtype=np.int8)
+    w = O.pack_q8(w_rm)
+    ws = (1e-3 + 9e-3 * g.random(rows)).astype(np.float32)
+    bias = g.standard_normal(rows).astype(np.float32)
+    out0 = g.standard_normal(T * os_).astype(np.float32)
+    keep_o, op = pinned_like(out0)
+    assert lib.pkb_gemm_q8_host(op.ctypes.data, os_, w.ctypes.data, ws.ctypes.data, bias.ctypes.data, rows,
+                                qp.ctypes.data, dp.ctypes.data, n, qb, T, 1, rmode) == 0
+    want = out0.copy()
+    O.gemm_q8(want, os_, w, ws, bias, rows, qo, do, n, qb, T, True, rmode)
+    assert same_bits(op, want), first_diff(op, want)
+    pkb.forget(w)
