@@ -335,7 +335,10 @@ bool pinned(const void* p, size_t bytes) {
 
 // A chunk's frames: its input and output bytes per frame kept near these
 // sizes, in whole tiles of 128 frames where the call has that many.
-constexpr size_t CHUNK_IN = 16u << 20, CHUNK_OUT = 32u << 20;
+#ifndef PKB_CHUNK_MB
+#define PKB_CHUNK_MB 16
+#endif
+constexpr size_t CHUNK_IN = size_t(PKB_CHUNK_MB) << 20, CHUNK_OUT = size_t(2 * PKB_CHUNK_MB) << 20;
 
 uint32_t chunk_frames(uint32_t T, size_t in_per_frame, size_t out_per_frame) {
     size_t tc = CHUNK_IN / (in_per_frame ? in_per_frame : 1);
