@@ -463,6 +463,102 @@ def producers_roofline(model, T: int) -> dict:
     return out
 
 
+def decoder_batched(model, T: int, segs: int = SEGMENTS, layers: int = 2, P_: int = 640, J: int = 640,
+                    vocab_out: int = 8208) -> dict:
+    """The TDT decoder's int8 products with the batch's segments stepped in
+    lockstep (SURVEY's "next" row: its T=1 gemvs become products of M = the
+    segment count): one step is, per LSTM layer, quantize + wx (4P x P) and
+    quantize + wh (4P x P, added), then quantize + jpred (J x P, bias) and
+    quantize + jout (vocab + 1 + durations padded to 16 = 8208 x J, bias),
+    every input a whole row a block (core/decoder.c:53-79). Timed as one CUDA
+    graph of a step, with CUDA events. Beside it jenc over the batch's frames
+    (J x D, qb = D, bias: pk_joint_frames, core/decoder.c:149-156)."""
+    torch, P = model.torch, model.P
+    s = torch.cuda.current_stream()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED + 123)
+    S = segs
+
+    def matrix(rows, n):
+        w_pk = torch.randint(-127, 128, (rows * n,), dtype=torch.int8, device="cuda", generator=g)
+        wp = torch.empty_like(w_pk)
+        P.repack_q8_dev(wp, w_pk, rows, n)
+        return wp, 1e-3 + 9e-3 * torch.rand(rows, device="cuda", generator=g)
+
+    G = 4 * P_
+    mats = [(matrix(G, P_), matrix(G, P_)) for _ in range(layers)]
+    jpred, jout = matrix(J, P_), matrix(vocab_out, J)
+    jpred_b, jout_b = torch.randn(J, device="cuda", generator=g), torch.randn(vocab_out, device="cuda", generator=g)
+    x = torch.randn(S * P_, device="cuda", generator=g)
+    h = [torch.randn(S * P_, device="cuda", generator=g) for _ in range(layers)]
+    z = torch.randn(S * J, device="cuda", generator=g).clamp_(min=0)
+    gates = torch.empty(S * G, device="cuda")
+    gp = torch.empty(S * J, device="cuda")
+    logit = torch.empty(S * vocab_out, device="cuda")
+    q = torch.empty(S * max(P_, J), dtype=torch.int8, device="cuda")
+    d = torch.empty(S, device="cuda")
+
+    def prod(out, rows, wm, bias, inp, n, add):
+        P.quantize_dev(q, d, inp, n, S, n, n)
+        P.gemm_q8_dev(out, rows, wm[0], wm[1], bias, rows, q, d, n, n, S, add)
+
+    def step():
+        inp = x
+        for l in range(layers):
+            prod(gates, G, mats[l][0], None, inp, P_, False)
+            prod(gates, G, mats[l][1], None, h[l], P_, True)
+            inp = h[l]  # the cell's float update (pk_k_lstm) is off the int8 path
+        prod(gp, J, jpred, jpred_b, inp, P_, False)
+        prod(logit, vocab_out, jout, jout_b, z, J, False)
+
+    for _ in range(3):
+        step()
+    s.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    graph.replay()
+    s.synchronize()
+    reps = 50
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(reps):
+        graph.replay()
+    e1.record(s)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    ops = 2.0 * S * (layers * 2 * G * P_ + J * P_ + vocab_out * J)
+    del graph
+    # jenc over the batch's frames
+    D_ = D
+    xe = torch.randn(T * D_, device="cuda", generator=g)
+    qe = torch.empty(T * D_, dtype=torch.int8, device="cuda")
+    de = torch.empty(T, device="cuda")
+    jenc = matrix(J, D_)
+    jenc_b = torch.randn(J, device="cuda", generator=g)
+    f = torch.empty(T * J, device="cuda")
+
+    def enc():
+        P.quantize_dev(qe, de, xe, D_, T, D_, D_)
+        P.gemm_q8_dev(f, J, jenc[0], jenc[1], jenc_b, J, qe, de, D_, D_, T, False)
+
+    for _ in range(3):
+        enc()
+    s.synchronize()
+    e0.record(s)
+    for _ in range(20):
+        enc()
+    e1.record(s)
+    e1.synchronize()
+    ems = e0.elapsed_time(e1) / 20
+    eops = 2.0 * T * J * D_
+    return {"segments": S, "step_us": ms * 1e3, "step_tops": ops / (ms * 1e-3) / 1e12,
+            "steps_per_s": 1e3 / ms, "launches_per_step": 4 * (2 * layers + 2),
+            "shapes": f"per layer wx, wh {G}x{P_}; jpred {J}x{P_}; jout {vocab_out}x{J}; M = {S}, qb = n",
+            "jenc_us": ems * 1e3, "jenc_tops": eops / (ems * 1e-3) / 1e12,
+            "jenc_shape": f"M {T} x N {J} x K {D_}, qb {D_}"}
+
+
 def e2e_host(prods, steps: int, seed: int, lanes: int) -> dict:
     """The same step through the reference-facing table (pk_kernels_cuda_b200:
     quantize and gemm_q8 on HOST buffers, copies inside each call), called
@@ -640,6 +736,7 @@ def run_ours(args) -> None:
     roof = kernel_roofline(model, prods, clk.get("sm_mhz")) if rank == 0 else None
     if roof is not None and not args.no_producers:
         roof["producers"] = producers_roofline(model, sum(sg[3] for sg in segs))
+        roof["decoder_batched"] = decoder_batched(model, sum(sg[3] for sg in segs))
     e2e = None
     if not args.no_e2e:
         # every rank at once through the host table, each on its own

@@ -267,3 +267,44 @@ def test_host_calls_on_page_locked_buffers(pkb, cuda_device, rmode):
     O.gemm_q8(want, os_, w, ws, bias, rows, qo, do, n, qb, T, True, rmode)
     assert same_bits(op, want), first_diff(op, want)
     pkb.forget(w)
+
+
+# -------------------------------------------- the decoder's products, batched --
+
+# The TDT decoder's int8 products (core/decoder.c:53-79, 149-156) with T the
+# number of segments stepped in lockstep: each LSTM layer's wx and wh
+# (4P x P, the second added to the first), jpred (J x P, bias), jout
+# (vocab + 1 + durations, padded to 16, x J, bias), every input a whole row a
+# block (qb = n); and jenc (J x D, qb = D, bias) over a chunk's frames.
+DECODER = [(2560, 640, 640, 0, 0), (2560, 640, 640, 1, 0), (640, 640, 640, 0, 1), (8208, 640, 640, 0, 1),
+           (640, 1024, 1024, 0, 1)]
+
+
+@pytest.mark.parametrize("T", [1, 7, 64])
+@pytest.mark.parametrize("rows,n,qb,add,bias", DECODER)
+def test_decoder_products_batched(pkb, cuda_device, rows, n, qb, add, bias, T):
+    import torch
+    g = np.random.default_rng(rows + n + T + add)
+    x = (g.standard_normal(T * n) * 3).astype(np.float32)
+    qo, do = O.quantize(x, n, qb)
+    w_rm = g.integers(-127, 128, (rows, n), dtype=np.int8)
+    w = O.pack_q8(w_rm)
+    ws = (1e-3 + 9e-3 * g.random(rows)).astype(np.float32)
+    b = g.standard_normal(rows).astype(np.float32) if bias else None
+    out0 = g.standard_normal(T * rows).astype(np.float32)
+    want = out0.copy()
+    O.gemm_q8(want, rows, w, ws, b, rows, qo, do, n, qb, T, bool(add))
+    # on the device: quantize, repack, product, as a decode step runs them
+    xd = torch.from_numpy(x).cuda()
+    q = torch.empty(T * n, dtype=torch.int8, device="cuda")
+    d = torch.empty(T * n // qb, dtype=torch.float32, device="cuda")
+    pkb.quantize_dev(q, d, xd, n, T, n, qb)
+    wp = torch.empty(rows * n, dtype=torch.int8, device="cuda")
+    pkb.repack_q8_dev(wp, torch.from_numpy(w).cuda(), rows, n)
+    out = torch.from_numpy(out0).cuda()
+    pkb.gemm_q8_dev(out, rows, wp, torch.from_numpy(ws).cuda(), None if b is None else torch.from_numpy(b).cuda(),
+                    rows, q, d, n, qb, T, bool(add))
+    torch.cuda.synchronize()
+    assert np.array_equal(q.cpu().numpy().reshape(T, n), qo) and same_bits(d.cpu().numpy().reshape(T, -1), do)
+    got = out.cpu().numpy()
+    assert same_bits(got, want), first_diff(got, want)
