@@ -559,6 +559,50 @@ def decoder_batched(model, T: int, segs: int = SEGMENTS, layers: int = 2, P_: in
             "jenc_shape": f"M {T} x N {J} x K {D_}, qb {D_}"}
 
 
+def panels_timing(model, T: int, dk: int = 128) -> dict:
+    """The attention's K and V products straight into its panels (SURVEY's
+    second "next" row: pk_panels_tile and pk_gemm_panels_on,
+    core/passes.c:119-196) at the batch's frame count, against the same
+    product into plain rows (D x D, qb 32), each timed with CUDA events."""
+    torch, P = model.torch, model.P
+    s = torch.cuda.current_stream()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED + 321)
+    x = torch.randn(T * D, device="cuda", generator=g)
+    q = torch.empty(T * D, dtype=torch.int8, device="cuda")
+    d = torch.empty(T * D // QB, device="cuda")
+    P.quantize_dev(q, d, x, D, T, D, QB)
+    w_pk = torch.randint(-127, 128, (D * D,), dtype=torch.int8, device="cuda", generator=g)
+    wp = torch.empty_like(w_pk)
+    P.repack_q8_dev(wp, w_pk, D, D)
+    ws = 1e-3 + 9e-3 * torch.rand(D, device="cuda", generator=g)
+    tpad = (T + 15) // 16 * 16
+    plain = torch.empty(T * D, device="cuda")
+    kp = torch.empty(D * tpad, device="cuda")
+    vp = torch.empty(D * T, device="cuda")
+
+    def timed(fn) -> float:
+        for _ in range(3):
+            fn()
+        s.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(20):
+            fn()
+        e1.record(s)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / 20
+
+    ops = 2.0 * T * D * D
+    t_plain = timed(lambda: P.gemm_q8_dev(plain, D, wp, ws, None, D, q, d, D, QB, T, False))
+    t_k = timed(lambda: P.gemm_q8_panels_dev(kp, P.PANELS_KP, 0, dk, tpad, wp, ws, D, q, d, D, QB, T))
+    t_v = timed(lambda: P.gemm_q8_panels_dev(vp, P.PANELS_V, 16 * T, 0, 0, wp, ws, D, q, d, D, QB, T))
+    return {"shape": f"M {T} x N {D} x K {D}, qb {QB}; K panels dk {dk}, {tpad} frames; V panels ps 16 T",
+            "plain_us": t_plain * 1e3, "k_panels_us": t_k * 1e3, "v_panels_us": t_v * 1e3,
+            "plain_tops": ops / (t_plain * 1e-3) / 1e12, "k_panels_tops": ops / (t_k * 1e-3) / 1e12,
+            "v_panels_tops": ops / (t_v * 1e-3) / 1e12}
+
+
 def e2e_host(prods, steps: int, seed: int, lanes: int) -> dict:
     """The same step through the reference-facing table (pk_kernels_cuda_b200:
     quantize and gemm_q8 on HOST buffers, copies inside each call), called
@@ -737,6 +781,7 @@ def run_ours(args) -> None:
     if roof is not None and not args.no_producers:
         roof["producers"] = producers_roofline(model, sum(sg[3] for sg in segs))
         roof["decoder_batched"] = decoder_batched(model, sum(sg[3] for sg in segs))
+        roof["panels"] = panels_timing(model, sum(sg[3] for sg in segs))
     e2e = None
     if not args.no_e2e:
         # every rank at once through the host table, each on its own

@@ -127,6 +127,24 @@ int pkb_gemm_q8_dev(void *stream, float *out, size_t os, const int8_t *wpack, co
                     const float *bias, uint32_t rows, const int8_t *q, const float *d, uint32_t n,
                     uint32_t qb, uint32_t T, int add, int rmode);
 
+/* The product straight into the attention's panels (pk_k_gemm_f32's
+ * layout), as the reference's encoder makes them (core/passes.c:119-196),
+ * on device buffers, for an attention that stays on the GPU. No bias and
+ * nothing added, as the reference's V, K and P products.
+ *   PKB_PANELS_V:  result (frame t, row r) at panels + (r/16) ps + 16 t + r%16
+ *                  (pk_gemm_panels_on: one product a 16-row panel, os 16;
+ *                  the reference's ps is 16 T)
+ *   PKB_PANELS_KP: result (frame t, row r = h dk + d) at
+ *                  panels + h tpad dk + (t/16) 16 dk + 16 d + t%16, frames T to
+ *                  tpad - 1 written as zeros (pk_panels_tile: K with tpad the
+ *                  frames rounded up to 16, P with its positions rounded up
+ *                  to 16 plus 16); dk a multiple of 16 dividing rows. */
+#define PKB_PANELS_V 1
+#define PKB_PANELS_KP 2
+int pkb_gemm_q8_panels_dev(void *stream, float *panels, int kind, size_t ps, uint32_t dk, uint32_t tpad,
+                           const int8_t *wpack, const float *ws, uint32_t rows, const int8_t *q, const float *d,
+                           uint32_t n, uint32_t qb, uint32_t T, int rmode);
+
 /* ---------------------------------------- fused producers (device) -- */
 
 /* The producers of the product's int8 inputs in the reference's encoder,

@@ -95,6 +95,10 @@ _SIGS = {
                                                ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint32,
                                                ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32,
                                                ctypes.c_int, ctypes.c_uint32, ctypes.c_int]),
+    "pkb_gemm_q8_panels_dev": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t,
+                                              ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p,
+                                              ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32,
+                                              ctypes.c_uint32, ctypes.c_uint32, ctypes.c_int]),
     "pkb_launch_count": (ctypes.c_uint64, []),
     "pkb_quantize_host_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,
                                                  ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]),
@@ -248,6 +252,16 @@ def dwconv_quantize_dev(q, d, out, os_: int, x, xs: int, T: int, C: int, w, b, K
     """glu_item + dw_item (core/encoder.c:160-183) on device buffers; out may be None."""
     _check(lib().pkb_dwconv_quantize_dev(_stream(stream), _ptr(q), _ptr(d), _ptr(out), os_, _ptr(x), xs, T, C, _ptr(w),
                                          _ptr(b), K, int(glu), qb, rmode))
+
+
+PANELS_V, PANELS_KP = 1, 2
+
+
+def gemm_q8_panels_dev(panels, kind: int, ps: int, dk: int, tpad: int, wpack, ws, rows: int, q, d, n: int, qb: int,
+                       T: int, rmode: int = RN, stream=None) -> None:
+    """The product into the attention's V or K/P panels (core/passes.c:119-196)."""
+    _check(lib().pkb_gemm_q8_panels_dev(_stream(stream), _ptr(panels), kind, ps, dk, tpad, _ptr(wpack), _ptr(ws), rows,
+                                        _ptr(q), _ptr(d), n, qb, T, rmode))
 
 
 def repack_q8_dev(wpack, w_pk, rows: int, n: int, stream=None) -> None:

@@ -192,6 +192,10 @@ int gemm_dev(cudaStream_t stream, float* out, size_t os, const int8_t* wpack, co
     g.tiles_m = (T + gemm_tile_rows() - 1) / gemm_tile_rows();
     g.tiles_n = (rows + gemm_tile_cols() - 1) / gemm_tile_cols();
     g.timeout = wait_limit();
+    g.pmode = 0;
+    g.dk = 0;
+    g.tpad = T;
+    g.ps = 0;
     // scales, row scales, biases and results through TMA where their rows
     // are whole 16-byte units
     CUtensorMap md, mo;
@@ -293,6 +297,61 @@ int dwconv_quantize_dev(cudaStream_t stream, int8_t* q, float* d, float* out, si
     return PKB_OK;
 }
 
+// The product straight into the attention's panels (kind PKB_PANELS_V or
+// PKB_PANELS_KP): no bias, nothing added, as the reference's V, K and P
+// products; the plain-store path, its index per kind.
+int gemm_panels_dev(cudaStream_t stream, float* panels, int kind, size_t ps, uint32_t dk, uint32_t tpad,
+                    const int8_t* wpack, const float* ws, uint32_t rows, const int8_t* q, const float* d, uint32_t n,
+                    uint32_t qb, uint32_t T, int rmode) {
+    int rc = check_act_shape(n, qb);
+    if (rc) return rc;
+    if ((rc = check_rmode(rmode))) return rc;
+    if (kind != PKB_PANELS_V && kind != PKB_PANELS_KP) return fail(PKB_EINVAL, "panels: kind %d", kind);
+    if (rows % 16) return fail(PKB_EINVAL, "rows = %u: a multiple of 16", rows);
+    if (kind == PKB_PANELS_V && ps < 16 * static_cast<size_t>(T))
+        return fail(PKB_EINVAL, "V panels: panel stride %zu below 16 T = %zu", ps, 16 * static_cast<size_t>(T));
+    if (kind == PKB_PANELS_KP) {
+        if (dk == 0 || dk % 16 || rows % dk)
+            return fail(PKB_EINVAL, "K/P panels: dk = %u, a multiple of 16 dividing rows = %u", dk, rows);
+        if (tpad < T || tpad % 16)
+            return fail(PKB_EINVAL, "K/P panels: tpad = %u, a multiple of 16 from T = %u", tpad, T);
+    }
+    if (!T || !rows) return PKB_OK;
+    if (!panels || !wpack || !ws || !q || !d) return fail(PKB_EINVAL, "panels: null pointer");
+    if (!aligned(q, 16) || !aligned(wpack, 16))
+        return fail(PKB_EINVAL, "panels: activations and weights must be 16-byte aligned");
+    if (!aligned(d, 4) || !aligned(panels, 4) || !aligned(ws, 4))
+        return fail(PKB_EINVAL, "panels: misaligned float buffer");
+    Device* dev;
+    if ((rc = current_device(&dev))) return rc;
+    CUtensorMap ma, mb;
+    if ((rc = make_map(&ma, q, T, n, gemm_tile_rows(), gemm_box_k()))) return rc;
+    if ((rc = make_map(&mb, wpack, rows, n, gemm_tile_cols(), gemm_box_k()))) return rc;
+    GemmArgs g;
+    g.out = panels;
+    g.ws = ws;
+    g.bias = nullptr;
+    g.d = d;
+    g.err = dev->err;
+    g.os = rows;
+    g.rows = rows;
+    g.n = n;
+    g.qb = qb;
+    g.T = T;
+    g.add = 0;
+    g.pmode = kind == PKB_PANELS_V ? 1u : 2u;
+    g.dk = dk;
+    g.tpad = kind == PKB_PANELS_KP ? tpad : T;
+    g.ps = ps;
+    // K/P's tiles reach its padding, whose frames it writes as zeros
+    g.tiles_m = (g.tpad + gemm_tile_rows() - 1) / gemm_tile_rows();
+    g.tiles_n = (rows + gemm_tile_cols() - 1) / gemm_tile_cols();
+    g.timeout = wait_limit();
+    PKB_CUDA(launch_gemm_q8(ma, mb, nullptr, nullptr, g, dev->sms, rmode, stream), "panels launch");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return PKB_OK;
+}
+
 int repack_dev(cudaStream_t stream, int8_t* wpack, const int8_t* w_pk, uint32_t rows, uint32_t n) {
     if (rows % 16 || n % 32 || n == 0) return fail(PKB_EINVAL, "repack: rows %u (16s) by n %u (32s)", rows, n);
     if (!rows) return PKB_OK;
@@ -382,6 +441,13 @@ int pkb_dwconv_quantize_dev(void* stream, int8_t* q, float* d, float* out, size_
                             int rmode) {
     return pkb::dwconv_quantize_dev(static_cast<cudaStream_t>(stream), q, d, out, os, x, xs, T, C, w, b, K, glu, qb,
                                     rmode);
+}
+
+int pkb_gemm_q8_panels_dev(void* stream, float* panels, int kind, size_t ps, uint32_t dk, uint32_t tpad,
+                           const int8_t* wpack, const float* ws, uint32_t rows, const int8_t* q, const float* d,
+                           uint32_t n, uint32_t qb, uint32_t T, int rmode) {
+    return gemm_panels_dev(static_cast<cudaStream_t>(stream), panels, kind, ps, dk, tpad, wpack, ws, rows, q, d, n, qb,
+                           T, rmode);
 }
 
 int pkb_repack_q8_dev(void* stream, int8_t* wpack, const int8_t* w_pk, uint32_t rows, uint32_t n) {

@@ -183,6 +183,14 @@ __device__ __forceinline__ void epi_block(Acc& acc, uint32_t ta, float dv, uint6
     for (int h = 0; h < EPI_HALVES; h++) chain32<RM, EXACT_SUM>(acc, sv[h], dv, h);
 }
 
+// Where result (frame t, output row r) goes on the plain-store path: the
+// rows of out, or V's panels (pk_gemm_panels_on, core/passes.c:119-141:
+// panel r/16 at (r/16) ps, its frames 16 floats apart).
+__device__ __forceinline__ size_t out_at(const GemmArgs& g, uint32_t t, uint32_t r) {
+    if (g.pmode == 1) return static_cast<size_t>(r >> 4) * g.ps + 16 * static_cast<size_t>(t) + (r & 15);
+    return static_cast<size_t>(t) * g.os + r;
+}
+
 // SPB: K steps a block (1, 2 or 4, with n a multiple of BK: every stage
 // starts a block and holds four K steps), or 0 for any qb and n.
 // TIO (a multiple of four blocks a tile; the scales' rows, the results' rows
@@ -634,10 +642,31 @@ __global__ void __launch_bounds__(THREADS, 1)
                         bulk_commit();
                     }
                 }
+            } else if (g.pmode == 2) {
+                // K and P panels (pk_panels_tile, core/passes.c:143-196): frame
+                // t, dimension d of head h at h tpad dk + (t/16) 16 dk + 16 d +
+                // t%16, frames T .. tpad-1 zeros; from the sums as they are (a
+                // lane a frame), so 16 lanes store 64 contiguous bytes. The
+                // reference's K and P products have no bias and add nothing.
+                const uint32_t tt = frame0 + lane;
+                float ws_l[EPI_HALVES];
+#pragma unroll
+                for (int h = 0; h < EPI_HALVES; h++)
+                    ws_l[h] = col0 + 32 * h + lane < g.rows ? __ldg(g.ws + col0 + 32 * h + lane) : 0.0f;
+#pragma unroll
+                for (int j = 0; j < EPI_COLS; j++) {
+                    const uint32_t col = col0 + j;
+                    const float w = __shfl_sync(0xffffffffu, ws_l[j / 32], j % 32);
+                    if (col < g.rows && tt < g.tpad) {
+                        const float v = tt < g.T ? mul_r<RM>(acc_at(acc, j), w) : 0.0f;
+                        const uint32_t hd = col / g.dk, dd = col - hd * g.dk;
+                        g.out[(static_cast<size_t>(hd) * g.tpad + (tt & ~15u)) * g.dk + 16 * dd + (tt & 15)] = v;
+                    }
+                }
             } else {
                 // through shared memory, a group of 32 output rows at a time, so
                 // that a lane owns one output row (a column of the tile) and
-                // each store is 32 consecutive floats
+                // each store is 32 consecutive floats (V panels: 16 of them)
 #pragma unroll
                 for (int h = 0; h < EPI_HALVES; h++) {
 #pragma unroll
@@ -655,7 +684,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                             for (int i = 0; i < 8; i++) {
                                 const uint32_t tt = tr0 + i0 + i;
-                                old[i] = (cvalid && tt < g.T) ? g.out[static_cast<size_t>(tt) * g.os + col] : 0.0f;
+                                old[i] = (cvalid && tt < g.T) ? g.out[out_at(g, tt, col)] : 0.0f;
                             }
                         }
 #pragma unroll
@@ -665,7 +694,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                                 float v = mul_r<RM>(tw[(i0 + i) * EPI_PITCH + lane], wsv);
                                 if (g.bias) v = add_r<RM>(v, bv);
                                 if (g.add) v = add_r<RM>(old[i], v);
-                                g.out[static_cast<size_t>(tt) * g.os + col] = v;
+                                g.out[out_at(g, tt, col)] = v;
                             }
                         }
                     }

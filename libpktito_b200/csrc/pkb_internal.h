@@ -30,6 +30,12 @@ struct GemmArgs {
     uint32_t rows, n, qb, T, add;
     uint32_t tiles_m, tiles_n;
     long long timeout;     // SM clock cycles a wait may last
+    // where the results go (the attention's panels, core/passes.c:119-196):
+    // 0 out[t*os + r]; 1 V panels, (t, r) at (r/16) ps + 16 t + r%16;
+    // 2 K/P panels, (t, r = h dk + d) at h tpad dk + (t/16) 16 dk + 16 d + t%16,
+    // frames T .. tpad-1 written as zeros
+    uint32_t pmode, dk, tpad;
+    unsigned long long ps;
 };
 
 int gemm_tile_rows();   // frames a tile (TMA box of the activations)

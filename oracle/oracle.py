@@ -65,6 +65,8 @@ def olib() -> ctypes.CDLL:
         l.oracle_layernorm_quantize.argtypes = [vp, vp, vp, sz, u32, u32, u32, vp, vp, f32, i32]
         l.oracle_silu_quantize.argtypes = [vp, vp, vp, sz, u32, u32, u32, i32]
         l.oracle_dwconv_quantize.argtypes = [vp, vp, vp, sz, vp, sz, u32, u32, vp, vp, u32, i32, u32, i32]
+        l.oracle_panels_kp.argtypes = [vp, vp, u32, u32, u32, u32]
+        l.oracle_panels_kp.restype = None
         for f in (l.oracle_set_rint_style, l.oracle_expf, l.oracle_sigmoidf, l.oracle_layernorm,
                   l.oracle_layernorm_quantize, l.oracle_silu_quantize, l.oracle_dwconv_quantize):
             f.restype = None
@@ -386,3 +388,53 @@ def ref_dwconv_quantize(x: np.ndarray, xs: int, T: int, C: int, w: np.ndarray, b
                 k.quantize(ctypes.byref(act), out.ctypes.data + 4 * (t * C + c0), nc)
     _with_mode(rmode, run)
     return q, d, out
+
+
+# ------------------------------------------------- the attention's panels --
+
+PKPASSES_SO = os.path.join(REF_DIR, "libpkpasses.so")
+
+
+def panels_kp(src: np.ndarray, n: int, np_: int, D: int, dk: int) -> np.ndarray:
+    """pk_panels_tile (core/passes.c:169-196) over a whole matrix: src [n][D]
+    floats into K/P panels of np_ frames (the rest zeros)."""
+    src = np.ascontiguousarray(src, np.float32).reshape(-1)
+    dst = np.empty((D // dk) * np_ * dk, np.float32)
+    olib().oracle_panels_kp(_p(dst), _p(src), n, np_, D, dk)
+    return dst
+
+
+def panels_v(w: np.ndarray, ws: np.ndarray, rows: int, q: np.ndarray, d: np.ndarray, n: int, qb: int, T: int,
+             ps: int, rmode: int = RN) -> np.ndarray:
+    """pk_gemm_panels_on (core/passes.c:119-141): the product one 16-row panel
+    a call, each with os 16 into panel r/16 at (r/16) ps."""
+    out = np.zeros((rows // 16 - 1) * ps + 16 * T, np.float32)
+    for r in range(0, rows, 16):
+        part = out[(r // 16) * ps:]
+        olib().oracle_gemm_q8(_p(part), 16, _p(w[r * n:]), _p(ws[r:]), None, 16, _p(q), _p(d), n, qb, T, 0, rmode)
+    return out
+
+
+class _Panels(ctypes.Structure):
+    """pk_panels (core/passes.h:53)"""
+    _fields_ = [("dst", ctypes.c_void_p), ("src", ctypes.c_void_p), ("n", ctypes.c_uint32), ("np", ctypes.c_uint32),
+                ("D", ctypes.c_uint32), ("dk", ctypes.c_uint32)]
+
+
+def have_passes() -> bool:
+    return os.path.exists(PKPASSES_SO)
+
+
+def ref_panels_kp(src: np.ndarray, n: int, np_: int, D: int, dk: int) -> np.ndarray:
+    """The reference's own pk_panels_tile (libpkpasses.so) over the whole
+    matrix as one tile: rows 0..D, frames 0..n (the last, so the padding is
+    written)."""
+    lib = ctypes.CDLL(PKPASSES_SO)
+    src = np.ascontiguousarray(src, np.float32).reshape(-1)
+    dst = np.full((D // dk) * np_ * dk, np.nan, np.float32)
+    arg = _Panels(_p(dst), _p(src), n, np_, D, dk)
+    f = lib.pk_panels_tile
+    f.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_int]
+    f.restype = None
+    f(ctypes.addressof(arg), 0, D, 0, n, 0)
+    return dst

@@ -378,3 +378,18 @@ void oracle_dwconv_quantize(int8_t *q, float *d, float *out, size_t os, const fl
         free(o);
     free(h);
 }
+
+/* ------------------------------------------------- the attention's panels -- */
+
+/* pk_panels_tile (core/passes.c:169-196) over a whole matrix: src's n rows
+ * of D floats (frame j of row r at src[j*D + r]) into K/P panels,
+ * (dimension d of head h, frame j) at dst[((h*np + j/16)*dk + d)*16 + j%16],
+ * frames n .. np-1 zeros. */
+void oracle_panels_kp(float *dst, const float *src, uint32_t n, uint32_t np, uint32_t D, uint32_t dk) {
+    for (uint32_t r = 0; r < D; r++) {
+        const uint32_t h = r / dk, d = r % dk;
+        for (uint32_t j = 0; j < np; j++)
+            dst[(((size_t)h * np + (j / 16) * 16) * dk) + (size_t)d * 16 + j % 16] =
+                j < n ? src[(size_t)j * D + r] : 0.0f;
+    }
+}

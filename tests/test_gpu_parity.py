@@ -308,3 +308,46 @@ def test_decoder_products_batched(pkb, cuda_device, rows, n, qb, add, bias, T):
     assert np.array_equal(q.cpu().numpy().reshape(T, n), qo) and same_bits(d.cpu().numpy().reshape(T, -1), do)
     got = out.cpu().numpy()
     assert same_bits(got, want), first_diff(got, want)
+
+
+# ------------------------------------------------- the attention's panels --
+
+PANELS = [(37, 256, 1024, 32, 64, 48), (750, 1024, 1024, 32, 128, 752), (1499, 1024, 1024, 32, 128, 1520),
+          (129, 128, 256, 64, 32, 144), (5, 64, 640, 640, 16, 16),
+          (1407, 256, 1024, 32, 128, 1424)]  # P's padding reaching a tile past the frames
+
+
+@pytest.mark.parametrize("T,rows,n,qb,dk,tpad", PANELS)
+@pytest.mark.parametrize("rmode", [O.RN, O.RZ])
+def test_product_into_panels(pkb, cuda_device, T, rows, n, qb, dk, tpad, rmode):
+    """The product straight into the attention's panels: K/P as
+    pk_panels_tile lays them (from the product's rows, padding zeros), V as
+    pk_gemm_panels_on's one call a 16-row panel; the floats beyond V's
+    panels (ps > 16 T) untouched."""
+    import torch
+    g = np.random.default_rng(T + rows + dk + rmode)
+    x = g.standard_normal(T * n).astype(np.float32)
+    qo, do = O.quantize(x, n, qb)
+    w = O.pack_q8(g.integers(-127, 128, (rows, n), dtype=np.int8))
+    ws = (1e-3 + 9e-3 * g.random(rows)).astype(np.float32)
+    ws[::5] *= -1  # negative row scales: padding must still be +0
+    plain = np.zeros(T * rows, np.float32)
+    O.gemm_q8(plain, rows, w, ws, None, rows, qo, do, n, qb, T, False, rmode)
+    want_kp = O.panels_kp(plain, T, tpad, rows, dk)
+    ps = 16 * T + 48
+    want_v = np.full((rows // 16 - 1) * ps + 16 * T + 48, 7.5, np.float32)
+    got_v_oracle = O.panels_v(w, ws, rows, qo, do, n, qb, T, ps, rmode)
+    for r in range(0, rows, 16):
+        want_v[(r // 16) * ps:(r // 16) * ps + 16 * T] = got_v_oracle[(r // 16) * ps:(r // 16) * ps + 16 * T]
+    qd, dd = torch.from_numpy(qo.reshape(-1)).cuda(), torch.from_numpy(do.reshape(-1)).cuda()
+    wp = torch.empty(rows * n, dtype=torch.int8, device="cuda")
+    pkb.repack_q8_dev(wp, torch.from_numpy(w).cuda(), rows, n)
+    wsd = torch.from_numpy(ws).cuda()
+    kp = torch.full((want_kp.size,), float("nan"), device="cuda")
+    pkb.gemm_q8_panels_dev(kp, pkb.PANELS_KP, 0, dk, tpad, wp, wsd, rows, qd, dd, n, qb, T, rmode)
+    vp = torch.full((want_v.size,), 7.5, device="cuda")
+    pkb.gemm_q8_panels_dev(vp, pkb.PANELS_V, ps, 0, 0, wp, wsd, rows, qd, dd, n, qb, T, rmode)
+    torch.cuda.synchronize()
+    got_kp, got_v = kp.cpu().numpy(), vp.cpu().numpy()
+    assert same_bits(got_kp, want_kp), first_diff(got_kp, want_kp)
+    assert same_bits(got_v, want_v), first_diff(got_v, want_v)

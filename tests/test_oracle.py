@@ -246,3 +246,25 @@ def test_exp_and_sigmoid_properties():
     special = np.array([0.0, np.nan, np.inf, -np.inf, 1000.0, -1000.0], np.float32)
     e = O.expf(special)
     assert e[0] == 1.0 and e[1] == e[5] == e[3] and e[2] == e[4] and np.isfinite(e).all()
+
+
+# ------------------------------------------------------ the attention's panels --
+
+def test_golden_panels():
+    """The oracle's K/P panel layout is the reference's pk_panels_tile's
+    (tests/golden/make_panels_golden.py), padding zeros included."""
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "panels_golden.npz"))
+    cases = sorted({k.split("/")[1] for k in g.files})
+    assert len(cases) >= 5
+    for i in cases:
+        n, np_, D, dk = (int(v) for v in g[f"kp/{i}/meta"])
+        assert O.panels_kp(g[f"kp/{i}/src"], n, np_, D, dk).tobytes() == g[f"kp/{i}/dst"].tobytes(), i
+
+
+@pytest.mark.skipif(not O.have_passes(), reason="oracle/_ref/libpkpasses.so not built")
+def test_live_reference_panels():
+    g = np.random.default_rng(5)
+    for n, D, dk in [(750, 1024, 128), (1499, 1024, 128), (63, 192, 64)]:
+        for np_ in ((n + 15) // 16 * 16, (n + 15) // 16 * 16 + 16):
+            src = g.standard_normal(n * D).astype(np.float32)
+            assert O.panels_kp(src, n, np_, D, dk).tobytes() == O.ref_panels_kp(src, n, np_, D, dk).tobytes()
