@@ -159,6 +159,20 @@ int quantize_dev(cudaStream_t stream, int8_t* q, float* d, const float* x, size_
     return PKB_OK;
 }
 
+// A tensor map of the block scales d [T][nb] (nb a multiple of 4, d 16-byte
+// aligned): boxes of gemm_scale_box() blocks by gemm_tile_rows() frames.
+int make_scale_map(CUtensorMap* md, const float* d, uint32_t nb, uint32_t T) {
+    cuuint32_t estr[2] = {1, 1};
+    cuuint64_t ddims[2] = {nb, T};
+    cuuint64_t dstrides[1] = {static_cast<cuuint64_t>(nb) * 4};
+    cuuint32_t dbox[2] = {static_cast<cuuint32_t>(gemm_scale_box()), static_cast<cuuint32_t>(gemm_tile_rows())};
+    CUresult r = g_encode(md, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(d), ddims, dstrides, dbox, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(PKB_ECUDA, "cuTensorMapEncodeTiled (scales) failed (%d)", static_cast<int>(r));
+    return PKB_OK;
+}
+
 int gemm_dev(cudaStream_t stream, float* out, size_t os, const int8_t* wpack, const float* ws, const float* bias,
              uint32_t rows, const int8_t* q, const float* d, uint32_t n, uint32_t qb, uint32_t T, int add, int rmode) {
     int rc = check_act_shape(n, qb);
@@ -204,20 +218,14 @@ int gemm_dev(cudaStream_t stream, float* out, size_t os, const int8_t* wpack, co
     const uint32_t nb = n / qb;
     if (nb % 4 == 0 && aligned(d, 16) && os % 4 == 0 && aligned(out, 16) && aligned(ws, 16) &&
         (!bias || aligned(bias, 16))) {
+        if ((rc = make_scale_map(&md, d, nb, T))) return rc;
         cuuint32_t estr[2] = {1, 1};
-        cuuint64_t ddims[2] = {nb, T};
-        cuuint64_t dstrides[1] = {static_cast<cuuint64_t>(nb) * 4};
-        cuuint32_t dbox[2] = {static_cast<cuuint32_t>(gemm_scale_box()), static_cast<cuuint32_t>(gemm_tile_rows())};
-        CUresult r = g_encode(&md, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(d), ddims, dstrides, dbox,
-                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        if (r != CUDA_SUCCESS) return fail(PKB_ECUDA, "cuTensorMapEncodeTiled (scales) failed (%d)", static_cast<int>(r));
         cuuint64_t odims[2] = {rows, T};
         cuuint64_t ostrides[1] = {static_cast<cuuint64_t>(os) * 4};
         cuuint32_t obox[2] = {static_cast<cuuint32_t>(gemm_out_box()), static_cast<cuuint32_t>(gemm_out_box())};
-        r = g_encode(&mo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, out, odims, ostrides, obox, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        CUresult r = g_encode(&mo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, out, odims, ostrides, obox, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) return fail(PKB_ECUDA, "cuTensorMapEncodeTiled (results) failed (%d)", static_cast<int>(r));
         mdp = &md;
         mop = &mo;
@@ -299,7 +307,13 @@ int dwconv_quantize_dev(cudaStream_t stream, int8_t* q, float* d, float* out, si
 
 // The product straight into the attention's panels (kind PKB_PANELS_V or
 // PKB_PANELS_KP): no bias, nothing added, as the reference's V, K and P
-// products; the plain-store path, its index per kind.
+// products. Where n / qb is a multiple of 4 and the buffers (and V's panel
+// stride) whole 16-byte units, the results leave through TMA stores of a
+// panel-shaped map: V as (row in panel 16, frame T, panel rows/16), boxes of
+// 16 x 32 x 2 with a 64-byte swizzle; K/P as (frame in panel 16, dimension
+// dk, panel tpad/16, head rows/dk), boxes of 16 x 16 x 2 x 1, so a box never
+// crosses a head and the map clips the frames past tpad. Otherwise the
+// plain-store path, its index per kind.
 int gemm_panels_dev(cudaStream_t stream, float* panels, int kind, size_t ps, uint32_t dk, uint32_t tpad,
                     const int8_t* wpack, const float* ws, uint32_t rows, const int8_t* q, const float* d, uint32_t n,
                     uint32_t qb, uint32_t T, int rmode) {
@@ -347,7 +361,36 @@ int gemm_panels_dev(cudaStream_t stream, float* panels, int kind, size_t ps, uin
     g.tiles_m = (g.tpad + gemm_tile_rows() - 1) / gemm_tile_rows();
     g.tiles_n = (rows + gemm_tile_cols() - 1) / gemm_tile_cols();
     g.timeout = wait_limit();
-    PKB_CUDA(launch_gemm_q8(ma, mb, nullptr, nullptr, g, dev->sms, rmode, stream), "panels launch");
+    CUtensorMap md, mo;
+    const CUtensorMap* mdp = nullptr;
+    const CUtensorMap* mop = nullptr;
+    const uint32_t nb = n / qb;
+    if (nb % 4 == 0 && aligned(d, 16) && aligned(panels, 16) && aligned(ws, 16) &&
+        (kind == PKB_PANELS_KP || ps % 4 == 0)) {
+        if ((rc = make_scale_map(&md, d, nb, T))) return rc;
+        cuuint32_t estr[4] = {1, 1, 1, 1};
+        CUresult r;
+        if (kind == PKB_PANELS_V) {
+            cuuint64_t odims[3] = {16, T, rows / 16};
+            cuuint64_t ostrides[2] = {64, static_cast<cuuint64_t>(ps) * 4};
+            cuuint32_t obox[3] = {16, 32, 2};
+            r = g_encode(&mo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, panels, odims, ostrides, obox, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        } else {
+            cuuint64_t odims[4] = {16, dk, tpad / 16, rows / dk};
+            cuuint64_t ostrides[3] = {64, 64 * static_cast<cuuint64_t>(dk),
+                                      4 * static_cast<cuuint64_t>(tpad) * dk};
+            cuuint32_t obox[4] = {16, 16, 2, 1};
+            r = g_encode(&mo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, panels, odims, ostrides, obox, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        }
+        if (r != CUDA_SUCCESS) return fail(PKB_ECUDA, "cuTensorMapEncodeTiled (panels) failed (%d)", static_cast<int>(r));
+        mdp = &md;
+        mop = &mo;
+    }
+    PKB_CUDA(launch_gemm_q8(ma, mb, mdp, mop, g, dev->sms, rmode, stream), "panels launch");
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return PKB_OK;
 }

@@ -278,6 +278,22 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
                  : "memory");
 }
 
+// The same for 3-D and 4-D maps (the attention's panels): x is 0 at every
+// call site, the other coordinates non-negative.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int x, int y, int z, int w) {
+    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "r"(w)
+                 : "memory");
+}
+
 // Closes the thread's current bulk group of TMA stores.
 // Per-thread asynchronous copies into shared memory (LDGSTS): 16 or 4
 // bytes, tracked in groups that the copying thread waits for itself (a

@@ -193,18 +193,22 @@ __device__ __forceinline__ size_t out_at(const GemmArgs& g, uint32_t t, uint32_t
 
 // SPB: K steps a block (1, 2 or 4, with n a multiple of BK: every stage
 // starts a block and holds four K steps), or 0 for any qb and n.
-// TIO (a multiple of four blocks a tile; the scales' rows, the results' rows
-// and the row scales and biases whole 16-byte units): the block scales come
-// through a TMA ring (map_d), the row scales and biases through a bulk-copy
-// ring, the results leave through TMA stores (map_o), so the epilogue's
-// loop holds no global load (on B200 a global load in flight there costs
-// the chain as much as one waited for at once); otherwise plain loads and
-// stores.
-template <int RM, bool EXACT_SUM, bool TIO, int SPB>
+// OM, where the results go: 0 plain loads and stores (rows or panels by
+// g.pmode, through out_at); otherwise (a multiple of four blocks a tile; the
+// scales' rows, the results' rows and the row scales and biases whole
+// 16-byte units) the block scales come through a TMA ring (map_d), the row
+// scales and biases through a bulk-copy ring, and the results leave through
+// TMA stores of map_o: 1 rows, 2 V panels, 3 K/P panels. The epilogue's loop
+// then holds no global load (on B200 a global load in flight there costs the
+// chain as much as one waited for at once). The panel layouts are separate
+// instances: a run-time choice in the store code cost the rows' instance 9 %
+// on B200.
+template <int RM, bool EXACT_SUM, int OM, int SPB>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_q8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    const __grid_constant__ CUtensorMap map_d, const __grid_constant__ CUtensorMap map_o,
                    const GemmArgs g) {
+    constexpr bool TIO = OM != 0;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float* epi = reinterpret_cast<float*>(smem + NSTAGE * STAGE_BYTES);
@@ -499,9 +503,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 
             // the warp's boxes of the results: group h is 32 output rows from
             // col0 + 32 h by 32 frames from frame0; a group past the last row
-            // is not stored (the groups that are live come first)
+            // is not stored (the groups that are live come first); K/P panels
+            // also take the padding's frames, as zeros
             const uint32_t col0 = n0 + EPI_COLS * cgroup, frame0 = m0 + lane_base;
-            const bool live = col0 < g.rows && frame0 < g.T;
+            const bool live = col0 < g.rows && frame0 < (OM == 3 ? g.tpad : g.T);
             uint32_t nlive = 0;
 #pragma unroll
             for (int h = 0; h < EPI_HALVES; h++) nlive += (live && col0 + 32 * h < g.rows) ? 1u : 0u;
@@ -593,8 +598,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                     ws_l[h] = in ? wsv[32 * h + lane] : 0.0f;
                     b_l[h] = (g.bias && in) ? wsv[BN + 32 * h + lane] : 0.0f;
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&wsempty[wsl]);
+                // the slot goes back now (K/P panels: once staged, as their
+                // staging reads the row scales from it)
+                if constexpr (OM != 3) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&wsempty[wsl]);
+                }
                 wcnt++;
                 if (live) {
                     if (g.add) {
@@ -610,7 +619,61 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int h = 0; h < EPI_HALVES; h++) {
                         if (h >= static_cast<int>(nlive)) break;  // warp-uniform
-                        uint8_t* row = stg + h * STG_BYTES + lane * 128;
+                        uint8_t* box = stg + h * STG_BYTES;
+                        if constexpr (OM == 2) {
+                            // V panels (pk_gemm_panels_on, core/passes.c:119-141):
+                            // the box is 2 panels x 32 frames x 16 output rows,
+                            // 64-byte rows whose 16-byte chunks the map's 64-byte
+                            // swizzle permutes by the row (bank-conflict free
+                            // for a quarter-warp); frames past T are clipped
+#pragma unroll
+                            for (int rp = 0; rp < 2; rp++) {
+#pragma unroll
+                                for (int k = 0; k < 4; k++) {
+                                    float v[4];
+#pragma unroll
+                                    for (int e = 0; e < 4; e++) {
+                                        const int j = 16 * rp + 4 * k + e;
+                                        v[e] = mul_r<RM>(acc_at(acc, 32 * h + j), __shfl_sync(0xffffffffu, ws_l[h], j));
+                                    }
+                                    *reinterpret_cast<float4*>(box + (rp * 32 + lane) * 64 +
+                                                               ((k ^ ((lane >> 1) & 3)) << 4)) =
+                                        make_float4(v[0], v[1], v[2], v[3]);
+                                }
+                            }
+                            continue;
+                        }
+                        if constexpr (OM == 3) {
+                            // K/P panels (pk_panels_tile, core/passes.c:143-196):
+                            // two boxes of 16 dimensions x 2 panels x 16 frames,
+                            // one a 16-column half (each within one head); the
+                            // padding's frames are zeros. A column pair at a
+                            // time: one packed multiply by the pair's row scales
+                            // (a broadcast load of the ring), then two stores,
+                            // lanes 16-31 (the second panel) storing the pair's
+                            // columns the other way round, so a store's 32 lanes
+                            // cover 32 distinct banks. The product is not added
+                            // to (a packed multiply feeding a packed add would be
+                            // fused).
+                            const uint32_t half = lane >> 4;
+                            const bool pad = frame0 + 32 > g.T;  // warp-uniform
+                            const bool real = frame0 + lane < g.T;
+                            float* fa = reinterpret_cast<float*>(box) + half * 256 + (lane & 15) + 16 * half;
+                            float* fz = reinterpret_cast<float*>(box) + half * 256 + (lane & 15) + 16 - 16 * half;
+#pragma unroll
+                            for (int i = 0; i < 16; i++) {
+                                const uint64_t w2 = *reinterpret_cast<const uint64_t*>(wsv + 32 * h + 2 * i);
+                                uint64_t pr = mul2_r<RM>(acc[16 * h + i], w2);
+                                if (pad && !real) pr = 0;  // +0, +0
+                                float p0, p1;
+                                unpack2(pr, p0, p1);
+                                const int slot = (i >> 3) * 512 + (2 * i & 15) * 16;  // column 2i's place
+                                fa[slot] = half ? p1 : p0;
+                                fz[slot] = half ? p0 : p1;
+                            }
+                            continue;
+                        }
+                        uint8_t* row = box + lane * 128;
 #pragma unroll
                         for (int k = 0; k < 8; k++) {
                             float4* c4 = reinterpret_cast<float4*>(row + ((k ^ (lane & 7)) << 4));
@@ -636,11 +699,31 @@ __global__ void __launch_bounds__(THREADS, 1)
                     fence_async_smem();
                     __syncwarp();
                     if (lane == 0) {
-                        for (uint32_t h = 0; h < nlive; h++)
-                            tma_store_2d(&map_o, stg + h * STG_BYTES, static_cast<int>(col0 + 32 * h),
-                                         static_cast<int>(frame0));
+                        for (uint32_t h = 0; h < nlive; h++) {
+                            const uint32_t c = col0 + 32 * h;
+                            if constexpr (OM == 2) {
+                                // (row in panel, frame, panel)
+                                tma_store_3d(&map_o, stg + h * STG_BYTES, 0, static_cast<int>(frame0),
+                                             static_cast<int>(c >> 4));
+                            } else if constexpr (OM == 3) {
+                                // (frame in panel, dimension, panel, head) a half;
+                                // rows a multiple of 16, so a half is all in or out
+                                for (uint32_t s = 0; s < 2 && c + 16 * s < g.rows; s++) {
+                                    const uint32_t cs = c + 16 * s, hd = cs / g.dk;
+                                    tma_store_4d(&map_o, stg + h * STG_BYTES + s * 2048, 0,
+                                                 static_cast<int>(cs - hd * g.dk), static_cast<int>(frame0 >> 4),
+                                                 static_cast<int>(hd));
+                                }
+                            } else {
+                                tma_store_2d(&map_o, stg + h * STG_BYTES, static_cast<int>(c), static_cast<int>(frame0));
+                            }
+                        }
                         bulk_commit();
                     }
+                }
+                if constexpr (OM == 3) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&wsempty[wsl]);
                 }
             } else if (g.pmode == 2) {
                 // K and P panels (pk_panels_tile, core/passes.c:143-196): frame
@@ -722,24 +805,35 @@ __global__ void __launch_bounds__(THREADS, 1)
 using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs);
 
 // The instance for these arguments: the staged MMA paths where qb is 32, 64
-// or 128 and n a multiple of BK, the TMA path where the results have a
-// tensor map.
-template <int RM, bool EXACT_SUM>
-static KernelFn pick(uint32_t n, uint32_t qb, bool dtma) {
+// or 128 and n a multiple of BK; om as the kernel's OM (0 where the results
+// have no tensor map).
+template <int RM, bool EXACT_SUM, int OM>
+static KernelFn pick_om(uint32_t n, uint32_t qb) {
     if constexpr (EXACT_SUM) {
         const uint32_t spb = qb / KSTEP;
-        if (n % BK == 0 && spb == 1) return dtma ? gemm_q8_kernel<RM, true, true, 1> : gemm_q8_kernel<RM, true, false, 1>;
-        if (n % BK == 0 && spb == 2) return dtma ? gemm_q8_kernel<RM, true, true, 2> : gemm_q8_kernel<RM, true, false, 2>;
-        if (n % BK == 0 && spb == 4) return dtma ? gemm_q8_kernel<RM, true, true, 4> : gemm_q8_kernel<RM, true, false, 4>;
+        if (n % BK == 0 && spb == 1) return gemm_q8_kernel<RM, true, OM, 1>;
+        if (n % BK == 0 && spb == 2) return gemm_q8_kernel<RM, true, OM, 2>;
+        if (n % BK == 0 && spb == 4) return gemm_q8_kernel<RM, true, OM, 4>;
     }
-    return dtma ? gemm_q8_kernel<RM, EXACT_SUM, true, 0> : gemm_q8_kernel<RM, EXACT_SUM, false, 0>;
+    return gemm_q8_kernel<RM, EXACT_SUM, OM, 0>;
+}
+
+template <int RM, bool EXACT_SUM>
+static KernelFn pick(uint32_t n, uint32_t qb, int om) {
+    switch (om) {
+    case 0: return pick_om<RM, EXACT_SUM, 0>(n, qb);
+    case 1: return pick_om<RM, EXACT_SUM, 1>(n, qb);
+    case 2: return pick_om<RM, EXACT_SUM, 2>(n, qb);
+    default: return pick_om<RM, EXACT_SUM, 3>(n, qb);
+    }
 }
 
 template <int RM, bool EXACT_SUM>
 static cudaError_t launch_rm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap* md,
                              const CUtensorMap* mo, const GemmArgs& g, int grid, cudaStream_t stream) {
     const bool tio = md != nullptr && mo != nullptr;
-    const KernelFn kern = pick<RM, EXACT_SUM>(g.n, g.qb, tio);
+    const int om = tio ? 1 + static_cast<int>(g.pmode) : 0;
+    const KernelFn kern = pick<RM, EXACT_SUM>(g.n, g.qb, om);
     return launch_pdl(kern, dim3(grid), dim3(THREADS), SMEM_BYTES, stream, ma, mb, tio ? *md : ma,
                       tio ? *mo : ma, g);
 }
@@ -747,13 +841,13 @@ static cudaError_t launch_rm(const CUtensorMap& ma, const CUtensorMap& mb, const
 // Every instance's dynamic shared memory allowance, on the current device.
 template <int RM, bool EXACT_SUM>
 static cudaError_t prepare_rm() {
-    const KernelFn k[8] = {gemm_q8_kernel<RM, EXACT_SUM, false, 0>, gemm_q8_kernel<RM, EXACT_SUM, true, 0>,
-                           pick<RM, EXACT_SUM>(BK, 32, false),       pick<RM, EXACT_SUM>(BK, 32, true),
-                           pick<RM, EXACT_SUM>(BK, 64, false),       pick<RM, EXACT_SUM>(BK, 64, true),
-                           pick<RM, EXACT_SUM>(BK, 128, false),      pick<RM, EXACT_SUM>(BK, 128, true)};
-    for (auto f : k) {
-        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-        if (e != cudaSuccess) return e;
+    for (int om = 0; om < 4; om++) {
+        const KernelFn k[4] = {pick<RM, EXACT_SUM>(BK + 1, 32, om), pick<RM, EXACT_SUM>(BK, 32, om),
+                               pick<RM, EXACT_SUM>(BK, 64, om), pick<RM, EXACT_SUM>(BK, 128, om)};
+        for (auto f : k) {
+            cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+            if (e != cudaSuccess) return e;
+        }
     }
     return cudaSuccess;
 }

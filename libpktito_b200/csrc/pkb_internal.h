@@ -49,10 +49,11 @@ cudaError_t prepare_gemm_q8();
 // map_d: a tensor map of the block scales d [T][n/qb] (float32, boxes of
 // gemm_scale_box() blocks by gemm_tile_rows() frames); map_o: one of the
 // results out [T][rows] (float32, row stride os, boxes of gemm_out_box() by
-// gemm_out_box(), 128-byte swizzle). Both are given only where n / qb is a
-// multiple of 4 and d, out, ws and bias are 16-byte aligned, os a multiple
-// of 4; the kernel then moves scales, row scales, biases and results with
-// TMA. Null: plain loads and stores.
+// gemm_out_box(), 128-byte swizzle), or for pmode 1 and 2 one of the panels
+// (3-D for V, 4-D for K/P, laid out as the kernel stages them). Both are
+// given only where n / qb is a multiple of 4 and d, out, ws and bias are
+// 16-byte aligned, os (V: ps) a multiple of 4; the kernel then moves scales,
+// row scales, biases and results with TMA. Null: plain loads and stores.
 cudaError_t launch_gemm_q8(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap* map_d,
                            const CUtensorMap* map_o, const GemmArgs& g, int num_sms, int rmode, cudaStream_t stream);
 int gemm_out_box();     // frames and output rows of a TMA box of the results

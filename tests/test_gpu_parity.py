@@ -314,16 +314,21 @@ def test_decoder_products_batched(pkb, cuda_device, rows, n, qb, add, bias, T):
 
 PANELS = [(37, 256, 1024, 32, 64, 48), (750, 1024, 1024, 32, 128, 752), (1499, 1024, 1024, 32, 128, 1520),
           (129, 128, 256, 64, 32, 144), (5, 64, 640, 640, 16, 16),
-          (1407, 256, 1024, 32, 128, 1424)]  # P's padding reaching a tile past the frames
+          (1407, 256, 1024, 32, 128, 1424),  # P's padding reaching a tile past the frames
+          (100, 144, 512, 32, 48, 112),  # heads of 48: a group of 32 columns spans two heads; rows % 32 = 16
+          (300, 80, 256, 32, 16, 336)]  # heads of 16, padding past a whole panel of frames
 
 
 @pytest.mark.parametrize("T,rows,n,qb,dk,tpad", PANELS)
 @pytest.mark.parametrize("rmode", [O.RN, O.RZ])
-def test_product_into_panels(pkb, cuda_device, T, rows, n, qb, dk, tpad, rmode):
+@pytest.mark.parametrize("off", [0, 1])
+def test_product_into_panels(pkb, cuda_device, T, rows, n, qb, dk, tpad, rmode, off):
     """The product straight into the attention's panels: K/P as
     pk_panels_tile lays them (from the product's rows, padding zeros), V as
     pk_gemm_panels_on's one call a 16-row panel; the floats beyond V's
-    panels (ps > 16 T) untouched."""
+    panels (ps > 16 T) untouched. off 0: 16-byte aligned panels, the TMA
+    stores of panel-shaped maps where n / qb is a multiple of 4; off 1: the
+    panels one float in, the plain-store path."""
     import torch
     g = np.random.default_rng(T + rows + dk + rmode)
     x = g.standard_normal(T * n).astype(np.float32)
@@ -343,11 +348,12 @@ def test_product_into_panels(pkb, cuda_device, T, rows, n, qb, dk, tpad, rmode):
     wp = torch.empty(rows * n, dtype=torch.int8, device="cuda")
     pkb.repack_q8_dev(wp, torch.from_numpy(w).cuda(), rows, n)
     wsd = torch.from_numpy(ws).cuda()
-    kp = torch.full((want_kp.size,), float("nan"), device="cuda")
+    kp = torch.full((want_kp.size + off,), float("nan"), device="cuda")[off:]
     pkb.gemm_q8_panels_dev(kp, pkb.PANELS_KP, 0, dk, tpad, wp, wsd, rows, qd, dd, n, qb, T, rmode)
-    vp = torch.full((want_v.size,), 7.5, device="cuda")
+    vp = torch.full((want_v.size + off,), 7.5, device="cuda")[off:]
     pkb.gemm_q8_panels_dev(vp, pkb.PANELS_V, ps, 0, 0, wp, wsd, rows, qd, dd, n, qb, T, rmode)
     torch.cuda.synchronize()
+    assert pkb.device_errors(0) == 0
     got_kp, got_v = kp.cpu().numpy(), vp.cpu().numpy()
     assert same_bits(got_kp, want_kp), first_diff(got_kp, want_kp)
     assert same_bits(got_v, want_v), first_diff(got_v, want_v)
