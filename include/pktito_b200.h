@@ -138,7 +138,10 @@ int pkb_gemm_q8_dev(void *stream, float *out, size_t os, const int8_t *wpack, co
  *                  panels + h tpad dk + (t/16) 16 dk + 16 d + t%16, frames T to
  *                  tpad - 1 written as zeros (pk_panels_tile: K with tpad the
  *                  frames rounded up to 16, P with its positions rounded up
- *                  to 16 plus 16); dk a multiple of 16 dividing rows. */
+ *                  to 16 plus 16); dk a multiple of 16 dividing rows.
+ * Fastest where n / qb is a multiple of 4 and panels, d and ws are 16-byte
+ * aligned (and, for V, ps a multiple of 4): the results then leave by TMA
+ * stores of panel-shaped boxes; otherwise by plain stores, same bytes. */
 #define PKB_PANELS_V 1
 #define PKB_PANELS_KP 2
 int pkb_gemm_q8_panels_dev(void *stream, float *panels, int kind, size_t ps, uint32_t dk, uint32_t tpad,

@@ -240,13 +240,14 @@ def pinned_like(a: np.ndarray) -> tuple[object, np.ndarray]:
 
 
 @pytest.mark.parametrize("rmode", [O.RN, O.RU])
-def test_host_calls_on_page_locked_buffers(pkb, cuda_device, rmode):
+@pytest.mark.parametrize("os_,add", [(272, 1), (256, 1), (256, 0)])
+def test_host_calls_on_page_locked_buffers(pkb, cuda_device, rmode, os_, add):
     """Page-locked activations and results take the direct-DMA path (no
-    host staging): several chunks, a strided output with the floats between
-    rows untouched, a product that adds to its output, with bias; the same
-    bytes as the oracle."""
+    host staging): several chunks; a strided output with the floats between
+    rows untouched, or rows back to back; a product that adds to its output
+    or overwrites it, with bias; the same bytes as the oracle."""
     lib = pkb.lib()
-    T, n, qb, xs, rows, os_ = 40000, 1024, 32, 1040, 256, 272
+    T, n, qb, xs, rows = 40000, 1024, 32, 1040, 256
     g = np.random.default_rng(17 + rmode)
     x = g.standard_normal(T * xs).astype(np.float32)
     keep_x, xp = pinned_like(x)
@@ -262,9 +263,9 @@ def test_host_calls_on_page_locked_buffers(pkb, cuda_device, rmode):
     out0 = g.standard_normal(T * os_).astype(np.float32)
     keep_o, op = pinned_like(out0)
     assert lib.pkb_gemm_q8_host(op.ctypes.data, os_, w.ctypes.data, ws.ctypes.data, bias.ctypes.data, rows,
-                                qp.ctypes.data, dp.ctypes.data, n, qb, T, 1, rmode) == 0
+                                qp.ctypes.data, dp.ctypes.data, n, qb, T, add, rmode) == 0
     want = out0.copy()
-    O.gemm_q8(want, os_, w, ws, bias, rows, qo, do, n, qb, T, True, rmode)
+    O.gemm_q8(want, os_, w, ws, bias, rows, qo, do, n, qb, T, bool(add), rmode)
     assert same_bits(op, want), first_diff(op, want)
     pkb.forget(w)
 
