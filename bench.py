@@ -916,6 +916,35 @@ def run_producers_only() -> None:
                       "launches": P.launch_count(), "device_errors": P.device_errors(0)}))
 
 
+def run_panels_only() -> None:
+    """The attention's K and V products at the batch's frame count (M 11521
+    x N 1024 x K 1024, qb 32; dk 128): one launch each into plain rows, K
+    panels and V panels, in that order (the ncu capture's case: 12 MB of
+    activations in, 47 MB of results out each)."""
+    import torch
+    import libpktito_b200 as P
+    T = sum(s[3] for s in segments(0))
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(SEED)
+    x = torch.randn(T * D, device=dev, generator=g)
+    q = torch.empty(T * D, dtype=torch.int8, device=dev)
+    d = torch.empty(T * D // QB, device=dev)
+    w_pk = torch.randint(-127, 128, (D * D,), dtype=torch.int8, device=dev, generator=g)
+    wp = torch.empty_like(w_pk)
+    ws = 1e-3 + 9e-3 * torch.rand(D, device=dev, generator=g)
+    tpad = (T + 15) // 16 * 16
+    plain, kp, vp = (torch.empty(T * D, device=dev), torch.empty(D * tpad, device=dev),
+                     torch.empty(D * T, device=dev))
+    P.quantize_dev(q, d, x, D, T, D, QB)
+    P.repack_q8_dev(wp, w_pk, D, D)
+    P.gemm_q8_dev(plain, D, wp, ws, None, D, q, d, D, QB, T, False)
+    P.gemm_q8_panels_dev(kp, P.PANELS_KP, 0, 128, tpad, wp, ws, D, q, d, D, QB, T)
+    P.gemm_q8_panels_dev(vp, P.PANELS_V, 16 * T, 0, 0, wp, ws, D, q, d, D, QB, T)
+    torch.cuda.synchronize()
+    print(json.dumps({"panels_only": f"M {T} x N {D} x K {D} qb {QB}: rows, K panels (dk 128), V panels",
+                      "launches": P.launch_count(), "device_errors": P.device_errors(0)}))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -935,9 +964,14 @@ def main() -> None:
                     help="only the dominant product (FF up at the batch's M), 3 launches: the ncu capture's case")
     ap.add_argument("--producers-only", action="store_true",
                     help="only the fused producers at the batch's frame count, 2 launches each: the ncu capture's case")
+    ap.add_argument("--panels-only", action="store_true",
+                    help="only the K/V products into plain rows, K panels and V panels, 1 launch each: the ncu "
+                         "capture's case")
     args = ap.parse_args()
     if args.kernel_only:
         run_kernel_only()
+    elif args.panels_only:
+        run_panels_only()
     elif args.producers_only:
         run_producers_only()
     elif args.impl == "reference":
