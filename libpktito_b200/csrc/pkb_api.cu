@@ -102,6 +102,7 @@ int current_device(Device** out) {
             PKB_CUDA(cudaGetSymbolAddress(&sym, g_device_error), "cudaGetSymbolAddress");
             d.err = static_cast<uint32_t*>(sym);
             PKB_CUDA(prepare_gemm_q8(), "kernel attributes");
+            prepare_quantize();
             d.sms = prop.multiProcessorCount;
             wait_limit();
             d.ready = true;

@@ -79,6 +79,9 @@ cudaError_t launch_pdl(void (*kern)(Params...), dim3 grid, dim3 block, size_t sm
 
 cudaError_t launch_quantize(int8_t* q, float* d, const float* x, size_t xs, uint32_t T, uint32_t n, uint32_t qb,
                             int rmode, int num_sms, cudaStream_t stream);
+// The plain quantizer's grid sizes (CTAs resident an SM), once at the
+// device's set-up.
+void prepare_quantize();
 
 cudaError_t launch_silu_quantize(int8_t* q, float* d, const float* u, size_t us, uint32_t T, uint32_t n,
                                  uint32_t qb, int rmode, int num_sms, cudaStream_t stream);

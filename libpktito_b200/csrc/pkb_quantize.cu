@@ -14,10 +14,10 @@
 //
 // Layout of the work: a block of 32 is 4 threads of 8 inputs (two 16-byte
 // loads each), a block of 64 8 threads of 8, so a warp takes 8 or 4 blocks
-// at once (and four such chunks a pass, their loads in flight together) and
+// at once (and two such chunks a pass, their loads in flight together) and
 // reduces each within its thread group by shuffles; wider blocks (qb = n, up
 // to 16384) take a warp each, in two passes over the block. Warps stride over
-// the blocks, grid sized to the SMs.
+// the blocks, the grid one wave of the CTAs an SM holds.
 //
 // repack: PK_Q8 panels (core/pkf.h:28-41: 16 rows by 4 inputs in 64-byte
 // groups) to plain rows of n bytes, which the product's TMA tiles read.
@@ -45,9 +45,11 @@ __device__ __forceinline__ float amax4(float4 v) {
 
 // Blocks of QB = 32 or 64 inputs, E inputs (E / 4 16-byte loads) a thread,
 // QB / E threads a block. A warp takes 32 / (QB / E) blocks a chunk and U
-// chunks a pass, loading all of them before reducing any: many 16-byte
-// loads in flight a thread keep HBM busy (measured on B200 at qb 32: one a
-// thread 2.7 TB/s, four 3.6-4.0, eight 4.4-5.1). IDX is the index type,
+// chunks a pass, loading all of them before reducing any: several 16-byte
+// loads in flight a thread keep HBM busy (measured on B200 at qb 32, grid of
+// eight CTAs an SM: one a thread 2.7 TB/s, four 3.6-4.0, eight 4.4-5.1; with
+// the grid one resident wave, four loads of two chunks beat eight of four,
+// whose registers leave fewer CTAs on an SM). IDX is the index type,
 // 32-bit wherever T * n / qb fits. SILU: each input goes through the
 // reference's SiLU first (siluq_tile, core/encoder.c:150-158: k_silu on the
 // row, then pk_quant_part).
@@ -136,6 +138,12 @@ __device__ __forceinline__ void quantize_narrow_body(int8_t* __restrict__ q, flo
 #ifndef PKB_SILU_U
 #define PKB_SILU_U 2
 #endif
+// chunks a pass for the plain form (measured on B200 at T 11521, qb 32, with
+// the grid one wave of resident CTAs: two 11.9 / 40.4 us for n 1024 / 4096,
+// four 13.5 / 42.3, eight 20.9 / 82.0 with one CTA an SM)
+#ifndef PKB_Q_U
+#define PKB_Q_U 2
+#endif
 
 template <int RM, int QB, int E, bool SILU>
 __global__ void __launch_bounds__(256) quantize_narrow(int8_t* __restrict__ q, float* __restrict__ d,
@@ -143,7 +151,7 @@ __global__ void __launch_bounds__(256) quantize_narrow(int8_t* __restrict__ q, f
                                                        uint32_t n, bool vec) {
     pdl_trigger();
     pdl_wait();
-    constexpr int U = SILU ? PKB_SILU_U : 4;
+    constexpr int U = SILU ? PKB_SILU_U : PKB_Q_U;
     const uint32_t nb = n / QB;
     const uint64_t total = static_cast<uint64_t>(T) * nb;
     if (total <= 0xFFFFFFF0ull)
@@ -192,6 +200,33 @@ __global__ void __launch_bounds__(256) quantize_wide(int8_t* __restrict__ q, flo
     }
 }
 
+// CTAs of a narrow instance resident on an SM at once (its registers decide),
+// asked once: the grid is one wave of them, each warp striding over the rest
+// of the blocks (measured on B200: a grid of eight 256-thread CTAs an SM ran
+// as 2.7 waves of the three that fit, and the partial last wave cost 5-20 %)
+template <int RM, int QB, int E, bool SILU>
+size_t narrow_resident() {
+    static const size_t r = [] {
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, quantize_narrow<RM, QB, E, SILU>, 256, 0) !=
+                cudaSuccess ||
+            per_sm < 1)
+            per_sm = 1;
+        return static_cast<size_t>(per_sm);
+    }();
+    return r;
+}
+
+template <int RM, bool SILU>
+size_t resident(uint32_t qb, bool q8) {
+    // the SiLU form is instruction-bound and keeps eight CTAs an SM (one
+    // resident wave measured 71.4 us against 67.8-69.5 on n 4096)
+    if constexpr (SILU) return 8;
+    if (qb == 32) return q8 ? narrow_resident<RM, 32, 8, SILU>() : narrow_resident<RM, 32, 4, SILU>();
+    if (qb == 64) return q8 ? narrow_resident<RM, 64, PKB_Q64_E, SILU>() : narrow_resident<RM, 64, 4, SILU>();
+    return 8;  // the wide form: a warp a block, eight CTAs an SM
+}
+
 template <int RM, bool SILU>
 cudaError_t quantize_rm(int8_t* q, float* d, const float* x, size_t xs, uint32_t T, uint32_t n, uint32_t qb,
                         int num_sms, cudaStream_t stream) {
@@ -202,9 +237,9 @@ cudaError_t quantize_rm(int8_t* q, float* d, const float* x, size_t xs, uint32_t
     const bool q8 = reinterpret_cast<uintptr_t>(q) % 8 == 0;
     const int e = qb == 32 ? (q8 ? 8 : 4) : qb == 64 ? (q8 ? PKB_Q64_E : 4) : 0;
     // blocks a 256-thread CTA takes a pass: 8 warps x U chunks x blocks a chunk
-    const size_t per_cta = e ? 8 * (SILU ? PKB_SILU_U : 4) * (32 / (qb / e)) : 8;
+    const size_t per_cta = e ? 8 * (SILU ? PKB_SILU_U : PKB_Q_U) * (32 / (qb / e)) : 8;
     size_t grid = (blocks + per_cta - 1) / per_cta;
-    const size_t cap = static_cast<size_t>(num_sms) * 8;
+    const size_t cap = static_cast<size_t>(num_sms) * resident<RM, SILU>(qb, q8);
     if (grid > cap) grid = cap;
     if (grid == 0) grid = 1;
     const dim3 g(static_cast<unsigned>(grid)), b(256);
@@ -266,6 +301,18 @@ cudaError_t launch_repack_q8(int8_t* wpack, const int8_t* w_pk, uint32_t rows, u
     if (grid == 0) grid = 1;
     return launch_pdl(repack_q8, dim3(static_cast<unsigned>(grid)), dim3(256), 0, stream,
                       reinterpret_cast<uint32_t*>(wpack), reinterpret_cast<const uint32_t*>(w_pk), rows, n);
+}
+
+// Every narrow instance's residency asked once, at the device's set-up
+// (outside any stream capture, before the first launch needs it).
+void prepare_quantize() {
+    for (uint32_t qb : {32u, 64u})
+        for (bool q8 : {false, true}) {
+            resident<0, false>(qb, q8);
+            resident<1, false>(qb, q8);
+            resident<2, false>(qb, q8);
+            resident<3, false>(qb, q8);
+        }
 }
 
 }  // namespace pkb
