@@ -11,7 +11,9 @@
  *
  *  - pkb_*_dev: the same arithmetic on device-resident buffers, enqueued on a
  *    caller's CUDA stream and returning at once; for callers that keep a
- *    batch of segments on the GPU.
+ *    batch of segments on the GPU. The first call on a device sets the
+ *    device up (the kernels' shared-memory limits, their grid sizes); make it
+ *    before capturing a stream into a CUDA graph.
  *
  * Every function returns PKB_OK (0) or a nonzero pkb_status; the message of
  * the calling thread's last failure is pkb_last_error(). Nothing falls back
