@@ -466,8 +466,8 @@ def producers_roofline(model, T: int) -> dict:
 def decoder_batched(model, T: int, segs: int = SEGMENTS, layers: int = 2, P_: int = 640, J: int = 640,
                     vocab_out: int = 8208) -> dict:
     """The TDT decoder's int8 products with the batch's segments stepped in
-    lockstep (SURVEY's "next" row: its T=1 gemvs become products of M = the
-    segment count): one step is, per LSTM layer, quantize + wx (4P x P) and
+    lockstep (core/decoder.c:53-79, 149-156: stepped together, its T=1 gemvs
+    become products of M = the segment count): one step is, per LSTM layer, quantize + wx (4P x P) and
     quantize + wh (4P x P, added), then quantize + jpred (J x P, bias) and
     quantize + jout (vocab + 1 + durations padded to 16 = 8208 x J, bias),
     every input a whole row a block (core/decoder.c:53-79). Timed as one CUDA
@@ -560,9 +560,9 @@ def decoder_batched(model, T: int, segs: int = SEGMENTS, layers: int = 2, P_: in
 
 
 def panels_timing(model, T: int, dk: int = 128) -> dict:
-    """The attention's K and V products straight into its panels (SURVEY's
-    second "next" row: pk_panels_tile and pk_gemm_panels_on,
-    core/passes.c:119-196) at the batch's frame count, against the same
+    """The attention's K and V products straight into its panels
+    (pk_panels_tile and pk_gemm_panels_on, core/passes.c:119-196) at the
+    batch's frame count, against the same
     product into plain rows (D x D, qb 32), each timed with CUDA events."""
     torch, P = model.torch, model.P
     s = torch.cuda.current_stream()
