@@ -55,6 +55,7 @@ D, F, C = 1024, 4096, 256
 QB = 32
 SEED = 20261201
 CONCURRENT = ("q", "k", "v", "pos")  # a layer's products that read no other's results
+CHECK_LAYERS = (-1, 0, LAYERS - 1)  # the subsampling (-1) and the layers whose results are checked
 
 
 # ---------------------------------------------------------------- workload --
@@ -241,14 +242,16 @@ def cpu_baseline(prods, min_s: float = 10.0) -> dict:
 
 class Model:
     """Device-resident weights (PK_Q8 bytes repacked once, as at load time),
-    activations and outputs for one rank's workload."""
+    activations and outputs for one rank's workload. Every product has an
+    output buffer of its own, so that after a step each product's results
+    are still there to be checked."""
 
     def __init__(self, prods, dev, seed):
         import torch
         import libpktito_b200 as P
         self.P, self.torch = P, torch
         g = torch.Generator(device=dev).manual_seed(seed)
-        self.w, self.ws, self.bias = {}, {}, {}
+        self.w, self.ws, self.bias, self.w_pk = {}, {}, {}, {}
         for p in prods:
             key = (p["layer"], p["name"])
             if key in self.w:
@@ -261,28 +264,24 @@ class Model:
             wpack = torch.empty(rows * n, dtype=torch.int8, device=dev)
             P.repack_q8_dev(wpack, w_pk, rows, n)
             self.w[key] = wpack
+            if p["layer"] in CHECK_LAYERS:
+                self.w_pk[key] = w_pk  # the model file's bytes, for the parity check
             self.ws[key] = (1e-3 + 9e-3 * torch.rand(rows, device=dev, generator=g)).float()
             self.bias[key] = torch.randn(rows, device=dev, generator=g) if p["bias"] else None
-        self.x, self.q, self.d, self.out = {}, {}, {}, {}
+        self.x, self.q, self.d = {}, {}, {}
         for p in prods:
             xk = (p["M"], p["n"])
             if xk not in self.x:
                 self.x[xk] = torch.randn(p["M"] * p["n"], device=dev, generator=g)
                 self.q[xk] = torch.empty(p["M"] * p["n"], dtype=torch.int8, device=dev)
                 self.d[xk] = torch.empty(p["M"] * p["n"] // QB, dtype=torch.float32, device=dev)
-            ok = self.out_key(p)
-            if ok not in self.out:
-                self.out[ok] = torch.zeros(p["M"] * p["rows"], device=dev)
+        self.out = [torch.zeros(p["M"] * p["rows"], device=dev) for p in prods]
         self.prods = prods
         # q, k, v and the position product of a layer depend on no one of
         # them (core/encoder.c:347-352): they run side by side on streams of
-        # their own, each into its own output
+        # their own
         self.side = [torch.cuda.Stream(dev) for _ in range(len(CONCURRENT))]
         torch.cuda.synchronize()
-
-    @staticmethod
-    def out_key(p):
-        return (p["M"], p["rows"], p["name"] if p["name"] in CONCURRENT else "")
 
     def step(self):
         P, torch = self.P, self.torch
@@ -295,9 +294,10 @@ class Model:
                 P.quantize_dev(self.q[xk], self.d[xk], self.x[xk], p["n"], p["M"], p["n"], QB, stream=s.cuda_stream)
                 held[xk] = p["inp"]
 
-        def gemm(p, s):
+        def gemm(i, s):
+            p = self.prods[i]
             key, xk = (p["layer"], p["name"]), (p["M"], p["n"])
-            P.gemm_q8_dev(self.out[self.out_key(p)], p["rows"], self.w[key], self.ws[key], self.bias[key], p["rows"],
+            P.gemm_q8_dev(self.out[i], p["rows"], self.w[key], self.ws[key], self.bias[key], p["rows"],
                           self.q[xk], self.d[xk], p["n"], QB, p["M"], bool(p["add"]), stream=s.cuda_stream)
 
         prods = self.prods
@@ -306,19 +306,82 @@ class Model:
             p = prods[i]
             if p["name"] != CONCURRENT[0]:
                 quantize(p, s0)
-                gemm(p, s0)
+                gemm(i, s0)
                 i += 1
                 continue
-            group = prods[i:i + len(CONCURRENT)]
-            assert [g["name"] for g in group] == list(CONCURRENT)
-            for g in group:  # their inputs, once, before the fork
-                quantize(g, s0)
-            for g, s in zip(group, self.side):
+            group = list(range(i, i + len(CONCURRENT)))
+            assert [prods[j]["name"] for j in group] == list(CONCURRENT)
+            for j in group:  # their inputs, once, before the fork
+                quantize(prods[j], s0)
+            for j, s in zip(group, self.side):
                 s.wait_stream(s0)
-                gemm(g, s)
+                gemm(j, s)
             for s in self.side:
                 s0.wait_stream(s)
             i += len(CONCURRENT)
+
+
+def parity_check(model, graph, world: int) -> dict:
+    """Ties the timed step's results to the reference's bits. After the timed
+    region, the step runs once more exactly as it was timed (the same CUDA
+    graph: programmatic dependent launch, q/k/v/pos on side streams, about
+    20 tiles a CTA at the batch's M), and every product of the subsampling
+    and of layers CHECK_LAYERS is compared byte for byte with the
+    reference's own kernels on the same inputs: each product's float input
+    quantized by the reference, its results computed by the reference from
+    those bytes (for the products that add, onto the results the replay
+    found). The checker is the backend the reference's picker chooses on
+    this host (amx-int8 on an AMX Xeon; the reference's q8check holds it to
+    ref's bits), built from its sources into oracle/_ref and run on the
+    host's cores; nothing timed runs through it."""
+    torch = model.torch
+    try:
+        from oracle import oracle as O
+        if not O.have_fast():
+            raise FileNotFoundError("oracle/_ref/libcpubench.so is not built")
+        backend = O.fast_backend()
+    except Exception as e:  # noqa: BLE001
+        return {"checked": 0, "equal": 0, "unavailable": str(e)}
+    prods = model.prods
+    idx = [i for i, p in enumerate(prods) if p["layer"] in CHECK_LAYERS]
+    before = {i: model.out[i].cpu().numpy() for i in idx if prods[i]["add"]}
+    if graph is not None:
+        graph.replay()
+    else:
+        model.step()
+    torch.cuda.synchronize()
+    threads = max(1, (os.cpu_count() or 1) // max(1, world))
+    checked = equal = 0
+    bad = []
+    qd = {}
+    for xk in sorted({(prods[i]["M"], prods[i]["n"]) for i in idx}):
+        M, n = xk
+        q, d = O.fast_quantize(model.x[xk].cpu().numpy(), n, QB, M, threads=threads)
+        same = (np.array_equal(model.q[xk].cpu().numpy().reshape(M, n), q) and
+                model.d[xk].cpu().numpy().tobytes() == d.tobytes())
+        checked += 1
+        equal += int(same)
+        if not same:
+            bad.append(f"quantize M {M} x n {n}")
+        qd[xk] = (q, d)
+    for i in idx:
+        p = prods[i]
+        key, xk = (p["layer"], p["name"]), (p["M"], p["n"])
+        want = before[i].copy() if p["add"] else np.empty(p["M"] * p["rows"], np.float32)
+        b = model.bias[key].cpu().numpy() if model.bias[key] is not None else None
+        O.fast_gemm_q8(want, p["rows"], model.w_pk[key].cpu().numpy(), model.ws[key].cpu().numpy(), b, p["rows"],
+                       qd[xk][0], qd[xk][1], p["n"], QB, p["M"], bool(p["add"]), threads=threads)
+        same = model.out[i].cpu().numpy().tobytes() == want.tobytes()
+        checked += 1
+        equal += int(same)
+        if not same:
+            bad.append(f"{p['name']} layer {p['layer']}")
+    return {"checked": checked, "equal": equal, "products": len(idx), "quantized_inputs": checked - len(idx),
+            "layers": [l for l in CHECK_LAYERS if l >= 0], "subsampling": -1 in CHECK_LAYERS,
+            "path": "the timed CUDA graph replayed once more (PDL, q/k/v/pos on side streams, the batch's M)",
+            "checker": f"the reference's {backend} backend (its picker's choice; held to ref's bits by its own "
+                       "q8check), built from its sources into oracle/_ref, on the host's cores",
+            "mismatches": bad[:8]}
 
 
 def kernel_roofline(model, prods, sm_mhz: float | None) -> dict:
@@ -327,8 +390,9 @@ def kernel_roofline(model, prods, sm_mhz: float | None) -> dict:
     measured peak; beside it the fraction of the fp32 bound its epilogue
     chain has at this qb, and the quantizer's HBM rate on the same input."""
     torch, P = model.torch, model.P
-    p = next(x for x in prods if x["name"] == "ff1_up")
-    key, xk, ok = (p["layer"], p["name"]), (p["M"], p["n"]), model.out_key(p)
+    ok = next(i for i, x in enumerate(prods) if x["name"] == "ff1_up")
+    p = prods[ok]
+    key, xk = (p["layer"], p["name"]), (p["M"], p["n"])
     s = torch.cuda.current_stream()
     for _ in range(3):
         P.gemm_q8_dev(model.out[ok], p["rows"], model.w[key], model.ws[key], None, p["rows"], model.q[xk],
@@ -387,7 +451,32 @@ def kernel_roofline(model, prods, sm_mhz: float | None) -> dict:
     quant = {"ms_per_launch": qms, "gbs": qbytes / (qms * 1e-3) / 1e9, "peak_gbs": hbm,
              "frac": qbytes / (qms * 1e-3) / 1e9 / hbm, "bytes_per_launch": qbytes,
              "shape": f"T {p['M']} x n {p['n']}, qb {QB}"}
+    # fast mode (the reference's qb 64, core/encoder.c:56, core/asr.c:151) on
+    # the same shape: half the epilogue's chain per output
+    fast = None
+    if QB == 32 and p["n"] % 64 == 0:
+        q64 = torch.empty_like(model.q[xk])
+        d64 = torch.empty(p["M"] * p["n"] // 64, device=q64.device)
+        P.quantize_dev(q64, d64, x, p["n"], p["M"], p["n"], 64)
+        run64 = lambda: P.gemm_q8_dev(model.out[ok], p["rows"], model.w[key], model.ws[key], None, p["rows"], q64,
+                                      d64, p["n"], 64, p["M"], False)
+        for _ in range(3):
+            run64()
+        s.synchronize()
+        e0.record(s)
+        for _ in range(reps):
+            run64()
+        e1.record(s)
+        e1.synchronize()
+        ms64 = e0.elapsed_time(e1) / reps
+        a64 = 2.0 * p["M"] * p["rows"] * p["n"] / (ms64 * 1e-3) / 1e12
+        lane64 = 2.0 * p["M"] * p["rows"] * (p["n"] // 64)
+        fast = {"qb": 64, "ms_per_launch": ms64, "achieved": a64, "frac": a64 / peak,
+                "epilogue_fp32_frac": lane64 / (ms64 * 1e-3) / fp32_peak,
+                "note": "the same product in fast mode (blocks of 64), timed alone with CUDA events"}
+        del q64, d64
     return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "fast_mode_qb64": fast,
             "traffic": traffic, "kernel": "pkb::gemm::gemm_q8_kernel",
             "shape": f"M {p['M']} x N {p['rows']} x K {p['n']}, qb {QB}", "ms_per_launch": ms,
             "peak_note": src + "; int8 dense is twice bf16 dense on B200 (4.5 vs 2.25 PFLOP/s nominal)",
@@ -776,6 +865,12 @@ def run_ours(args) -> None:
         raise RuntimeError("a kernel reported a timeout during the timed steps")
     ms, ops_job, audio_job = job_totals(dist, dev, ms, ops, audio_seconds(segs))
     used_graph = graph is not None
+    parity = parity_check(model, graph, world)
+    if dist:  # every rank checked its own share; the job's counts are the sums
+        c = torch.tensor([parity["checked"], parity["equal"]], dtype=torch.float64, device=dev)
+        dist.all_reduce(c, op=dist.ReduceOp.SUM)
+        parity["checked"], parity["equal"] = int(c[0].item()), int(c[1].item())
+        parity["ranks"] = world
     del graph  # released before the process group goes (it holds no collective, but keep the order safe)
     roof = kernel_roofline(model, prods, clk.get("sm_mhz")) if rank == 0 else None
     if roof is not None and not args.no_producers:
@@ -788,7 +883,7 @@ def run_ours(args) -> None:
         # segments; the job's time is the slowest rank's
         if dist:
             dist.barrier(device_ids=[local])
-        e = e2e_host(prods, args.e2e_steps, SEED + 7 + rank, args.e2e_lanes)
+        e = e2e_host(prods, args.e2e_steps or args.steps, SEED + 7 + rank, args.e2e_lanes)
         sec, e_ops, e_audio = job_totals(dist, dev, e["seconds_per_step"], ops, audio_seconds(segs))
         h2d, d2h = job_totals(dist, dev, 0.0, e["h2d_bytes_per_step"], e["d2h_bytes_per_step"])[1:]
         e2e = {"value": e_ops / sec / 1e12, "unit": "TOPS",
@@ -796,7 +891,7 @@ def run_ours(args) -> None:
                "audio_s_per_s": e_audio / sec,
                "path": "pk_kernels_cuda_b200 table (quantize + gemm_q8 on host buffers: activations and results "
                        "page-locked, weights in ordinary memory), whole matrices a call, "
-                       f"{args.e2e_lanes} lanes of calls at once on each rank", "steps": args.e2e_steps,
+                       f"{args.e2e_lanes} lanes of calls at once on each rank", "steps": args.e2e_steps or args.steps,
                "lanes": args.e2e_lanes}
     cpu = cpu_baseline(prods) if (rank == 0 and world == 1 and not args.no_cpu) else None
     if dist:
@@ -816,7 +911,7 @@ def run_ours(args) -> None:
                                 "GPUs longest first" if args.scaling == "strong" else
                                 "configs[3] batched encoder, weak scaling: 64 segments of 2-30 s per GPU") +
                                ", 24 layers x 11 products + 3 subsampling products, 196 quantizations (q, k, v share "
-                               "one input; the position input is quantized once), qb 32",
+                               f"one input; the position input is quantized once), qb {QB}",
                    "segments_rank0": len(segs), "encoder_frames_rank0": t3, "layers": LAYERS, "d_model": D,
                    "ff_dim": F, "qb": QB, "global_batch": nseg, "seq_len": t3 // max(1, len(segs)),
                    "parallelism": f"dp{world}", "l2": "no flush: each step streams 576 MiB of weights and "
@@ -825,38 +920,103 @@ def run_ours(args) -> None:
         "audio_s_per_s": audio_job / (ms_step * 1e-3),
         "ops_per_step": ops_job, "wall_s": wall,
         "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "clocks": clk,
-        "roofline": roof, "cpu_baseline": cpu,
+        "roofline": roof, "cpu_baseline": cpu, "parity": parity,
     }
     print(json.dumps(line))
+    if parity["equal"] != parity["checked"]:
+        print(f"parity: {parity['checked'] - parity['equal']} of {parity['checked']} checks differ from the "
+              f"reference: {parity['mismatches']}", file=sys.stderr)
+        sys.exit(3)
+
+
+def reference_step(prods, seed: int, threads: int):
+    """The step on the reference's own CPU int8 path: the backend its picker
+    chooses on this host (backend/kernels.c:277-305; amx-int8 on an AMX
+    Xeon), built from its sources into oracle/_ref, driven over `threads`
+    threads as its passes deal work (quantize in items of 16 columns,
+    core/passes.c:39-46; products in slices of 64 rows, core/passes.c:60-109).
+    Every product of the step, each input quantized once as the GPU arm does,
+    on seeded random weights and N(0,1) inputs of the same shapes. Returns
+    (step function, backend name) or (None, why)."""
+    import ctypes
+    so = os.path.join(ROOT, "oracle", "_ref", "libcpubench.so")
+    if not os.path.exists(so):
+        return None, "oracle/_ref/libcpubench.so (the reference's backends, built from its sources) is not built"
+    lib = ctypes.CDLL(so)
+    vp, u32, sz = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_size_t
+    lib.cpub_backend.restype = ctypes.c_char_p
+    lib.cpub_backend.argtypes = [ctypes.c_char_p, sz]
+    lib.cpub_quantize.restype = None
+    lib.cpub_quantize.argtypes = [vp, vp, vp, sz, u32, u32, u32, ctypes.c_int]
+    lib.cpub_gemm.restype = None
+    lib.cpub_gemm.argtypes = [vp, sz, vp, vp, vp, u32, vp, vp, u32, u32, u32, ctypes.c_int, ctypes.c_int]
+    backend = lib.cpub_backend(None, 0).decode()
+    rng = np.random.default_rng(seed)
+    w, ws, bias, x, q, d, out = {}, {}, {}, {}, {}, {}, {}
+    for p in prods:
+        key, xk, ok = (p["layer"], p["name"]), (p["M"], p["n"]), (p["M"], p["rows"])
+        if key not in w:
+            w[key] = rng.integers(-127, 128, p["rows"] * p["n"], dtype=np.int8)
+            ws[key] = (1e-3 + 9e-3 * rng.random(p["rows"])).astype(np.float32)
+            bias[key] = rng.standard_normal(p["rows"], dtype=np.float32) if p["bias"] else None
+        if xk not in x:
+            x[xk] = rng.standard_normal(p["M"] * p["n"], dtype=np.float32)
+            q[xk] = np.empty(p["M"] * p["n"], np.int8)
+            d[xk] = np.empty(p["M"] * p["n"] // QB, np.float32)
+        if ok not in out:
+            out[ok] = np.zeros(p["M"] * p["rows"], np.float32)
+    ptr = lambda a: 0 if a is None else a.ctypes.data
+
+    def step():
+        held = {}
+        for p in prods:
+            key, xk, ok = (p["layer"], p["name"]), (p["M"], p["n"]), (p["M"], p["rows"])
+            if held.get(xk) != p["inp"]:
+                lib.cpub_quantize(ptr(q[xk]), ptr(d[xk]), ptr(x[xk]), p["n"], p["n"], QB, p["M"], threads)
+                held[xk] = p["inp"]
+            lib.cpub_gemm(ptr(out[ok]), p["rows"], ptr(w[key]), ptr(ws[key]), ptr(bias[key]), p["rows"], ptr(q[xk]),
+                          ptr(d[xk]), p["n"], QB, p["M"], p["add"], threads)
+
+    return step, backend
 
 
 def run_reference(args) -> None:
+    """The reference arm: the same workload (this arm's rank 0 share at
+    --gpus 1, i.e. the whole batch) through the reference's own CPU int8 path
+    on all host cores, every one of the step's products each step. Under
+    torchrun only rank 0 runs."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     segs = segments(0)
     prods = products(segs)
     ops = step_ops(prods)
-    cpu = None
+    cores = os.cpu_count() or 1
+    step, backend = reference_step(prods, SEED + 77, cores)
+    if step is None:
+        print(json.dumps({"impl": "reference", "unavailable": backend}))
+        return
+    for _ in range(args.warmup):
+        step()
     times = []
-    for i in range(args.warmup + args.steps):
-        c = cpu_baseline(prods, min_s=8.0)
-        if c["value"] is None:
-            print(json.dumps({"impl": "reference", "unavailable": c["sample"]}))
-            return
-        if i >= args.warmup:
-            times.append(c["value"])
-        cpu = c
-    value = float(np.median(times))
-    step_s = ops / (value * 1e12)
-    cpu["value"] = value
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    step_s = float(sum(times)) / len(times)
+    value = ops / step_s / 1e12
+    cpu = {"value": value, "unit": "TOPS", "cores": cores, "kind": "reference", "backend": backend,
+           "sample": f"the whole step ({len(prods)} products and their quantizations at the batch's M) every step, "
+                     f"{args.steps} timed steps after {args.warmup} warm-up steps; median step "
+                     f"{float(np.median(times)):.3f} s"}
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic (seeded segments, random int8 weights, N(0,1) activations)",
-            "config": {"workload": "configs[3] batched encoder (as the GPU arm); each step times the reference's "
-                                   "CPU backend on a sample (subsampling + one layer's products at the batch's M) "
-                                   "and scales to the step", "segments": SEGMENTS, "layers": LAYERS, "qb": QB},
+            "config": {"workload": "configs[3] batched encoder (the GPU arm's whole batch): 64 segments of 2-30 s, "
+                                   "24 layers x 11 products + 3 subsampling products, every product timed every "
+                                   f"step, qb {QB}", "segments": SEGMENTS, "layers": LAYERS, "qb": QB,
+                       "encoder_frames": sum(sg[3] for sg in segs)},
             "audio_s_per_s": audio_seconds(segs) / step_s,
             "cpu_baseline": cpu,
             "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -951,7 +1111,9 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--qb", type=int, choices=[32, 64], default=32,
+                    help="blocks of the activations' quantization: 32, or 64 in the reference's fast mode")
+    ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the e2e leg (default: --steps)")
     ap.add_argument("--e2e-lanes", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -968,6 +1130,8 @@ def main() -> None:
                     help="only the K/V products into plain rows, K panels and V panels, 1 launch each: the ncu "
                          "capture's case")
     args = ap.parse_args()
+    global QB
+    QB = args.qb
     if args.kernel_only:
         run_kernel_only()
     elif args.panels_only:

@@ -97,15 +97,20 @@ int pkb_quantize_host(int8_t *q, float *d, uint32_t n, uint32_t qb, uint32_t T, 
  * rows a multiple of 16, w at its first row), scales ws, optional bias, and
  * the activations q/d of n inputs in blocks of qb. The floats of out between
  * rows and os are left as they were. The matrix is uploaded once and kept on
- * the device, keyed by its host address and checked against a host copy of
- * its bytes on every call; pkb_forget drops it. */
+ * the device, indexed by its host address range (calls on slices of one
+ * matrix share one device copy); each call compares sampled lines of its
+ * weights with the bytes uploaded (the whole range up to 256 KiB) and
+ * uploads them again where they differ. A caller that rewrites or unmaps
+ * weights calls pkb_forget first, as the reference's read-only mapping of
+ * the model never changes while the model is loaded. */
 int pkb_gemm_q8_host(float *out, size_t os, const int8_t *w, const float *ws, const float *bias,
                      uint32_t rows, const int8_t *q, const float *d, uint32_t n, uint32_t qb,
                      uint32_t T, int add, int rmode);
 
 /* Drops every cached matrix whose host bytes overlap [p, p + bytes), on
- * every device; for a caller about to unmap or rewrite weights. Not to be
- * called while another thread runs a product on those weights. */
+ * every device; for a caller about to unmap or rewrite weights. A product
+ * running on those weights meanwhile finishes on the copy it holds, whose
+ * device memory is freed when it returns. */
 int pkb_forget(const void *p, size_t bytes);
 
 /* ------------------------------------------------ device-resident path -- */
@@ -210,11 +215,13 @@ uint64_t pkb_launch_count(void);
  * library holds until the process exits; the columns are copied straight from
  * the caller's memory. T * n * (5 + 4/qb) bytes (each of the three parts
  * rounded up to 256) must fit in it, or the call fails with PKB_EINVAL and
- * does nothing. The first call on a device asks the runtime for the array's
- * address on that device; make it before starting any stream capture. Calls
- * share the array: calls in one process are serialized and each waits for
- * its GPU work before returning, because two calls whose GPU work overlapped
- * would race on it.
+ * does nothing. It runs on the device pkb_set_thread_device bound the calling
+ * thread to (device 0 by default), as the other host-pointer calls do, and
+ * reads the device's error word as they do. The first call on a device asks
+ * the runtime for the array's address on that device; make it before
+ * starting any stream capture. Calls share the array: calls in one process
+ * are serialized and each waits for its GPU work before returning, on every
+ * path, because two calls whose GPU work overlapped would race on it.
  * No counterpart in the reference: its backends never allocate per call. */
 int pkb_quantize_host_noalloc(int8_t *q, float *d, uint32_t n, uint32_t qb, uint32_t T, const float *x,
                               size_t xs, int rmode);

@@ -211,15 +211,19 @@ int gemm_dev(cudaStream_t stream, float* out, size_t os, const int8_t* wpack, co
     g.dk = 0;
     g.tpad = T;
     g.ps = 0;
-    // scales, row scales, biases and results through TMA where their rows
-    // are whole 16-byte units
+    // row scales, biases and results through TMA where their rows are whole
+    // 16-byte units; the block scales too, except for blocks of whole boxes
     CUtensorMap md, mo;
     const CUtensorMap* mdp = nullptr;
     const CUtensorMap* mop = nullptr;
     const uint32_t nb = n / qb;
-    if (nb % 4 == 0 && aligned(d, 16) && os % 4 == 0 && aligned(out, 16) && aligned(ws, 16) &&
+    const bool wide = gemm_wide_blocks(n, qb);
+    if ((wide || (nb % 4 == 0 && aligned(d, 16))) && os % 4 == 0 && aligned(out, 16) && aligned(ws, 16) &&
         (!bias || aligned(bias, 16))) {
-        if ((rc = make_scale_map(&md, d, nb, T))) return rc;
+        if (!wide) {
+            if ((rc = make_scale_map(&md, d, nb, T))) return rc;
+            mdp = &md;
+        }
         cuuint32_t estr[2] = {1, 1};
         cuuint64_t odims[2] = {rows, T};
         cuuint64_t ostrides[1] = {static_cast<cuuint64_t>(os) * 4};
@@ -228,7 +232,6 @@ int gemm_dev(cudaStream_t stream, float* out, size_t os, const int8_t* wpack, co
                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                               CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) return fail(PKB_ECUDA, "cuTensorMapEncodeTiled (results) failed (%d)", static_cast<int>(r));
-        mdp = &md;
         mop = &mo;
     }
     PKB_CUDA(launch_gemm_q8(ma, mb, mdp, mop, g, dev->sms, rmode, stream), "gemm_q8 launch");
@@ -366,9 +369,13 @@ int gemm_panels_dev(cudaStream_t stream, float* panels, int kind, size_t ps, uin
     const CUtensorMap* mdp = nullptr;
     const CUtensorMap* mop = nullptr;
     const uint32_t nb = n / qb;
-    if (nb % 4 == 0 && aligned(d, 16) && aligned(panels, 16) && aligned(ws, 16) &&
+    const bool wide = gemm_wide_blocks(n, qb);
+    if ((wide || (nb % 4 == 0 && aligned(d, 16))) && aligned(panels, 16) && aligned(ws, 16) &&
         (kind == PKB_PANELS_KP || ps % 4 == 0)) {
-        if ((rc = make_scale_map(&md, d, nb, T))) return rc;
+        if (!wide) {
+            if ((rc = make_scale_map(&md, d, nb, T))) return rc;
+            mdp = &md;
+        }
         cuuint32_t estr[4] = {1, 1, 1, 1};
         CUresult r;
         if (kind == PKB_PANELS_V) {
@@ -388,7 +395,6 @@ int gemm_panels_dev(cudaStream_t stream, float* panels, int kind, size_t ps, uin
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         }
         if (r != CUDA_SUCCESS) return fail(PKB_ECUDA, "cuTensorMapEncodeTiled (panels) failed (%d)", static_cast<int>(r));
-        mdp = &md;
         mop = &mo;
     }
     PKB_CUDA(launch_gemm_q8(ma, mb, mdp, mop, g, dev->sms, rmode, stream), "panels launch");

@@ -95,6 +95,7 @@ constexpr int DS_BYTES = BM * DBLK * 4;
 constexpr int WS_BYTES = 2 * BN * 4;  // a tile's row scales, then its biases
 constexpr int NWS = 2;             // slots of their ring (a tile each)
 constexpr int SEED_K = 16;         // K of the bf16 MMA that writes the accumulator's start value
+constexpr int WIDE = 8;            // SPB of the staged path for blocks of whole stages (qb = 256, 384, ...)
 constexpr int SEED_BYTES = 128 * SEED_K * 2;  // one 128-row bf16 operand tile of it
 constexpr int BAR_BYTES = 512;
 constexpr int SMEM_BYTES =
@@ -192,13 +193,17 @@ __device__ __forceinline__ size_t out_at(const GemmArgs& g, uint32_t t, uint32_t
 }
 
 // SPB: K steps a block (1, 2 or 4, with n a multiple of BK: every stage
-// starts a block and holds four K steps), or 0 for any qb and n.
+// starts a block and holds four K steps), WIDE (qb a multiple of BK, at least
+// 2 BK, with n a multiple of BK: a block spans whole stages, as qb = n does
+// for the decoder's and the joint's products), or 0 for any qb and n.
 // OM, where the results go: 0 plain loads and stores (rows or panels by
-// g.pmode, through out_at); otherwise (a multiple of four blocks a tile; the
-// scales' rows, the results' rows and the row scales and biases whole
-// 16-byte units) the block scales come through a TMA ring (map_d), the row
-// scales and biases through a bulk-copy ring, and the results leave through
-// TMA stores of map_o: 1 rows, 2 V panels, 3 K/P panels. The epilogue's loop
+// g.pmode, through out_at); otherwise (the results' rows and the row scales
+// and biases whole 16-byte units) the row scales and biases come through a
+// bulk-copy ring and the results leave through TMA stores of map_o: 1 rows,
+// 2 V panels, 3 K/P panels; and, except on the WIDE path (a few blocks a
+// tile, each hundreds of tensor-core cycles long), the block scales come
+// through a TMA ring (map_d; a multiple of four blocks a tile, the scales'
+// rows whole 16-byte units). The epilogue's loop
 // then holds no global load (on B200 a global load in flight there costs the
 // chain as much as one waited for at once). The panel layouts are separate
 // instances: a run-time choice in the store code cost the rows' instance 9 %
@@ -209,6 +214,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                    const __grid_constant__ CUtensorMap map_d, const __grid_constant__ CUtensorMap map_o,
                    const GemmArgs g) {
     constexpr bool TIO = OM != 0;
+    constexpr bool DRING = TIO && SPB != WIDE;  // block scales through the TMA ring
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float* epi = reinterpret_cast<float*>(smem + NSTAGE * STAGE_BYTES);
@@ -270,10 +276,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (warp == TMA_WARP && lane == 0) {
         tma_prefetch_map(&map_a);
         tma_prefetch_map(&map_b);
-        if constexpr (TIO) {
-            tma_prefetch_map(&map_d);
-            tma_prefetch_map(&map_o);
-        }
+        if constexpr (DRING) tma_prefetch_map(&map_d);
+        if constexpr (TIO) tma_prefetch_map(&map_o);
     }
     tc_fence_before();
     __syncthreads();
@@ -316,7 +320,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 uint32_t dk = 0;  // the tile's next chunk of scales
                 for (uint32_t c = 0; ok && c < nc; c++, it++) {
-                    if constexpr (TIO) {
+                    if constexpr (DRING) {
                         // the scales of every chunk of blocks starting in this
                         // stage's K range, into the scales ring (the box's x,
                         // a multiple of 8 floats, is 16-byte aligned; blocks
@@ -383,7 +387,51 @@ __global__ void __launch_bounds__(THREADS, 1)
             // after the CTA's last block when that one is alone).
             uint32_t blk = 0;  // blocks issued or passed (all tiles)
             auto pair_bar = [&](uint32_t b) { return &tfull[(b >> 1) & 1]; };
-            if constexpr (SPB != 0) {
+            if constexpr (SPB == WIDE) {
+                // Blocks of whole stages: a stage holds four K steps of one
+                // block, unrolled; block b's pair goes to thread (b / 2) & 1,
+                // which issues all its stages; the other thread passes them
+                // (both release every stage).
+                const uint32_t spc = g.qb / BK;  // stages a block
+                for (uint32_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+                    uint32_t kst = 0;  // the stage's place in its block
+                    for (uint32_t c = 0; c < nc && ok; c++) {
+                        if (!mbar_wait(&full[s], sph, abort, limit)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t b = blk;
+                        if (((b >> 1) & 1) == me) {
+                            const uint64_t adesc = desc0 + ((s * STAGE_BYTES) >> 4);
+                            const uint64_t bdesc = adesc + (A_BYTES >> 4);
+                            const uint32_t slot = b & (NTMEM - 1);
+                            const uint32_t ta = tbase + slot * BN;
+                            if (kst == 0) {
+                                if (!mbar_wait(&tempty[slot], ((b >> 2) & 1) ^ 1, abort, limit)) {
+                                    ok = false;
+                                    break;
+                                }
+                                tc_fence_after();
+                                if constexpr (EXACT_SUM) umma_bf16(ta, seed_a, seed_b, sdesc_i, 0u);
+                            }
+#pragma unroll
+                            for (uint32_t j = 0; j < 4; j++)
+                                umma_i8(ta, adesc + 2 * j, bdesc + 2 * j, idesc, EXACT_SUM ? 1u : (kst | j));
+                            if (kst + 1 == spc && (b & 1)) umma_commit(pair_bar(b));
+                        }
+                        umma_commit(&empty[s]);
+                        if (++kst == spc) {
+                            kst = 0;
+                            blk++;
+                        }
+                        if (++s == NSTAGE) {
+                            s = 0;
+                            sph ^= 1;
+                        }
+                    }
+                }
+                if (ok && (blk & 1) && (((blk - 1) >> 1) & 1) == me) umma_commit(pair_bar(blk - 1));
+            } else if constexpr (SPB != 0) {
                 // Staged: every stage starts a block and holds 4 / SPB whole
                 // blocks; pair P goes to thread P & 1, so each thread issues
                 // into two slots of its own and the two threads' MMAs,
@@ -522,7 +570,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
             }
 
-            if constexpr (TIO) {
+            if constexpr (DRING) {
                 // four blocks an iteration, two pairs; the frame's four scales
                 // one 16-byte shared load out of the chunk of eight blocks
                 // the scales ring holds (one wait a chunk)
@@ -815,6 +863,7 @@ static KernelFn pick_om(uint32_t n, uint32_t qb) {
         if (n % BK == 0 && spb == 2) return gemm_q8_kernel<RM, true, OM, 2>;
         if (n % BK == 0 && spb == 4) return gemm_q8_kernel<RM, true, OM, 4>;
     }
+    if (n % BK == 0 && qb % BK == 0 && qb >= 2 * BK) return gemm_q8_kernel<RM, EXACT_SUM, OM, WIDE>;
     return gemm_q8_kernel<RM, EXACT_SUM, OM, 0>;
 }
 
@@ -831,10 +880,10 @@ static KernelFn pick(uint32_t n, uint32_t qb, int om) {
 template <int RM, bool EXACT_SUM>
 static cudaError_t launch_rm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap* md,
                              const CUtensorMap* mo, const GemmArgs& g, int grid, cudaStream_t stream) {
-    const bool tio = md != nullptr && mo != nullptr;
+    const bool tio = mo != nullptr;
     const int om = tio ? 1 + static_cast<int>(g.pmode) : 0;
     const KernelFn kern = pick<RM, EXACT_SUM>(g.n, g.qb, om);
-    return launch_pdl(kern, dim3(grid), dim3(THREADS), SMEM_BYTES, stream, ma, mb, tio ? *md : ma,
+    return launch_pdl(kern, dim3(grid), dim3(THREADS), SMEM_BYTES, stream, ma, mb, md ? *md : ma,
                       tio ? *mo : ma, g);
 }
 
@@ -842,8 +891,9 @@ static cudaError_t launch_rm(const CUtensorMap& ma, const CUtensorMap& mb, const
 template <int RM, bool EXACT_SUM>
 static cudaError_t prepare_rm() {
     for (int om = 0; om < 4; om++) {
-        const KernelFn k[4] = {pick<RM, EXACT_SUM>(BK + 1, 32, om), pick<RM, EXACT_SUM>(BK, 32, om),
-                               pick<RM, EXACT_SUM>(BK, 64, om), pick<RM, EXACT_SUM>(BK, 128, om)};
+        const KernelFn k[5] = {pick<RM, EXACT_SUM>(BK + 1, 32, om), pick<RM, EXACT_SUM>(BK, 32, om),
+                               pick<RM, EXACT_SUM>(BK, 64, om), pick<RM, EXACT_SUM>(BK, 128, om),
+                               pick<RM, EXACT_SUM>(BK, 2 * BK, om)};
         for (auto f : k) {
             cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
             if (e != cudaSuccess) return e;
@@ -859,6 +909,9 @@ int gemm_tile_cols() { return gemm::BN; }
 int gemm_box_k() { return gemm::BK; }
 
 int gemm_out_box() { return 32; }
+bool gemm_wide_blocks(uint32_t n, uint32_t qb) {
+    return n % gemm::BK == 0 && qb % gemm::BK == 0 && qb >= 2 * gemm::BK;
+}
 int gemm_scale_box() { return gemm::DBLK; }
 
 cudaError_t prepare_gemm_q8() {

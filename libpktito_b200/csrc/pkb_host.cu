@@ -22,8 +22,9 @@
 // (the reference's pool calls a backend from every worker, core/pool.c:
 // 115-122, on disjoint outputs): each calling thread has its own streams and
 // staging, grown as needed and kept; matrices are uploaded once per device
-// and shared, keyed by host address and checked against a host copy of their
-// bytes on every call.
+// and shared, indexed by host address range, the slices of one matrix
+// absorbed into one device copy, and every call checks sampled lines of its
+// weights against the bytes uploaded (the matrices section below).
 
 #include <cuda_runtime.h>
 
@@ -35,7 +36,9 @@
 #include <deque>
 #include <functional>
 #include <memory>
+#include <map>
 #include <mutex>
+#include <shared_mutex>
 #include <thread>
 #include <vector>
 
@@ -93,18 +96,6 @@ class CopyPool {
             const size_t b0 = (bytes * p / parts) & ~size_t(63), b1 = p + 1 == parts ? bytes : (bytes * (p + 1) / parts) & ~size_t(63);
             memcpy(static_cast<char*>(dst) + b0, static_cast<const char*>(src) + b0, b1 - b0);
         });
-    }
-
-    bool equal(const void* a, const void* b, size_t bytes) {
-        std::atomic<bool> same{true};
-        const int parts = split(bytes, bytes / 4096 + 1);
-        run(parts, [&](int p) {
-            const size_t b0 = (bytes * p / parts) & ~size_t(63), b1 = p + 1 == parts ? bytes : (bytes * (p + 1) / parts) & ~size_t(63);
-            if (same.load(std::memory_order_relaxed) &&
-                memcmp(static_cast<const char*>(a) + b0, static_cast<const char*>(b) + b0, b1 - b0))
-                same = false;
-        });
-        return same;
     }
 
   private:
@@ -350,75 +341,227 @@ uint32_t chunk_frames(uint32_t T, size_t in_per_frame, size_t out_per_frame) {
 }
 
 // ------------------------------------------------------------- matrices --
+//
+// Weights are uploaded once per device and kept. A call names a run of whole
+// 16-row panels (w at a panel boundary, rows a multiple of 16) of a PK_Q8
+// matrix in host memory, often from inside it (the reference's passes call
+// with w + r0 * cols, core/passes.c:60-72). The repack is panel-local: the
+// rows of panel p, repacked, occupy the same bytes the panel did. So a device
+// copy of host bytes [lo, hi) serves any call whose range lies inside it in
+// the same panel phase, and the slices of one matrix, whatever their order
+// and size, are absorbed into one device copy as they arrive: a slice next
+// to or over an existing copy makes a copy of the union, the old rows moved
+// device to device, only the new slice's bytes uploaded.
+//
+// Each call checks that its host bytes are still the ones uploaded by
+// comparing sampled 64-byte lines with the host copy kept at upload (a
+// fixed number a call, at positions that move from call to call, so the
+// cost is O(1) and repeated calls cover the whole range; ranges up to
+// FULL_CHECK bytes are compared whole). Bytes that differ retire the copy
+// and the call uploads its range again. The reference's weights are a
+// read-only mapping of the model file that lives until the model is freed;
+// a caller that rewrites weights in place, or unmaps them, calls pkb_forget
+// first.
 
-// A matrix uploaded to one device: the host bytes it came from, a copy of
-// them to tell whether they still are what was uploaded, and its repacked
-// rows on the device.
-struct Matrix {
-    const int8_t* host;
-    uint32_t rows, n;
-    int dev;
-    std::vector<int8_t> shadow;
-    int8_t* wpack;
+constexpr size_t LINE = 64;              // bytes a sampled line
+constexpr int SAMPLES = 32;              // lines checked a call
+constexpr size_t FULL_CHECK = 256 << 10; // ranges compared whole up to this
+
+// Device memory freed when the last call that uses it returns.
+struct DevBuf {
+    int dev = -1;
+    int8_t* p = nullptr;
+    ~DevBuf() {
+        if (!p) return;
+        int cur = -1;
+        if (cudaGetDevice(&cur) != cudaSuccess) return;  // the runtime is gone at exit
+        cudaSetDevice(dev);
+        cudaFree(p);
+        cudaSetDevice(cur);
+    }
 };
 
-std::mutex g_mat_mu;
-std::vector<Matrix*> g_mats;
-std::vector<Matrix*> g_stale;  // replaced while maybe in use elsewhere: freed by pkb_forget
+// A device copy of host bytes [lo, hi): panels of 16 rows of n, repacked.
+struct Matrix {
+    uintptr_t lo, hi;
+    uint32_t n;
+    std::shared_ptr<DevBuf> buf;
+    std::atomic<uint32_t> probe{0};  // moves the sampled lines from call to call
+};
+
+// Host bytes as they were uploaded, in pieces over disjoint ranges.
+struct Piece {
+    uintptr_t hi;
+    std::shared_ptr<std::vector<int8_t>> bytes;
+};
+
+struct DeviceCache {
+    std::shared_mutex mu;  // the two maps
+    std::map<uintptr_t, std::shared_ptr<Matrix>> mats;  // by lo; disjoint
+    std::map<uintptr_t, Piece> pieces;                  // by lo; disjoint
+    std::mutex upload_mu;  // one upload at a time on the device
+};
+
+DeviceCache g_cache[MAX_DEV];
+
+// The matrix copy holding [a, a + bytes) of n-input rows in its panel
+// phase, or null. Under at least a shared lock.
+std::shared_ptr<Matrix> find_copy(DeviceCache& c, uintptr_t a, size_t bytes, uint32_t n) {
+    auto it = c.mats.upper_bound(a);
+    if (it == c.mats.begin()) return nullptr;
+    --it;
+    const std::shared_ptr<Matrix>& m = it->second;
+    if (m->n != n || a + bytes > m->hi || (a - m->lo) % (16 * static_cast<size_t>(n))) return nullptr;
+    return m;
+}
+
+// Whether host bytes [p, p + len) equal the uploaded ones. Under at least a
+// shared lock.
+bool same_as_uploaded(DeviceCache& c, uintptr_t p, size_t len) {
+    while (len) {
+        auto it = c.pieces.upper_bound(p);
+        if (it == c.pieces.begin()) return false;
+        --it;
+        if (p >= it->second.hi) return false;
+        const size_t take = std::min(len, static_cast<size_t>(it->second.hi - p));
+        if (memcmp(reinterpret_cast<const void*>(p), it->second.bytes->data() + (p - it->first), take)) return false;
+        p += take;
+        len -= take;
+    }
+    return true;
+}
+
+bool still_uploaded(DeviceCache& c, Matrix& m, uintptr_t a, size_t bytes) {
+    if (bytes <= FULL_CHECK) return same_as_uploaded(c, a, bytes);
+    const size_t lines = bytes / LINE;
+    const uint32_t k = m.probe.fetch_add(1, std::memory_order_relaxed);
+    // the first and last lines, and lines spread evenly from an offset that
+    // advances by a large odd step each call
+    if (!same_as_uploaded(c, a, LINE) || !same_as_uploaded(c, a + bytes - LINE, LINE)) return false;
+    const size_t stride = lines / (SAMPLES - 2);
+    const size_t off = (static_cast<size_t>(k) * 0x9E3779B1u) % (stride ? stride : 1);
+    for (int i = 0; i < SAMPLES - 2; i++) {
+        const size_t line = off + i * stride;
+        if (line >= lines) break;
+        if (!same_as_uploaded(c, a + line * LINE, LINE)) return false;
+    }
+    return true;
+}
+
+// Drops the pieces' bytes over [lo, hi), keeping what lies outside. Under
+// the exclusive lock.
+void drop_pieces(DeviceCache& c, uintptr_t lo, uintptr_t hi) {
+    auto it = c.pieces.upper_bound(lo);
+    if (it != c.pieces.begin()) --it;
+    std::vector<std::pair<uintptr_t, Piece>> keep;
+    while (it != c.pieces.end() && it->first < hi) {
+        const uintptr_t plo = it->first, phi = it->second.hi;
+        if (phi <= lo) {
+            ++it;
+            continue;
+        }
+        const int8_t* src = it->second.bytes->data();
+        if (plo < lo)
+            keep.push_back({plo, Piece{lo, std::make_shared<std::vector<int8_t>>(src, src + (lo - plo))}});
+        if (phi > hi)
+            keep.push_back({hi, Piece{phi, std::make_shared<std::vector<int8_t>>(src + (hi - plo), src + (phi - plo))}});
+        it = c.pieces.erase(it);
+    }
+    for (auto& k : keep) c.pieces.emplace(k.first, std::move(k.second));
+}
 
 // The device rows for `rows` rows of the PK_Q8 matrix at host address w (a
-// run of whole panels, possibly from inside a matrix uploaded before).
-int weights_for(Pipe& p, const int8_t* w, uint32_t rows, uint32_t n, const int8_t** wpack) {
-    const size_t bytes = static_cast<size_t>(rows) * n;
-    Matrix* hit = nullptr;
-    size_t row0 = 0;
+// run of whole panels, possibly from inside a matrix), and the copy that
+// holds them, which the caller keeps until its kernels have run.
+int weights_for(Pipe& p, const int8_t* w, uint32_t rows, uint32_t n, const int8_t** wpack,
+                std::shared_ptr<Matrix>* hold) {
+    DeviceCache& c = g_cache[p.dev];
+    const uintptr_t a = reinterpret_cast<uintptr_t>(w);
+    const size_t bytes = static_cast<size_t>(rows) * n, panel = 16 * static_cast<size_t>(n);
     {
-        std::lock_guard<std::mutex> lock(g_mat_mu);
-        for (Matrix* m : g_mats) {
-            if (m->dev != p.dev || m->n != n) continue;
-            const uintptr_t lo = reinterpret_cast<uintptr_t>(m->host);
-            const uintptr_t a = reinterpret_cast<uintptr_t>(w);
-            if (a < lo || a + bytes > lo + static_cast<size_t>(m->rows) * n) continue;
-            if ((a - lo) % (16 * static_cast<size_t>(n))) continue;  // not on a panel boundary
-            hit = m;
-            row0 = (a - lo) / n;
-            break;
+        std::shared_lock<std::shared_mutex> lock(c.mu);
+        std::shared_ptr<Matrix> m = find_copy(c, a, bytes, n);
+        if (m && still_uploaded(c, *m, a, bytes)) {
+            *wpack = m->buf->p + (a - m->lo);
+            *hold = std::move(m);
+            return PKB_OK;
         }
     }
-    if (hit && CopyPool::get().equal(hit->shadow.data() + row0 * n, w, bytes)) {
-        *wpack = hit->wpack + row0 * n;
-        return PKB_OK;
-    }
-    if (hit) {  // the bytes at that address changed: retire the old upload
-        std::lock_guard<std::mutex> lock(g_mat_mu);
-        for (size_t i = 0; i < g_mats.size(); i++)
-            if (g_mats[i] == hit) {
-                g_mats.erase(g_mats.begin() + static_cast<long>(i));
-                g_stale.push_back(hit);
-                break;
+    std::lock_guard<std::mutex> up(c.upload_mu);
+    std::vector<std::shared_ptr<Matrix>> merge;  // the copies the new one absorbs
+    {
+        std::unique_lock<std::shared_mutex> lock(c.mu);
+        // another thread may have uploaded it meanwhile
+        std::shared_ptr<Matrix> m = find_copy(c, a, bytes, n);
+        if (m && still_uploaded(c, *m, a, bytes)) {
+            *wpack = m->buf->p + (a - m->lo);
+            *hold = std::move(m);
+            return PKB_OK;
+        }
+        if (m) {  // its bytes changed: retire the copy and what was kept of its bytes
+            drop_pieces(c, m->lo, m->hi);
+            c.mats.erase(m->lo);
+        }
+        // copies that overlap or touch [a, a + bytes) in its panel phase
+        // join it; any other overlapping copy (another n or phase) is retired
+        auto it = c.mats.upper_bound(a);
+        if (it != c.mats.begin()) --it;
+        while (it != c.mats.end() && it->first <= a + bytes) {
+            const std::shared_ptr<Matrix>& o = it->second;
+            if (o->hi < a) {
+                ++it;
+                continue;
             }
+            const bool joins = o->n == n && (a > o->lo ? a - o->lo : o->lo - a) % panel == 0;
+            const bool overlaps = o->lo < a + bytes && a < o->hi;
+            if (joins) {
+                merge.push_back(o);
+                it = c.mats.erase(it);
+            } else if (overlaps) {
+                drop_pieces(c, o->lo, o->hi);
+                it = c.mats.erase(it);
+            } else {
+                ++it;
+            }
+        }
     }
-    Matrix* m = new Matrix{w, rows, n, p.dev, std::vector<int8_t>(bytes), nullptr};
-    CopyPool::get().copy(m->shadow.data(), w, bytes);
-    cudaError_t e = cudaMalloc(&m->wpack, bytes);
-    if (e != cudaSuccess) {
-        delete m;
-        return cuda_err(e, "cudaMalloc (weights)");
+    uintptr_t lo = a, hi = a + bytes;
+    for (auto& o : merge) {
+        lo = std::min(lo, o->lo);
+        hi = std::max(hi, o->hi);
     }
-    // the panels through slot 0's staging, repacked into place
+    auto m = std::make_shared<Matrix>();
+    m->lo = lo;
+    m->hi = hi;
+    m->n = n;
+    m->buf = std::make_shared<DevBuf>();
+    m->buf->dev = p.dev;
+    HOST_CUDA(cudaMalloc(&m->buf->p, hi - lo), "cudaMalloc (weights)");
+    // the absorbed copies' rows, device to device, then this range's panels
+    // through slot 0's staging, repacked into place
     int rc = p.reserve(bytes, 0, 0);
     if (rc) return rc;
     HOST_CUDA(cudaStreamSynchronize(p.s_in), "cudaStreamSynchronize");
     HOST_CUDA(cudaStreamSynchronize(p.s_comp), "cudaStreamSynchronize");
-    CopyPool::get().copy(p.pin_in[0], w, bytes);
+    for (auto& o : merge)
+        HOST_CUDA(cudaMemcpyAsync(m->buf->p + (o->lo - lo), o->buf->p, o->hi - o->lo, cudaMemcpyDeviceToDevice,
+                                  p.s_comp),
+                  "weights move");
+    auto shadow = std::make_shared<std::vector<int8_t>>(bytes);
+    CopyPool::get().copy(shadow->data(), w, bytes);
+    CopyPool::get().copy(p.pin_in[0], shadow->data(), bytes);
     HOST_CUDA(cudaMemcpyAsync(p.dev_in[0], p.pin_in[0], bytes, cudaMemcpyHostToDevice, p.s_comp), "weights upload");
-    if ((rc = pkb_repack_q8_dev(p.s_comp, m->wpack, reinterpret_cast<int8_t*>(p.dev_in[0]), rows, n))) return rc;
+    if ((rc = pkb_repack_q8_dev(p.s_comp, m->buf->p + (a - lo), reinterpret_cast<int8_t*>(p.dev_in[0]), rows, n)))
+        return rc;
     HOST_CUDA(cudaStreamSynchronize(p.s_comp), "weights upload");
     {
-        std::lock_guard<std::mutex> lock(g_mat_mu);
-        g_mats.push_back(m);
+        std::unique_lock<std::shared_mutex> lock(c.mu);
+        drop_pieces(c, a, a + bytes);
+        c.pieces.emplace(a, Piece{a + bytes, std::move(shadow)});
+        c.mats.emplace(lo, m);
     }
-    *wpack = m->wpack;
+    *wpack = m->buf->p + (a - lo);
+    *hold = std::move(m);
     return PKB_OK;
 }
 
@@ -441,6 +584,9 @@ int check_shape(uint32_t n, uint32_t qb, int rmode) {
 }
 
 }  // namespace
+
+int thread_device() { return tl_device; }
+
 }  // namespace pkb
 
 using namespace pkb;
@@ -547,7 +693,8 @@ int pkb_gemm_q8_host(float* out, size_t os, const int8_t* w, const float* ws, co
     uint32_t* err;
     if ((rc = open_pipe(&p, &err))) return rc;
     const int8_t* wpack;
-    if ((rc = weights_for(*p, w, rows, n, &wpack))) return rc;
+    std::shared_ptr<Matrix> held;  // the weights' device copy, kept for the call
+    if ((rc = weights_for(*p, w, rows, n, &wpack, &held))) return rc;
     const uint32_t nb = n / qb;
     const size_t qrow = n, drow = static_cast<size_t>(nb) * 4, orow = static_cast<size_t>(rows) * 4;
     const uint32_t TC = chunk_frames(T, qrow + drow + (add ? orow : 0), orow);
@@ -645,33 +792,23 @@ int pkb_gemm_q8_host(float* out, size_t os, const int8_t* w, const float* ws, co
 }
 
 int pkb_forget(const void* ptr, size_t bytes) {
+    // the copies overlapping the range leave the cache at once; their device
+    // memory goes when the last call still using it returns
     const uintptr_t lo = reinterpret_cast<uintptr_t>(ptr), hi = lo + bytes;
-    std::vector<Matrix*> drop;
-    {
-        std::lock_guard<std::mutex> lock(g_mat_mu);
-        for (size_t i = 0; i < g_mats.size();) {
-            Matrix* m = g_mats[i];
-            const uintptr_t mlo = reinterpret_cast<uintptr_t>(m->host);
-            const uintptr_t mhi = mlo + static_cast<size_t>(m->rows) * m->n;
-            if (mlo < hi && lo < mhi) {
-                drop.push_back(m);
-                g_mats.erase(g_mats.begin() + static_cast<long>(i));
+    std::vector<std::shared_ptr<Matrix>> drop;
+    for (DeviceCache& c : g_cache) {
+        std::unique_lock<std::shared_mutex> lock(c.mu);
+        for (auto it = c.mats.begin(); it != c.mats.end();) {
+            if (it->second->lo < hi && lo < it->second->hi) {
+                drop_pieces(c, it->second->lo, it->second->hi);
+                drop.push_back(std::move(it->second));
+                it = c.mats.erase(it);
             } else {
-                i++;
+                ++it;
             }
         }
-        drop.insert(drop.end(), g_stale.begin(), g_stale.end());
-        g_stale.clear();
+        drop_pieces(c, lo, hi);
     }
-    int cur = -1;
-    cudaGetDevice(&cur);
-    for (Matrix* m : drop) {
-        cudaSetDevice(m->dev);
-        cudaDeviceSynchronize();
-        cudaFree(m->wpack);
-        delete m;
-    }
-    if (cur >= 0) cudaSetDevice(cur);
     return PKB_OK;
 }
 

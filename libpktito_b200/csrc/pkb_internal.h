@@ -19,6 +19,10 @@ int current_device_info(int* sms, uint32_t** err_word);
 // One more kernel launched (pkb_launch_count).
 void count_launch();
 
+// The device the calling thread's host-pointer calls run on
+// (pkb_set_thread_device; 0 until set).
+int thread_device();
+
 // Arguments of the product kernel (pkb_gemm.cu) besides its two tensor maps.
 struct GemmArgs {
     float* out;            // out[t*os + r]
@@ -50,13 +54,19 @@ cudaError_t prepare_gemm_q8();
 // gemm_scale_box() blocks by gemm_tile_rows() frames); map_o: one of the
 // results out [T][rows] (float32, row stride os, boxes of gemm_out_box() by
 // gemm_out_box(), 128-byte swizzle), or for pmode 1 and 2 one of the panels
-// (3-D for V, 4-D for K/P, laid out as the kernel stages them). Both are
-// given only where n / qb is a multiple of 4 and d, out, ws and bias are
-// 16-byte aligned, os (V: ps) a multiple of 4; the kernel then moves scales,
-// row scales, biases and results with TMA. Null: plain loads and stores.
+// (3-D for V, 4-D for K/P, laid out as the kernel stages them). map_o is
+// given only where out, ws and bias are 16-byte aligned and os (V: ps) a
+// multiple of 4: the kernel then moves row scales, biases and results with
+// TMA; and with it map_d, where n / qb is a multiple of 4 and d 16-byte
+// aligned, except for blocks of whole TMA boxes (gemm_wide_blocks), whose
+// few scales a tile are plain loads. Null: plain loads and stores.
 cudaError_t launch_gemm_q8(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap* map_d,
                            const CUtensorMap* map_o, const GemmArgs& g, int num_sms, int rmode, cudaStream_t stream);
 int gemm_out_box();     // frames and output rows of a TMA box of the results
+// Whether the product runs blocks of whole TMA boxes along K (qb a multiple
+// of gemm_box_k(), at least twice it, n a multiple of it): its block scales
+// are then not moved by TMA.
+bool gemm_wide_blocks(uint32_t n, uint32_t qb);
 int gemm_scale_box();   // blocks of scales a TMA box of them carries
 
 // Launches `kern` on `stream` with programmatic stream serialization allowed

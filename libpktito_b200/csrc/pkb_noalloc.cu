@@ -38,7 +38,6 @@ constexpr int MAX_DEV = 16;
 
 std::mutex g_noalloc_mu;
 unsigned char* g_noalloc_ptr[MAX_DEV];  // the array's device address, per device
-int g_noalloc_sms[MAX_DEV];
 bool g_noalloc_ready[MAX_DEV];
 
 int refuse(int code, const char* msg) { return pkb::set_error(code, "quantize (no allocation): %s", msg); }
@@ -63,19 +62,22 @@ extern "C" int pkb_quantize_host_noalloc(int8_t* q, float* d, uint32_t n, uint32
                                   "each part rounded up to 256, must fit in PKB_NOALLOC_BYTES)");
 
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEV)
-        return refuse(PKB_ENODEV, "no CUDA device");
+    // the device this thread's host-pointer calls run on
+    // (pkb_set_thread_device), made current as every host-pointer call does
+    const int dev = pkb::thread_device();
+    if (dev < 0 || dev >= MAX_DEV) return refuse(PKB_ENODEV, "device out of range");
+    if (cudaSetDevice(dev) != cudaSuccess) return refuse(PKB_ENODEV, "cudaSetDevice failed");
+    int sms = 0;
+    uint32_t* err_word = nullptr;
+    // the library's own set-up of the device (kernel attributes, the error
+    // word's address), once per device; allocates nothing
+    if (const int rc = pkb::current_device_info(&sms, &err_word)) return rc;
     if (!g_noalloc_ready[dev]) {
         // once per device, with it current: the array's device address
-        cudaDeviceProp prop;
-        if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess || prop.major != 10)
-            return refuse(PKB_ENODEV, "not an sm_100 device");
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p)
             return refuse(PKB_ECUDA, "cudaGetSymbolAddress of the fixed staging failed");
         g_noalloc_ptr[dev] = static_cast<unsigned char*>(p);
-        g_noalloc_sms[dev] = prop.multiProcessorCount;
         g_noalloc_ready[dev] = true;
     }
     unsigned char* base = g_noalloc_ptr[dev];
@@ -86,10 +88,24 @@ extern "C" int pkb_quantize_host_noalloc(int8_t* q, float* d, uint32_t n, uint32
     // the columns, n floats each, straight from the caller's memory
     cudaError_t e = cudaMemcpy2DAsync(dx, static_cast<size_t>(n) * 4, x, xs * 4, static_cast<size_t>(n) * 4, T,
                                       cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) e = pkb::launch_quantize(dq, dd, dx, n, T, n, qb, rmode, g_noalloc_sms[dev], s);
+    if (e == cudaSuccess) {
+        e = pkb::launch_quantize(dq, dd, dx, n, T, n, qb, rmode, sms, s);
+        if (e == cudaSuccess) pkb::count_launch();
+    }
     if (e == cudaSuccess) e = cudaMemcpyAsync(q, dq, qbytes, cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess) e = cudaMemcpyAsync(d, dd, dbytes, cudaMemcpyDeviceToHost, s);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    // the device's error word, as every host-pointer call reads it
+    uint32_t word = 0;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&word, err_word, sizeof word, cudaMemcpyDeviceToHost, s);
+    // on every path, the GPU work this call enqueued ends before the lock is
+    // dropped: another call must not find the array still in use
+    const cudaError_t e_sync = cudaStreamSynchronize(s);
+    if (e == cudaSuccess) e = e_sync;
     if (e != cudaSuccess) return pkb::set_error(PKB_ECUDA, "quantize (no allocation): %s", cudaGetErrorString(e));
+    if (word) {
+        const uint32_t zero = 0;
+        cudaMemcpy(err_word, &zero, sizeof zero, cudaMemcpyHostToDevice);
+        return pkb::set_error(PKB_ETIMEOUT, "quantize (no allocation): device error word 0x%x", word);
+    }
     return PKB_OK;
 }

@@ -56,9 +56,12 @@ int cpub_cores(void) { return pk_os_cores(); }
 
 typedef struct {
     float *out;
+    size_t os;
     const int8_t *w;
     const float *ws;
+    const float *bias;
     const float *x;
+    size_t xs;
     pk_act a;
     uint32_t rows;
     int add;
@@ -80,7 +83,7 @@ static void *worker(void *arg) {
             sub.q += (size_t)t0 * n;
             sub.d += (size_t)t0 * nb;
             sub.T = j->a.T - t0 < 16 ? j->a.T - t0 : 16;
-            pk_k_quantize(&sub, j->x + (size_t)t0 * n, n);
+            pk_k_quantize(&sub, j->x + (size_t)t0 * j->xs, j->xs);
         }
     }
     const uint32_t slices = (j->rows + 63) / 64;
@@ -89,7 +92,8 @@ static void *worker(void *arg) {
         if (i >= slices)
             return NULL;
         const uint32_t r0 = i * 64, nr = j->rows - r0 < 64 ? j->rows - r0 : 64;
-        pk_k_gemm_q8(j->out + r0, j->rows, j->w + (size_t)r0 * n, j->ws + r0, NULL, nr, &j->a, j->add);
+        pk_k_gemm_q8(j->out + r0, j->os, j->w + (size_t)r0 * n, j->ws + r0, j->bias ? j->bias + r0 : NULL, nr,
+                     &j->a, j->add);
     }
 }
 
@@ -97,6 +101,8 @@ static void run_phase(job *j, int phase, int threads) {
     pthread_t th[512];
     if (threads > 512)
         threads = 512;
+    if (threads < 1)
+        threads = 1;
     j->phase = phase;
     atomic_store(&j->next, 0);
     for (int k = 1; k < threads; k++)
@@ -104,6 +110,26 @@ static void run_phase(job *j, int phase, int threads) {
     worker(j);
     for (int k = 1; k < threads; k++)
         pthread_join(th[k], NULL);
+}
+
+/* The picked backend's quantize of T columns of n floats (column t at
+ * x + t*xs) in blocks of qb, in items of 16 columns over `threads` threads,
+ * as pk_quantize_on deals them (core/passes.c:39-46). */
+void cpub_quantize(int8_t *q, float *d, const float *x, size_t xs, uint32_t n, uint32_t qb, uint32_t T,
+                   int threads) {
+    job j = { NULL, 0, NULL, NULL, NULL, x, xs, { q, d, n, qb, T }, 0, 0, 0, 0 };
+    run_phase(&j, 0, threads);
+}
+
+/* The picked backend's product (pk_k_gemm_q8's contract, backend/kernels.h:
+ * 60-78) with rows x n PK_Q8 weights w, in slices of 64 rows dealt to
+ * `threads` threads from an atomic counter, as pk_gemm_on deals them
+ * (core/passes.c:60-109); every output is one call's, so the bits do not
+ * depend on the split. */
+void cpub_gemm(float *out, size_t os, const int8_t *w, const float *ws, const float *bias, uint32_t rows,
+               const int8_t *q, const float *d, uint32_t n, uint32_t qb, uint32_t T, int add, int threads) {
+    job j = { out, os, w, ws, bias, NULL, 0, { (int8_t *)q, (float *)d, n, qb, T }, rows, add, 0, 1 };
+    run_phase(&j, 1, threads);
 }
 
 /* Quantize T columns of n floats ~N(0,1) in blocks of qb, then the product
@@ -126,7 +152,7 @@ double cpub_time(uint32_t rows, uint32_t n, uint32_t T, uint32_t qb, int add, in
         ws[r] = 1e-3f + 9e-3f * (float)(next32(&s) >> 8) / 16777216.0f;
     for (size_t i = 0; i < (size_t)T * n; i++)
         x[i] = gauss(&s);
-    job j = { out, w, ws, x, { q, d, n, qb, T }, rows, add, 0, 0 };
+    job j = { out, rows, w, ws, NULL, x, n, { q, d, n, qb, T }, rows, add, 0, 0 };
     double best = 1e30, bestq = 0;
     for (int rep = 0; rep <= reps; rep++) {
         const double t0 = now_s();

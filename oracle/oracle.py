@@ -33,12 +33,27 @@ _or = None
 _ref = None
 
 
+def reference_tree() -> Optional[str]:
+    """The reference's source tree, where this machine has it: the
+    PKTITO_REFERENCE environment variable, else the reference_path the
+    checkout's BASELINE.json names; None where neither is a directory."""
+    path = os.environ.get("PKTITO_REFERENCE")
+    if not path:
+        try:
+            import json
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+                path = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            path = None
+    return path if path and os.path.isdir(path) else None
+
+
 def build() -> None:
     """liboracle.so always; the reference's code too where its sources are here."""
     subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
-    if os.path.isdir(os.environ.get("PKTITO_REFERENCE", "/root/reference")):
-        subprocess.run(["make", "-s", "-C", HERE, "ref",
-                        "REF=" + os.environ.get("PKTITO_REFERENCE", "/root/reference")], check=True)
+    ref = reference_tree()
+    if ref:
+        subprocess.run(["make", "-s", "-C", HERE, "ref", "REF=" + ref], check=True)
 
 
 def _p(a: Optional[np.ndarray]) -> int:
@@ -264,6 +279,64 @@ def ref_gemm_q8(out: np.ndarray, os_: int, w: np.ndarray, ws: np.ndarray, bias: 
     act = _Act(_p(q), _p(d), n, qb, T)
     k = _Table.in_dll(rlib(), "pk_kernels_ref")
     _with_mode(rmode, lambda: k.gemm_q8(_p(out), os_, _p(w), _p(ws), _p(bias), rows, ctypes.byref(act), int(add)))
+
+
+# ------------------------------- the reference's fastest backend, threaded --
+#
+# For checks at full size (the benchmark's M of 11,521 frames), where ref's
+# scalar loops would take minutes: the backend the reference's own picker
+# chooses on this CPU (amx-int8 on an AMX Xeon, backend/kernels.c:277-305),
+# which the reference's q8check holds to ref's bits byte for byte, driven over
+# all host cores the way its passes deal work (oracle/cpu_bench.c).
+
+CPUBENCH_SO = os.path.join(REF_DIR, "libcpubench.so")
+_cpub = None
+
+
+def have_fast() -> bool:
+    return os.path.exists(CPUBENCH_SO)
+
+
+def _cpublib() -> ctypes.CDLL:
+    global _cpub
+    if _cpub is None:
+        if not have_fast():
+            raise FileNotFoundError(CPUBENCH_SO + " is not built (make -C oracle ref)")
+        l = ctypes.CDLL(CPUBENCH_SO)
+        vp, u32, sz = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_size_t
+        l.cpub_backend.restype = ctypes.c_char_p
+        l.cpub_backend.argtypes = [ctypes.c_char_p, sz]
+        l.cpub_quantize.restype = None
+        l.cpub_quantize.argtypes = [vp, vp, vp, sz, u32, u32, u32, ctypes.c_int]
+        l.cpub_gemm.restype = None
+        l.cpub_gemm.argtypes = [vp, sz, vp, vp, vp, u32, vp, vp, u32, u32, u32, ctypes.c_int, ctypes.c_int]
+        l.cpub_backend(None, 0)  # the picker runs once, before any thread calls a kernel
+        _cpub = l
+    return _cpub
+
+
+def fast_backend() -> str:
+    return _cpublib().cpub_backend(None, 0).decode()
+
+
+def fast_quantize(x: np.ndarray, n: int, qb: int, T: int, xs: Optional[int] = None,
+                  threads: Optional[int] = None) -> tuple[np.ndarray, np.ndarray]:
+    """The picked backend's quantize (round to nearest), over all cores."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    q = np.empty((T, n), np.int8)
+    d = np.empty((T, n // qb), np.float32)
+    _cpublib().cpub_quantize(_p(q), _p(d), _p(x), xs or n, n, qb, T, threads or os.cpu_count() or 1)
+    return q, d
+
+
+def fast_gemm_q8(out: np.ndarray, os_: int, w: np.ndarray, ws: np.ndarray, bias: Optional[np.ndarray], rows: int,
+                 q: np.ndarray, d: np.ndarray, n: int, qb: int, T: int, add: bool,
+                 threads: Optional[int] = None) -> None:
+    """The picked backend's product into out (round to nearest), over all cores."""
+    for a in (out, w, ws, q, d) + ((bias,) if bias is not None else ()):
+        assert a.flags.c_contiguous
+    _cpublib().cpub_gemm(_p(out), os_, _p(w), _p(ws), _p(bias), rows, _p(q), _p(d), n, qb, T, int(add),
+                         threads or os.cpu_count() or 1)
 
 
 # ------------------------------------------------ the reference's generators --

@@ -358,3 +358,41 @@ def test_product_into_panels(pkb, cuda_device, T, rows, n, qb, dk, tpad, rmode, 
     got_kp, got_v = kp.cpu().numpy(), vp.cpu().numpy()
     assert same_bits(got_kp, want_kp), first_diff(got_kp, want_kp)
     assert same_bits(got_v, want_v), first_diff(got_v, want_v)
+
+
+# ------------------------------------------ blocks of whole stages (WIDE) --
+
+WIDE = [(300, 640, 1024, 1024, 0, 1), (129, 256, 512, 256, 1, 0), (1500, 384, 2048, 512, 1, 1),
+        (64, 8208, 640, 640, 0, 1), (257, 128, 1536, 384, 0, 0), (700, 512, 4096, 2048, 1, 0)]
+
+
+@pytest.mark.parametrize("T,rows,n,qb,add,bias", WIDE)
+@pytest.mark.parametrize("rmode", [O.RN, O.RD, O.RU, O.RZ])
+@pytest.mark.parametrize("off", [0, 1])
+def test_wide_blocks_on_device(pkb, cuda_device, T, rows, n, qb, add, bias, rmode, off):
+    """Blocks that span whole TMA boxes of K (qb = 256, 384, ... n: the
+    decoder's and the joint's products take qb = n), on the staged path that
+    issues a stage's four K steps unrolled into one accumulator; off 0 with
+    the results through TMA stores, off 1 (the results one float in) through
+    plain stores. Every rounding mode, against the oracle."""
+    import torch
+    g = np.random.default_rng(T + rows + n + qb + add + rmode)
+    x = (g.standard_normal(T * n) * 2).astype(np.float32)
+    qo, do = O.quantize(x, n, qb, rmode=rmode)
+    w = O.pack_q8(g.integers(-128, 128, (rows, n), dtype=np.int8))
+    ws = (1e-3 + 9e-3 * g.random(rows)).astype(np.float32)
+    ws[::7] *= -1
+    b = g.standard_normal(rows).astype(np.float32) if bias else None
+    out0 = g.standard_normal(T * rows + off).astype(np.float32)
+    want = out0.copy()
+    O.gemm_q8(want[off:], rows, w, ws, b, rows, qo, do, n, qb, T, bool(add), rmode=rmode)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    wp = torch.empty(rows * n, dtype=torch.int8, device="cuda")
+    pkb.repack_q8_dev(wp, dev(w), rows, n)
+    out = dev(out0)
+    pkb.gemm_q8_dev(out[off:], rows, wp, dev(ws), None if b is None else dev(b), rows, dev(qo), dev(do), n, qb, T,
+                    bool(add), rmode=rmode)
+    torch.cuda.synchronize()
+    assert pkb.device_errors(0) == 0
+    got = out.cpu().numpy()
+    assert same_bits(got, want), first_diff(got, want)

@@ -268,3 +268,24 @@ def test_live_reference_panels():
         for np_ in ((n + 15) // 16 * 16, (n + 15) // 16 * 16 + 16):
             src = g.standard_normal(n * D).astype(np.float32)
             assert O.panels_kp(src, n, np_, D, dk).tobytes() == O.ref_panels_kp(src, n, np_, D, dk).tobytes()
+
+
+@pytest.mark.skipif(not O.have_fast(), reason="the reference's backends are not built here")
+@pytest.mark.parametrize("T,rows,n,qb,add,bias", [(750, 4096, 1024, 32, 0, 0), (301, 1024, 4096, 64, 1, 0),
+                                                  (129, 640, 1024, 1024, 0, 1), (64, 256, 256, 32, 1, 1)])
+def test_fast_checker_is_the_oracle(T, rows, n, qb, add, bias):
+    """The full-size checker (the reference's picked backend, threaded as its
+    passes deal work) gives the oracle's bits: it may stand in for the
+    oracle where the oracle's scalar loops are too slow."""
+    x = O.seeded_normal(T * n, T + n)
+    q, d = O.fast_quantize(x, n, qb, T)
+    qo, do = O.quantize(x, n, qb)
+    assert np.array_equal(q, qo) and d.tobytes() == do.tobytes()
+    w = O.pack_q8(O.uniform_weights(rows, n, rows))
+    ws = (1e-3 + 9e-3 * np.random.default_rng(rows).random(rows)).astype(np.float32)
+    b = np.random.default_rng(n).standard_normal(rows).astype(np.float32) if bias else None
+    out0 = np.random.default_rng(T).standard_normal(T * rows).astype(np.float32)
+    got, want = out0.copy(), out0.copy()
+    O.fast_gemm_q8(got, rows, w, ws, b, rows, q, d, n, qb, T, bool(add))
+    O.gemm_q8(want, rows, w, ws, b, rows, qo, do, n, qb, T, bool(add))
+    assert got.tobytes() == want.tobytes()
