@@ -56,6 +56,8 @@ QB = 32
 SEED = 20261201
 CONCURRENT = ("q", "k", "v", "pos")  # a layer's products that read no other's results
 CHECK_LAYERS = (-1, 0, LAYERS - 1)  # the subsampling (-1) and the layers whose results are checked
+WORKLOAD = "batched"  # configs[3]; "longform": configs[4]
+J, VOCAB_OUT = 640, 8208  # the TDT joint: hidden width, outputs (8192 + 1 + 5 durations, padded to 16)
 
 
 # ---------------------------------------------------------------- workload --
@@ -71,6 +73,24 @@ def draw_segments(seed: int) -> list[tuple[float, int, int, int]]:
         t2 = (t1 + 1) // 2
         t3 = (t2 + 1) // 2
         out.append((float(sec), t0, t2, t3))
+    return out
+
+
+def longform_chunks() -> list[tuple[float, int, int, int]]:
+    """(seconds, T0, T2, T3) of the long-form workload's chunks:
+    the hour cut by the reference's own segmenter and chunker
+    (tests/golden/longform_chunks.json, written by
+    tests/golden/make_longform.py); mel frames = samples / hop 160
+    (pk_mel_frames, core/mel.c:32), each 2x subsampling stage ceil-halving."""
+    with open(os.path.join(ROOT, "tests", "golden", "longform_chunks.json")) as f:
+        doc = json.load(f)
+    out = []
+    for a, b in doc["chunks"]:
+        t0 = (b - a) // 160
+        t1 = (t0 + 1) // 2
+        t2 = (t1 + 1) // 2
+        t3 = (t2 + 1) // 2
+        out.append(((b - a) / doc["rate"], t0, t2, t3))
     return out
 
 
@@ -92,6 +112,9 @@ def segments(rank: int, world: int = 1, scaling: str = "strong") -> list[tuple[f
     """The rank's segments. Strong scaling (configs[3]: one batch of 64
     segments partitioned across the GPUs): the rank's share of the one draw.
     Weak scaling: a draw of 64 of its own."""
+    if WORKLOAD == "longform":
+        segs = longform_chunks()
+        return [segs[i] for i in partition(segs, world)[rank]]
     if scaling == "weak":
         return draw_segments(SEED + rank)
     segs = draw_segments(SEED)
@@ -128,8 +151,21 @@ def products(segs) -> list[dict]:
     return prods
 
 
-def step_ops(prods) -> float:
-    return float(sum(2.0 * p["M"] * p["rows"] * p["n"] for p in prods))
+def joint_steps(segs) -> list[int]:
+    """The long-form workload's TDT joint in lockstep over the rank's chunks
+    (core/decoder.c:121-147, one joint output a frame): at step i the chunks
+    still longer than i frames."""
+    if WORKLOAD != "longform" or not segs:
+        return []
+    return [sum(1 for sg in segs if sg[3] > i) for i in range(max(sg[3] for sg in segs))]
+
+
+def step_ops(prods, segs=None) -> float:
+    ops = float(sum(2.0 * p["M"] * p["rows"] * p["n"] for p in prods))
+    if segs is not None and WORKLOAD == "longform":
+        # jenc over every frame (pk_joint_frames, core/decoder.c:149-156), jout at each lockstep step
+        ops += 2.0 * sum(sg[3] for sg in segs) * J * D + sum(2.0 * m * VOCAB_OUT * J for m in joint_steps(segs))
+    return ops
 
 
 def audio_seconds(segs) -> float:
@@ -246,7 +282,7 @@ class Model:
     output buffer of its own, so that after a step each product's results
     are still there to be checked."""
 
-    def __init__(self, prods, dev, seed):
+    def __init__(self, prods, dev, seed, segs=None):
         import torch
         import libpktito_b200 as P
         self.P, self.torch = P, torch
@@ -277,6 +313,27 @@ class Model:
                 self.d[xk] = torch.empty(p["M"] * p["n"] // QB, dtype=torch.float32, device=dev)
         self.out = [torch.zeros(p["M"] * p["rows"], device=dev) for p in prods]
         self.prods = prods
+        self.joint = None
+        if segs is not None and WORKLOAD == "longform":
+            # the TDT joint: jenc over the rank's frames, then jout
+            # in lockstep over its chunks, every input a whole row a block
+            T3, steps = sum(sg[3] for sg in segs), joint_steps(segs)
+            mmax = max(steps)
+
+            def mat(rows, n):
+                w_pk = torch.randint(-127, 128, (rows * n,), dtype=torch.int8, device=dev, generator=g)
+                wp = torch.empty_like(w_pk)
+                P.repack_q8_dev(wp, w_pk, rows, n)
+                return (w_pk, wp, (1e-3 + 9e-3 * torch.rand(rows, device=dev, generator=g)).float(),
+                        torch.randn(rows, device=dev, generator=g))
+
+            self.joint = {"T3": T3, "steps": steps, "jenc": mat(J, D), "jout": mat(VOCAB_OUT, J),
+                          "xe": torch.randn(T3 * D, device=dev, generator=g),
+                          "qe": torch.empty(T3 * D, dtype=torch.int8, device=dev), "de": torch.empty(T3, device=dev),
+                          "f": torch.empty(T3 * J, device=dev),
+                          "z": torch.randn(mmax * J, device=dev, generator=g),
+                          "qz": torch.empty(mmax * J, dtype=torch.int8, device=dev),
+                          "dz": torch.empty(mmax, device=dev), "logits": torch.empty(mmax * VOCAB_OUT, device=dev)}
         # q, k, v and the position product of a layer depend on no one of
         # them (core/encoder.c:347-352): they run side by side on streams of
         # their own
@@ -319,6 +376,17 @@ class Model:
             for s in self.side:
                 s0.wait_stream(s)
             i += len(CONCURRENT)
+        jt = self.joint
+        if jt:
+            st = s0.cuda_stream
+            _, wp, ws, b = jt["jenc"]
+            P.quantize_dev(jt["qe"], jt["de"], jt["xe"], D, jt["T3"], D, D, stream=st)
+            P.gemm_q8_dev(jt["f"], J, wp, ws, b, J, jt["qe"], jt["de"], D, D, jt["T3"], False, stream=st)
+            _, wp, ws, b = jt["jout"]
+            for m in jt["steps"]:
+                P.quantize_dev(jt["qz"], jt["dz"], jt["z"], J, m, J, J, stream=st)
+                P.gemm_q8_dev(jt["logits"], VOCAB_OUT, wp, ws, b, VOCAB_OUT, jt["qz"], jt["dz"], J, J, m, False,
+                              stream=st)
 
 
 def parity_check(model, graph, world: int) -> dict:
@@ -376,7 +444,23 @@ def parity_check(model, graph, world: int) -> dict:
         equal += int(same)
         if not same:
             bad.append(f"{p['name']} layer {p['layer']}")
-    return {"checked": checked, "equal": equal, "products": len(idx), "quantized_inputs": checked - len(idx),
+    jt = model.joint
+    if jt:
+        # jenc over the frames, and jout at the last lockstep step
+        for name, x, M, n, rows, out in (("jenc", jt["xe"], jt["T3"], D, J, jt["f"]),
+                                         ("jout", jt["z"], jt["steps"][-1], J, VOCAB_OUT, jt["logits"])):
+            w_pk, _, ws, b = jt[name]
+            q, d = O.fast_quantize(x.cpu().numpy()[:M * n], n, n, M, threads=threads)
+            want = np.empty(M * rows, np.float32)
+            O.fast_gemm_q8(want, rows, w_pk.cpu().numpy(), ws.cpu().numpy(), b.cpu().numpy(), rows, q, d, n, n, M,
+                           False, threads=threads)
+            same = out.cpu().numpy()[:M * rows].tobytes() == want.tobytes()
+            checked += 1
+            equal += int(same)
+            if not same:
+                bad.append(name)
+    return {"checked": checked, "equal": equal, "products": len(idx) + (2 if jt else 0),
+            "quantized_inputs": checked - len(idx) - (2 if jt else 0),
             "layers": [l for l in CHECK_LAYERS if l >= 0], "subsampling": -1 in CHECK_LAYERS,
             "path": "the timed CUDA graph replayed once more (PDL, q/k/v/pos on side streams, the batch's M)",
             "checker": f"the reference's {backend} backend (its picker's choice; held to ref's bits by its own "
@@ -822,8 +906,8 @@ def run_ours(args) -> None:
     dev = torch.device("cuda", local)
     segs = segments(rank, world, args.scaling)
     prods = products(segs)
-    ops = step_ops(prods)
-    model = Model(prods, dev, SEED + 1000)  # one model, replicated on every GPU
+    ops = step_ops(prods, segs)
+    model = Model(prods, dev, SEED + 1000, segs)  # one model, replicated on every GPU
 
     def barrier():
         if dist:
@@ -883,15 +967,17 @@ def run_ours(args) -> None:
         # segments; the job's time is the slowest rank's
         if dist:
             dist.barrier(device_ids=[local])
-        e = e2e_host(prods, args.e2e_steps or args.steps, SEED + 7 + rank, args.e2e_lanes)
-        sec, e_ops, e_audio = job_totals(dist, dev, e["seconds_per_step"], ops, audio_seconds(segs))
+        e2e_steps = args.e2e_steps or (args.steps if WORKLOAD == "batched" else min(args.steps, 3))
+        e = e2e_host(prods, e2e_steps, SEED + 7 + rank, args.e2e_lanes)
+        sec, e_ops, e_audio = job_totals(dist, dev, e["seconds_per_step"], step_ops(prods), audio_seconds(segs))
         h2d, d2h = job_totals(dist, dev, 0.0, e["h2d_bytes_per_step"], e["d2h_bytes_per_step"])[1:]
         e2e = {"value": e_ops / sec / 1e12, "unit": "TOPS",
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                "audio_s_per_s": e_audio / sec,
                "path": "pk_kernels_cuda_b200 table (quantize + gemm_q8 on host buffers: activations and results "
                        "page-locked, weights in ordinary memory), whole matrices a call, "
-                       f"{args.e2e_lanes} lanes of calls at once on each rank", "steps": args.e2e_steps or args.steps,
+                       f"{args.e2e_lanes} lanes of calls at once on each rank; the encoder's products",
+               "steps": e2e_steps,
                "lanes": args.e2e_lanes}
     cpu = cpu_baseline(prods) if (rank == 0 and world == 1 and not args.no_cpu) else None
     if dist:
@@ -903,15 +989,24 @@ def run_ours(args) -> None:
     value = ops_job / (ms_step * 1e-3) / 1e12
     t3 = sum(s[3] for s in segs)
     nseg = SEGMENTS if args.scaling == "strong" else SEGMENTS * world
+    if WORKLOAD == "longform":
+        nseg = len(longform_chunks())
+        workload = ("configs[4] long-form: one hour of synthetic audio cut at its pauses by the reference's "
+                    f"segmenter and chunker into {nseg} chunks of up to 30.72 s, dealt across the GPUs longest "
+                    "first; per chunk the 24-layer encoder's 11 products a layer + 3 subsampling products, then "
+                    f"the TDT joint: jenc over every frame (qb 1024) and jout ({VOCAB_OUT} x {J}, qb 640) at each "
+                    f"lockstep decode step over the rank's chunks; qb {QB} in the encoder")
+    else:
+        workload = (("configs[3] batched encoder: one batch of 64 segments of 2-30 s dealt across the "
+                     "GPUs longest first" if args.scaling == "strong" else
+                     "configs[3] batched encoder, weak scaling: 64 segments of 2-30 s per GPU") +
+                    ", 24 layers x 11 products + 3 subsampling products, 196 quantizations (q, k, v share "
+                    f"one input; the position input is quantized once), qb {QB}")
     line = {
         "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": args.scaling,
         "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded segments, random int8 weights, N(0,1) activations)",
-        "config": {"workload": ("configs[3] batched encoder: one batch of 64 segments of 2-30 s dealt across the "
-                                "GPUs longest first" if args.scaling == "strong" else
-                                "configs[3] batched encoder, weak scaling: 64 segments of 2-30 s per GPU") +
-                               ", 24 layers x 11 products + 3 subsampling products, 196 quantizations (q, k, v share "
-                               f"one input; the position input is quantized once), qb {QB}",
+        "config": {"workload": workload,
                    "segments_rank0": len(segs), "encoder_frames_rank0": t3, "layers": LAYERS, "d_model": D,
                    "ff_dim": F, "qb": QB, "global_batch": nseg, "seq_len": t3 // max(1, len(segs)),
                    "parallelism": f"dp{world}", "l2": "no flush: each step streams 576 MiB of weights and "
@@ -1111,6 +1206,9 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["batched", "longform"], default="batched",
+                    help="batched: configs[3] (64 segments of 2-30 s); longform: configs[4] (an hour cut by the "
+                         "reference's segmenter, the TDT joint included)")
     ap.add_argument("--qb", type=int, choices=[32, 64], default=32,
                     help="blocks of the activations' quantization: 32, or 64 in the reference's fast mode")
     ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the e2e leg (default: --steps)")
@@ -1130,8 +1228,9 @@ def main() -> None:
                     help="only the K/V products into plain rows, K panels and V panels, 1 launch each: the ncu "
                          "capture's case")
     args = ap.parse_args()
-    global QB
+    global QB, WORKLOAD
     QB = args.qb
+    WORKLOAD = args.workload
     if args.kernel_only:
         run_kernel_only()
     elif args.panels_only:

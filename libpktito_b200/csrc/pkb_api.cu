@@ -151,7 +151,10 @@ int quantize_dev(cudaStream_t stream, int8_t* q, float* d, const float* x, size_
     if ((rc = check_rmode(rmode))) return rc;
     if (!T) return PKB_OK;
     if (!q || !d || !x) return fail(PKB_EINVAL, "quantize: null pointer");
-    if (xs < n) return fail(PKB_EINVAL, "quantize: column stride %zu below n = %u", xs, n);
+    // the contract reads column t at x + t xs: one column reads no stride
+    // (the reference's decoder passes its gemv's input so)
+    if (T > 1 && xs < n) return fail(PKB_EINVAL, "quantize: column stride %zu below n = %u", xs, n);
+    if (T == 1) xs = n;
     if (!aligned(q, 4) || !aligned(d, 4) || !aligned(x, 4)) return fail(PKB_EINVAL, "quantize: misaligned buffer");
     Device* dev;
     if ((rc = current_device(&dev))) return rc;
@@ -180,8 +183,11 @@ int gemm_dev(cudaStream_t stream, float* out, size_t os, const int8_t* wpack, co
     if (rc) return rc;
     if ((rc = check_rmode(rmode))) return rc;
     if (rows % 16) return fail(PKB_EINVAL, "rows = %u: a multiple of 16", rows);
-    if (os < rows) return fail(PKB_EINVAL, "output stride %zu below rows = %u", os, rows);
+    // out[t os + r]: one column of results reads no stride (the reference's
+    // decoder passes os 0 for its gemvs, core/decoder.c:56-63)
+    if (T > 1 && os < rows) return fail(PKB_EINVAL, "output stride %zu below rows = %u", os, rows);
     if (!T || !rows) return PKB_OK;
+    if (T == 1) os = rows;
     if (!out || !wpack || !ws || !q || !d) return fail(PKB_EINVAL, "gemm_q8: null pointer");
     if (!aligned(q, 16) || !aligned(wpack, 16))
         return fail(PKB_EINVAL, "gemm_q8: activations and weights must be 16-byte aligned");

@@ -607,7 +607,9 @@ int pkb_quantize_host(int8_t* q, float* d, uint32_t n, uint32_t qb, uint32_t T, 
     if (rc) return rc;
     if (!T) return PKB_OK;
     if (!q || !d || !x) return set_error(PKB_EINVAL, "quantize: null pointer");
-    if (xs < n) return set_error(PKB_EINVAL, "quantize: column stride %zu below n = %u", xs, n);
+    // column t at x + t xs: one column reads no stride
+    if (T > 1 && xs < n) return set_error(PKB_EINVAL, "quantize: column stride %zu below n = %u", xs, n);
+    if (T == 1) xs = n;
     Pipe* p;
     uint32_t* err;
     if ((rc = open_pipe(&p, &err))) return rc;
@@ -686,8 +688,11 @@ int pkb_gemm_q8_host(float* out, size_t os, const int8_t* w, const float* ws, co
     int rc = check_shape(n, qb, rmode);
     if (rc) return rc;
     if (rows % 16) return set_error(PKB_EINVAL, "rows = %u: a multiple of 16", rows);
-    if (os < rows) return set_error(PKB_EINVAL, "output stride %zu below rows = %u", os, rows);
+    // out[t os + r]: one column of results reads no stride (the reference's
+    // decoder passes os 0 for its gemvs, core/decoder.c:56-63)
+    if (T > 1 && os < rows) return set_error(PKB_EINVAL, "output stride %zu below rows = %u", os, rows);
     if (!T || !rows) return PKB_OK;
+    if (T == 1) os = rows;
     if (!out || !w || !ws || !q || !d) return set_error(PKB_EINVAL, "gemm_q8: null pointer");
     Pipe* p;
     uint32_t* err;

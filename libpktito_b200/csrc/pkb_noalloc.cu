@@ -53,7 +53,8 @@ extern "C" int pkb_quantize_host_noalloc(int8_t* q, float* d, uint32_t n, uint32
     if (rmode < PKB_RN || rmode > PKB_RZ) return refuse(PKB_EINVAL, "rounding mode");
     if (!T) return PKB_OK;
     if (!q || !d || !x) return refuse(PKB_EINVAL, "null pointer");
-    if (xs < n) return refuse(PKB_EINVAL, "column stride below n");
+    if (T > 1 && xs < n) return refuse(PKB_EINVAL, "column stride below n");
+    if (T == 1) xs = n;  // one column reads no stride
     const size_t xbytes = static_cast<size_t>(T) * n * 4;
     const size_t qbytes = static_cast<size_t>(T) * n, dbytes = static_cast<size_t>(T) * (n / qb) * 4;
     const size_t off_q = up256(xbytes), off_d = off_q + up256(qbytes), need = off_d + dbytes;

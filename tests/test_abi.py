@@ -63,7 +63,8 @@ def test_bad_rows_and_stride_refused(pkb):
     lib = pkb.lib()
     out = np.zeros(64, np.float32)
     assert lib.pkb_gemm_q8_host(out.ctypes.data, 32, None, None, None, 24, None, None, 32, 32, 1, 0, 0) == 1
-    assert lib.pkb_gemm_q8_host(out.ctypes.data, 8, None, None, None, 16, None, None, 32, 32, 1, 0, 0) == 1
+    assert lib.pkb_gemm_q8_host(out.ctypes.data, 8, None, None, None, 16, None, None, 32, 32, 2, 0, 0) == 1
+    assert b"output stride" in lib.pkb_last_error()
     assert lib.pkb_gemm_q8_host(out.ctypes.data, 16, None, None, None, 16, None, None, 32, 32, 1, 0, 7) == 1
     assert b"rounding mode" in lib.pkb_last_error()
 

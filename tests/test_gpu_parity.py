@@ -163,6 +163,34 @@ def test_random_products(pkb, cuda_device, rows, n, T, qb, add, bias):
     assert same_bits(got, want), first_diff(got, want)
 
 
+def test_one_column_reads_no_stride(pkb, cuda_device):
+    """The reference's decoder quantizes and multiplies one column at a time
+    with output stride 0 (core/decoder.c:53-63): the contract's out[t os + r]
+    and x + t xs read no stride for t = 0, so any stride is accepted there,
+    on host and device buffers."""
+    import torch
+    n, rows, qb = 640, 2560, 640
+    x = O.seeded_normal(n, 41)
+    q, d = pkb.quantize_host(x, n, qb, T=1, xs=0)
+    qo, do = O.quantize(x, n, qb)
+    assert np.array_equal(q, qo) and same_bits(d, do)
+    w = O.pack_q8(O.uniform_weights(rows, n, 42))
+    ws = np.linspace(1e-3, 1e-2, rows).astype(np.float32)
+    b = np.linspace(-1, 1, rows).astype(np.float32)
+    want = np.full(rows, 3.0, np.float32)
+    O.gemm_q8(want, rows, w, ws, b, rows, qo, do, n, qb, 1, True)
+    got = np.full(rows, 3.0, np.float32)
+    pkb.gemm_q8_host(got, 0, w, ws, b, rows, q, d, n, qb, 1, True)
+    assert same_bits(got, want), first_diff(got, want)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    wp = torch.empty(rows * n, dtype=torch.int8, device="cuda")
+    pkb.repack_q8_dev(wp, dev(w), rows, n)
+    out = torch.full((rows,), 3.0, device="cuda")
+    pkb.gemm_q8_dev(out, 0, wp, dev(ws), dev(b), rows, dev(qo), dev(do), n, qb, 1, True)
+    torch.cuda.synchronize()
+    assert same_bits(out.cpu().numpy(), want)
+
+
 def test_table_entry(pkb, cuda_device):
     """pk_kernels_cuda_b200, called as the reference's passes call a backend."""
     tab = pkb.Table()

@@ -85,5 +85,5 @@ def test_noalloc_runs_on_the_threads_device(pkb, cuda_device):
     th.join()
     assert seen["rc"] == 0, seen["err"]
     assert seen["device"] == dev
-    qo, do = O.quantize(x, n, qb)
+    qo, do = O.quantize(x, n, qb, T=T)
     assert np.array_equal(seen["q"], qo) and seen["d"].tobytes() == do.tobytes()
