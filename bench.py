@@ -865,6 +865,123 @@ def e2e_host(prods, steps: int, seed: int, lanes: int) -> dict:
     return {"seconds_per_step": sec, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
 
+def gemm_items(rows: int, T: int, nth: int) -> list[tuple[int, int, int, int]]:
+    """(r0, nr, c0, nc) of every call pk_gemm_on makes for a product
+    (core/passes.c:90-109): rows in steps of 256 where rows/256 >= 2 threads,
+    else 64; the frames in the chunk count (1..8, chunks of at least 48
+    frames, whole multiples of 12) that leaves the pool's last round least
+    idle."""
+    step = 256 if rows // 256 >= 2 * nth else 64
+    rb = (rows + step - 1) // step
+    best, best_idle, best_all = 1, 2 ** 32 - 1, 1
+    cc = 1
+    while cc <= 8 and (cc == 1 or T // cc >= 48):
+        items = rb * cc
+        all_ = (items + nth - 1) // nth * nth
+        if (all_ - items) * best_all < best_idle * all_:
+            best, best_idle, best_all = cc, all_ - items, all_
+        cc += 1
+    cstep = (T + best - 1) // best
+    cstep = (cstep + 11) // 12 * 12 if best > 1 else T
+    cc = (T + cstep - 1) // cstep
+    return [((i % rb) * step, min(step, rows - (i % rb) * step), (i // rb) * cstep,
+             min(cstep, T - (i // rb) * cstep)) for i in range(rb * cc)]
+
+
+def e2e_host_sliced(prods, steps: int, seed: int, nth: int) -> dict:
+    """The same step through the reference-facing table as the reference's
+    engine calls a backend: each input quantized in one call, then each
+    product in the calls pk_gemm_on makes (slices of 64 or 256 rows of the
+    PK_Q8 matrix from inside it, frames in column chunks), dealt to `nth`
+    host threads from a shared counter as its pool deals them
+    (core/pool.c:115-122); one product after another. Activations and results
+    page-locked, weights in ordinary memory, as e2e_host."""
+    import threading
+    import torch
+    import libpktito_b200 as P
+    tab = P.Table()
+    rng = np.random.default_rng(seed)
+    keep = []
+
+    def locked(nelem: int, dtype) -> np.ndarray:
+        t = torch.empty(nelem, dtype={np.float32: torch.float32, np.int8: torch.int8}[dtype], pin_memory=True)
+        keep.append(t)
+        return t.numpy()
+
+    w, ws, bias, xs, qs, ds, outs = {}, {}, {}, {}, {}, {}, {}
+    for p in prods:
+        key, xk, ok = (p["layer"], p["name"]), (p["M"], p["n"]), (p["M"], p["rows"])
+        if key not in w:
+            w[key] = rng.integers(-127, 128, p["rows"] * p["n"], dtype=np.int8)
+            ws[key] = (1e-3 + 9e-3 * rng.random(p["rows"])).astype(np.float32)
+            bias[key] = rng.standard_normal(p["rows"]).astype(np.float32) if p["bias"] else None
+        if xk not in xs:
+            xs[xk] = locked(p["M"] * p["n"], np.float32)
+            xs[xk][:] = rng.standard_normal(p["M"] * p["n"], dtype=np.float32)
+            qs[xk] = locked(p["M"] * p["n"], np.int8)
+            ds[xk] = locked(p["M"] * p["n"] // QB, np.float32)
+        if ok not in outs:
+            outs[ok] = locked(p["M"] * p["rows"], np.float32)
+            outs[ok][:] = 0.0
+    device = torch.cuda.current_device()
+    work = {"items": [], "next": 0, "p": None}
+    lock = threading.Lock()
+    start, done = threading.Barrier(nth + 1), threading.Barrier(nth + 1)
+    calls = [0]
+
+    def worker():
+        P.set_thread_device(device)
+        while True:
+            start.wait()
+            p = work["p"]
+            if p is None:
+                return
+            key, xk, ok = (p["layer"], p["name"]), (p["M"], p["n"]), (p["M"], p["rows"])
+            n, nb = p["n"], p["n"] // QB
+            while True:
+                with lock:
+                    i = work["next"]
+                    work["next"] += 1
+                if i >= len(work["items"]):
+                    break
+                r0, nr, c0, nc = work["items"][i]
+                act = P.PkAct(qs[xk][c0 * n:].ctypes.data, ds[xk][c0 * nb:].ctypes.data, n, QB, nc)
+                b = bias[key]
+                tab.gemm_q8(outs[ok][c0 * p["rows"] + r0:], p["rows"], w[key][r0 * n:], ws[key][r0:],
+                            None if b is None else b[r0:], nr, act, bool(p["add"]))
+            done.wait()
+
+    ts = [threading.Thread(target=worker, daemon=True) for _ in range(nth)]
+    for t in ts:
+        t.start()
+
+    def one():
+        held = {}
+        for p in prods:
+            xk = (p["M"], p["n"])
+            if held.get(xk) != p["inp"]:
+                tab.quantize(P.PkAct(qs[xk].ctypes.data, ds[xk].ctypes.data, p["n"], QB, p["M"]), xs[xk], p["n"])
+                held[xk] = p["inp"]
+            work["items"] = gemm_items(p["rows"], p["M"], nth)
+            work["next"] = 0
+            work["p"] = p
+            calls[0] += len(work["items"])
+            start.wait()
+            done.wait()
+
+    one()  # uploads and caches the weights
+    calls[0] = 0
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one()
+    sec = (time.perf_counter() - t0) / steps
+    work["p"] = None
+    start.wait()
+    for t in ts:
+        t.join()
+    return {"seconds_per_step": sec, "calls_per_step": calls[0] // max(1, steps), "threads": nth}
+
+
 # -------------------------------------------------------------- the arms --
 
 def dist_setup(gpus: int):
@@ -979,6 +1096,17 @@ def run_ours(args) -> None:
                        f"{args.e2e_lanes} lanes of calls at once on each rank; the encoder's products",
                "steps": e2e_steps,
                "lanes": args.e2e_lanes}
+    if e2e is not None and not args.no_sliced:
+        # the engine's call pattern (slices from a pool of host threads)
+        if dist:
+            dist.barrier(device_ids=[local])
+        sl = e2e_host_sliced(prods, max(1, min(args.steps, 3)), SEED + 11 + rank, args.e2e_threads)
+        sec, e_ops, _ = job_totals(dist, dev, sl["seconds_per_step"], step_ops(prods), audio_seconds(segs))
+        e2e["engine_sliced"] = {"value": e_ops / sec / 1e12, "unit": "TOPS", "calls_per_step": sl["calls_per_step"],
+                                "threads": sl["threads"], "steps": max(1, min(args.steps, 3)),
+                                "path": "pk_kernels_cuda_b200 table as the reference's engine calls it: each input "
+                                        "quantized in one call, each product in pk_gemm_on's slices of 64/256 rows "
+                                        "and column chunks (core/passes.c:90-109), dealt to a pool of host threads"}
     cpu = cpu_baseline(prods) if (rank == 0 and world == 1 and not args.no_cpu) else None
     if dist:
         dist.barrier(device_ids=[local])
@@ -1214,6 +1342,8 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the e2e leg (default: --steps)")
     ap.add_argument("--e2e-lanes", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-sliced", action="store_true", help="skip the e2e figure at the engine's slicing")
+    ap.add_argument("--e2e-threads", type=int, default=16, help="host threads of the engine-sliced e2e figure")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-producers", action="store_true", help="skip timing the fused producers (rank 0)")
     ap.add_argument("--no-graph", action="store_true")

@@ -98,6 +98,18 @@ class CopyPool {
         });
     }
 
+    bool equal(const void* a, const void* b, size_t bytes) {
+        std::atomic<bool> same{true};
+        const int parts = split(bytes, bytes / 4096 + 1);
+        run(parts, [&](int p) {
+            const size_t b0 = (bytes * p / parts) & ~size_t(63), b1 = p + 1 == parts ? bytes : (bytes * (p + 1) / parts) & ~size_t(63);
+            if (same.load(std::memory_order_relaxed) &&
+                memcmp(static_cast<const char*>(a) + b0, static_cast<const char*>(b) + b0, b1 - b0))
+                same = false;
+        });
+        return same;
+    }
+
   private:
     struct Job {
         std::function<void(int)> fn;
@@ -243,6 +255,13 @@ struct Pipe {
             for (cudaEvent_t* e : {&ev_in[i], &ev_comp[i], &ev_out[i]})
                 HOST_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "cudaEventCreate");
         HOST_CUDA(cudaMallocHost(&herr, sizeof(uint32_t)), "cudaMallocHost");
+        // the activation copies come from the device's stream-ordered pool:
+        // it keeps what is freed instead of returning it at every sync
+        cudaMemPool_t pool;
+        if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
+            uint64_t keep_all = UINT64_MAX;
+            cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep_all);
+        }
         return PKB_OK;
     }
 
@@ -307,6 +326,18 @@ struct Pipe {
 
 thread_local int tl_device = 0;
 thread_local Pipe tl_pipe;
+
+// Drains a pipe's streams when a call returns early (an error after work
+// was enqueued), so that nothing the call enqueued still runs when the
+// memory it uses (an activation copy, weights) may be freed.
+struct DrainOnReturn {
+    Pipe* p;
+    ~DrainOnReturn() {
+        if (!p) return;
+        for (cudaStream_t st : {p->s_in, p->s_comp, p->s_out})
+            if (st) cudaStreamSynchronize(st);
+    }
+};
 
 // Whether [p, p + bytes) is page-locked host memory (both of its ends: a
 // range that is not wholly so is still copied correctly, only not at DMA
@@ -565,6 +596,143 @@ int weights_for(Pipe& p, const int8_t* w, uint32_t rows, uint32_t n, const int8_
     return PKB_OK;
 }
 
+// ----------------------------------------------------------- activations --
+//
+// A product reads activations that a quantize call of this library wrote a
+// moment before: the reference's engine quantizes an input and then hands
+// the same host q and d to every product (and every slice of a product,
+// core/passes.c:60-109) that reads it. Each quantize call therefore keeps its
+// result on the device, with a host copy of the bytes and scales it wrote;
+// a product whose q and d lie inside one such result, at the same frames,
+// compares the caller's bytes with that copy (the whole range, split over
+// the copy pool) and, where they are the same, reads the device copy instead
+// of uploading them again. Bytes that differ (anything else wrote there) fail
+// the comparison and the call uploads them as usual, so the result is the
+// same either way; what the cache saves is PCIe traffic, paid for with host
+// memory reads. A new quantize call over the same host bytes replaces the
+// old result. The device copies are capped (PKB_ACT_CACHE_MB, default 4096;
+// 0 turns the cache off), the oldest dropped first.
+//
+// A call whose frames lie inside those of a call still in progress that
+// compared (or was itself covered so) skips the comparison: the caller may
+// not change the inputs of a call before it returns, so those bytes are
+// still the ones compared. The engine's slices of one column chunk (the
+// same frames, other rows) then compare the chunk once.
+
+struct ActCopy {
+    uintptr_t q0, d0;      // host addresses of frame 0's bytes and scales
+    uint32_t n, nb, T;
+    int8_t* dq = nullptr;  // device [T][n]
+    float* dd = nullptr;   // device [T][nb]
+    size_t cap_q = 0, cap_d = 0;  // their sizes in bytes
+    int dev = -1;
+    std::vector<int8_t> hq;  // the host bytes and scales as written
+    std::vector<float> hd;
+    std::mutex live_mu;     // frame ranges [first, second) of the calls in progress that read this copy
+    std::vector<std::pair<uint32_t, uint32_t>> live;
+    ~ActCopy() {
+        int cur = -1;
+        if (cudaGetDevice(&cur) != cudaSuccess) return;
+        cudaSetDevice(dev);
+        if (dq) cudaFreeAsync(dq, cudaStreamPerThread);
+        if (dd) cudaFreeAsync(dd, cudaStreamPerThread);
+        cudaSetDevice(cur);
+    }
+};
+
+struct ActCache {
+    std::shared_mutex mu;
+    std::map<uintptr_t, std::shared_ptr<ActCopy>> by_q;  // by q0; disjoint host ranges
+    std::deque<uintptr_t> order;                          // insertion order, for eviction
+    size_t bytes = 0;
+};
+
+ActCache g_acts[MAX_DEV];
+
+size_t act_cache_cap() {
+    static const size_t cap = [] {
+        const char* e = getenv("PKB_ACT_CACHE_MB");
+        return (e ? static_cast<size_t>(atoll(e)) : size_t(4096)) << 20;
+    }();
+    return cap;
+}
+
+// Drops the results overlapping host bytes [q, q + qbytes) or scales [d, d + dbytes);
+// returns one of them that no call still uses, for its memory to be reused.
+std::shared_ptr<ActCopy> act_forget(ActCache& c, uintptr_t q, size_t qbytes, uintptr_t d, size_t dbytes) {
+    std::shared_ptr<ActCopy> spare;
+    std::unique_lock<std::shared_mutex> lock(c.mu);
+    for (auto it = c.by_q.begin(); it != c.by_q.end();) {
+        const ActCopy& a = *it->second;
+        const uintptr_t aq1 = a.q0 + static_cast<size_t>(a.T) * a.n, ad1 = a.d0 + static_cast<size_t>(a.T) * a.nb * 4;
+        if ((a.q0 < q + qbytes && q < aq1) || (a.d0 < d + dbytes && d < ad1)) {
+            c.bytes -= static_cast<size_t>(a.T) * (a.n + 4 * a.nb);
+            if (it->second.use_count() == 1 && (!spare || a.T * static_cast<size_t>(a.n) > spare->hq.size()))
+                spare = it->second;
+            it = c.by_q.erase(it);
+        } else {
+            ++it;
+        }
+    }
+    return spare;
+}
+
+// A call's hold on frames [f0, f0 + T) of a device copy, released when the
+// call returns.
+struct ActHold {
+    std::shared_ptr<ActCopy> a;
+    std::pair<uint32_t, uint32_t> range;
+    ~ActHold() {
+        if (!a) return;
+        std::lock_guard<std::mutex> lock(a->live_mu);
+        for (auto it = a->live.begin(); it != a->live.end(); ++it)
+            if (*it == range) {
+                a->live.erase(it);
+                break;
+            }
+    }
+};
+
+// The device copy holding frames [f0, f0 + T) of q and d, after the caller's
+// bytes there were found to be the ones written; null otherwise.
+std::shared_ptr<ActCopy> act_find(int dev, const int8_t* q, const float* d, uint32_t n, uint32_t nb, uint32_t T,
+                                  uint32_t* f0, ActHold* hold) {
+    if (!act_cache_cap()) return nullptr;
+    ActCache& c = g_acts[dev];
+    std::shared_ptr<ActCopy> a;
+    {
+        std::shared_lock<std::shared_mutex> lock(c.mu);
+        auto it = c.by_q.upper_bound(reinterpret_cast<uintptr_t>(q));
+        if (it == c.by_q.begin()) return nullptr;
+        a = std::prev(it)->second;
+    }
+    const uintptr_t qa = reinterpret_cast<uintptr_t>(q);
+    if (a->n != n || a->nb != nb || (qa - a->q0) % n) return nullptr;
+    const size_t f = (qa - a->q0) / n;
+    if (f + T > a->T || reinterpret_cast<uintptr_t>(d) != a->d0 + f * nb * 4) return nullptr;
+    const std::pair<uint32_t, uint32_t> range(static_cast<uint32_t>(f), static_cast<uint32_t>(f + T));
+    bool covered = false;
+    {
+        std::lock_guard<std::mutex> lock(a->live_mu);
+        for (const auto& r : a->live)
+            if (r.first <= range.first && range.second <= r.second) covered = true;
+        if (covered) a->live.push_back(range);
+    }
+    if (!covered) {
+        // the caller's bytes and scales against the ones written
+        CopyPool& pool = CopyPool::get();
+        if (!pool.equal(q, a->hq.data() + f * n, static_cast<size_t>(T) * n) ||
+            !pool.equal(d, a->hd.data() + f * nb, static_cast<size_t>(T) * nb * 4))
+            return nullptr;
+        std::lock_guard<std::mutex> lock(a->live_mu);
+        a->live.push_back(range);
+    }
+    hold->a = a;
+    hold->range = range;
+    *f0 = static_cast<uint32_t>(f);
+    return a;
+}
+
 int open_pipe(Pipe** out, uint32_t** err_word) {
     Pipe& p = tl_pipe;
     int rc = p.open(tl_device);
@@ -621,6 +789,63 @@ int pkb_quantize_host(int8_t* q, float* d, uint32_t n, uint32_t qb, uint32_t T, 
     CopyPool& pool = CopyPool::get();
     const uint32_t nchunks = (T + TC - 1) / TC;
     auto frames = [&](uint32_t c) { return std::min(TC, T - c * TC); };
+    // the host bytes this call rewrites: older results over them are stale
+    ActCache& ac = g_acts[p->dev];
+    std::shared_ptr<ActCopy> spare =
+        act_forget(ac, reinterpret_cast<uintptr_t>(q), T * qrow, reinterpret_cast<uintptr_t>(d), T * drow);
+    // the result's device copy, kept for the products that read it; the
+    // memory of the result it replaces, where it is large enough and no call
+    // uses it, is taken over (no allocation, no fresh host pages)
+    std::shared_ptr<ActCopy> keep;
+    if (act_cache_cap() && T * (qrow + drow) <= act_cache_cap()) {
+        const bool reuse = spare && spare->cap_q >= T * qrow && spare->cap_d >= T * drow;
+        keep = reuse ? spare : std::make_shared<ActCopy>();
+        keep->q0 = reinterpret_cast<uintptr_t>(q);
+        keep->d0 = reinterpret_cast<uintptr_t>(d);
+        keep->n = n;
+        keep->nb = nb;
+        keep->T = T;
+        keep->dev = p->dev;
+        if (!reuse && (cudaMallocAsync(&keep->dq, T * qrow, p->s_comp) != cudaSuccess ||
+                       cudaMallocAsync(&keep->dd, T * drow, p->s_comp) != cudaSuccess)) {
+            cudaGetLastError();
+            keep.reset();  // no room: the call works as without the cache
+        } else if (!reuse) {
+            keep->cap_q = T * qrow;
+            keep->cap_d = T * drow;
+        }
+    }
+    spare.reset();
+    // declared after keep, so drained before keep's memory can go
+    DrainOnReturn drain{p};
+    // where chunk c's bytes and scales are made on the device
+    auto dq_of = [&](uint32_t c) -> int8_t* {
+        return keep ? keep->dq + static_cast<size_t>(c) * TC * qrow : reinterpret_cast<int8_t*>(p->dev_out[c & 1]);
+    };
+    auto dd_of = [&](uint32_t c) -> float* {
+        return keep ? keep->dd + static_cast<size_t>(c) * TC * nb : reinterpret_cast<float*>(p->dev_out[c & 1] + off_d);
+    };
+    // after the call's last copy: the host copy of what was written, and the entry
+    auto remember = [&]() {
+        if (!keep) return;
+        if (keep->hq.size() < T * qrow) keep->hq.resize(T * qrow);
+        if (keep->hd.size() < static_cast<size_t>(T) * nb) keep->hd.resize(static_cast<size_t>(T) * nb);
+        pool.copy(keep->hq.data(), q, T * qrow);
+        pool.copy(keep->hd.data(), d, T * drow);
+        std::unique_lock<std::shared_mutex> lock(ac.mu);
+        const size_t sz = T * (qrow + drow);
+        while (ac.bytes + sz > act_cache_cap() && !ac.order.empty()) {
+            auto it = ac.by_q.find(ac.order.front());
+            ac.order.pop_front();
+            if (it != ac.by_q.end()) {
+                ac.bytes -= static_cast<size_t>(it->second->T) * (it->second->n + 4 * it->second->nb);
+                ac.by_q.erase(it);
+            }
+        }
+        ac.by_q[keep->q0] = keep;
+        ac.order.push_back(keep->q0);
+        ac.bytes += sz;
+    };
     if (pinned(x, ((T - 1) * xs + n) * 4) && pinned(q, T * qrow) && pinned(d, T * drow)) {
         // page-locked: every chunk by DMA straight from x and into q and d
         for (uint32_t c = 0; c < nchunks; c++) {
@@ -634,19 +859,18 @@ int pkb_quantize_host(int8_t* q, float* d, uint32_t n, uint32_t qb, uint32_t T, 
             HOST_CUDA(cudaEventRecord(p->ev_in[s], p->s_in), "cudaEventRecord");
             HOST_CUDA(cudaStreamWaitEvent(p->s_comp, p->ev_in[s], 0), "cudaStreamWaitEvent");
             if (c >= 2) HOST_CUDA(cudaStreamWaitEvent(p->s_comp, p->ev_out[s], 0), "cudaStreamWaitEvent");
-            if ((rc = pkb_quantize_dev(p->s_comp, reinterpret_cast<int8_t*>(p->dev_out[s]),
-                                       reinterpret_cast<float*>(p->dev_out[s] + off_d),
-                                       reinterpret_cast<const float*>(p->dev_in[s]), n, tc, n, qb, rmode)))
+            if ((rc = pkb_quantize_dev(p->s_comp, dq_of(c), dd_of(c), reinterpret_cast<const float*>(p->dev_in[s]), n,
+                                       tc, n, qb, rmode)))
                 return rc;
             HOST_CUDA(cudaEventRecord(p->ev_comp[s], p->s_comp), "cudaEventRecord");
             HOST_CUDA(cudaStreamWaitEvent(p->s_out, p->ev_comp[s], 0), "cudaStreamWaitEvent");
-            HOST_CUDA(cudaMemcpyAsync(q + t0 * qrow, p->dev_out[s], tc * qrow, cudaMemcpyDeviceToHost, p->s_out),
-                      "download");
-            HOST_CUDA(cudaMemcpyAsync(d + t0 * nb, p->dev_out[s] + off_d, tc * drow, cudaMemcpyDeviceToHost, p->s_out),
-                      "download");
+            HOST_CUDA(cudaMemcpyAsync(q + t0 * qrow, dq_of(c), tc * qrow, cudaMemcpyDeviceToHost, p->s_out), "download");
+            HOST_CUDA(cudaMemcpyAsync(d + t0 * nb, dd_of(c), tc * drow, cudaMemcpyDeviceToHost, p->s_out), "download");
             HOST_CUDA(cudaEventRecord(p->ev_out[s], p->s_out), "cudaEventRecord");
         }
-        return p->finish(err);
+        if ((rc = p->finish(err))) return rc;
+        remember();
+        return PKB_OK;
     }
     auto take_out = [&](uint32_t c) -> int {  // chunk c's bytes and scales to the caller
         const int s = c & 1;
@@ -665,22 +889,21 @@ int pkb_quantize_host(int8_t* q, float* d, uint32_t n, uint32_t qb, uint32_t T, 
         HOST_CUDA(cudaEventRecord(p->ev_in[s], p->s_in), "cudaEventRecord");
         HOST_CUDA(cudaStreamWaitEvent(p->s_comp, p->ev_in[s], 0), "cudaStreamWaitEvent");
         if (c >= 2) HOST_CUDA(cudaStreamWaitEvent(p->s_comp, p->ev_out[s], 0), "cudaStreamWaitEvent");
-        if ((rc = pkb_quantize_dev(p->s_comp, reinterpret_cast<int8_t*>(p->dev_out[s]),
-                                   reinterpret_cast<float*>(p->dev_out[s] + off_d),
-                                   reinterpret_cast<const float*>(p->dev_in[s]), n, tc, n, qb, rmode)))
+        if ((rc = pkb_quantize_dev(p->s_comp, dq_of(c), dd_of(c), reinterpret_cast<const float*>(p->dev_in[s]), n, tc,
+                                   n, qb, rmode)))
             return rc;
         HOST_CUDA(cudaEventRecord(p->ev_comp[s], p->s_comp), "cudaEventRecord");
         HOST_CUDA(cudaStreamWaitEvent(p->s_out, p->ev_comp[s], 0), "cudaStreamWaitEvent");
-        HOST_CUDA(cudaMemcpyAsync(p->pin_out[s], p->dev_out[s], tc * qrow, cudaMemcpyDeviceToHost, p->s_out),
-                  "download");
-        HOST_CUDA(cudaMemcpyAsync(p->pin_out[s] + off_d, p->dev_out[s] + off_d, tc * drow, cudaMemcpyDeviceToHost,
-                                  p->s_out),
+        HOST_CUDA(cudaMemcpyAsync(p->pin_out[s], dq_of(c), tc * qrow, cudaMemcpyDeviceToHost, p->s_out), "download");
+        HOST_CUDA(cudaMemcpyAsync(p->pin_out[s] + off_d, dd_of(c), tc * drow, cudaMemcpyDeviceToHost, p->s_out),
                   "download");
         HOST_CUDA(cudaEventRecord(p->ev_out[s], p->s_out), "cudaEventRecord");
         if (c >= 1 && (rc = take_out(c - 1))) return rc;
     }
     if ((rc = p->finish(err))) return rc;
-    return take_out(nchunks - 1);
+    if ((rc = take_out(nchunks - 1))) return rc;
+    remember();
+    return PKB_OK;
 }
 
 int pkb_gemm_q8_host(float* out, size_t os, const int8_t* w, const float* ws, const float* bias, uint32_t rows,
@@ -716,6 +939,21 @@ int pkb_gemm_q8_host(float* out, size_t os, const int8_t* w, const float* ws, co
     const float* dbias = bias ? reinterpret_cast<const float*>(p->dev_vec + up256(orow)) : nullptr;
     const uint32_t nchunks = (T + TC - 1) / TC;
     auto frames = [&](uint32_t c) { return std::min(TC, T - c * TC); };
+    // activations this library quantized and that are still the caller's
+    // bytes: read from their device copy, not uploaded again
+    uint32_t f0 = 0;
+    ActHold act_hold;
+    const std::shared_ptr<ActCopy> cached = act_find(p->dev, q, d, n, nb, T, &f0, &act_hold);
+    // declared after the holds on the weights and the activations, so drained before they go
+    DrainOnReturn drain{p};
+    auto qsrc = [&](uint32_t c) -> const int8_t* {
+        return cached ? cached->dq + (static_cast<size_t>(f0) + static_cast<size_t>(c) * TC) * qrow
+                      : reinterpret_cast<const int8_t*>(p->dev_in[c & 1]);
+    };
+    auto dsrc = [&](uint32_t c) -> const float* {
+        return cached ? cached->dd + (static_cast<size_t>(f0) + static_cast<size_t>(c) * TC) * nb
+                      : reinterpret_cast<const float*>(p->dev_in[c & 1] + off_d);
+    };
     if (pinned(q, T * qrow) && pinned(d, T * drow) && pinned(out, ((T - 1) * os + rows) * 4)) {
         // page-locked: every chunk by DMA straight from q, d (and the rows
         // added to) and into out at its stride
@@ -727,10 +965,12 @@ int pkb_gemm_q8_host(float* out, size_t os, const int8_t* w, const float* ws, co
                 HOST_CUDA(cudaStreamWaitEvent(p->s_in, p->ev_comp[s], 0), "cudaStreamWaitEvent");
                 HOST_CUDA(cudaStreamWaitEvent(p->s_in, p->ev_out[s], 0), "cudaStreamWaitEvent");
             }
-            HOST_CUDA(cudaMemcpyAsync(p->dev_in[s], q + t0 * qrow, tc * qrow, cudaMemcpyHostToDevice, p->s_in),
-                      "upload");
-            HOST_CUDA(cudaMemcpyAsync(p->dev_in[s] + off_d, d + t0 * nb, tc * drow, cudaMemcpyHostToDevice, p->s_in),
-                      "upload");
+            if (!cached) {
+                HOST_CUDA(cudaMemcpyAsync(p->dev_in[s], q + t0 * qrow, tc * qrow, cudaMemcpyHostToDevice, p->s_in),
+                          "upload");
+                HOST_CUDA(cudaMemcpyAsync(p->dev_in[s] + off_d, d + t0 * nb, tc * drow, cudaMemcpyHostToDevice, p->s_in),
+                          "upload");
+            }
             if (add)
                 HOST_CUDA(cudaMemcpy2DAsync(p->dev_out[s], orow, out + t0 * os, os * 4, orow, tc,
                                             cudaMemcpyHostToDevice, p->s_in),
@@ -739,8 +979,7 @@ int pkb_gemm_q8_host(float* out, size_t os, const int8_t* w, const float* ws, co
             HOST_CUDA(cudaStreamWaitEvent(p->s_comp, p->ev_in[s], 0), "cudaStreamWaitEvent");
             if (c >= 2) HOST_CUDA(cudaStreamWaitEvent(p->s_comp, p->ev_out[s], 0), "cudaStreamWaitEvent");
             if ((rc = pkb_gemm_q8_dev(p->s_comp, reinterpret_cast<float*>(p->dev_out[s]), rows, wpack, dws, dbias,
-                                      rows, reinterpret_cast<const int8_t*>(p->dev_in[s]),
-                                      reinterpret_cast<const float*>(p->dev_in[s] + off_d), n, qb, tc, add, rmode)))
+                                      rows, qsrc(c), dsrc(c), n, qb, tc, add, rmode)))
                 return rc;
             HOST_CUDA(cudaEventRecord(p->ev_comp[s], p->s_comp), "cudaEventRecord");
             HOST_CUDA(cudaStreamWaitEvent(p->s_out, p->ev_comp[s], 0), "cudaStreamWaitEvent");
@@ -762,8 +1001,10 @@ int pkb_gemm_q8_host(float* out, size_t os, const int8_t* w, const float* ws, co
         const uint32_t tc = frames(c);
         const size_t t0 = static_cast<size_t>(c) * TC;
         if (c >= 2) HOST_CUDA(cudaEventSynchronize(p->ev_in[s]), "cudaEventSynchronize");
-        pool.copy(p->pin_in[s], q + t0 * qrow, tc * qrow);
-        pool.copy(p->pin_in[s] + off_d, d + t0 * nb, tc * drow);
+        if (!cached) {
+            pool.copy(p->pin_in[s], q + t0 * qrow, tc * qrow);
+            pool.copy(p->pin_in[s] + off_d, d + t0 * nb, tc * drow);
+        }
         if (add) {
             // the residual the product adds to: its rows, packed, into the
             // output slot (its previous chunk there was taken out already)
@@ -773,8 +1014,9 @@ int pkb_gemm_q8_host(float* out, size_t os, const int8_t* w, const float* ws, co
             HOST_CUDA(cudaStreamWaitEvent(p->s_in, p->ev_comp[s], 0), "cudaStreamWaitEvent");
             HOST_CUDA(cudaStreamWaitEvent(p->s_in, p->ev_out[s], 0), "cudaStreamWaitEvent");
         }
-        HOST_CUDA(cudaMemcpyAsync(p->dev_in[s], p->pin_in[s], off_d + tc * drow, cudaMemcpyHostToDevice, p->s_in),
-                  "upload");
+        if (!cached)
+            HOST_CUDA(cudaMemcpyAsync(p->dev_in[s], p->pin_in[s], off_d + tc * drow, cudaMemcpyHostToDevice, p->s_in),
+                      "upload");
         if (add)
             HOST_CUDA(cudaMemcpyAsync(p->dev_out[s], p->pin_out[s], tc * orow, cudaMemcpyHostToDevice, p->s_in),
                       "upload");
@@ -782,8 +1024,7 @@ int pkb_gemm_q8_host(float* out, size_t os, const int8_t* w, const float* ws, co
         HOST_CUDA(cudaStreamWaitEvent(p->s_comp, p->ev_in[s], 0), "cudaStreamWaitEvent");
         if (c >= 2) HOST_CUDA(cudaStreamWaitEvent(p->s_comp, p->ev_out[s], 0), "cudaStreamWaitEvent");
         if ((rc = pkb_gemm_q8_dev(p->s_comp, reinterpret_cast<float*>(p->dev_out[s]), rows, wpack, dws, dbias, rows,
-                                  reinterpret_cast<const int8_t*>(p->dev_in[s]),
-                                  reinterpret_cast<const float*>(p->dev_in[s] + off_d), n, qb, tc, add, rmode)))
+                                  qsrc(c), dsrc(c), n, qb, tc, add, rmode)))
             return rc;
         HOST_CUDA(cudaEventRecord(p->ev_comp[s], p->s_comp), "cudaEventRecord");
         HOST_CUDA(cudaStreamWaitEvent(p->s_out, p->ev_comp[s], 0), "cudaStreamWaitEvent");
@@ -814,6 +1055,7 @@ int pkb_forget(const void* ptr, size_t bytes) {
         }
         drop_pieces(c, lo, hi);
     }
+    for (ActCache& c : g_acts) act_forget(c, lo, bytes, lo, bytes);
     return PKB_OK;
 }
 

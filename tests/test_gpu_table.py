@@ -205,3 +205,53 @@ def test_benchmark_path_at_full_size(pkb, cuda_device):
         got = out.cpu().numpy()
         assert got.tobytes() == want.tobytes(), f"{name}: {int((got.view(np.uint32) != want.view(np.uint32)).sum())} differ"
     del graph
+
+
+@pytest.mark.parametrize("pinned", [False, True])
+def test_quantized_activations_reused_only_while_unchanged(pkb, cuda_device, pinned):
+    """A product reads the device copy of activations this library quantized
+    only while the caller's bytes and scales are still the ones written:
+    unchanged (whole range and a run of frames from inside it), one byte
+    changed, one scale changed, and the buffer quantized again - every call
+    the oracle's bits for the bytes the caller holds at that moment."""
+    import torch
+    T, n, qb, rows = 300, 1024, 32, 256
+    x = O.seeded_normal(T * n, 91)
+
+    def buf(a):
+        if not pinned:
+            return a.copy(), None
+        t = torch.empty(a.size, dtype={np.dtype(np.float32): torch.float32, np.dtype(np.int8): torch.int8}[a.dtype],
+                        pin_memory=True)
+        v = t.numpy()
+        v[:] = a
+        return v, t
+
+    q, tq = buf(np.zeros(T * n, np.int8))
+    d, td = buf(np.zeros(T * n // qb, np.float32))
+    out, to = buf(np.zeros(T * rows, np.float32))
+    w = O.pack_q8(O.uniform_weights(rows, n, 92))
+    ws = np.linspace(1e-3, 1e-2, rows).astype(np.float32)
+    tab = pkb.Table()
+    tab.quantize(pkb.PkAct(q.ctypes.data, d.ctypes.data, n, qb, T), x, n)
+
+    def check(label, t0=0, tn=T):
+        out[:] = 0
+        act = pkb.PkAct(q[t0 * n:].ctypes.data, d[t0 * (n // qb):].ctypes.data, n, qb, tn)
+        tab.gemm_q8(out, rows, w, ws, None, rows, act, False)
+        want = np.zeros(tn * rows, np.float32)
+        O.gemm_q8(want, rows, w, ws, None, rows, q[t0 * n:(t0 + tn) * n].copy(),
+                  d[t0 * (n // qb):(t0 + tn) * (n // qb)].copy(), n, qb, tn, False)
+        assert out[:tn * rows].tobytes() == want.tobytes(), label
+
+    check("unchanged")
+    check("frames 37..236 from inside", 37, 200)
+    q[5 * n + 17] = np.int8(-q[5 * n + 17] - 1)
+    check("one byte changed")
+    d[3] = np.float32(d[3] * 2)
+    check("one scale changed")
+    x2 = O.seeded_normal(T * n, 93)
+    tab.quantize(pkb.PkAct(q.ctypes.data, d.ctypes.data, n, qb, T), x2, n)
+    check("quantized again")
+    pkb.forget(q)
+    del tq, td, to
