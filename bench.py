@@ -822,20 +822,6 @@ def e2e_host(prods, steps: int, seed: int, lanes: int) -> dict:
                 outs[ok] = locked(p["M"] * p["rows"], np.float32)
                 outs[ok][:] = 0.0
         bufs.append((qs, ds, outs))
-    # the bytes each call copies: a quantize takes x in and gives q, d back;
-    # a product takes q, d, row scales, biases (and the results it adds to)
-    # in and gives its results back
-    h2d = d2h = 0
-    for lp in lane_prods:
-        held = {}
-        for p in lp:
-            nb, xk = p["n"] // QB, (p["M"], p["n"])
-            if held.get(xk) != p["inp"]:
-                h2d += p["M"] * p["n"] * 4
-                d2h += p["M"] * (p["n"] + 4 * nb)
-                held[xk] = p["inp"]
-            h2d += p["M"] * (p["n"] + 4 * nb) + 8 * p["rows"] + (p["M"] * p["rows"] * 4 if p["add"] else 0)
-            d2h += p["M"] * p["rows"] * 4
     device = __import__("torch").cuda.current_device()
 
     def lane(i: int):
@@ -858,11 +844,18 @@ def e2e_host(prods, steps: int, seed: int, lanes: int) -> dict:
             t.join()
 
     one()  # uploads and caches the weights, grows each lane's staging
+    # the bytes the library copied, as it counts them: a quantize takes x in
+    # and gives q, d back; a product takes q, d (unless it reads the device
+    # copy of the quantize that made them), row scales, biases and the rows
+    # it adds to in and gives its results back
+    up0, down0 = P.host_bytes()
     t0 = time.perf_counter()
     for _ in range(steps):
         one()
     sec = (time.perf_counter() - t0) / steps
-    return {"seconds_per_step": sec, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+    up1, down1 = P.host_bytes()
+    return {"seconds_per_step": sec, "h2d_bytes_per_step": (up1 - up0) // steps,
+            "d2h_bytes_per_step": (down1 - down0) // steps}
 
 
 def gemm_items(rows: int, T: int, nth: int) -> list[tuple[int, int, int, int]]:
@@ -971,15 +964,18 @@ def e2e_host_sliced(prods, steps: int, seed: int, nth: int) -> dict:
 
     one()  # uploads and caches the weights
     calls[0] = 0
+    up0, down0 = P.host_bytes()
     t0 = time.perf_counter()
     for _ in range(steps):
         one()
     sec = (time.perf_counter() - t0) / steps
+    up1, down1 = P.host_bytes()
     work["p"] = None
     start.wait()
     for t in ts:
         t.join()
-    return {"seconds_per_step": sec, "calls_per_step": calls[0] // max(1, steps), "threads": nth}
+    return {"seconds_per_step": sec, "calls_per_step": calls[0] // max(1, steps), "threads": nth,
+            "h2d_bytes_per_step": (up1 - up0) // steps, "d2h_bytes_per_step": (down1 - down0) // steps}
 
 
 # -------------------------------------------------------------- the arms --
@@ -1093,16 +1089,20 @@ def run_ours(args) -> None:
                "audio_s_per_s": e_audio / sec,
                "path": "pk_kernels_cuda_b200 table (quantize + gemm_q8 on host buffers: activations and results "
                        "page-locked, weights in ordinary memory), whole matrices a call, "
-                       f"{args.e2e_lanes} lanes of calls at once on each rank; the encoder's products",
+                       f"{args.e2e_lanes} lanes of calls at once on each rank; the encoder's products; "
+                       "bytes as the library counts its copies (pkb_host_bytes): a product whose q and d "
+                       "are a quantize result still held on the device does not upload them",
                "steps": e2e_steps,
                "lanes": args.e2e_lanes}
-    if e2e is not None and not args.no_sliced:
-        # the engine's call pattern (slices from a pool of host threads)
-        if dist:
-            dist.barrier(device_ids=[local])
+    if e2e is not None and not args.no_sliced and world == 1:
+        # the engine's call pattern (slices from a pool of host threads); one
+        # GPU only, as the pool's threads of several ranks would share the
+        # host's cores
         sl = e2e_host_sliced(prods, max(1, min(args.steps, 3)), SEED + 11 + rank, args.e2e_threads)
         sec, e_ops, _ = job_totals(dist, dev, sl["seconds_per_step"], step_ops(prods), audio_seconds(segs))
         e2e["engine_sliced"] = {"value": e_ops / sec / 1e12, "unit": "TOPS", "calls_per_step": sl["calls_per_step"],
+                                "h2d_bytes_per_step": int(sl["h2d_bytes_per_step"]),
+                                "d2h_bytes_per_step": int(sl["d2h_bytes_per_step"]),
                                 "threads": sl["threads"], "steps": max(1, min(args.steps, 3)),
                                 "path": "pk_kernels_cuda_b200 table as the reference's engine calls it: each input "
                                         "quantized in one call, each product in pk_gemm_on's slices of 64/256 rows "

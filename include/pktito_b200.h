@@ -201,6 +201,14 @@ int pkb_dwconv_quantize_dev(void *stream, int8_t *q, float *d, float *out, size_
  * device: the evidence a benchmark reports for its own kernels' work. */
 uint64_t pkb_launch_count(void);
 
+/* Bytes the host-pointer calls (pkb_*_host, the cuda-b200 table) copied
+ * from host to device (*up: inputs, row scales, weights when uploaded) and
+ * back (*down: results, the device error word), since the process started,
+ * on every device. Activations a product reads from the device copy of a
+ * quantize result count nothing. No counterpart in the reference. Either
+ * pointer may be null. */
+void pkb_host_bytes(uint64_t* up, uint64_t* down);
+
 /* ------------------------------------------------- without allocating -- */
 
 /* Bytes of the fixed device staging pkb_quantize_host_noalloc works in. */

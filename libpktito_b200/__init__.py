@@ -100,6 +100,7 @@ _SIGS = {
                                               ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32,
                                               ctypes.c_uint32, ctypes.c_uint32, ctypes.c_int]),
     "pkb_launch_count": (ctypes.c_uint64, []),
+    "pkb_host_bytes": (None, [ctypes.c_void_p, ctypes.c_void_p]),
     "pkb_quantize_host_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,
                                                  ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]),
 }
@@ -162,6 +163,13 @@ def device_errors(dev: int = 0) -> int:
 
 def launch_count() -> int:
     return int(lib().pkb_launch_count())
+
+
+def host_bytes() -> tuple[int, int]:
+    """(host to device, device to host) bytes the host-pointer calls copied."""
+    up, down = ctypes.c_uint64(), ctypes.c_uint64()
+    lib().pkb_host_bytes(ctypes.byref(up), ctypes.byref(down))
+    return int(up.value), int(down.value)
 
 
 def _ptr(a) -> int:

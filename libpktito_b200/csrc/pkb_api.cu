@@ -27,6 +27,7 @@ constexpr int MAX_DEV = 16;
 
 thread_local char tl_err[512];
 std::atomic<uint64_t> g_launches{0};
+std::atomic<uint64_t> g_up{0}, g_down{0};
 
 int fail(int code, const char* fmt, ...) {
     va_list ap;
@@ -434,6 +435,11 @@ int current_device_info(int* sms, uint32_t** err_word) {
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
+void count_host_bytes(size_t up, size_t down) {
+    g_up.fetch_add(up, std::memory_order_relaxed);
+    g_down.fetch_add(down, std::memory_order_relaxed);
+}
+
 int set_error(int code, const char* fmt, ...) {
     va_list ap;
     va_start(ap, fmt);
@@ -479,6 +485,11 @@ int pkb_device_errors(int device, uint32_t* word) {
 }
 
 uint64_t pkb_launch_count(void) { return g_launches.load(); }
+
+void pkb_host_bytes(uint64_t* up, uint64_t* down) {
+    if (up) *up = g_up.load();
+    if (down) *down = g_down.load();
+}
 
 size_t pkb_wpack_bytes(uint32_t rows, uint32_t n) { return static_cast<size_t>(rows) * n; }
 

@@ -220,6 +220,32 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
 }
 
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// mbar_wait by polling: test_wait never suspends the thread, and the abort
+// flag and the clock are read once every 256 tries; the same bounds.
+__device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity, volatile int* abort, long long limit) {
+    if (mbar_test_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (uint32_t i = 0;; i++) {
+        if (mbar_test_wait(bar, parity)) return true;
+        if ((i & 255) == 255) {
+            if (*abort) return false;
+            if (clock64() - t0 > limit) return false;
+        }
+    }
+}
+
 // The same wait without the abort flag, still bounded: for a role that has
 // given up and must let its own copies or MMAs in flight land before the CTA
 // frees its shared memory and TMEM.

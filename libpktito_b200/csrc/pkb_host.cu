@@ -311,6 +311,7 @@ struct Pipe {
     // All three streams drained; the device error word read and cleared.
     int finish(uint32_t* err_word) {
         HOST_CUDA(cudaMemcpyAsync(herr, err_word, sizeof(uint32_t), cudaMemcpyDeviceToHost, s_out), "error word read");
+        count_host_bytes(0, sizeof(uint32_t));
         HOST_CUDA(cudaStreamSynchronize(s_in), "cudaStreamSynchronize");
         HOST_CUDA(cudaStreamSynchronize(s_comp), "cudaStreamSynchronize");
         HOST_CUDA(cudaStreamSynchronize(s_out), "cudaStreamSynchronize");
@@ -582,6 +583,7 @@ int weights_for(Pipe& p, const int8_t* w, uint32_t rows, uint32_t n, const int8_
     CopyPool::get().copy(shadow->data(), w, bytes);
     CopyPool::get().copy(p.pin_in[0], shadow->data(), bytes);
     HOST_CUDA(cudaMemcpyAsync(p.dev_in[0], p.pin_in[0], bytes, cudaMemcpyHostToDevice, p.s_comp), "weights upload");
+    count_host_bytes(bytes, 0);
     if ((rc = pkb_repack_q8_dev(p.s_comp, m->buf->p + (a - lo), reinterpret_cast<int8_t*>(p.dev_in[0]), rows, n)))
         return rc;
     HOST_CUDA(cudaStreamSynchronize(p.s_comp), "weights upload");
@@ -868,6 +870,7 @@ int pkb_quantize_host(int8_t* q, float* d, uint32_t n, uint32_t qb, uint32_t T, 
             HOST_CUDA(cudaMemcpyAsync(d + t0 * nb, dd_of(c), tc * drow, cudaMemcpyDeviceToHost, p->s_out), "download");
             HOST_CUDA(cudaEventRecord(p->ev_out[s], p->s_out), "cudaEventRecord");
         }
+        count_host_bytes(T * xrow, T * (qrow + drow));
         if ((rc = p->finish(err))) return rc;
         remember();
         return PKB_OK;
@@ -900,6 +903,7 @@ int pkb_quantize_host(int8_t* q, float* d, uint32_t n, uint32_t qb, uint32_t T, 
         HOST_CUDA(cudaEventRecord(p->ev_out[s], p->s_out), "cudaEventRecord");
         if (c >= 1 && (rc = take_out(c - 1))) return rc;
     }
+    count_host_bytes(T * xrow, T * (qrow + drow));
     if ((rc = p->finish(err))) return rc;
     if ((rc = take_out(nchunks - 1))) return rc;
     remember();
@@ -935,6 +939,7 @@ int pkb_gemm_q8_host(float* out, size_t os, const int8_t* w, const float* ws, co
     if (bias) memcpy(p->pin_vec + up256(orow), bias, orow);
     HOST_CUDA(cudaMemcpyAsync(p->dev_vec, p->pin_vec, up256(orow) + orow, cudaMemcpyHostToDevice, p->s_comp),
               "upload");
+    count_host_bytes(up256(orow) + orow, 0);
     const float* dws = reinterpret_cast<const float*>(p->dev_vec);
     const float* dbias = bias ? reinterpret_cast<const float*>(p->dev_vec + up256(orow)) : nullptr;
     const uint32_t nchunks = (T + TC - 1) / TC;
@@ -988,6 +993,7 @@ int pkb_gemm_q8_host(float* out, size_t os, const int8_t* w, const float* ws, co
                       "download");
             HOST_CUDA(cudaEventRecord(p->ev_out[s], p->s_out), "cudaEventRecord");
         }
+        count_host_bytes(T * ((cached ? 0 : qrow + drow) + (add ? orow : 0)), T * orow);
         return p->finish(err);
     }
     auto take_out = [&](uint32_t c) -> int {  // chunk c's rows of out, at the caller's stride
@@ -1033,6 +1039,7 @@ int pkb_gemm_q8_host(float* out, size_t os, const int8_t* w, const float* ws, co
         HOST_CUDA(cudaEventRecord(p->ev_out[s], p->s_out), "cudaEventRecord");
         if (c >= 1 && (rc = take_out(c - 1))) return rc;
     }
+    count_host_bytes(T * ((cached ? 0 : qrow + drow) + (add ? orow : 0)), T * orow);
     if ((rc = p->finish(err))) return rc;
     return take_out(nchunks - 1);
 }

@@ -19,6 +19,9 @@ int current_device_info(int* sms, uint32_t** err_word);
 // One more kernel launched (pkb_launch_count).
 void count_launch();
 
+// Bytes a host-pointer call copied host to device and back (pkb_host_bytes).
+void count_host_bytes(size_t up, size_t down);
+
 // The device the calling thread's host-pointer calls run on
 // (pkb_set_thread_device; 0 until set).
 int thread_device();

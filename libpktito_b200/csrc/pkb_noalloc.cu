@@ -103,6 +103,7 @@ extern "C" int pkb_quantize_host_noalloc(int8_t* q, float* d, uint32_t n, uint32
     const cudaError_t e_sync = cudaStreamSynchronize(s);
     if (e == cudaSuccess) e = e_sync;
     if (e != cudaSuccess) return pkb::set_error(PKB_ECUDA, "quantize (no allocation): %s", cudaGetErrorString(e));
+    pkb::count_host_bytes(static_cast<size_t>(T) * n * 4, qbytes + dbytes + sizeof word);
     if (word) {
         const uint32_t zero = 0;
         cudaMemcpy(err_word, &zero, sizeof zero, cudaMemcpyHostToDevice);

@@ -233,25 +233,37 @@ def test_quantized_activations_reused_only_while_unchanged(pkb, cuda_device, pin
     w = O.pack_q8(O.uniform_weights(rows, n, 92))
     ws = np.linspace(1e-3, 1e-2, rows).astype(np.float32)
     tab = pkb.Table()
+    pkb.forget(w)  # an earlier matrix may have had this address
+    up0, down0 = pkb.host_bytes()
     tab.quantize(pkb.PkAct(q.ctypes.data, d.ctypes.data, n, qb, T), x, n)
+    up1, down1 = pkb.host_bytes()
+    assert (up1 - up0, down1 - down0) == (T * n * 4, T * (n + 4 * (n // qb)) + 4)
 
-    def check(label, t0=0, tn=T):
+    def check(label, t0=0, tn=T, reused=True, weights=False):
         out[:] = 0
         act = pkb.PkAct(q[t0 * n:].ctypes.data, d[t0 * (n // qb):].ctypes.data, n, qb, tn)
+        up0, down0 = pkb.host_bytes()
         tab.gemm_q8(out, rows, w, ws, None, rows, act, False)
+        up1, down1 = pkb.host_bytes()
         want = np.zeros(tn * rows, np.float32)
         O.gemm_q8(want, rows, w, ws, None, rows, q[t0 * n:(t0 + tn) * n].copy(),
                   d[t0 * (n // qb):(t0 + tn) * (n // qb)].copy(), n, qb, tn, False)
         assert out[:tn * rows].tobytes() == want.tobytes(), label
+        # the copies the call counted: row scales (and the biases' slot),
+        # the activations unless their device copy was read, the weights
+        # when uploaded; the results and the error word back
+        up = 2 * rows * 4 + (0 if reused else tn * (n + 4 * (n // qb))) + (rows * n if weights else 0)
+        assert (up1 - up0, down1 - down0) == (up, tn * rows * 4 + 4), label
 
-    check("unchanged")
+    check("unchanged", weights=True)
     check("frames 37..236 from inside", 37, 200)
     q[5 * n + 17] = np.int8(-q[5 * n + 17] - 1)
-    check("one byte changed")
+    check("one byte changed", reused=False)
     d[3] = np.float32(d[3] * 2)
-    check("one scale changed")
+    check("one scale changed", reused=False)
     x2 = O.seeded_normal(T * n, 93)
     tab.quantize(pkb.PkAct(q.ctypes.data, d.ctypes.data, n, qb, T), x2, n)
     check("quantized again")
     pkb.forget(q)
+    pkb.forget(w)
     del tq, td, to
