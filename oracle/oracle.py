@@ -82,6 +82,11 @@ def olib() -> ctypes.CDLL:
         l.oracle_dwconv_quantize.argtypes = [vp, vp, vp, sz, vp, sz, u32, u32, vp, vp, u32, i32, u32, i32]
         l.oracle_panels_kp.argtypes = [vp, vp, u32, u32, u32, u32]
         l.oracle_panels_kp.restype = None
+        l.oracle_gemm_f32.argtypes = [vp, sz, vp, u32, u32, u32, vp, sz, u32, vp, sz, i32, i32]
+        l.oracle_softmax.argtypes = [vp, sz, u32, u32, f32, i32]
+        l.oracle_attention.argtypes = [vp, sz, vp, sz, vp, vp, vp, vp, vp, u32, u32, u32, i32]
+        for f in (l.oracle_gemm_f32, l.oracle_softmax, l.oracle_attention):
+            f.restype = None
         for f in (l.oracle_set_rint_style, l.oracle_expf, l.oracle_sigmoidf, l.oracle_layernorm,
                   l.oracle_layernorm_quantize, l.oracle_silu_quantize, l.oracle_dwconv_quantize):
             f.restype = None
@@ -240,6 +245,28 @@ def dwconv_quantize(x: np.ndarray, xs: int, T: int, C: int, w: np.ndarray, b: np
     return q, d, out
 
 
+def gemm_f32(out: np.ndarray, os_: int, w: np.ndarray, ld: int, rows: int, n: int, x: np.ndarray, xs: int, T: int,
+             bias: Optional[np.ndarray], bs: int, relu: bool, rmode: int = RN, w_off: int = 0) -> None:
+    """k_gemm_f32 (backend/ref/kernels.c:90-105) into out (written in place);
+    w_off: the float of w the call's w points at (a run inside the panels)."""
+    olib().oracle_gemm_f32(_p(out), os_, _p(w) + 4 * w_off, ld, rows, n, _p(x), xs, T, _p(bias), bs, int(relu),
+                           rmode)
+
+
+def softmax(x: np.ndarray, xs: int, T: int, n: int, scale: float, rmode: int = RN) -> None:
+    """k_softmax (backend/ref/kernels.c:134-147) on T rows, in place."""
+    olib().oracle_softmax(_p(x), xs, T, n, float(np.float32(scale)), rmode)
+
+
+def attention(q: np.ndarray, qs: int, kp: np.ndarray, pp: np.ndarray, vp: np.ndarray, bias_u: np.ndarray,
+              bias_v: np.ndarray, T: int, D: int, H: int, rmode: int = RN) -> np.ndarray:
+    """att_item (core/encoder.c:280-326) over every head and query: o [T][D]."""
+    o = np.zeros((T, D), np.float32)
+    olib().oracle_attention(_p(o), D, _p(_f32(q)), qs, _p(_f32(kp)), _p(_f32(pp)), _p(_f32(vp)), _p(_f32(bias_u)),
+                            _p(_f32(bias_v)), T, D, H, rmode)
+    return o
+
+
 def _f32(a: np.ndarray) -> np.ndarray:
     a = np.ascontiguousarray(a, np.float32).reshape(-1)
     return a
@@ -279,6 +306,68 @@ def ref_gemm_q8(out: np.ndarray, os_: int, w: np.ndarray, ws: np.ndarray, bias: 
     act = _Act(_p(q), _p(d), n, qb, T)
     k = _Table.in_dll(rlib(), "pk_kernels_ref")
     _with_mode(rmode, lambda: k.gemm_q8(_p(out), os_, _p(w), _p(ws), _p(bias), rows, ctypes.byref(act), int(add)))
+
+
+def ref_gemm_f32(out: np.ndarray, os_: int, w: np.ndarray, ld: int, rows: int, n: int, x: np.ndarray, xs: int,
+                 T: int, bias: Optional[np.ndarray], bs: int, relu: bool, rmode: int = RN, w_off: int = 0) -> None:
+    k = _Table.in_dll(rlib(), "pk_kernels_ref")
+    _with_mode(rmode, lambda: k.gemm_f32(_p(out), os_, _p(w) + 4 * w_off, ld, rows, n, _p(x), xs, T, _p(bias), bs,
+                                         int(relu)))
+
+
+def ref_softmax(x: np.ndarray, xs: int, T: int, n: int, scale: float, rmode: int = RN) -> None:
+    k = _Table.in_dll(rlib(), "pk_kernels_ref")
+    scale = float(np.float32(scale))  # a float already: ctypes' conversion would round in the mode
+
+    def run():
+        for t in range(T):
+            k.softmax(_p(x) + 4 * t * xs, n, scale)
+    _with_mode(rmode, run)
+
+
+def ref_attention(q: np.ndarray, qs: int, kp: np.ndarray, pp: np.ndarray, vp: np.ndarray, bias_u: np.ndarray,
+                  bias_v: np.ndarray, T: int, D: int, H: int, block: int = 16) -> np.ndarray:
+    """att_item (core/encoder.c:280-326) as the reference runs it, under
+    round-to-nearest: per head and block of `block` queries (PK_ATT_BLOCK,
+    core/asr.h:16), the query rows with each position bias (numpy's float32
+    adds), its ref backend's gemm_f32 for the scores over Tp keys and for the
+    position products over the block's window of rows from a panel
+    boundary, the scores plus their positions, its softmax row by row, and
+    its gemm_f32 for the weighted values."""
+    k = _Table.in_dll(rlib(), "pk_kernels_ref")
+    q = _f32(q)
+    kp, pp, vp, bias_u, bias_v = _f32(kp), _f32(pp), _f32(vp), _f32(bias_u), _f32(bias_v)
+    dk = D // H
+    Tp = (T + 15) // 16 * 16
+    Pp = (2 * T - 1 + 15) // 16 * 16 + 16
+    o = np.zeros((T, D), np.float32)
+    scale = np.float32(1.0) / np.sqrt(np.float32(dk))
+    for h in range(H):
+        for i0 in range(0, T, block):
+            i1 = min(i0 + block, T)
+            nq = i1 - i0
+            qh = q.reshape(-1)[:].view(np.float32)
+            rows_q = np.stack([qh[(i0 + i) * qs + h * dk:(i0 + i) * qs + h * dk + dk] for i in range(nq)])
+            qu = np.ascontiguousarray(rows_q + bias_u[h * dk:(h + 1) * dk], np.float32)
+            qv = np.ascontiguousarray(rows_q + bias_v[h * dk:(h + 1) * dk], np.float32)
+            sc = np.zeros(nq * Tp, np.float32)
+            k.gemm_f32(_p(sc), Tp, _p(kp) + 4 * h * Tp * dk, dk, Tp, dk, _p(qu), dk, nq, 0, 0, 0)
+            m_lo, m_hi = T - i1, 2 * T - 2 - i0
+            m_a = m_lo & ~15
+            rows = (m_hi + 1 - m_a + 15) // 16 * 16
+            bd = np.zeros(nq * rows, np.float32)
+            k.gemm_f32(_p(bd), rows, _p(pp) + 4 * (h * Pp * dk + (m_a // 16) * dk * 16), dk, rows, dk, _p(qv), dk,
+                       nq, 0, 0, 0)
+            for i in range(i0, i1):
+                srow = sc[(i - i0) * Tp:(i - i0) * Tp + T]
+                b0 = (i - i0) * rows + (T - 1 - i) - m_a
+                srow[:] = srow + bd[b0:b0 + T]
+                k.softmax(_p(sc) + 4 * (i - i0) * Tp, T, float(scale))
+            out = np.zeros(nq * D, np.float32)
+            k.gemm_f32(_p(out) + 4 * h * dk, D, _p(vp) + 4 * h * (dk // 16) * T * 16, T, dk, T, _p(sc), Tp, nq,
+                       0, 0, 0)
+            o[i0:i1, h * dk:(h + 1) * dk] = out.reshape(nq, D)[:, h * dk:(h + 1) * dk]
+    return o
 
 
 # ------------------------------- the reference's fastest backend, threaded --

@@ -19,6 +19,11 @@
  *   oracle_dwconv_quantize     glu_item + dw_item, core/encoder.c:160-183
  *                    (k_glu :157-161, k_dwconv :163-177)
  *   oracle_expf, oracle_sigmoidf  pk_expf, pk_sigmoidf, core/vmath.h:93-151
+ *   and the attention's float work that reads the products' K, P and V panels:
+ *   oracle_gemm_f32   k_gemm_f32, backend/ref/kernels.c:90-105 (contract
+ *                    backend/kernels.h:88-103)
+ *   oracle_softmax    k_softmax, backend/ref/kernels.c:134-147
+ *   oracle_attention  att_item, core/encoder.c:280-326, every head and query
  *
  * Both take the rounding mode as an argument (PKB_RN/RD/RU/RZ, the codes of
  * include/pktito_b200.h) and run their float arithmetic under it, since the
@@ -392,4 +397,117 @@ void oracle_panels_kp(float *dst, const float *src, uint32_t n, uint32_t np, uin
             dst[(((size_t)h * np + (j / 16) * 16) * dk) + (size_t)d * 16 + j % 16] =
                 j < n ? src[(size_t)j * D + r] : 0.0f;
     }
+}
+
+/* ---------------------------------------- the attention's float products -- */
+
+/* k_gemm_f32 (backend/ref/kernels.c:90-105; contract backend/kernels.h:88-103)
+ * in the current mode: w in panels of 16 rows, ld k to a panel, w at the
+ * first k of the run; each of a panel's 16 outputs for column t is one fused
+ * chain over k from +0, then + the bias (bias[t*bs + r], or + 0.0f without
+ * one), then the ReLU (v > 0 ? v : 0). out may be bias itself (os == bs). */
+static void or_gemm_f32(float *out, size_t os, const float *w, uint32_t ld, uint32_t rows, uint32_t n,
+                        const float *x, size_t xs, uint32_t T, const float *bias, size_t bs, int relu) {
+    for (uint32_t t = 0; t < T; t++)
+        for (uint32_t p = 0; p < rows / 16; p++) {
+            const float *wp = w + (size_t)p * ld * 16, *xt = x + (size_t)t * xs;
+            float acc[16] = { 0 };
+            for (uint32_t k = 0; k < n; k++)
+                for (int i = 0; i < 16; i++)
+                    acc[i] = fmaf(wp[16 * (size_t)k + i], xt[k], acc[i]);
+            for (int i = 0; i < 16; i++) {
+                const float v = acc[i] + (bias ? bias[(size_t)t * bs + 16 * p + i] : 0.0f);
+                out[(size_t)t * os + 16 * p + i] = relu ? (v > 0 ? v : 0) : v;
+            }
+        }
+}
+
+void oracle_gemm_f32(float *out, size_t os, const float *w, uint32_t ld, uint32_t rows, uint32_t n, const float *x,
+                     size_t xs, uint32_t T, const float *bias, size_t bs, int relu, int rmode) {
+    const int was = fegetround();
+    fesetround(fe_of(rmode));
+    or_gemm_f32(out, os, w, ld, rows, n, x, xs, T, bias, bs, relu);
+    fesetround(was);
+}
+
+/* k_softmax (backend/ref/kernels.c:134-147) on one row, in place: y = x *
+ * scale and its maximum (fmaxf, so a NaN is passed over), e = pk_expf(y -
+ * m), the sum of the e in 16 lanes folded 8, 4, 2, 1, then e * (1 / sum). */
+static void or_softmax(float *x, uint32_t n, float scale) {
+    float m = -INFINITY;
+    for (uint32_t i = 0; i < n; i++) {
+        x[i] = x[i] * scale;
+        m = fmaxf(m, x[i]);
+    }
+    float acc[16] = { 0 };
+    for (uint32_t i = 0; i < n; i++) {
+        x[i] = or_expf(x[i] - m);
+        acc[i % 16] = acc[i % 16] + x[i];
+    }
+    const float inv = 1.0f / or_fold16(acc);
+    for (uint32_t i = 0; i < n; i++)
+        x[i] = x[i] * inv;
+}
+
+/* T rows of n scores, row t at x + t*xs, each softmaxed in place */
+void oracle_softmax(float *x, size_t xs, uint32_t T, uint32_t n, float scale, int rmode) {
+    const int was = fegetround();
+    fesetround(fe_of(rmode));
+    for (uint32_t t = 0; t < T; t++)
+        or_softmax(x + (size_t)t * xs, n, scale);
+    fesetround(was);
+}
+
+/* att_item (core/encoder.c:280-326) for every head and every query of one
+ * segment of T frames, in the current mode. q: rows of D floats at stride
+ * qs; kp, pp: the K and P panels (head h at kp + h*Tp*dk and pp + h*Pp*dk,
+ * Tp = T rounded up to 16, Pp = 2T-1 rounded up to 16, plus 16); vp: the V
+ * panels (head h at vp + h*(dk/16)*T*16). Query i of head h:
+ *
+ *   qu = q_i + bias_u, qv = q_i + bias_v                  (per dimension)
+ *   s_k = (qu . K_k + 0) + (qv . P_{T-1-i+k} + 0)         each dot one fused chain over d
+ *   softmax(s, T, 1 / sqrtf(dk))
+ *   o_i = V^T s + 0                                       one fused chain over k
+ *
+ * The reference takes the position products over a window of rows per
+ * block of 16 queries, and its queries in blocks: neither changes a value,
+ * so this takes them query by query. */
+void oracle_attention(float *o, size_t os, const float *q, size_t qs, const float *kp, const float *pp,
+                      const float *vp, const float *bias_u, const float *bias_v, uint32_t T, uint32_t D, uint32_t H,
+                      int rmode) {
+    const int was = fegetround();
+    fesetround(fe_of(rmode));
+    const uint32_t dk = D / H, Tp = (T + 15) & ~15u, Pp = ((2 * T - 1 + 15) & ~15u) + 16;
+    float *qu = malloc(dk * sizeof *qu), *qv = malloc(dk * sizeof *qv), *s = malloc((size_t)T * sizeof *s);
+    const float scale = 1.0f / sqrtf((float)dk);
+    for (uint32_t h = 0; h < H; h++) {
+        const float *kh = kp + (size_t)h * Tp * dk, *ph = pp + (size_t)h * Pp * dk;
+        const float *vh = vp + (size_t)h * (dk / 16) * T * 16;
+        for (uint32_t i = 0; i < T; i++) {
+            for (uint32_t d = 0; d < dk; d++) {
+                qu[d] = q[(size_t)i * qs + h * dk + d] + bias_u[h * dk + d];
+                qv[d] = q[(size_t)i * qs + h * dk + d] + bias_v[h * dk + d];
+            }
+            for (uint32_t k = 0; k < T; k++) {
+                const uint32_t r = T - 1 - i + k;
+                float a = 0.0f, b = 0.0f;
+                for (uint32_t d = 0; d < dk; d++) {
+                    a = fmaf(kh[((size_t)(k / 16) * dk + d) * 16 + k % 16], qu[d], a);
+                    b = fmaf(ph[((size_t)(r / 16) * dk + d) * 16 + r % 16], qv[d], b);
+                }
+                s[k] = (a + 0.0f) + (b + 0.0f);
+            }
+            or_softmax(s, T, scale);
+            for (uint32_t d = 0; d < dk; d++) {
+                float acc = 0.0f;
+                for (uint32_t k = 0; k < T; k++)
+                    acc = fmaf(vh[((size_t)(d / 16) * T + k) * 16 + d % 16], s[k], acc);
+                o[(size_t)i * os + h * dk + d] = acc + 0.0f;
+            }
+        }
+    }
+    free(qu);
+    free(qv);
+    free(s);
+    fesetround(was);
 }

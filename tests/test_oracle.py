@@ -289,3 +289,68 @@ def test_fast_checker_is_the_oracle(T, rows, n, qb, add, bias):
     O.fast_gemm_q8(got, rows, w, ws, b, rows, q, d, n, qb, T, bool(add))
     O.gemm_q8(want, rows, w, ws, b, rows, qo, do, n, qb, T, bool(add))
     assert got.tobytes() == want.tobytes()
+
+
+# ------------------------------------------- the attention's float products --
+
+ATT_GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "attention_golden.npz")
+
+
+@pytest.fixture(scope="module")
+def att_golden():
+    return np.load(ATT_GOLDEN)
+
+
+def test_golden_gemm_f32_and_softmax(att_golden):
+    """k_gemm_f32 and k_softmax as restated give the reference's ref bits on
+    its kcheck-style cases (tests/golden/make_attention_golden.py): runs of
+    panels from inside a row, odd n and strides, no bias / one / a bias a
+    column written in place, ReLU, and awkward values (zeros of both signs,
+    subnormals, large ones)."""
+    from tests.golden import make_attention_golden as G
+    n = 0
+    for i, (meta, w, x, b) in enumerate(G.gemm_f32_cases()):
+        assert G.run_gemm_f32(O.gemm_f32, meta, w, x, b).tobytes() == att_golden[f"gf/{i}/out"].tobytes(), meta
+        n += 1
+    for i, s in enumerate(G.softmax_cases()):
+        O.softmax(s, s.size, 1, s.size, 0.0883883476)
+        assert s.tobytes() == att_golden[f"sm/{i}/y"].tobytes(), i
+        n += 1
+    assert n == 64
+
+
+def test_golden_attention(att_golden):
+    """att_item restated query by query equals the reference's own blocked
+    run of it (blocks of 16, the position window from a panel boundary)."""
+    from tests.golden import make_attention_golden as G
+    for i, (T, D, H) in enumerate(G.ATT):
+        q, kp, pp, vp, bu, bv = G.att_inputs(T, D, H, 300 + i)
+        o = O.attention(q, D, kp, pp, vp, bu, bv, T, D, H)
+        assert o.tobytes() == att_golden[f"att/{i}/o"].tobytes(), (T, D, H)
+
+
+@needs_ref
+@pytest.mark.parametrize("rmode", [O.RN, O.RD, O.RU, O.RZ])
+def test_live_reference_gemm_f32_and_softmax(rmode):
+    """The same restatements against the reference's ref live, in every
+    rounding mode (the softmax's exp with the compiled ref's rint)."""
+    from tests.golden import make_attention_golden as G
+    for meta, w, x, b in G.gemm_f32_cases():
+        got = G.run_gemm_f32(lambda *a, **k: O.gemm_f32(*a, rmode=rmode, **k), meta, w, x, b)
+        want = G.run_gemm_f32(lambda *a, **k: O.ref_gemm_f32(*a, rmode=rmode, **k), meta, w, x, b)
+        assert got.tobytes() == want.tobytes(), (meta, rmode)
+    for s in G.softmax_cases():
+        s1, s2 = s.copy(), s.copy()
+        with O.rint_style():
+            O.softmax(s1, s.size, 1, s.size, 0.0883883476, rmode)
+        O.ref_softmax(s2, s.size, 1, s.size, 0.0883883476, rmode)
+        assert s1.tobytes() == s2.tobytes(), (s.size, rmode)
+
+
+@needs_ref
+def test_live_reference_attention():
+    from tests.golden import make_attention_golden as G
+    for T, D, H in [(3, 32, 1), (31, 128, 2), (48, 64, 4), (70, 128, 1)]:
+        q, kp, pp, vp, bu, bv = G.att_inputs(T, D, H, T + D)
+        want = O.ref_attention(q, D, kp, pp, vp, bu, bv, T, D, H)
+        assert O.attention(q, D, kp, pp, vp, bu, bv, T, D, H).tobytes() == want.tobytes(), (T, D, H)
