@@ -52,6 +52,7 @@ METRIC = "int8 GEMM TOPS (% of B200 int8 peak); encoder audio-s/s at 1/2/4/8 GPU
 SEGMENTS = 64
 LAYERS = 24
 D, F, C = 1024, 4096, 256
+HEADS = 8  # the FastConformer's attention heads (dk 128)
 QB = 32
 SEED = 20261201
 CONCURRENT = ("q", "k", "v", "pos")  # a layer's products that read no other's results
@@ -636,6 +637,91 @@ def producers_roofline(model, T: int) -> dict:
     return out
 
 
+def attention_inputs(torch, Ts: list[int], seed: int):
+    """Seeded q, K, V and P rows of a batch of segments (the products'
+    outputs: frames one segment after another, P's 2T - 1 rows a segment
+    likewise), the position biases and the segment table."""
+    M, Rs = sum(Ts), sum(2 * t - 1 for t in Ts)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    q, k, v = (torch.randn(M * D, device="cuda", generator=g) for _ in range(3))
+    p = torch.randn(Rs * D, device="cuda", generator=g)
+    bu, bv = (0.1 * torch.randn(D, device="cuda", generator=g) for _ in range(2))
+    segs, f, r = [], 0, 0
+    for t in Ts:
+        segs.append((t, f, r))
+        f += t
+        r += 2 * t - 1
+    return q, k, v, p, bu, bv, segs
+
+
+def attention_check(torch, o, q, k, v, p, bu, bv, segs, picks) -> dict:
+    """The attention's outputs of the picked segments against the oracle's
+    att_item (core/encoder.c:280-326), K, P and V laid out as its panels."""
+    from oracle import oracle as O
+    dk = D // HEADS
+    qh, kh, vh, ph, oh = (t.view(-1, D).cpu().numpy() for t in (q, k, v, p, o))
+    bu_h, bv_h = bu.cpu().numpy(), bv.cpu().numpy()
+    bad = []
+    for i in picks:
+        T, f, r = segs[i]
+        R = 2 * T - 1
+        Tp, Pp = (T + 15) // 16 * 16, (R + 15) // 16 * 16 + 16
+        kp = O.panels_kp(np.ascontiguousarray(kh[f:f + T]).reshape(-1), T, Tp, D, dk)
+        pp = O.panels_kp(np.ascontiguousarray(ph[r:r + R]).reshape(-1), R, Pp, D, dk)
+        vp = np.ascontiguousarray(vh[f:f + T].reshape(T, D // 16, 16).transpose(1, 0, 2)).reshape(-1)
+        want = O.attention(np.ascontiguousarray(qh[f:f + T]), D, kp, pp, vp, bu_h, bv_h, T, D, HEADS)
+        if oh[f:f + T].tobytes() != want.tobytes():
+            bad.append(int(T))
+    return {"checked_segments": [int(segs[i][0]) for i in picks], "equal": len(picks) - len(bad), "mismatches": bad,
+            "checker": "the oracle's att_item (oracle/q8_oracle.c), pinned to the reference's ref backend"}
+
+
+def attention_timing(model, segs, sm_mhz) -> dict:
+    """The attention's float work of one layer (att_item, core/encoder.c:
+    280-326: every head and block of 16 queries of every segment) in one
+    launch of pkb_attention_rows_dev, K, V and P as the products' rows,
+    timed with CUDA events (the batch's q, K, V and P are 190 MB, over L2).
+    FLOPs: 2 x 3 T^2 dk a head (the scores, the position products at the
+    pairs the softmax reads, the weighted values); peak: the FP32 pipe's 128
+    lanes a cycle per SM (2 FLOPs an FMA) at the clock sampled in the timed
+    region. Then the shortest, a middle and the longest segment's outputs
+    against the oracle."""
+    torch, P = model.torch, model.P
+    Ts = [sg[3] for sg in segs]
+    q, k, v, p, bu, bv, sl = attention_inputs(torch, Ts, SEED + 123)
+    o = torch.empty(sum(Ts) * D, device="cuda")
+    s = torch.cuda.current_stream()
+
+    def run():
+        P.attention_rows_dev(o, D, q, D, k, D, v, D, p, D, bu, bv, D, HEADS, sl)
+
+    for _ in range(3):
+        run()
+    s.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10
+    e0.record(s)
+    for _ in range(reps):
+        run()
+    e1.record(s)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    dk = D // HEADS
+    flops = sum(6.0 * HEADS * t * t * dk for t in Ts)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    mhz = float(sm_mhz or 1965.0)
+    peak = sms * 128 * 2 * mhz * 1e6
+    order = sorted(range(len(Ts)), key=lambda i: Ts[i])
+    picks = [order[0], order[len(order) // 2], order[-1]]
+    return {"us": ms * 1e3, "tflops": flops / (ms * 1e-3) / 1e12, "peak_tflops": peak / 1e12,
+            "frac": flops / (ms * 1e-3) / peak, "bound": "fp32",
+            "peak_note": f"nominal: {sms} SMs x 128 FP32 lanes x 2 FLOPs at the sampled {mhz:.0f} MHz",
+            "flops_per_launch": flops, "segments": len(Ts), "frames": sum(Ts), "heads": HEADS, "dk": dk,
+            "launches_per_step": LAYERS,
+            "parity": attention_check(torch, o, q, k, v, p, bu, bv, sl, picks)}
+
+
 def decoder_batched(model, T: int, segs: int = SEGMENTS, layers: int = 2, P_: int = 640, J: int = 640,
                     vocab_out: int = 8208) -> dict:
     """The TDT decoder's int8 products with the batch's segments stepped in
@@ -1074,6 +1160,7 @@ def run_ours(args) -> None:
         roof["producers"] = producers_roofline(model, sum(sg[3] for sg in segs))
         roof["decoder_batched"] = decoder_batched(model, sum(sg[3] for sg in segs))
         roof["panels"] = panels_timing(model, sum(sg[3] for sg in segs))
+        roof["attention"] = attention_timing(model, segs, clk.get("sm_mhz"))
     e2e = None
     if not args.no_e2e:
         # every rank at once through the host table, each on its own
@@ -1328,6 +1415,21 @@ def run_panels_only() -> None:
                       "launches": P.launch_count(), "device_errors": P.device_errors(0)}))
 
 
+def run_attention_only() -> None:
+    """One layer's attention over the batch's 64 segments (the ncu capture's
+    case: 190 MB of q, K, V and P rows in, 47 MB of o out), one launch."""
+    import torch
+    import libpktito_b200 as P
+    torch.cuda.set_device(0)
+    Ts = [s[3] for s in segments(0)]
+    q, k, v, p, bu, bv, sl = attention_inputs(torch, Ts, SEED + 123)
+    o = torch.empty(sum(Ts) * D, device="cuda")
+    P.attention_rows_dev(o, D, q, D, k, D, v, D, p, D, bu, bv, D, HEADS, sl)
+    torch.cuda.synchronize()
+    print(json.dumps({"attention_only": f"{len(Ts)} segments, {sum(Ts)} frames, D {D}, {HEADS} heads",
+                      "launches": P.launch_count(), "device_errors": P.device_errors(0)}))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -1354,6 +1456,8 @@ def main() -> None:
                     help="only the dominant product (FF up at the batch's M), 3 launches: the ncu capture's case")
     ap.add_argument("--producers-only", action="store_true",
                     help="only the fused producers at the batch's frame count, 2 launches each: the ncu capture's case")
+    ap.add_argument("--attention-only", action="store_true",
+                    help="only one layer's attention over the batch, 1 launch: the ncu capture's case")
     ap.add_argument("--panels-only", action="store_true",
                     help="only the K/V products into plain rows, K panels and V panels, 1 launch each: the ncu "
                          "capture's case")
@@ -1367,6 +1471,8 @@ def main() -> None:
         run_panels_only()
     elif args.producers_only:
         run_producers_only()
+    elif args.attention_only:
+        run_attention_only()
     elif args.impl == "reference":
         run_reference(args)
     else:

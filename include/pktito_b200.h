@@ -197,6 +197,63 @@ int pkb_dwconv_quantize_dev(void *stream, int8_t *q, float *d, float *out, size_
                             uint32_t T, uint32_t C, const float *w, const float *b, uint32_t K, int glu,
                             uint32_t qb, int rmode);
 
+/* --------------------------------- the attention's float work (device) -- */
+
+/* pk_k_gemm_f32 (backend/kernels.h:88-103; backend/ref/kernels.c:90-105) on
+ * device buffers, enqueued on stream, bit for bit the reference's ref: w in
+ * panels of 16 rows, ld k to a panel, w at the first k of the run this call
+ * takes; out[t*os + r] = chain over k of fmaf(w(r, k), x[t*xs + k]) from +0,
+ * plus bias[t*bs + r] (bs 0: one bias for every column) or plus 0.0f without
+ * one, then max(v, 0) if relu. rows a multiple of 16; out may be bias
+ * itself (os == bs), no other argument may overlap out. The reference's
+ * table entry on host pointers is pkb_gemm_f32_host. */
+int pkb_gemm_f32_dev(void *stream, float *out, size_t os, const float *w, uint32_t ld, uint32_t rows, uint32_t n,
+                     const float *x, size_t xs, uint32_t T, const float *bias, size_t bs, int relu, int rmode);
+
+/* pk_k_softmax (backend/kernels.h:124-130; backend/ref/kernels.c:134-147)
+ * on T rows of n scores (row t at x + t*xs), each in place, on device
+ * buffers: y = x * scale, m = max(y), e = pk_expf(y - m), x = e * (1 / sum(e))
+ * with the sum in the reference's 16 lanes. One row is the table's call;
+ * pkb_softmax_host takes it on host memory. */
+int pkb_softmax_dev(void *stream, float *x, size_t xs, uint32_t T, uint32_t n, float scale, int rmode);
+
+/* att_item (core/encoder.c:280-326) over every head and query of one
+ * segment of T frames, on device buffers, bit for bit the reference's:
+ * query i of head h against key k scores
+ *   ((q_i + bias_u) . K_k + 0) + ((q_i + bias_v) . P_{T-1-i+k} + 0),
+ * each dot one chain of fmaf over the head's dk dimensions; those T scores
+ * through pk_k_softmax with scale 1 / sqrtf(dk); o_i = the chain over k of
+ * fmaf(V_k, weight_k) + 0, into o + i*os + h*dk. q: rows of D floats at
+ * stride qs. kp, pp and vp as the reference lays them out (and
+ * pkb_gemm_q8_panels_dev writes them): K panels of Tp = T rounded up to 16
+ * frames a head, P panels of Pp = (2T - 1 rounded up to 16) + 16 positions
+ * a head (PKB_PANELS_KP layout), V panels of ps = 16 T (PKB_PANELS_V).
+ * D = H * dk, dk a multiple of 16 up to 256; kp, pp, vp 16-byte aligned.
+ * T is bounded by shared memory (PKB_EINVAL beyond it; about 1,400 frames
+ * at dk 128). No counterpart in the backend table: the reference runs this
+ * in core/encoder.c from the table's gemm_f32 and softmax. */
+int pkb_attention_dev(void *stream, float *o, size_t os, const float *q, size_t qs, const float *kp,
+                      const float *pp, const float *vp, const float *bias_u, const float *bias_v, uint32_t T,
+                      uint32_t D, uint32_t H, int rmode);
+
+/* A segment of a batch for pkb_attention_rows_dev: T frames, its rows of
+ * q, K, V and o from frame f, its 2T - 1 rows of P from row p. */
+typedef struct {
+    uint32_t T, f, p;
+} pkb_att_segment;
+
+/* The same attention over a batch of segments in one launch, with q, K, V
+ * and P as plain rows of D floats (the products' own output, the batch's
+ * frames one after another): segment s's frame j at q + (f + j)*qs, K at
+ * k + (f + j)*ks, V at v + (f + j)*vs, o at o + (f + j)*os; its position row
+ * r at p + (p + r)*ps. k, p, v 16-byte aligned, ks, ps, vs multiples of 4.
+ * segs is host memory, read before the call returns. No counterpart in the
+ * backend table. */
+int pkb_attention_rows_dev(void *stream, float *o, size_t os, const float *q, size_t qs, const float *k, size_t ks,
+                           const float *v, size_t vs, const float *p, size_t ps, const float *bias_u,
+                           const float *bias_v, uint32_t D, uint32_t H, const pkb_att_segment *segs, uint32_t nseg,
+                           int rmode);
+
 /* Launches of libpktito_b200 kernels since the process started, on every
  * device: the evidence a benchmark reports for its own kernels' work. */
 uint64_t pkb_launch_count(void);

@@ -99,6 +99,21 @@ _SIGS = {
                                               ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p,
                                               ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32,
                                               ctypes.c_uint32, ctypes.c_uint32, ctypes.c_int]),
+    "pkb_gemm_f32_dev": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+                                        ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p,
+                                        ctypes.c_size_t, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t,
+                                        ctypes.c_int, ctypes.c_int]),
+    "pkb_softmax_dev": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint32,
+                                       ctypes.c_uint32, ctypes.c_float, ctypes.c_int]),
+    "pkb_attention_dev": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+                                         ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,
+                                         ctypes.c_uint32, ctypes.c_int]),
+    "pkb_attention_rows_dev": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+                                              ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+                                              ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+                                              ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p,
+                                              ctypes.c_uint32, ctypes.c_int]),
     "pkb_launch_count": (ctypes.c_uint64, []),
     "pkb_host_bytes": (None, [ctypes.c_void_p, ctypes.c_void_p]),
     "pkb_quantize_host_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,
@@ -270,6 +285,41 @@ def gemm_q8_panels_dev(panels, kind: int, ps: int, dk: int, tpad: int, wpack, ws
     """The product into the attention's V or K/P panels (core/passes.c:119-196)."""
     _check(lib().pkb_gemm_q8_panels_dev(_stream(stream), _ptr(panels), kind, ps, dk, tpad, _ptr(wpack), _ptr(ws), rows,
                                         _ptr(q), _ptr(d), n, qb, T, rmode))
+
+
+def gemm_f32_dev(out, os_: int, w, ld: int, rows: int, n: int, x, xs: int, T: int, bias, bs: int, relu: bool,
+                 rmode: int = RN, stream=None, w_off: int = 0) -> None:
+    """pk_k_gemm_f32 (backend/ref/kernels.c:90-105) on device buffers; w_off:
+    the float of w the call's run of panels starts at."""
+    _check(lib().pkb_gemm_f32_dev(_stream(stream), _ptr(out), os_, _ptr(w) + 4 * w_off, ld, rows, n, _ptr(x), xs, T,
+                                  _ptr(bias), bs, int(relu), rmode))
+
+
+def softmax_dev(x, xs: int, T: int, n: int, scale: float, rmode: int = RN, stream=None) -> None:
+    """pk_k_softmax (backend/ref/kernels.c:134-147) on T rows in place."""
+    _check(lib().pkb_softmax_dev(_stream(stream), _ptr(x), xs, T, n, float(np.float32(scale)), rmode))
+
+
+def attention_dev(o, os_: int, q, qs: int, kp, pp, vp, bias_u, bias_v, T: int, D: int, H: int, rmode: int = RN,
+                  stream=None) -> None:
+    """att_item (core/encoder.c:280-326) over one segment's heads and queries,
+    K, P and V in the reference's panel layouts."""
+    _check(lib().pkb_attention_dev(_stream(stream), _ptr(o), os_, _ptr(q), qs, _ptr(kp), _ptr(pp), _ptr(vp),
+                                   _ptr(bias_u), _ptr(bias_v), T, D, H, rmode))
+
+
+class AttSegment(ctypes.Structure):
+    _fields_ = [("T", ctypes.c_uint32), ("f", ctypes.c_uint32), ("p", ctypes.c_uint32)]
+
+
+def attention_rows_dev(o, os_: int, q, qs: int, k, ks: int, v, vs: int, p, ps: int, bias_u, bias_v, D: int, H: int,
+                       segs, rmode: int = RN, stream=None) -> None:
+    """The attention over a batch of segments, q, K, V and P as rows; segs:
+    (T, first frame, first position row) a segment."""
+    arr = (AttSegment * max(1, len(segs)))(*[AttSegment(*s) for s in segs])
+    _check(lib().pkb_attention_rows_dev(_stream(stream), _ptr(o), os_, _ptr(q), qs, _ptr(k), ks, _ptr(v), vs,
+                                        _ptr(p), ps, _ptr(bias_u), _ptr(bias_v), D, H, ctypes.addressof(arr),
+                                        len(segs), rmode))
 
 
 def repack_q8_dev(wpack, w_pk, rows: int, n: int, stream=None) -> None:

@@ -103,6 +103,7 @@ int current_device(Device** out) {
             PKB_CUDA(cudaGetSymbolAddress(&sym, g_device_error), "cudaGetSymbolAddress");
             d.err = static_cast<uint32_t*>(sym);
             PKB_CUDA(prepare_gemm_q8(), "kernel attributes");
+            PKB_CUDA(prepare_attention(), "kernel attributes");
             prepare_quantize();
             d.sms = prop.multiProcessorCount;
             wait_limit();
@@ -422,6 +423,112 @@ int repack_dev(cudaStream_t stream, int8_t* wpack, const int8_t* w_pk, uint32_t 
     return PKB_OK;
 }
 
+// ------------------------------------------------ the attention's floats --
+
+int gemm_f32_dev(cudaStream_t stream, float* out, size_t os, const float* w, uint32_t ld, uint32_t rows, uint32_t n,
+                 const float* x, size_t xs, uint32_t T, const float* bias, size_t bs, int relu, int rmode) {
+    int rc;
+    if ((rc = check_rmode(rmode))) return rc;
+    if (rows % 16) return fail(PKB_EINVAL, "gemm_f32: rows = %u, a multiple of 16", rows);
+    if (n > ld) return fail(PKB_EINVAL, "gemm_f32: n = %u beyond the panels' ld = %u", n, ld);
+    if (!T || !rows) return PKB_OK;
+    if (!out || !w || (n && !x)) return fail(PKB_EINVAL, "gemm_f32: null pointer");
+    if (T > 1 && os < rows) return fail(PKB_EINVAL, "gemm_f32: output stride %zu below rows = %u", os, rows);
+    if (T > 1 && xs < n) return fail(PKB_EINVAL, "gemm_f32: column stride %zu below n = %u", xs, n);
+    if (bias && bs && bs < rows) return fail(PKB_EINVAL, "gemm_f32: bias stride %zu below rows = %u", bs, rows);
+    if (T == 1) os = xs = rows;  // one column reads no stride
+    if (!aligned(out, 4) || !aligned(w, 4) || !aligned(x, 4) || (bias && !aligned(bias, 4)))
+        return fail(PKB_EINVAL, "gemm_f32: misaligned buffer");
+    if (T > 65535u * 32u) return fail(PKB_EINVAL, "gemm_f32: T = %u columns, at most %u", T, 65535u * 32u);
+    Device* dev;
+    if ((rc = current_device(&dev))) return rc;
+    PKB_CUDA(launch_gemm_f32(out, os, w, ld, rows, n, x, T == 1 ? n : xs, T, bias, bs, relu, rmode, stream),
+             "gemm_f32 launch");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return PKB_OK;
+}
+
+int softmax_dev(cudaStream_t stream, float* x, size_t xs, uint32_t T, uint32_t n, float scale, int rmode) {
+    int rc;
+    if ((rc = check_rmode(rmode))) return rc;
+    if (!T || !n) return PKB_OK;
+    if (!x) return fail(PKB_EINVAL, "softmax: null pointer");
+    if (T > 1 && xs < n) return fail(PKB_EINVAL, "softmax: row stride %zu below n = %u", xs, n);
+    if (!aligned(x, 4)) return fail(PKB_EINVAL, "softmax: misaligned buffer");
+    Device* dev;
+    if ((rc = current_device(&dev))) return rc;
+    PKB_CUDA(launch_softmax(x, T == 1 ? n : xs, T, n, scale, rmode, dev->sms, stream), "softmax launch");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return PKB_OK;
+}
+
+// The attention over segments (panels: one segment in the reference's
+// panel layouts; else rows), in launches of up to ATT_MAX_SEG segments, one
+// CTA a head and block of queries.
+int attention_dev(cudaStream_t stream, bool panels, float* o, size_t os, const float* q, size_t qs, const float* k,
+                  size_t ks, const float* v, size_t vs, const float* p, size_t ps, const float* bias_u,
+                  const float* bias_v, uint32_t D, uint32_t H, const pkb_att_segment* segs, uint32_t nseg, int rmode) {
+    int rc;
+    if ((rc = check_rmode(rmode))) return rc;
+    if (!H || !D || D % H || (D / H) % 16 || D / H > 256)
+        return fail(PKB_EINVAL, "attention: D = %u, H = %u: heads of a multiple of 16 up to 256", D, H);
+    if (!nseg) return PKB_OK;
+    if (!segs || !o || !q || !k || !v || !p || !bias_u || !bias_v) return fail(PKB_EINVAL, "attention: null pointer");
+    if (!aligned(o, 4) || !aligned(q, 4) || !aligned(bias_u, 4) || !aligned(bias_v, 4) || !aligned(k, 16) ||
+        !aligned(v, 16) || !aligned(p, 16))
+        return fail(PKB_EINVAL, "attention: misaligned buffer (K, P and V 16-byte aligned)");
+    if (!panels && (ks % 4 || vs % 4 || ps % 4))
+        return fail(PKB_EINVAL, "attention: K, V and P row strides must be multiples of 4 floats");
+    const uint32_t dk = D / H;
+    Device* dev;
+    if ((rc = current_device(&dev))) return rc;
+    const size_t smem_max = attention_smem_max();
+    for (uint32_t s0 = 0; s0 < nseg; s0 += ATT_MAX_SEG) {
+        AttArgs a = {};
+        a.o = o;
+        a.q = q;
+        a.k = k;
+        a.p = p;
+        a.v = v;
+        a.bu = bias_u;
+        a.bv = bias_v;
+        a.os = os;
+        a.qs = qs;
+        a.ks = ks;
+        a.ps = ps;
+        a.vs = vs;
+        a.dk = dk;
+        uint32_t tmax = 0;
+        uint64_t items = 0;
+        for (uint32_t s = s0; s < nseg && s < s0 + ATT_MAX_SEG; s++) {
+            const pkb_att_segment& g = segs[s];
+            if (!g.T) continue;
+            if (g.T > 1 && (os < D || qs < D || (!panels && (ks < D || vs < D))))
+                return fail(PKB_EINVAL, "attention: a row stride below D = %u", D);
+            if (!panels && 2 * static_cast<uint64_t>(g.T) - 1 > 1 && ps < D)
+                return fail(PKB_EINVAL, "attention: P's row stride %zu below D = %u", ps, D);
+            a.seg[a.nseg] = AttSeg{g.T, g.f, g.p, static_cast<uint32_t>(items)};
+            a.nseg++;
+            items += static_cast<uint64_t>(H) * ((g.T + attention_block() - 1) / attention_block());
+            tmax = g.T > tmax ? g.T : tmax;
+        }
+        if (!a.nseg) continue;
+        if (items >= (1ull << 31)) return fail(PKB_EINVAL, "attention: %llu blocks in one launch", (unsigned long long)items);
+        a.items = static_cast<uint32_t>(items);
+        // the scores' rows hold T, the position products' the widest window
+        // (T + 30 rounded up to 16)
+        a.sp = (tmax + 15) & ~15u;
+        a.bp = (tmax + 30 + 15) & ~15u;
+        const size_t smem = attention_smem(dk, a.sp, a.bp);
+        if (smem > smem_max)
+            return fail(PKB_EINVAL, "attention: T = %u needs %zu bytes of shared memory a block, above %zu", tmax, smem,
+                        smem_max);
+        PKB_CUDA(launch_attention(a, panels, rmode, stream), "attention launch");
+        g_launches.fetch_add(1, std::memory_order_relaxed);
+    }
+    return PKB_OK;
+}
+
 }  // namespace
 
 int current_device_info(int* sms, uint32_t** err_word) {
@@ -508,6 +615,32 @@ int pkb_dwconv_quantize_dev(void* stream, int8_t* q, float* d, float* out, size_
                             int rmode) {
     return pkb::dwconv_quantize_dev(static_cast<cudaStream_t>(stream), q, d, out, os, x, xs, T, C, w, b, K, glu, qb,
                                     rmode);
+}
+
+int pkb_gemm_f32_dev(void* stream, float* out, size_t os, const float* w, uint32_t ld, uint32_t rows, uint32_t n,
+                     const float* x, size_t xs, uint32_t T, const float* bias, size_t bs, int relu, int rmode) {
+    return pkb::gemm_f32_dev(static_cast<cudaStream_t>(stream), out, os, w, ld, rows, n, x, xs, T, bias, bs, relu,
+                             rmode);
+}
+
+int pkb_softmax_dev(void* stream, float* x, size_t xs, uint32_t T, uint32_t n, float scale, int rmode) {
+    return pkb::softmax_dev(static_cast<cudaStream_t>(stream), x, xs, T, n, scale, rmode);
+}
+
+int pkb_attention_dev(void* stream, float* o, size_t os, const float* q, size_t qs, const float* kp, const float* pp,
+                      const float* vp, const float* bias_u, const float* bias_v, uint32_t T, uint32_t D, uint32_t H,
+                      int rmode) {
+    const pkb_att_segment seg = {T, 0, 0};
+    return pkb::attention_dev(static_cast<cudaStream_t>(stream), true, o, os, q, qs, kp, 0, vp, 0, pp, 0, bias_u,
+                              bias_v, D, H, &seg, 1, rmode);
+}
+
+int pkb_attention_rows_dev(void* stream, float* o, size_t os, const float* q, size_t qs, const float* k, size_t ks,
+                           const float* v, size_t vs, const float* p, size_t ps, const float* bias_u,
+                           const float* bias_v, uint32_t D, uint32_t H, const pkb_att_segment* segs, uint32_t nseg,
+                           int rmode) {
+    return pkb::attention_dev(static_cast<cudaStream_t>(stream), false, o, os, q, qs, k, ks, v, vs, p, ps, bias_u,
+                              bias_v, D, H, segs, nseg, rmode);
 }
 
 int pkb_gemm_q8_panels_dev(void* stream, float* panels, int kind, size_t ps, uint32_t dk, uint32_t tpad,

@@ -107,6 +107,44 @@ cudaError_t launch_dwconv_quantize(int8_t* q, float* d, float* out, size_t os, c
                                    uint32_t C, const float* w, const float* bias, uint32_t K, bool glu, uint32_t qb,
                                    int rmode, cudaStream_t stream);
 
+// ----------------------------------------- the attention's float work --
+// (pkb_attn.cu)
+
+cudaError_t launch_gemm_f32(float* out, size_t os, const float* w, uint32_t ld, uint32_t rows, uint32_t n,
+                            const float* x, size_t xs, uint32_t T, const float* bias, size_t bs, int relu, int rmode,
+                            cudaStream_t stream);
+cudaError_t launch_softmax(float* x, size_t xs, uint32_t T, uint32_t n, float scale, int rmode, int num_sms,
+                           cudaStream_t stream);
+
+constexpr int ATT_MAX_SEG = 128;  // segments one attention launch takes
+
+// One segment of an attention launch: T frames; its q, o (and, laid out as
+// rows, K and V) rows from frame f; its P rows from row p; its CTAs from
+// item0 (H blocks of queries a head).
+struct AttSeg {
+    uint32_t T, f, p, item0;
+};
+
+struct AttArgs {
+    float* o;
+    const float *q, *k, *p, *v, *bu, *bv;
+    unsigned long long os, qs, ks, ps, vs;  // row strides, in floats (rows layout)
+    uint32_t dk, nseg, items;
+    uint32_t sp, bp;  // shared-memory row lengths of the scores and the position products
+    AttSeg seg[ATT_MAX_SEG];
+};
+
+// Shared memory a CTA takes for heads of dk and rows of sp and bp floats.
+size_t attention_smem(uint32_t dk, uint32_t sp, uint32_t bp);
+uint32_t attention_block();  // queries a CTA
+// panels: K, P, V as the reference's panels (one segment); else as rows.
+cudaError_t launch_attention(const AttArgs& a, bool panels, int rmode, cudaStream_t stream);
+// Lets the attention kernels take the device's largest shared memory (once,
+// at the device's set-up).
+cudaError_t prepare_attention();
+// The dynamic shared memory an attention CTA may take (set by prepare_attention).
+size_t attention_smem_max();
+
 cudaError_t launch_repack_q8(int8_t* wpack, const int8_t* w_pk, uint32_t rows, uint32_t n, int num_sms,
                              cudaStream_t stream);
 
