@@ -515,11 +515,8 @@ int attention_dev(cudaStream_t stream, bool panels, float* o, size_t os, const f
         if (!a.nseg) continue;
         if (items >= (1ull << 31)) return fail(PKB_EINVAL, "attention: %llu blocks in one launch", (unsigned long long)items);
         a.items = static_cast<uint32_t>(items);
-        // the scores' rows hold T, the position products' the widest window
-        // (T + 30 rounded up to 16)
-        a.sp = (tmax + 15) & ~15u;
-        a.bp = (tmax + 30 + 15) & ~15u;
-        const size_t smem = attention_smem(dk, a.sp, a.bp);
+        a.sp = (tmax + 15) & ~15u;  // the scores' rows hold T
+        const size_t smem = attention_smem(dk, a.sp);
         if (smem > smem_max)
             return fail(PKB_EINVAL, "attention: T = %u needs %zu bytes of shared memory a block, above %zu", tmax, smem,
                         smem_max);

@@ -149,23 +149,52 @@ __global__ void __launch_bounds__(SM_THREADS)
 
 constexpr int AQ = 16;           // queries a CTA: PK_ATT_BLOCK (core/asr.h:16)
 constexpr int A_THREADS = 128;
-constexpr int ACH = 64;          // keys, positions or values a staged chunk
+constexpr int AKC = 64;          // keys (or positions) a staged unit of K (P)
 
-// One CTA: head h, queries i0 .. i0 + nq - 1 of one segment of T frames.
+// The dimensions a unit of K or P carries: all of a head of up to 64,
+// else half (up to 128) or a quarter (up to 256), at most 64 and a
+// multiple of 4.
+__host__ __device__ __forceinline__ uint32_t att_dh(uint32_t dk) { return dk <= 64 ? dk : dk <= 128 ? dk / 2 : dk / 4; }
+// The keys a staged unit of V carries (all dk of them).
+__host__ __device__ __forceinline__ uint32_t att_vch(uint32_t dk) { return dk <= 128 ? 32 : 16; }
+
+// floats of one staging buffer: the larger of a K/P unit and a V unit in
+// either layout, with the padding that keeps a quarter-warp's 16-byte
+// loads on distinct bank groups
+__host__ __device__ __forceinline__ uint32_t att_buf(uint32_t dk) {
+    const uint32_t dh = att_dh(dk), vch = att_vch(dk);
+    const uint32_t kp_rows = AKC * (dh + 4), kp_pan = (AKC / 16) * (16 * dh + 16);
+    const uint32_t v_rows = vch * (dk + 4), v_pan = (dk / 16) * (16 * vch + 16);
+    uint32_t m = kp_rows > kp_pan ? kp_rows : kp_pan;
+    m = m > v_rows ? m : v_rows;
+    return m > v_pan ? m : v_pan;
+}
+
+// One CTA: head h, queries i0 .. i0 + nq - 1 (nq <= 16) of one segment of T
+// frames. Shared memory:
 //
-//   qu, qv   the queries plus each position bias, AQ rows of dk (+4)
-//   ST       a chunk of 64 rows of K, P or V (row j, dimension d at
-//            ST[j (dk + 4) + d]: 16-byte rows offset by one bank group, so
-//            the 8 lanes of a quarter-warp reading 8 rows hit 8 groups)
+//   qu, qv   the queries plus each position bias, AQ rows of dk + 4
+//   ST[2]    two staging buffers: the K, P and V units go through them in
+//            turn, the next unit's copies (cp.async) in flight while the
+//            CTA computes on the current one
 //   S        the scores, then the weights: AQ rows of SP >= T
-//   B        the position products over the block's window: AQ rows of BP
 //
-// Scores and position products: thread (kq, qp) takes queries 2 qp, 2 qp + 1
-// and rows kq, kq + 16, kq + 32, kq + 48 of each chunk, 8 chains over d,
-// 4 dimensions a step (two 16-byte loads of queries, four of rows, 32
-// FMAs). The weighted values: tile u = (query quad, dimension quad), 4 x 4
-// chains over k, 4 keys a step (four 16-byte loads of weights, four of
-// values, 64 FMAs).
+// The units, in order: K in chunks of 64 keys, each in pieces of dh
+// dimensions (the scores' chains run on across the pieces, d ascending);
+// P the same over the block's window of positions; V in chunks of VCH keys.
+// A K/P unit in the rows layout is row-major (key j, dimension d at
+// j (dh + 4) + d); in the panels layout it keeps the reference's order
+// (16-key groups, each dh dimensions of 16 keys, groups 16 dh + 16 apart).
+// V rows: key k, dimension d at k (dk + 4) + d; V panels: 16-dimension
+// panels of VCH keys, 16 VCH + 16 apart.
+//
+// Scores and position products: thread (kq, qp) takes queries 2 qp and
+// 2 qp + 1 and four keys of each chunk (rows: kq + 16 e; panels: 4 kq + e),
+// 8 chains over d, 4 dimensions a step (two 16-byte loads of queries, four
+// of K or P, 32 FMAs). Each position product is added to the score it
+// belongs to as soon as its chain is done: the pairs (query i, position
+// row T-1-i+k) are one to one with the scores (i, k). The weighted values:
+// tile (query quad, dimension quad), 4 x 4 chains over k, 4 keys a step.
 template <int RM, bool PANELS>
 __global__ void __launch_bounds__(A_THREADS) attention_kernel(const __grid_constant__ AttArgs a) {
     extern __shared__ __align__(16) float sm[];
@@ -185,28 +214,78 @@ __global__ void __launch_bounds__(A_THREADS) attention_kernel(const __grid_const
     }
     __syncthreads();
     const AttSeg sg = a.seg[s_seg];
-    const uint32_t T = sg.T, dk = a.dk, DS = dk + 4;
+    const uint32_t T = sg.T, dk = a.dk, DS = dk + 4, SP = a.sp;
+    const uint32_t dh = att_dh(dk), nh = dk / dh, vch = att_vch(dk), BUF = att_buf(dk);
     const uint32_t nqb = (T + AQ - 1) / AQ, local = blockIdx.x - sg.item0;
     const uint32_t h = local / nqb, i0 = (local % nqb) * AQ;
     const uint32_t nq = min(static_cast<uint32_t>(AQ), T - i0), i1 = i0 + nq;
     const uint32_t R = 2 * T - 1;
     // the position window: rows T - 1 - i + k for the block's queries i and
-    // keys k, from a panel boundary (as the reference takes it; a value
-    // does not depend on it)
+    // keys k, from a panel boundary (as the reference takes it)
     const uint32_t w0 = (T - i1) & ~15u, W = ((2 * T - 1 - i0 - w0) + 15) & ~15u;
     float* qu = sm;
     float* qv = qu + AQ * DS;
     float* ST = qv + AQ * DS;
-    float* S = ST + ACH * DS;
-    float* B = S + AQ * a.sp;
-    const uint32_t SP = a.sp, BP = a.bp;
+    float* S = ST + 2 * BUF;
 
-    // K, P and V of this segment and head
     const uint32_t Tp = (T + 15) & ~15u, Pp = ((R + 15) & ~15u) + 16;
     const float* kh = PANELS ? a.k + static_cast<size_t>(h) * Tp * dk : a.k + static_cast<size_t>(sg.f) * a.ks + h * dk;
     const float* ph = PANELS ? a.p + static_cast<size_t>(h) * Pp * dk : a.p + static_cast<size_t>(sg.p) * a.ps + h * dk;
     const float* vh = PANELS ? a.v + static_cast<size_t>(h) * (dk / 16) * T * 16
                              : a.v + static_cast<size_t>(sg.f) * a.vs + h * dk;
+
+    const uint32_t nkc = (T + AKC - 1) / AKC, npc = (W + AKC - 1) / AKC;
+    const uint32_t nK = nkc * nh, nP = npc * nh, nV = (T + vch - 1) / vch, U = nK + nP + nV;
+
+    // issues unit u's copies into buffer b (rows past the data are skipped:
+    // their results are never read)
+    auto issue = [&](uint32_t u, float* b) {
+        if (u < nK + nP) {
+            const bool isk = u < nK;
+            const uint32_t cu = isk ? u : u - nK, c = cu / nh, d0 = (cu % nh) * dh;
+            const uint32_t j0 = isk ? c * AKC : w0 + c * AKC;
+            const float* src = isk ? kh : ph;
+            const uint32_t valid = PANELS ? (isk ? Tp : Pp) : (isk ? T : R);
+            if constexpr (PANELS) {
+                // 16-key group g: dh x 16 floats at ((j0/16 + g) dk + d0) 16
+                const uint32_t n4 = dh * 4;  // 16-byte pieces a group
+                for (uint32_t e = tid; e < (AKC / 16) * n4; e += A_THREADS) {
+                    const uint32_t g = e / n4, o = e % n4;
+                    if (j0 + 16 * g < valid)
+                        cp_async16(b + g * (16 * dh + 16) + 4 * o,
+                                   src + (static_cast<size_t>(j0 / 16 + g) * dk + d0) * 16 + 4 * o);
+                }
+            } else {
+                const unsigned long long rs = isk ? a.ks : a.ps;
+                const uint32_t n4 = dh / 4;
+                for (uint32_t e = tid; e < AKC * n4; e += A_THREADS) {
+                    const uint32_t jj = e / n4, o = e % n4;
+                    if (j0 + jj < valid)
+                        cp_async16(b + jj * (dh + 4) + 4 * o, src + static_cast<size_t>(j0 + jj) * rs + d0 + 4 * o);
+                }
+            }
+        } else {
+            const uint32_t c0 = (u - nK - nP) * vch;
+            if constexpr (PANELS) {
+                // 16-dimension panel dp: vch x 16 floats at (dp T + c0) 16
+                const uint32_t n4 = vch * 4;
+                for (uint32_t e = tid; e < (dk / 16) * n4; e += A_THREADS) {
+                    const uint32_t dp = e / n4, o = e % n4;
+                    if (c0 + o / 4 < T)
+                        cp_async16(b + dp * (16 * vch + 16) + 4 * o, vh + (static_cast<size_t>(dp) * T + c0) * 16 + 4 * o);
+                }
+            } else {
+                const uint32_t n4 = dk / 4;
+                for (uint32_t e = tid; e < vch * n4; e += A_THREADS) {
+                    const uint32_t kk = e / n4, o = e % n4;
+                    if (c0 + kk < T) cp_async16(b + kk * DS + 4 * o, vh + static_cast<size_t>(c0 + kk) * a.vs + 4 * o);
+                }
+            }
+        }
+        cp_async_commit();
+    };
+
+    issue(0, ST);
 
     // the block's queries with each position bias (core/encoder.c:302-309)
     for (uint32_t e = tid; e < AQ * dk; e += A_THREADS) {
@@ -221,168 +300,158 @@ __global__ void __launch_bounds__(A_THREADS) attention_kernel(const __grid_const
         qv[i * DS + d] = v;
     }
 
-    // rows j0 .. j0 + 63 of K (kind 0) or P (kind 1) into ST, zeros past the end
-    auto stage_kp = [&](const float* src, unsigned long long rs, uint32_t j0, uint32_t valid, uint32_t np) {
-        if constexpr (PANELS) {
-            // (row j, dimension d) at ((j/16) dk + d) 16 + j%16: four rows a 16-byte load
-            for (uint32_t e = tid; e < (ACH / 4) * dk; e += A_THREADS) {
-                const uint32_t d = e % dk, jq = e / dk, j = j0 + 4 * jq;
-                float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                if (j < np) v = *reinterpret_cast<const float4*>(src + (static_cast<size_t>(j / 16) * dk + d) * 16 + j % 16);
-                ST[(4 * jq + 0) * DS + d] = v.x;
-                ST[(4 * jq + 1) * DS + d] = v.y;
-                ST[(4 * jq + 2) * DS + d] = v.z;
-                ST[(4 * jq + 3) * DS + d] = v.w;
-            }
-            (void)rs;
-            (void)valid;
-        } else {
-            for (uint32_t e = tid; e < ACH * (dk / 4); e += A_THREADS) {
-                const uint32_t d4 = e % (dk / 4), jj = e / (dk / 4), j = j0 + jj;
-                float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                if (j < valid) v = *reinterpret_cast<const float4*>(src + static_cast<size_t>(j) * rs + 4 * d4);
-                *reinterpret_cast<float4*>(&ST[jj * DS + 4 * d4]) = v;
-            }
-            (void)np;
-        }
-    };
-
-    // scores (kind 0: against qu into S) and position products (kind 1:
-    // against qv into B), each + 0 as gemm_f32 adds its absent bias
     const uint32_t kq = tid % 16, qp = tid / 16;
-    for (int kind = 0; kind < 2; kind++) {
-        const float* qrow = kind == 0 ? qu : qv;
-        const uint32_t start = kind == 0 ? 0 : w0, count = kind == 0 ? T : W;
-        float* dst = kind == 0 ? S : B;
-        const uint32_t dstride = kind == 0 ? SP : BP;
-        for (uint32_t c0 = 0; c0 < count; c0 += ACH) {
-            __syncthreads();  // ST is free, the queries are in
-            if (kind == 0)
-                stage_kp(kh, a.ks, c0, T, Tp);
-            else
-                stage_kp(ph, a.ps, start + c0, R, Pp);
-            __syncthreads();
-            float acc[2][4];
+    float acc[2][4];
+    float vacc[2][4][4];
 #pragma unroll
-            for (int q2 = 0; q2 < 2; q2++)
-#pragma unroll
-                for (int e = 0; e < 4; e++) acc[q2][e] = 0.0f;
-            const float* q0 = qrow + (2 * qp) * DS;
-            const float* q1 = q0 + DS;
-            for (uint32_t d = 0; d < dk; d += 4) {
-                const float4 a0 = *reinterpret_cast<const float4*>(q0 + d);
-                const float4 a1 = *reinterpret_cast<const float4*>(q1 + d);
-                float4 r[4];
-#pragma unroll
-                for (int e = 0; e < 4; e++) r[e] = *reinterpret_cast<const float4*>(&ST[(kq + 16 * e) * DS + d]);
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    acc[0][e] = fma_r<RM>(r[e].x, a0.x, acc[0][e]);
-                    acc[1][e] = fma_r<RM>(r[e].x, a1.x, acc[1][e]);
-                }
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    acc[0][e] = fma_r<RM>(r[e].y, a0.y, acc[0][e]);
-                    acc[1][e] = fma_r<RM>(r[e].y, a1.y, acc[1][e]);
-                }
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    acc[0][e] = fma_r<RM>(r[e].z, a0.z, acc[0][e]);
-                    acc[1][e] = fma_r<RM>(r[e].z, a1.z, acc[1][e]);
-                }
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    acc[0][e] = fma_r<RM>(r[e].w, a0.w, acc[0][e]);
-                    acc[1][e] = fma_r<RM>(r[e].w, a1.w, acc[1][e]);
-                }
-            }
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const uint32_t j = c0 + kq + 16 * e;
-                if (j < count) {
-                    dst[(2 * qp) * dstride + j] = add_r<RM>(acc[0][e], 0.0f);
-                    dst[(2 * qp + 1) * dstride + j] = add_r<RM>(acc[1][e], 0.0f);
-                }
-            }
-        }
-    }
-    __syncthreads();
-
-    // each query's scores plus its positions, then its softmax (core/encoder.c:315-321)
-    const float scale = div_r<RM>(1.0f, sqrt_r<RM>(static_cast<float>(dk)));
-    for (uint32_t i = warp; i < nq; i += A_THREADS / 32) {
-        float* srow = S + i * SP;
-        const float* brow = B + i * BP + (T - 1 - (i0 + i)) - w0;
-        for (uint32_t k = lane; k < T; k += 32) srow[k] = add_r<RM>(srow[k], brow[k]);
-        __syncwarp();
-        softmax_row<RM>(srow, T, scale, lane);
-    }
-
-    // the weighted values (core/encoder.c:323-324): o = V^T s + 0
-    const uint32_t ntiles = dk;  // (AQ / 4) query quads x (dk / 4) dimension quads
-    float acc[2][4][4];
-#pragma unroll
-    for (int u = 0; u < 2; u++)
+    for (int x = 0; x < 2; x++)
 #pragma unroll
         for (int i = 0; i < 4; i++)
 #pragma unroll
-            for (int e = 0; e < 4; e++) acc[u][i][e] = 0.0f;
-    for (uint32_t c0 = 0; c0 < T; c0 += ACH) {
-        __syncthreads();  // the weights are in; ST is free
-        if constexpr (PANELS) {
-            // (key j, dimension d) at ((d/16) T + j) 16 + d%16: four dimensions a 16-byte load
-            for (uint32_t e = tid; e < ACH * (dk / 4); e += A_THREADS) {
-                const uint32_t d4 = e % (dk / 4), jj = e / (dk / 4), j = c0 + jj, d = 4 * d4;
-                float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                if (j < T) v = *reinterpret_cast<const float4*>(vh + (static_cast<size_t>(d / 16) * T + j) * 16 + d % 16);
-                *reinterpret_cast<float4*>(&ST[jj * DS + d]) = v;
-            }
+            for (int e = 0; e < 4; e++) vacc[x][i][e] = 0.0f;
+    const float scale = div_r<RM>(1.0f, sqrt_r<RM>(static_cast<float>(dk)));
+
+    for (uint32_t u = 0; u < U; u++) {
+        float* b = ST + (u & 1) * BUF;
+        if (u + 1 < U) {
+            issue(u + 1, ST + ((u + 1) & 1) * BUF);
+            cp_async_wait<1>();
         } else {
-            stage_kp(vh, a.vs, c0, T, T);
+            cp_async_wait<0>();
         }
-        __syncthreads();
-        const uint32_t kc = min(static_cast<uint32_t>(ACH), T - c0);
+        __syncthreads();  // unit u has landed for every thread (and the queries are in)
+        if (u < nK + nP) {
+            const bool isk = u < nK;
+            const uint32_t cu = isk ? u : u - nK, c = cu / nh, part = cu % nh, d0 = part * dh;
+            if (part == 0) {
 #pragma unroll
-        for (int u = 0; u < 2; u++) {
-            const uint32_t tile = tid + u * A_THREADS;
-            if (tile >= ntiles) break;
-            const uint32_t dq = tile % (dk / 4), qg = tile / (dk / 4);
-            const float* w0r = S + (4 * qg) * SP + c0;
-            uint32_t kk = 0;
-            for (; kk + 4 <= kc; kk += 4) {
-                float4 p[4];
+                for (int x = 0; x < 2; x++)
 #pragma unroll
-                for (int i = 0; i < 4; i++) p[i] = *reinterpret_cast<const float4*>(w0r + i * SP + kk);
+                    for (int e = 0; e < 4; e++) acc[x][e] = 0.0f;
+            }
+            const float* q0 = (isk ? qu : qv) + (2 * qp) * DS + d0;
+            const float* q1 = q0 + DS;
+            for (uint32_t dd = 0; dd < dh; dd += 4) {
+                const float4 a0 = *reinterpret_cast<const float4*>(q0 + dd);
+                const float4 a1 = *reinterpret_cast<const float4*>(q1 + dd);
+                if constexpr (PANELS) {
+                    // keys 4 kq .. 4 kq + 3 at dimension dd + t
+                    const float* gb = b + (kq / 4) * (16 * dh + 16) + 4 * (kq % 4);
 #pragma unroll
-                for (int s = 0; s < 4; s++) {
-                    const float4 v = *reinterpret_cast<const float4*>(&ST[(kk + s) * DS + 4 * dq]);
+                    for (int t = 0; t < 4; t++) {
+                        const float4 r = *reinterpret_cast<const float4*>(gb + (dd + t) * 16);
+                        const float q0t = t == 0 ? a0.x : t == 1 ? a0.y : t == 2 ? a0.z : a0.w;
+                        const float q1t = t == 0 ? a1.x : t == 1 ? a1.y : t == 2 ? a1.z : a1.w;
+                        acc[0][0] = fma_r<RM>(r.x, q0t, acc[0][0]);
+                        acc[1][0] = fma_r<RM>(r.x, q1t, acc[1][0]);
+                        acc[0][1] = fma_r<RM>(r.y, q0t, acc[0][1]);
+                        acc[1][1] = fma_r<RM>(r.y, q1t, acc[1][1]);
+                        acc[0][2] = fma_r<RM>(r.z, q0t, acc[0][2]);
+                        acc[1][2] = fma_r<RM>(r.z, q1t, acc[1][2]);
+                        acc[0][3] = fma_r<RM>(r.w, q0t, acc[0][3]);
+                        acc[1][3] = fma_r<RM>(r.w, q1t, acc[1][3]);
+                    }
+                } else {
+                    // keys kq + 16 e, dimensions dd .. dd + 3
+                    float4 r[4];
 #pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        const float pk = s == 0 ? p[i].x : s == 1 ? p[i].y : s == 2 ? p[i].z : p[i].w;
-                        acc[u][i][0] = fma_r<RM>(v.x, pk, acc[u][i][0]);
-                        acc[u][i][1] = fma_r<RM>(v.y, pk, acc[u][i][1]);
-                        acc[u][i][2] = fma_r<RM>(v.z, pk, acc[u][i][2]);
-                        acc[u][i][3] = fma_r<RM>(v.w, pk, acc[u][i][3]);
+                    for (int e = 0; e < 4; e++) r[e] = *reinterpret_cast<const float4*>(b + (kq + 16 * e) * (dh + 4) + dd);
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        acc[0][e] = fma_r<RM>(r[e].x, a0.x, acc[0][e]);
+                        acc[1][e] = fma_r<RM>(r[e].x, a1.x, acc[1][e]);
+                    }
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        acc[0][e] = fma_r<RM>(r[e].y, a0.y, acc[0][e]);
+                        acc[1][e] = fma_r<RM>(r[e].y, a1.y, acc[1][e]);
+                    }
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        acc[0][e] = fma_r<RM>(r[e].z, a0.z, acc[0][e]);
+                        acc[1][e] = fma_r<RM>(r[e].z, a1.z, acc[1][e]);
+                    }
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        acc[0][e] = fma_r<RM>(r[e].w, a0.w, acc[0][e]);
+                        acc[1][e] = fma_r<RM>(r[e].w, a1.w, acc[1][e]);
                     }
                 }
             }
-            for (; kk < kc; kk++) {
-                const float4 v = *reinterpret_cast<const float4*>(&ST[kk * DS + 4 * dq]);
+            if (part == nh - 1) {
+                // the chains are done: + 0 as gemm_f32 adds its absent bias;
+                // a score is stored, a position product added to its score
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const float pk = w0r[i * SP + kk];
-                    acc[u][i][0] = fma_r<RM>(v.x, pk, acc[u][i][0]);
-                    acc[u][i][1] = fma_r<RM>(v.y, pk, acc[u][i][1]);
-                    acc[u][i][2] = fma_r<RM>(v.z, pk, acc[u][i][2]);
-                    acc[u][i][3] = fma_r<RM>(v.w, pk, acc[u][i][3]);
+                for (int e = 0; e < 4; e++) {
+                    const uint32_t jl = c * AKC + (PANELS ? 4 * kq + e : kq + 16 * e);
+#pragma unroll
+                    for (int x = 0; x < 2; x++) {
+                        const uint32_t i = 2 * qp + x;
+                        const float v = add_r<RM>(acc[x][e], 0.0f);
+                        if (isk) {
+                            if (jl < T) S[i * SP + jl] = v;
+                        } else if (i < nq) {
+                            // position row w0 + jl is the score (i, k) with k = w0 + jl - (T - 1 - (i0 + i))
+                            const int k = static_cast<int>(w0 + jl) - static_cast<int>(T - 1 - (i0 + i));
+                            if (k >= 0 && k < static_cast<int>(T) && jl < W) S[i * SP + k] = add_r<RM>(S[i * SP + k], v);
+                        }
+                    }
+                }
+            }
+        } else {
+            if (u == nK + nP) {
+                // every score has its position: each query's softmax
+                // (core/encoder.c:315-321), while the first V units land
+                for (uint32_t i = warp; i < nq; i += A_THREADS / 32) softmax_row<RM>(S + i * SP, T, scale, lane);
+                __syncthreads();
+            }
+            const uint32_t c0 = (u - nK - nP) * vch, kc = min(vch, T - c0);
+#pragma unroll
+            for (int x = 0; x < 2; x++) {
+                const uint32_t tile = tid + x * A_THREADS;
+                if (tile >= dk) break;  // (AQ / 4) query quads x (dk / 4) dimension quads
+                const uint32_t dq = tile % (dk / 4), qg = tile / (dk / 4);
+                const float* wr = S + (4 * qg) * SP + c0;
+                const float* vb = PANELS ? b + (dq / 4) * (16 * vch + 16) + 4 * (dq % 4) : b + 4 * dq;
+                const uint32_t vstep = PANELS ? 16 : DS;
+                uint32_t kk = 0;
+                for (; kk + 4 <= kc; kk += 4) {
+                    float4 p[4];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) p[i] = *reinterpret_cast<const float4*>(wr + i * SP + kk);
+#pragma unroll
+                    for (int t = 0; t < 4; t++) {
+                        const float4 v = *reinterpret_cast<const float4*>(vb + (kk + t) * vstep);
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            const float pk = t == 0 ? p[i].x : t == 1 ? p[i].y : t == 2 ? p[i].z : p[i].w;
+                            vacc[x][i][0] = fma_r<RM>(v.x, pk, vacc[x][i][0]);
+                            vacc[x][i][1] = fma_r<RM>(v.y, pk, vacc[x][i][1]);
+                            vacc[x][i][2] = fma_r<RM>(v.z, pk, vacc[x][i][2]);
+                            vacc[x][i][3] = fma_r<RM>(v.w, pk, vacc[x][i][3]);
+                        }
+                    }
+                }
+                for (; kk < kc; kk++) {
+                    const float4 v = *reinterpret_cast<const float4*>(vb + kk * vstep);
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float pk = wr[i * SP + kk];
+                        vacc[x][i][0] = fma_r<RM>(v.x, pk, vacc[x][i][0]);
+                        vacc[x][i][1] = fma_r<RM>(v.y, pk, vacc[x][i][1]);
+                        vacc[x][i][2] = fma_r<RM>(v.z, pk, vacc[x][i][2]);
+                        vacc[x][i][3] = fma_r<RM>(v.w, pk, vacc[x][i][3]);
+                    }
                 }
             }
         }
+        __syncthreads();  // buffer u & 1 is free for unit u + 2
     }
+    // o = V^T s + 0 (core/encoder.c:323-324)
 #pragma unroll
-    for (int u = 0; u < 2; u++) {
-        const uint32_t tile = tid + u * A_THREADS;
-        if (tile >= ntiles) break;
+    for (int x = 0; x < 2; x++) {
+        const uint32_t tile = tid + x * A_THREADS;
+        if (tile >= dk) break;
         const uint32_t dq = tile % (dk / 4), qg = tile / (dk / 4);
 #pragma unroll
         for (int i = 0; i < 4; i++) {
@@ -390,7 +459,7 @@ __global__ void __launch_bounds__(A_THREADS) attention_kernel(const __grid_const
             if (qi >= nq) break;
             float* orow = a.o + static_cast<size_t>(sg.f + i0 + qi) * a.os + h * dk + 4 * dq;
 #pragma unroll
-            for (int e = 0; e < 4; e++) orow[e] = add_r<RM>(acc[u][i][e], 0.0f);
+            for (int e = 0; e < 4; e++) orow[e] = add_r<RM>(vacc[x][i][e], 0.0f);
         }
     }
 }
@@ -463,8 +532,10 @@ cudaError_t launch_softmax(float* x, size_t xs, uint32_t T, uint32_t n, float sc
     }
 }
 
-size_t attention_smem(uint32_t dk, uint32_t sp, uint32_t bp) {
-    return (static_cast<size_t>(2 * AQ + ACH) * (dk + 4) + static_cast<size_t>(AQ) * (sp + bp)) * sizeof(float);
+size_t attention_smem(uint32_t dk, uint32_t sp) {
+    return (static_cast<size_t>(2 * AQ) * (dk + 4) + 2 * static_cast<size_t>(att_buf(dk)) +
+            static_cast<size_t>(AQ) * sp) *
+           sizeof(float);
 }
 
 uint32_t attention_block() { return AQ; }
@@ -483,7 +554,7 @@ cudaError_t prepare_attention() {
 size_t attention_smem_max() { return g_att_dyn_max; }
 
 cudaError_t launch_attention(const AttArgs& a, bool panels, int rmode, cudaStream_t stream) {
-    const size_t smem = attention_smem(a.dk, a.sp, a.bp);
+    const size_t smem = attention_smem(a.dk, a.sp);
     if (panels) {
         switch (rmode) {
         case 1: return attention_rm<1, true>(a, smem, stream);

@@ -130,12 +130,12 @@ struct AttArgs {
     const float *q, *k, *p, *v, *bu, *bv;
     unsigned long long os, qs, ks, ps, vs;  // row strides, in floats (rows layout)
     uint32_t dk, nseg, items;
-    uint32_t sp, bp;  // shared-memory row lengths of the scores and the position products
+    uint32_t sp;  // the scores' shared-memory row length (T rounded up to 16)
     AttSeg seg[ATT_MAX_SEG];
 };
 
-// Shared memory a CTA takes for heads of dk and rows of sp and bp floats.
-size_t attention_smem(uint32_t dk, uint32_t sp, uint32_t bp);
+// Shared memory a CTA takes for heads of dk and score rows of sp floats.
+size_t attention_smem(uint32_t dk, uint32_t sp);
 uint32_t attention_block();  // queries a CTA
 // panels: K, P, V as the reference's panels (one segment); else as rows.
 cudaError_t launch_attention(const AttArgs& a, bool panels, int rmode, cudaStream_t stream);
