@@ -94,19 +94,19 @@ __global__ void __launch_bounds__(GF_THREADS)
 
 // --------------------------------------------------------------- softmax --
 
-// k_softmax on one row of n in memory (global or shared) by one warp, lane
-// i taking elements i, i + 32, ...: y = x * scale and its maximum (fmaxf
+// k_softmax on one row of n in memory (global or shared; element i at
+// x[i xs]) by one warp, lane i taking elements i, i + 32, ...: y = x * scale and its maximum (fmaxf
 // passes a NaN over; the sign of a zero maximum changes no e below, as
 // y - (+-0) is y for y != 0 and pk_expf(+-0) is 1), e = pk_expf(y - m), the
 // sum of the e in the reference's 16 lanes (element i into lane i % 16, in
 // order: lane l < 16 adds its own then lane l + 16's element of each 32)
 // folded 8, 4, 2, 1, then e * (1 / sum).
 template <int RM>
-__device__ __forceinline__ void softmax_row(float* x, uint32_t n, float scale, uint32_t lane) {
+__device__ __forceinline__ void softmax_row(float* x, uint32_t xs, uint32_t n, float scale, uint32_t lane) {
     float m = -INFINITY;
     for (uint32_t i = lane; i < n; i += 32) {
-        const float y = mul_r<RM>(x[i], scale);
-        x[i] = y;
+        const float y = mul_r<RM>(x[i * xs], scale);
+        x[i * xs] = y;
         m = fmaxf(m, y);
     }
 #pragma unroll
@@ -116,8 +116,8 @@ __device__ __forceinline__ void softmax_row(float* x, uint32_t n, float scale, u
         const uint32_t i = base + lane;
         float e = 0.0f;
         if (i < n) {
-            e = pk_exp<RM>(sub_r<RM>(x[i], m));
-            x[i] = e;
+            e = pk_exp<RM>(sub_r<RM>(x[i * xs], m));
+            x[i * xs] = e;
         }
         const float hi = __shfl_down_sync(0xffffffffu, e, 16);
         if (lane < 16) {
@@ -131,7 +131,7 @@ __device__ __forceinline__ void softmax_row(float* x, uint32_t n, float scale, u
         if (lane < static_cast<uint32_t>(h)) acc = add_r<RM>(acc, o);
     }
     const float inv = rcp_r<RM>(__shfl_sync(0xffffffffu, acc, 0));
-    for (uint32_t i = lane; i < n; i += 32) x[i] = mul_r<RM>(x[i], inv);
+    for (uint32_t i = lane; i < n; i += 32) x[i * xs] = mul_r<RM>(x[i * xs], inv);
 }
 
 constexpr int SM_THREADS = 256;
@@ -142,61 +142,65 @@ __global__ void __launch_bounds__(SM_THREADS)
     softmax_kernel(float* x, unsigned long long xs, uint32_t T, uint32_t n, float scale) {
     const uint32_t lane = threadIdx.x % 32;
     for (uint32_t t = blockIdx.x * (SM_THREADS / 32) + threadIdx.x / 32; t < T; t += gridDim.x * (SM_THREADS / 32))
-        softmax_row<RM>(x + static_cast<size_t>(t) * xs, n, scale, lane);
+        softmax_row<RM>(x + static_cast<size_t>(t) * xs, 1, n, scale, lane);
 }
 
 // ------------------------------------------------------------- attention --
 
-constexpr int AQ = 16;           // queries a CTA: PK_ATT_BLOCK (core/asr.h:16)
-constexpr int A_THREADS = 128;
-constexpr int AKC = 64;          // keys (or positions) a staged unit of K (P)
+constexpr int AQ = 32;           // queries a CTA (two of the reference's PK_ATT_BLOCK, core/asr.h:16)
+constexpr int A_THREADS = 256;
+constexpr int AKU = 128;         // keys (or positions) a unit of K (P)
+constexpr int AVU = 32;          // keys a unit of V
+constexpr int AQS = AQ + 4;      // row stride of the transposed queries and scores
 
-// The dimensions a unit of K or P carries: all of a head of up to 64,
-// else half (up to 128) or a quarter (up to 256), at most 64 and a
-// multiple of 4.
-__host__ __device__ __forceinline__ uint32_t att_dh(uint32_t dk) { return dk <= 64 ? dk : dk <= 128 ? dk / 2 : dk / 4; }
-// The keys a staged unit of V carries (all dk of them).
-__host__ __device__ __forceinline__ uint32_t att_vch(uint32_t dk) { return dk <= 128 ? 32 : 16; }
+// The dimensions a unit of K or P carries (a multiple of 16 dividing dk).
+__host__ __device__ __forceinline__ uint32_t att_dh(uint32_t dk) { return dk % 32 ? 16 : 32; }
 
-// floats of one staging buffer: the larger of a K/P unit and a V unit in
-// either layout, with the padding that keeps a quarter-warp's 16-byte
-// loads on distinct bank groups
+// floats of one staging buffer: the larger of a K/P unit and a V unit (up
+// to 128 dimensions) in either layout, with the padding that keeps a
+// quarter-warp's 16-byte loads on distinct bank groups
 __host__ __device__ __forceinline__ uint32_t att_buf(uint32_t dk) {
-    const uint32_t dh = att_dh(dk), vch = att_vch(dk);
-    const uint32_t kp_rows = AKC * (dh + 4), kp_pan = (AKC / 16) * (16 * dh + 16);
-    const uint32_t v_rows = vch * (dk + 4), v_pan = (dk / 16) * (16 * vch + 16);
+    const uint32_t dh = att_dh(dk), dv = dk < 128 ? dk : 128;
+    const uint32_t kp_rows = AKU * (dh + 4), kp_pan = (AKU / 16) * (16 * dh + 16);
+    const uint32_t v_rows = AVU * (dv + 4), v_pan = (dv / 16) * (16 * AVU + 16);
     uint32_t m = kp_rows > kp_pan ? kp_rows : kp_pan;
     m = m > v_rows ? m : v_rows;
     return m > v_pan ? m : v_pan;
 }
 
-// One CTA: head h, queries i0 .. i0 + nq - 1 (nq <= 16) of one segment of T
+// One CTA: head h, queries i0 .. i0 + nq - 1 (nq <= 32) of one segment of T
 // frames. Shared memory:
 //
-//   qu, qv   the queries plus each position bias, AQ rows of dk + 4
-//   ST[2]    two staging buffers: the K, P and V units go through them in
-//            turn, the next unit's copies (cp.async) in flight while the
-//            CTA computes on the current one
-//   S        the scores, then the weights: AQ rows of SP >= T
+//   QT     the queries plus a position bias, transposed: dimension d of
+//          query i at QT[d AQS + i] (first q + bias_u; q + bias_v once the
+//          scores are done)
+//   ST[2]  two staging buffers that the K, P and V units go through in
+//          turn, the next unit's copies (cp.async) in flight while the CTA
+//          computes on the current one
+//   SC     the scores, then the weights, transposed: key k of query i at
+//          SC[k AQS + i], SP rows
 //
-// The units, in order: K in chunks of 64 keys, each in pieces of dh
-// dimensions (the scores' chains run on across the pieces, d ascending);
-// P the same over the block's window of positions; V in chunks of VCH keys.
-// A K/P unit in the rows layout is row-major (key j, dimension d at
-// j (dh + 4) + d); in the panels layout it keeps the reference's order
-// (16-key groups, each dh dimensions of 16 keys, groups 16 dh + 16 apart).
-// V rows: key k, dimension d at k (dk + 4) + d; V panels: 16-dimension
-// panels of VCH keys, 16 VCH + 16 apart.
+// The units, in order: K in chunks of 128 keys, each in pieces of dh
+// dimensions (a score's chain runs on across the pieces, d ascending); P the
+// same over the block's window of positions; V in chunks of 32 keys, in
+// passes of up to 128 dimensions. Rows layout: a K/P unit is row-major (key
+// j, dimension d at j (dh + 4) + d), a V unit too (k (dv + 4) + d). Panels
+// layout: the reference's order, padded (16-key groups of dh x 16, 16 dh +
+// 16 apart; 16-dimension panels of 32 x 16, 528 apart).
 //
-// Scores and position products: thread (kq, qp) takes queries 2 qp and
-// 2 qp + 1 and four keys of each chunk (rows: kq + 16 e; panels: 4 kq + e),
-// 8 chains over d, 4 dimensions a step (two 16-byte loads of queries, four
-// of K or P, 32 FMAs). Each position product is added to the score it
-// belongs to as soon as its chain is done: the pairs (query i, position
-// row T-1-i+k) are one to one with the scores (i, k). The weighted values:
-// tile (query quad, dimension quad), 4 x 4 chains over k, 4 keys a step.
-template <int RM, bool PANELS>
-__global__ void __launch_bounds__(A_THREADS) attention_kernel(const __grid_constant__ AttArgs a) {
+// Scores and position products: lane (qq, ko) of warp w takes queries
+// 4 qq .. 4 qq + 3 and 4 keys of the warp's 16 (rows: 16 w + ko + 4 e;
+// panels: 16 w + 4 ko + e), 16 chains over d, 4 dimensions a step: 4
+// 16-byte loads of queries (8 distinct in a warp: one wavefront), 4 of K or
+// P (4 distinct on distinct bank groups: one wavefront), 64 FMAs. A score is
+// stored as 4 queries' 16 bytes; each position product is added to the
+// score it belongs to as soon as its chain is done (the pairs (query i,
+// position T-1-i+k) are one to one with the scores (i, k)). The weighted
+// values: lane (vq, vo) of warp w takes queries 4 vq .. 4 vq + 3 and
+// dimensions 4 (4 w + vo) .. + 3 of the pass, 16 chains over k, a key a
+// step: the 4 queries' weights in one 16-byte load, 4 values in another.
+template <int RM, bool PANELS, int DH>
+__global__ void __launch_bounds__(A_THREADS, 2) attention_kernel(const __grid_constant__ AttArgs a) {
     extern __shared__ __align__(16) float sm[];
     __shared__ uint32_t s_seg;
     const uint32_t tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
@@ -214,19 +218,19 @@ __global__ void __launch_bounds__(A_THREADS) attention_kernel(const __grid_const
     }
     __syncthreads();
     const AttSeg sg = a.seg[s_seg];
-    const uint32_t T = sg.T, dk = a.dk, DS = dk + 4, SP = a.sp;
-    const uint32_t dh = att_dh(dk), nh = dk / dh, vch = att_vch(dk), BUF = att_buf(dk);
+    constexpr uint32_t dh = DH;  // att_dh(dk), the launch's choice
+    const uint32_t T = sg.T, dk = a.dk;
+    const uint32_t nh = dk / dh, BUF = att_buf(dk);
     const uint32_t nqb = (T + AQ - 1) / AQ, local = blockIdx.x - sg.item0;
     const uint32_t h = local / nqb, i0 = (local % nqb) * AQ;
     const uint32_t nq = min(static_cast<uint32_t>(AQ), T - i0), i1 = i0 + nq;
     const uint32_t R = 2 * T - 1;
     // the position window: rows T - 1 - i + k for the block's queries i and
-    // keys k, from a panel boundary (as the reference takes it)
+    // keys k, from a panel boundary
     const uint32_t w0 = (T - i1) & ~15u, W = ((2 * T - 1 - i0 - w0) + 15) & ~15u;
-    float* qu = sm;
-    float* qv = qu + AQ * DS;
-    float* ST = qv + AQ * DS;
-    float* S = ST + 2 * BUF;
+    float* QT = sm;
+    float* ST = QT + dk * AQS;
+    float* SC = ST + 2 * BUF;
 
     const uint32_t Tp = (T + 15) & ~15u, Pp = ((R + 15) & ~15u) + 16;
     const float* kh = PANELS ? a.k + static_cast<size_t>(h) * Tp * dk : a.k + static_cast<size_t>(sg.f) * a.ks + h * dk;
@@ -234,22 +238,22 @@ __global__ void __launch_bounds__(A_THREADS) attention_kernel(const __grid_const
     const float* vh = PANELS ? a.v + static_cast<size_t>(h) * (dk / 16) * T * 16
                              : a.v + static_cast<size_t>(sg.f) * a.vs + h * dk;
 
-    const uint32_t nkc = (T + AKC - 1) / AKC, npc = (W + AKC - 1) / AKC;
-    const uint32_t nK = nkc * nh, nP = npc * nh, nV = (T + vch - 1) / vch, U = nK + nP + nV;
+    const uint32_t nkc = (T + AKU - 1) / AKU, npc = (W + AKU - 1) / AKU, nvc = (T + AVU - 1) / AVU;
+    const uint32_t npass = (dk + 127) / 128;
+    const uint32_t nK = nkc * nh, nP = npc * nh, U = nK + nP + npass * nvc;
 
-    // issues unit u's copies into buffer b (rows past the data are skipped:
-    // their results are never read)
+    // issues unit u's copies into buffer b; rows past the data are skipped
+    // (their results are never read)
     auto issue = [&](uint32_t u, float* b) {
         if (u < nK + nP) {
             const bool isk = u < nK;
             const uint32_t cu = isk ? u : u - nK, c = cu / nh, d0 = (cu % nh) * dh;
-            const uint32_t j0 = isk ? c * AKC : w0 + c * AKC;
+            const uint32_t j0 = isk ? c * AKU : w0 + c * AKU;
             const float* src = isk ? kh : ph;
-            const uint32_t valid = PANELS ? (isk ? Tp : Pp) : (isk ? T : R);
             if constexpr (PANELS) {
                 // 16-key group g: dh x 16 floats at ((j0/16 + g) dk + d0) 16
-                const uint32_t n4 = dh * 4;  // 16-byte pieces a group
-                for (uint32_t e = tid; e < (AKC / 16) * n4; e += A_THREADS) {
+                const uint32_t valid = isk ? Tp : Pp, n4 = dh * 4;
+                for (uint32_t e = tid; e < (AKU / 16) * n4; e += A_THREADS) {
                     const uint32_t g = e / n4, o = e % n4;
                     if (j0 + 16 * g < valid)
                         cp_async16(b + g * (16 * dh + 16) + 4 * o,
@@ -257,58 +261,52 @@ __global__ void __launch_bounds__(A_THREADS) attention_kernel(const __grid_const
                 }
             } else {
                 const unsigned long long rs = isk ? a.ks : a.ps;
-                const uint32_t n4 = dh / 4;
-                for (uint32_t e = tid; e < AKC * n4; e += A_THREADS) {
+                const uint32_t valid = isk ? T : R, n4 = dh / 4;
+                for (uint32_t e = tid; e < AKU * n4; e += A_THREADS) {
                     const uint32_t jj = e / n4, o = e % n4;
                     if (j0 + jj < valid)
                         cp_async16(b + jj * (dh + 4) + 4 * o, src + static_cast<size_t>(j0 + jj) * rs + d0 + 4 * o);
                 }
             }
         } else {
-            const uint32_t c0 = (u - nK - nP) * vch;
+            const uint32_t vu = u - nK - nP, pass = vu / nvc, c0 = (vu % nvc) * AVU;
+            const uint32_t e0 = pass * 128, dv = min(128u, dk - e0);
             if constexpr (PANELS) {
-                // 16-dimension panel dp: vch x 16 floats at (dp T + c0) 16
-                const uint32_t n4 = vch * 4;
-                for (uint32_t e = tid; e < (dk / 16) * n4; e += A_THREADS) {
+                // 16-dimension panel dp: 32 x 16 floats at ((e0/16 + dp) T + c0) 16
+                const uint32_t n4 = AVU * 4;
+                for (uint32_t e = tid; e < (dv / 16) * n4; e += A_THREADS) {
                     const uint32_t dp = e / n4, o = e % n4;
                     if (c0 + o / 4 < T)
-                        cp_async16(b + dp * (16 * vch + 16) + 4 * o, vh + (static_cast<size_t>(dp) * T + c0) * 16 + 4 * o);
+                        cp_async16(b + dp * (16 * AVU + 16) + 4 * o,
+                                   vh + (static_cast<size_t>(e0 / 16 + dp) * T + c0) * 16 + 4 * o);
                 }
             } else {
-                const uint32_t n4 = dk / 4;
-                for (uint32_t e = tid; e < vch * n4; e += A_THREADS) {
+                const uint32_t n4 = dv / 4;
+                for (uint32_t e = tid; e < AVU * n4; e += A_THREADS) {
                     const uint32_t kk = e / n4, o = e % n4;
-                    if (c0 + kk < T) cp_async16(b + kk * DS + 4 * o, vh + static_cast<size_t>(c0 + kk) * a.vs + 4 * o);
+                    if (c0 + kk < T)
+                        cp_async16(b + kk * (dv + 4) + 4 * o, vh + static_cast<size_t>(c0 + kk) * a.vs + e0 + 4 * o);
                 }
             }
         }
         cp_async_commit();
     };
 
-    issue(0, ST);
-
-    // the block's queries with each position bias (core/encoder.c:302-309)
-    for (uint32_t e = tid; e < AQ * dk; e += A_THREADS) {
-        const uint32_t i = e / dk, d = e % dk;
-        float u = 0.0f, v = 0.0f;
-        if (i < nq) {
-            const float qd = a.q[static_cast<size_t>(sg.f + i0 + i) * a.qs + h * dk + d];
-            u = add_r<RM>(qd, a.bu[h * dk + d]);
-            v = add_r<RM>(qd, a.bv[h * dk + d]);
+    // the block's queries with a position bias, transposed (core/encoder.c:302-309)
+    auto load_queries = [&](const float* bias) {
+        for (uint32_t e = tid; e < AQ * dk; e += A_THREADS) {
+            const uint32_t i = e / dk, d = e % dk;
+            float v = 0.0f;
+            if (i < nq) v = add_r<RM>(a.q[static_cast<size_t>(sg.f + i0 + i) * a.qs + h * dk + d], bias[h * dk + d]);
+            QT[d * AQS + i] = v;
         }
-        qu[i * DS + d] = u;
-        qv[i * DS + d] = v;
-    }
+    };
 
-    const uint32_t kq = tid % 16, qp = tid / 16;
-    float acc[2][4];
-    float vacc[2][4][4];
-#pragma unroll
-    for (int x = 0; x < 2; x++)
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-#pragma unroll
-            for (int e = 0; e < 4; e++) vacc[x][i][e] = 0.0f;
+    issue(0, ST);
+    load_queries(a.bu);
+
+    const uint32_t qq = lane % 8, ko = lane / 8;  // query quad, key (or dimension) lane group
+    float acc[4][4];
     const float scale = div_r<RM>(1.0f, sqrt_r<RM>(static_cast<float>(dk)));
 
     for (uint32_t u = 0; u < U; u++) {
@@ -319,148 +317,139 @@ __global__ void __launch_bounds__(A_THREADS) attention_kernel(const __grid_const
         } else {
             cp_async_wait<0>();
         }
+        if (u == nK) {
+            // the scores are done with q + bias_u (the barrier ending unit
+            // nK - 1): q + bias_v in its place
+            load_queries(a.bv);
+        }
         __syncthreads();  // unit u has landed for every thread (and the queries are in)
         if (u < nK + nP) {
             const bool isk = u < nK;
             const uint32_t cu = isk ? u : u - nK, c = cu / nh, part = cu % nh, d0 = part * dh;
             if (part == 0) {
 #pragma unroll
-                for (int x = 0; x < 2; x++)
+                for (int i = 0; i < 4; i++)
 #pragma unroll
-                    for (int e = 0; e < 4; e++) acc[x][e] = 0.0f;
+                    for (int e = 0; e < 4; e++) acc[i][e] = 0.0f;
             }
-            const float* q0 = (isk ? qu : qv) + (2 * qp) * DS + d0;
-            const float* q1 = q0 + DS;
-            for (uint32_t dd = 0; dd < dh; dd += 4) {
-                const float4 a0 = *reinterpret_cast<const float4*>(q0 + dd);
-                const float4 a1 = *reinterpret_cast<const float4*>(q1 + dd);
-                if constexpr (PANELS) {
-                    // keys 4 kq .. 4 kq + 3 at dimension dd + t
-                    const float* gb = b + (kq / 4) * (16 * dh + 16) + 4 * (kq % 4);
+            // a warp whose 16 keys (positions) all lie past the data skips the unit
+            const bool idle = c * AKU + 16 * warp >= (isk ? T : W);
+            if (!idle) {
+                const float* qb = QT + d0 * AQS + 4 * qq;
+#pragma unroll
+                for (uint32_t dd = 0; dd < dh; dd += 4) {
+                    float4 q[4];
+#pragma unroll
+                    for (int t = 0; t < 4; t++) q[t] = *reinterpret_cast<const float4*>(qb + (dd + t) * AQS);
+                    float4 k[4];
+                    if constexpr (PANELS) {
+                        // keys 16 w + 4 ko .. + 3 at dimension dd + t
+#pragma unroll
+                        for (int t = 0; t < 4; t++)
+                            k[t] = *reinterpret_cast<const float4*>(b + warp * (16 * dh + 16) + (dd + t) * 16 + 4 * ko);
+                    } else {
+                        // key 16 w + ko + 4 e, dimensions dd .. dd + 3
+#pragma unroll
+                        for (int e = 0; e < 4; e++)
+                            k[e] = *reinterpret_cast<const float4*>(b + (16 * warp + ko + 4 * e) * (dh + 4) + dd);
+                    }
 #pragma unroll
                     for (int t = 0; t < 4; t++) {
-                        const float4 r = *reinterpret_cast<const float4*>(gb + (dd + t) * 16);
-                        const float q0t = t == 0 ? a0.x : t == 1 ? a0.y : t == 2 ? a0.z : a0.w;
-                        const float q1t = t == 0 ? a1.x : t == 1 ? a1.y : t == 2 ? a1.z : a1.w;
-                        acc[0][0] = fma_r<RM>(r.x, q0t, acc[0][0]);
-                        acc[1][0] = fma_r<RM>(r.x, q1t, acc[1][0]);
-                        acc[0][1] = fma_r<RM>(r.y, q0t, acc[0][1]);
-                        acc[1][1] = fma_r<RM>(r.y, q1t, acc[1][1]);
-                        acc[0][2] = fma_r<RM>(r.z, q0t, acc[0][2]);
-                        acc[1][2] = fma_r<RM>(r.z, q1t, acc[1][2]);
-                        acc[0][3] = fma_r<RM>(r.w, q0t, acc[0][3]);
-                        acc[1][3] = fma_r<RM>(r.w, q1t, acc[1][3]);
-                    }
-                } else {
-                    // keys kq + 16 e, dimensions dd .. dd + 3
-                    float4 r[4];
+                        const float qv[4] = {q[t].x, q[t].y, q[t].z, q[t].w};
 #pragma unroll
-                    for (int e = 0; e < 4; e++) r[e] = *reinterpret_cast<const float4*>(b + (kq + 16 * e) * (dh + 4) + dd);
+                        for (int e = 0; e < 4; e++) {
+                            float kv;
+                            if constexpr (PANELS)
+                                kv = e == 0 ? k[t].x : e == 1 ? k[t].y : e == 2 ? k[t].z : k[t].w;
+                            else
+                                kv = t == 0 ? k[e].x : t == 1 ? k[e].y : t == 2 ? k[e].z : k[e].w;
 #pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        acc[0][e] = fma_r<RM>(r[e].x, a0.x, acc[0][e]);
-                        acc[1][e] = fma_r<RM>(r[e].x, a1.x, acc[1][e]);
-                    }
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        acc[0][e] = fma_r<RM>(r[e].y, a0.y, acc[0][e]);
-                        acc[1][e] = fma_r<RM>(r[e].y, a1.y, acc[1][e]);
-                    }
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        acc[0][e] = fma_r<RM>(r[e].z, a0.z, acc[0][e]);
-                        acc[1][e] = fma_r<RM>(r[e].z, a1.z, acc[1][e]);
-                    }
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        acc[0][e] = fma_r<RM>(r[e].w, a0.w, acc[0][e]);
-                        acc[1][e] = fma_r<RM>(r[e].w, a1.w, acc[1][e]);
+                            for (int i = 0; i < 4; i++) acc[i][e] = fma_r<RM>(kv, qv[i], acc[i][e]);
+                        }
                     }
                 }
             }
-            if (part == nh - 1) {
+            if (part == nh - 1 && !idle) {
                 // the chains are done: + 0 as gemm_f32 adds its absent bias;
                 // a score is stored, a position product added to its score
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
-                    const uint32_t jl = c * AKC + (PANELS ? 4 * kq + e : kq + 16 * e);
+                    const uint32_t jl = c * AKU + 16 * warp + (PANELS ? 4 * ko + e : ko + 4 * e);
+                    if (isk) {
+                        if (jl < T) {
+                            float4 v;
+                            v.x = add_r<RM>(acc[0][e], 0.0f);
+                            v.y = add_r<RM>(acc[1][e], 0.0f);
+                            v.z = add_r<RM>(acc[2][e], 0.0f);
+                            v.w = add_r<RM>(acc[3][e], 0.0f);
+                            *reinterpret_cast<float4*>(SC + jl * AQS + 4 * qq) = v;
+                        }
+                    } else if (jl < W) {
 #pragma unroll
-                    for (int x = 0; x < 2; x++) {
-                        const uint32_t i = 2 * qp + x;
-                        const float v = add_r<RM>(acc[x][e], 0.0f);
-                        if (isk) {
-                            if (jl < T) S[i * SP + jl] = v;
-                        } else if (i < nq) {
-                            // position row w0 + jl is the score (i, k) with k = w0 + jl - (T - 1 - (i0 + i))
-                            const int k = static_cast<int>(w0 + jl) - static_cast<int>(T - 1 - (i0 + i));
-                            if (k >= 0 && k < static_cast<int>(T) && jl < W) S[i * SP + k] = add_r<RM>(S[i * SP + k], v);
+                        for (int i = 0; i < 4; i++) {
+                            // position row w0 + jl is the score (qi, k), k = w0 + jl - (T - 1 - (i0 + qi))
+                            const uint32_t qi = 4 * qq + i;
+                            const int k = static_cast<int>(w0 + jl) - static_cast<int>(T - 1 - (i0 + qi));
+                            if (qi < nq && k >= 0 && k < static_cast<int>(T))
+                                SC[k * AQS + qi] = add_r<RM>(SC[k * AQS + qi], add_r<RM>(acc[i][e], 0.0f));
                         }
                     }
                 }
             }
         } else {
-            if (u == nK + nP) {
+            const uint32_t vu = u - nK - nP, pass = vu / nvc, cc = vu % nvc, c0 = cc * AVU;
+            const uint32_t e0 = pass * 128, dv = min(128u, dk - e0), kc = min(static_cast<uint32_t>(AVU), T - c0);
+            if (vu == 0) {
                 // every score has its position: each query's softmax
                 // (core/encoder.c:315-321), while the first V units land
-                for (uint32_t i = warp; i < nq; i += A_THREADS / 32) softmax_row<RM>(S + i * SP, T, scale, lane);
+                for (uint32_t i = warp; i < nq; i += A_THREADS / 32) softmax_row<RM>(SC + i, AQS, T, scale, lane);
                 __syncthreads();
             }
-            const uint32_t c0 = (u - nK - nP) * vch, kc = min(vch, T - c0);
+            if (cc == 0) {
 #pragma unroll
-            for (int x = 0; x < 2; x++) {
-                const uint32_t tile = tid + x * A_THREADS;
-                if (tile >= dk) break;  // (AQ / 4) query quads x (dk / 4) dimension quads
-                const uint32_t dq = tile % (dk / 4), qg = tile / (dk / 4);
-                const float* wr = S + (4 * qg) * SP + c0;
-                const float* vb = PANELS ? b + (dq / 4) * (16 * vch + 16) + 4 * (dq % 4) : b + 4 * dq;
-                const uint32_t vstep = PANELS ? 16 : DS;
-                uint32_t kk = 0;
-                for (; kk + 4 <= kc; kk += 4) {
-                    float4 p[4];
+                for (int i = 0; i < 4; i++)
 #pragma unroll
-                    for (int i = 0; i < 4; i++) p[i] = *reinterpret_cast<const float4*>(wr + i * SP + kk);
-#pragma unroll
-                    for (int t = 0; t < 4; t++) {
-                        const float4 v = *reinterpret_cast<const float4*>(vb + (kk + t) * vstep);
-#pragma unroll
-                        for (int i = 0; i < 4; i++) {
-                            const float pk = t == 0 ? p[i].x : t == 1 ? p[i].y : t == 2 ? p[i].z : p[i].w;
-                            vacc[x][i][0] = fma_r<RM>(v.x, pk, vacc[x][i][0]);
-                            vacc[x][i][1] = fma_r<RM>(v.y, pk, vacc[x][i][1]);
-                            vacc[x][i][2] = fma_r<RM>(v.z, pk, vacc[x][i][2]);
-                            vacc[x][i][3] = fma_r<RM>(v.w, pk, vacc[x][i][3]);
-                        }
-                    }
-                }
-                for (; kk < kc; kk++) {
+                    for (int e = 0; e < 4; e++) acc[i][e] = 0.0f;
+            }
+            const uint32_t vo = ko + 4 * warp;  // dimensions 4 vo .. 4 vo + 3 of the pass
+            if (vo < dv / 4) {
+                const float* wr = SC + c0 * AQS + 4 * qq;
+                const float* vb = PANELS ? b + (vo / 4) * (16 * AVU + 16) + 4 * (vo % 4) : b + 4 * vo;
+                const uint32_t vstep = PANELS ? 16 : dv + 4;
+                // a key: the 4 queries' weights, 4 values, 16 FMAs
+                auto one = [&](uint32_t kk) {
+                    const float4 p = *reinterpret_cast<const float4*>(wr + kk * AQS);
                     const float4 v = *reinterpret_cast<const float4*>(vb + kk * vstep);
+                    const float pv[4] = {p.x, p.y, p.z, p.w};
 #pragma unroll
                     for (int i = 0; i < 4; i++) {
-                        const float pk = wr[i * SP + kk];
-                        vacc[x][i][0] = fma_r<RM>(v.x, pk, vacc[x][i][0]);
-                        vacc[x][i][1] = fma_r<RM>(v.y, pk, vacc[x][i][1]);
-                        vacc[x][i][2] = fma_r<RM>(v.z, pk, vacc[x][i][2]);
-                        vacc[x][i][3] = fma_r<RM>(v.w, pk, vacc[x][i][3]);
+                        acc[i][0] = fma_r<RM>(v.x, pv[i], acc[i][0]);
+                        acc[i][1] = fma_r<RM>(v.y, pv[i], acc[i][1]);
+                        acc[i][2] = fma_r<RM>(v.z, pv[i], acc[i][2]);
+                        acc[i][3] = fma_r<RM>(v.w, pv[i], acc[i][3]);
+                    }
+                };
+                if (kc == AVU) {
+#pragma unroll
+                    for (uint32_t kk = 0; kk < AVU; kk++) one(kk);
+                } else {
+                    for (uint32_t kk = 0; kk < kc; kk++) one(kk);
+                }
+                if (cc == nvc - 1) {
+                    // o = V^T s + 0 (core/encoder.c:323-324), this pass's dimensions
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const uint32_t qi = 4 * qq + i;
+                        if (qi < nq) {
+                            float* orow = a.o + static_cast<size_t>(sg.f + i0 + qi) * a.os + h * dk + e0 + 4 * vo;
+#pragma unroll
+                            for (int e = 0; e < 4; e++) orow[e] = add_r<RM>(acc[i][e], 0.0f);
+                        }
                     }
                 }
             }
         }
         __syncthreads();  // buffer u & 1 is free for unit u + 2
-    }
-    // o = V^T s + 0 (core/encoder.c:323-324)
-#pragma unroll
-    for (int x = 0; x < 2; x++) {
-        const uint32_t tile = tid + x * A_THREADS;
-        if (tile >= dk) break;
-        const uint32_t dq = tile % (dk / 4), qg = tile / (dk / 4);
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const uint32_t qi = 4 * qg + i;
-            if (qi >= nq) break;
-            float* orow = a.o + static_cast<size_t>(sg.f + i0 + qi) * a.os + h * dk + 4 * dq;
-#pragma unroll
-            for (int e = 0; e < 4; e++) orow[e] = add_r<RM>(vacc[x][i][e], 0.0f);
-        }
     }
 }
 
@@ -482,7 +471,10 @@ cudaError_t softmax_rm(float* x, size_t xs, uint32_t T, uint32_t n, float scale,
 
 template <int RM, bool PANELS>
 cudaError_t attention_rm(const AttArgs& a, size_t smem, cudaStream_t stream) {
-    attention_kernel<RM, PANELS><<<a.items, A_THREADS, smem, stream>>>(a);
+    if (att_dh(a.dk) == 32)
+        attention_kernel<RM, PANELS, 32><<<a.items, A_THREADS, smem, stream>>>(a);
+    else
+        attention_kernel<RM, PANELS, 16><<<a.items, A_THREADS, smem, stream>>>(a);
     return cudaGetLastError();
 }
 
@@ -504,8 +496,10 @@ cudaError_t allow_smem(Kern kern, int optin) {
 
 template <int RM>
 cudaError_t prepare_attention_rm(int optin) {
-    cudaError_t e = allow_smem(attention_kernel<RM, true>, optin);
-    if (e == cudaSuccess) e = allow_smem(attention_kernel<RM, false>, optin);
+    cudaError_t e = allow_smem(attention_kernel<RM, true, 32>, optin);
+    if (e == cudaSuccess) e = allow_smem(attention_kernel<RM, false, 32>, optin);
+    if (e == cudaSuccess) e = allow_smem(attention_kernel<RM, true, 16>, optin);
+    if (e == cudaSuccess) e = allow_smem(attention_kernel<RM, false, 16>, optin);
     return e;
 }
 
@@ -533,8 +527,7 @@ cudaError_t launch_softmax(float* x, size_t xs, uint32_t T, uint32_t n, float sc
 }
 
 size_t attention_smem(uint32_t dk, uint32_t sp) {
-    return (static_cast<size_t>(2 * AQ) * (dk + 4) + 2 * static_cast<size_t>(att_buf(dk)) +
-            static_cast<size_t>(AQ) * sp) *
+    return (static_cast<size_t>(dk) * AQS + 2 * static_cast<size_t>(att_buf(dk)) + static_cast<size_t>(sp) * AQS) *
            sizeof(float);
 }
 
