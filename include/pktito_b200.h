@@ -7,7 +7,9 @@
  *  - pkb_*_host: the reference's backend contract, host pointers in and out,
  *    synchronous. These are what the cuda-b200 entry of the reference's
  *    backend table calls (libpktito_b200/csrc/cuda_b200.c exports
- *    `pk_kernels_cuda_b200`, the table of backend/kernels.h:242-278).
+ *    `pk_kernels_cuda_b200`, the table of backend/kernels.h:242-278, and
+ *    `pk_kernels_cuda_b200_f32`, the same with the attention's float
+ *    kernels gemm_f32 and softmax on the GPU too).
  *
  *  - pkb_*_dev: the same arithmetic on device-resident buffers, enqueued on a
  *    caller's CUDA stream and returning at once; for callers that keep a
@@ -209,6 +211,16 @@ int pkb_dwconv_quantize_dev(void *stream, int8_t *q, float *d, float *out, size_
  * table entry on host pointers is pkb_gemm_f32_host. */
 int pkb_gemm_f32_dev(void *stream, float *out, size_t os, const float *w, uint32_t ld, uint32_t rows, uint32_t n,
                      const float *x, size_t xs, uint32_t T, const float *bias, size_t bs, int relu, int rmode);
+
+/* The table's gemm_f32 on host memory (what pk_kernels_cuda_b200_f32 calls):
+ * the run of panels, the columns and the biases go up, the results' rows
+ * come back at their stride (only out[t*os + r] for r < rows is written, as
+ * the contract says). Synchronous; the calling thread's device. */
+int pkb_gemm_f32_host(float *out, size_t os, const float *w, uint32_t ld, uint32_t rows, uint32_t n,
+                      const float *x, size_t xs, uint32_t T, const float *bias, size_t bs, int relu, int rmode);
+
+/* The table's softmax on one row of n floats of host memory, in place. */
+int pkb_softmax_host(float *x, uint32_t n, float scale, int rmode);
 
 /* pk_k_softmax (backend/kernels.h:124-130; backend/ref/kernels.c:134-147)
  * on T rows of n scores (row t at x + t*xs), each in place, on device

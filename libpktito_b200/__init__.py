@@ -114,6 +114,11 @@ _SIGS = {
                                               ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
                                               ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p,
                                               ctypes.c_uint32, ctypes.c_int]),
+    "pkb_gemm_f32_host": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_uint32,
+                                         ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t,
+                                         ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int,
+                                         ctypes.c_int]),
+    "pkb_softmax_host": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_float, ctypes.c_int]),
     "pkb_launch_count": (ctypes.c_uint64, []),
     "pkb_host_bytes": (None, [ctypes.c_void_p, ctypes.c_void_p]),
     "pkb_quantize_host_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,

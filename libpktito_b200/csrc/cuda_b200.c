@@ -23,6 +23,20 @@
  * program that loads this table has it (pk_kernels_ref, declared weak here
  * so that the table also loads where only the int8 path is used).
  *
+ * A second table, pk_kernels_cuda_b200_f32 ("cuda-b200-f32"), also runs the
+ * attention's float kernels on the GPU:
+ *
+ *   gemm_f32  pk_k_gemm_f32's contract (backend/kernels.h:88-103)  -> pkb_gemm_f32_host
+ *   softmax   pk_k_softmax's contract (backend/kernels.h:124-130)  -> pkb_softmax_host
+ *
+ * (ref's bits, backend/ref/kernels.c:90-105 and 134-147). Every such call
+ * crosses PCIe: the engine calls them per head, block of 16 queries and
+ * score row (core/encoder.c:291-325), and the decoder and the VAD call
+ * gemm_f32 for small products, so cuda-b200 keeps them on the host and this
+ * table is the one to pick where the float products should run on the GPU
+ * (the attention over whole segments on device buffers is
+ * pkb_attention_dev / pkb_attention_rows_dev).
+ *
  * Built inside the reference's tree (backend/cuda-b200/kernels.c with
  * -DPK_CUDA_B200_IN_TREE) it takes the reference's own kernels.h; built
  * here it takes include/pk_kernels_abi.h, the same layout.
@@ -85,6 +99,19 @@ static void k_gemm_f32(float *out, size_t os, const float *w, uint32_t ld, uint3
     ref("gemm_f32")->gemm_f32(out, os, w, ld, rows, n, x, xs, T, bias, bs, relu);
 }
 
+static void k_gemm_f32_gpu(float *out, size_t os, const float *w, uint32_t ld, uint32_t rows, uint32_t n,
+                           const float *x, size_t xs, uint32_t T, const float *bias, size_t bs, int relu) {
+    const int rc = pkb_gemm_f32_host(out, os, w, ld, rows, n, x, xs, T, bias, bs, relu, rounding_now());
+    if (rc)
+        die("gemm_f32", rc);
+}
+
+static void k_softmax_gpu(float *x, uint32_t n, float scale) {
+    const int rc = pkb_softmax_host(x, n, scale, rounding_now());
+    if (rc)
+        die("softmax", rc);
+}
+
 static void k_layernorm(float *out, size_t os, const float *x, size_t xs, uint32_t T, uint32_t n,
                         const float *w, const float *b, float eps) {
     ref("layernorm")->layernorm(out, os, x, xs, T, n, w, b, eps);
@@ -145,6 +172,26 @@ const pk_kernels pk_kernels_cuda_b200 = {
     k_gemm_f32,
     k_layernorm,
     k_softmax,
+    k_silu,
+    k_gelu,
+    k_glu,
+    k_dwconv,
+    k_conv3x3s2,
+    k_lstm,
+    k_stft,
+    k_resample,
+};
+
+const pk_kernels pk_kernels_cuda_b200_f32 = {
+    "cuda-b200-f32",
+    "cuda-b200-f32 (cuda-b200, with gemm_f32 and softmax on the GPU too)",
+    needs,
+    0,
+    k_quantize,
+    k_gemm_q8,
+    k_gemm_f32_gpu,
+    k_layernorm,
+    k_softmax_gpu,
     k_silu,
     k_gelu,
     k_glu,

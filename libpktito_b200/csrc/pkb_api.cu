@@ -432,7 +432,7 @@ int gemm_f32_dev(cudaStream_t stream, float* out, size_t os, const float* w, uin
     if (rows % 16) return fail(PKB_EINVAL, "gemm_f32: rows = %u, a multiple of 16", rows);
     if (n > ld) return fail(PKB_EINVAL, "gemm_f32: n = %u beyond the panels' ld = %u", n, ld);
     if (!T || !rows) return PKB_OK;
-    if (!out || !w || (n && !x)) return fail(PKB_EINVAL, "gemm_f32: null pointer");
+    if (!out || (n && (!w || !x))) return fail(PKB_EINVAL, "gemm_f32: null pointer");
     if (T > 1 && os < rows) return fail(PKB_EINVAL, "gemm_f32: output stride %zu below rows = %u", os, rows);
     if (T > 1 && xs < n) return fail(PKB_EINVAL, "gemm_f32: column stride %zu below n = %u", xs, n);
     if (bias && bs && bs < rows) return fail(PKB_EINVAL, "gemm_f32: bias stride %zu below rows = %u", bs, rows);

@@ -150,19 +150,31 @@ __global__ void __launch_bounds__(SM_THREADS)
 constexpr int AQ = 32;           // queries a CTA (two of the reference's PK_ATT_BLOCK, core/asr.h:16)
 constexpr int A_THREADS = 256;
 constexpr int AKU = 128;         // keys (or positions) a unit of K (P)
-constexpr int AVU = 32;          // keys a unit of V
 constexpr int AQS = AQ + 4;      // row stride of the transposed queries and scores
 
-// The dimensions a unit of K or P carries (a multiple of 16 dividing dk).
-__host__ __device__ __forceinline__ uint32_t att_dh(uint32_t dk) { return dk % 32 ? 16 : 32; }
+// The staging: units of K and P carry DH dimensions of 128 keys, units of
+// V DH keys of up to 128 dimensions, through NBUF buffers (the copies of
+// NBUF - 1 units in flight while the CTA computes on one). Measured on B200
+// over the benchmark's batch: DH 32 with 2 buffers 871 us, DH 16 with 2
+// 1004 us, DH 16 with 3 994 us (more units, more barriers).
+#ifndef PKB_ATT_DH
+#define PKB_ATT_DH 32
+#endif
+#ifndef PKB_ATT_NBUF
+#define PKB_ATT_NBUF 2
+#endif
+constexpr int ADH = PKB_ATT_DH, ANB = PKB_ATT_NBUF;
 
-// floats of one staging buffer: the larger of a K/P unit and a V unit (up
-// to 128 dimensions) in either layout, with the padding that keeps a
-// quarter-warp's 16-byte loads on distinct bank groups
-__host__ __device__ __forceinline__ uint32_t att_buf(uint32_t dk) {
-    const uint32_t dh = att_dh(dk), dv = dk < 128 ? dk : 128;
+// the unit depth a head of dk takes: ADH where it divides dk, else 16
+__host__ __device__ __forceinline__ uint32_t att_dh(uint32_t dk) { return dk % ADH ? 16 : ADH; }
+
+// floats of one staging buffer: the larger of a K/P unit and a V unit in
+// either layout, with the padding that keeps a quarter-warp's 16-byte loads
+// on distinct bank groups
+__host__ __device__ __forceinline__ uint32_t att_buf(uint32_t dk, uint32_t dh) {
+    const uint32_t dv = dk < 128 ? dk : 128, av = dh;
     const uint32_t kp_rows = AKU * (dh + 4), kp_pan = (AKU / 16) * (16 * dh + 16);
-    const uint32_t v_rows = AVU * (dv + 4), v_pan = (dv / 16) * (16 * AVU + 16);
+    const uint32_t v_rows = av * (dv + 4), v_pan = (dv / 16) * (16 * av + 16);
     uint32_t m = kp_rows > kp_pan ? kp_rows : kp_pan;
     m = m > v_rows ? m : v_rows;
     return m > v_pan ? m : v_pan;
@@ -199,7 +211,7 @@ __host__ __device__ __forceinline__ uint32_t att_buf(uint32_t dk) {
 // values: lane (vq, vo) of warp w takes queries 4 vq .. 4 vq + 3 and
 // dimensions 4 (4 w + vo) .. + 3 of the pass, 16 chains over k, a key a
 // step: the 4 queries' weights in one 16-byte load, 4 values in another.
-template <int RM, bool PANELS, int DH>
+template <int RM, bool PANELS, int DH, int NBUF>
 __global__ void __launch_bounds__(A_THREADS, 2) attention_kernel(const __grid_constant__ AttArgs a) {
     extern __shared__ __align__(16) float sm[];
     __shared__ uint32_t s_seg;
@@ -218,9 +230,9 @@ __global__ void __launch_bounds__(A_THREADS, 2) attention_kernel(const __grid_co
     }
     __syncthreads();
     const AttSeg sg = a.seg[s_seg];
-    constexpr uint32_t dh = DH;  // att_dh(dk), the launch's choice
+    constexpr uint32_t dh = DH, AVU = DH;
     const uint32_t T = sg.T, dk = a.dk;
-    const uint32_t nh = dk / dh, BUF = att_buf(dk);
+    const uint32_t nh = dk / dh, BUF = att_buf(dk, dh);
     const uint32_t nqb = (T + AQ - 1) / AQ, local = blockIdx.x - sg.item0;
     const uint32_t h = local / nqb, i0 = (local % nqb) * AQ;
     const uint32_t nq = min(static_cast<uint32_t>(AQ), T - i0), i1 = i0 + nq;
@@ -230,7 +242,7 @@ __global__ void __launch_bounds__(A_THREADS, 2) attention_kernel(const __grid_co
     const uint32_t w0 = (T - i1) & ~15u, W = ((2 * T - 1 - i0 - w0) + 15) & ~15u;
     float* QT = sm;
     float* ST = QT + dk * AQS;
-    float* SC = ST + 2 * BUF;
+    float* SC = ST + NBUF * BUF;
 
     const uint32_t Tp = (T + 15) & ~15u, Pp = ((R + 15) & ~15u) + 16;
     const float* kh = PANELS ? a.k + static_cast<size_t>(h) * Tp * dk : a.k + static_cast<size_t>(sg.f) * a.ks + h * dk;
@@ -292,17 +304,31 @@ __global__ void __launch_bounds__(A_THREADS, 2) attention_kernel(const __grid_co
         cp_async_commit();
     };
 
-    // the block's queries with a position bias, transposed (core/encoder.c:302-309)
+    // the block's queries with a position bias, transposed (core/encoder.c:
+    // 302-309); eight loads of each in flight a thread
     auto load_queries = [&](const float* bias) {
-        for (uint32_t e = tid; e < AQ * dk; e += A_THREADS) {
-            const uint32_t i = e / dk, d = e % dk;
-            float v = 0.0f;
-            if (i < nq) v = add_r<RM>(a.q[static_cast<size_t>(sg.f + i0 + i) * a.qs + h * dk + d], bias[h * dk + d]);
-            QT[d * AQS + i] = v;
+        for (uint32_t e0 = tid; e0 < AQ * dk; e0 += 8 * A_THREADS) {
+            float qv[8], bv[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const uint32_t e = e0 + j * A_THREADS, i = e / dk, d = e % dk;
+                qv[j] = bv[j] = 0.0f;
+                if (e < AQ * dk && i < nq) {
+                    qv[j] = a.q[static_cast<size_t>(sg.f + i0 + i) * a.qs + h * dk + d];
+                    bv[j] = bias[h * dk + d];
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const uint32_t e = e0 + j * A_THREADS, i = e / dk, d = e % dk;
+                if (e < AQ * dk) QT[d * AQS + i] = i < nq ? add_r<RM>(qv[j], bv[j]) : 0.0f;
+            }
         }
     };
 
-    issue(0, ST);
+#pragma unroll
+    for (int j = 0; j < NBUF - 1; j++)
+        if (j < static_cast<int>(U)) issue(j, ST + j * BUF);
     load_queries(a.bu);
 
     const uint32_t qq = lane % 8, ko = lane / 8;  // query quad, key (or dimension) lane group
@@ -310,13 +336,15 @@ __global__ void __launch_bounds__(A_THREADS, 2) attention_kernel(const __grid_co
     const float scale = div_r<RM>(1.0f, sqrt_r<RM>(static_cast<float>(dk)));
 
     for (uint32_t u = 0; u < U; u++) {
-        float* b = ST + (u & 1) * BUF;
-        if (u + 1 < U) {
-            issue(u + 1, ST + ((u + 1) & 1) * BUF);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
+        float* b = ST + (u % NBUF) * BUF;
+        // unit u + NBUF - 1 into the buffer unit u - 1 left (free since the
+        // barrier ending unit u - 1); an empty group past the end keeps the
+        // count of groups in flight the same
+        if (u + NBUF - 1 < U)
+            issue(u + NBUF - 1, ST + ((u + NBUF - 1) % NBUF) * BUF);
+        else
+            cp_async_commit();
+        cp_async_wait<NBUF - 1>();
         if (u == nK) {
             // the scores are done with q + bias_u (the barrier ending unit
             // nK - 1): q + bias_v in its place
@@ -449,7 +477,7 @@ __global__ void __launch_bounds__(A_THREADS, 2) attention_kernel(const __grid_co
                 }
             }
         }
-        __syncthreads();  // buffer u & 1 is free for unit u + 2
+        __syncthreads();  // buffer u % NBUF is free for unit u + NBUF
     }
 }
 
@@ -471,10 +499,10 @@ cudaError_t softmax_rm(float* x, size_t xs, uint32_t T, uint32_t n, float scale,
 
 template <int RM, bool PANELS>
 cudaError_t attention_rm(const AttArgs& a, size_t smem, cudaStream_t stream) {
-    if (att_dh(a.dk) == 32)
-        attention_kernel<RM, PANELS, 32><<<a.items, A_THREADS, smem, stream>>>(a);
+    if (att_dh(a.dk) == ADH)
+        attention_kernel<RM, PANELS, ADH, ANB><<<a.items, A_THREADS, smem, stream>>>(a);
     else
-        attention_kernel<RM, PANELS, 16><<<a.items, A_THREADS, smem, stream>>>(a);
+        attention_kernel<RM, PANELS, 16, ANB><<<a.items, A_THREADS, smem, stream>>>(a);
     return cudaGetLastError();
 }
 
@@ -496,10 +524,10 @@ cudaError_t allow_smem(Kern kern, int optin) {
 
 template <int RM>
 cudaError_t prepare_attention_rm(int optin) {
-    cudaError_t e = allow_smem(attention_kernel<RM, true, 32>, optin);
-    if (e == cudaSuccess) e = allow_smem(attention_kernel<RM, false, 32>, optin);
-    if (e == cudaSuccess) e = allow_smem(attention_kernel<RM, true, 16>, optin);
-    if (e == cudaSuccess) e = allow_smem(attention_kernel<RM, false, 16>, optin);
+    cudaError_t e = allow_smem(attention_kernel<RM, true, ADH, ANB>, optin);
+    if (e == cudaSuccess) e = allow_smem(attention_kernel<RM, false, ADH, ANB>, optin);
+    if (ADH != 16 && e == cudaSuccess) e = allow_smem(attention_kernel<RM, true, 16, ANB>, optin);
+    if (ADH != 16 && e == cudaSuccess) e = allow_smem(attention_kernel<RM, false, 16, ANB>, optin);
     return e;
 }
 
@@ -527,7 +555,8 @@ cudaError_t launch_softmax(float* x, size_t xs, uint32_t T, uint32_t n, float sc
 }
 
 size_t attention_smem(uint32_t dk, uint32_t sp) {
-    return (static_cast<size_t>(dk) * AQS + 2 * static_cast<size_t>(att_buf(dk)) + static_cast<size_t>(sp) * AQS) *
+    return (static_cast<size_t>(dk) * AQS + ANB * static_cast<size_t>(att_buf(dk, att_dh(dk))) +
+            static_cast<size_t>(sp) * AQS) *
            sizeof(float);
 }
 

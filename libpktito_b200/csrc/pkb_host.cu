@@ -1044,6 +1044,75 @@ int pkb_gemm_q8_host(float* out, size_t os, const int8_t* w, const float* ws, co
     return take_out(nchunks - 1);
 }
 
+// pk_k_gemm_f32 on host memory: the run of panels, the columns, the biases
+// (or, where out is the bias, out's rows) up, the product on the device, the
+// results' rows back at their stride (only [t os, t os + rows): the engine's
+// other threads may write the rest of those rows at the same time).
+int pkb_gemm_f32_host(float* out, size_t os, const float* w, uint32_t ld, uint32_t rows, uint32_t n, const float* x,
+                      size_t xs, uint32_t T, const float* bias, size_t bs, int relu, int rmode) {
+    if (rmode < PKB_RN || rmode > PKB_RZ) return set_error(PKB_EINVAL, "rounding mode %d", rmode);
+    if (rows % 16) return set_error(PKB_EINVAL, "gemm_f32: rows = %u, a multiple of 16", rows);
+    if (n > ld) return set_error(PKB_EINVAL, "gemm_f32: n = %u beyond the panels' ld = %u", n, ld);
+    if (!T || !rows) return PKB_OK;
+    if (!out || !w || (n && !x)) return set_error(PKB_EINVAL, "gemm_f32: null pointer");
+    // column t at x + t xs, out + t os, bias + t bs: one column reads no stride
+    if (T == 1) os = xs = bs = 0;
+    if (T > 1 && os < rows) return set_error(PKB_EINVAL, "gemm_f32: output stride %zu below rows = %u", os, rows);
+    if (T > 1 && xs < n) return set_error(PKB_EINVAL, "gemm_f32: column stride %zu below n = %u", xs, n);
+    if (T > 1 && bias && bs && bs < rows) return set_error(PKB_EINVAL, "gemm_f32: bias stride %zu below rows = %u", bs, rows);
+    const bool alias = bias && bias == out;
+    if (alias && bs != os) return set_error(PKB_EINVAL, "gemm_f32: out is the bias but bs %zu != os %zu", bs, os);
+    Pipe* p;
+    uint32_t* err;
+    int rc;
+    if ((rc = open_pipe(&p, &err))) return rc;
+    DrainOnReturn drain{p};
+    const size_t orow = static_cast<size_t>(rows) * 4;
+    const size_t wbytes = n ? ((static_cast<size_t>(rows / 16) - 1) * ld + n) * 64 : 0;
+    const size_t xbytes = n ? ((static_cast<size_t>(T) - 1) * xs + n) * 4 : 0;
+    const size_t bbytes = bias && !alias ? ((bs ? (static_cast<size_t>(T) - 1) * bs : 0) + rows) * 4 : 0;
+    const size_t off_x = up256(wbytes), off_b = off_x + up256(xbytes);
+    if ((rc = p->reserve(off_b + bbytes, static_cast<size_t>(T) * orow, 0))) return rc;
+    const cudaStream_t s = p->s_comp;
+    if (wbytes) HOST_CUDA(cudaMemcpyAsync(p->dev_in[0], w, wbytes, cudaMemcpyHostToDevice, s), "upload");
+    if (xbytes) HOST_CUDA(cudaMemcpyAsync(p->dev_in[0] + off_x, x, xbytes, cudaMemcpyHostToDevice, s), "upload");
+    if (bbytes) HOST_CUDA(cudaMemcpyAsync(p->dev_in[0] + off_b, bias, bbytes, cudaMemcpyHostToDevice, s), "upload");
+    float* dout = reinterpret_cast<float*>(p->dev_out[0]);
+    if (alias)  // the biases are out's rows: up into the results' slot, packed
+        HOST_CUDA(cudaMemcpy2DAsync(dout, orow, out, os * 4, orow, T, cudaMemcpyHostToDevice, s), "upload");
+    const float* dbias = alias ? dout : bias ? reinterpret_cast<const float*>(p->dev_in[0] + off_b) : nullptr;
+    const size_t dbs = alias ? rows : bs;
+    if ((rc = pkb_gemm_f32_dev(s, dout, rows, reinterpret_cast<const float*>(p->dev_in[0]), ld, rows, n,
+                               reinterpret_cast<const float*>(p->dev_in[0] + off_x), T > 1 ? xs : n, T, dbias, dbs, relu,
+                               rmode)))
+        return rc;
+    HOST_CUDA(cudaMemcpy2DAsync(out, (T > 1 ? os : rows) * 4, dout, orow, orow, T, cudaMemcpyDeviceToHost, s),
+              "download");
+    count_host_bytes(wbytes + xbytes + bbytes + (alias ? T * orow : 0), T * orow);
+    return p->finish(err);
+}
+
+// pk_k_softmax on one row of host memory, in place.
+int pkb_softmax_host(float* x, uint32_t n, float scale, int rmode) {
+    if (rmode < PKB_RN || rmode > PKB_RZ) return set_error(PKB_EINVAL, "rounding mode %d", rmode);
+    if (!n) return PKB_OK;
+    if (!x) return set_error(PKB_EINVAL, "softmax: null pointer");
+    Pipe* p;
+    uint32_t* err;
+    int rc;
+    if ((rc = open_pipe(&p, &err))) return rc;
+    DrainOnReturn drain{p};
+    const size_t bytes = static_cast<size_t>(n) * 4;
+    if ((rc = p->reserve(0, bytes, 0))) return rc;
+    const cudaStream_t s = p->s_comp;
+    float* dx = reinterpret_cast<float*>(p->dev_out[0]);
+    HOST_CUDA(cudaMemcpyAsync(dx, x, bytes, cudaMemcpyHostToDevice, s), "upload");
+    if ((rc = pkb_softmax_dev(s, dx, n, 1, n, scale, rmode))) return rc;
+    HOST_CUDA(cudaMemcpyAsync(x, dx, bytes, cudaMemcpyDeviceToHost, s), "download");
+    count_host_bytes(bytes, bytes);
+    return p->finish(err);
+}
+
 int pkb_forget(const void* ptr, size_t bytes) {
     // the copies overlapping the range leave the cache at once; their device
     // memory goes when the last call still using it returns

@@ -37,7 +37,7 @@ def test_table_symbol_and_id(pkb):
 
 def test_dynamic_symbols_with_nm(pkb):
     out = subprocess.run(["nm", "-D", "--defined-only", pkb.LIB_PATH], capture_output=True, text=True).stdout
-    for name in declared_functions() + ["pk_kernels_cuda_b200"]:
+    for name in declared_functions() + ["pk_kernels_cuda_b200", "pk_kernels_cuda_b200_f32"]:
         assert re.search(r"\b%s\b" % name, out), name
 
 

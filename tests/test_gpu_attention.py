@@ -201,3 +201,24 @@ def test_attention_refuses_what_it_cannot_take(pkb, cuda_device):
     with pytest.raises(pkb.PkbError):
         pkb.attention_dev(buf, 1024, buf, 1024, buf, buf, buf, buf, buf, 4000, 1024, 8)  # T 4000
     assert pkb.launch_count() == launches
+
+
+def test_host_entries_of_the_table(pkb, cuda_device, golden):
+    """pkb_gemm_f32_host and pkb_softmax_host (the cuda-b200-f32 table's
+    gemm_f32 and softmax) on host memory: kcheck's draws, a bias a column
+    written in place among them, the reference's bits; the bytes of out
+    between the rows left as they were."""
+    import ctypes
+    lib = pkb.lib()
+    for i, (meta, w, x, b) in enumerate(G.gemm_f32_cases()):
+        rows, ld, k0, n, T, xs, bias_kind, relu, os_ = meta
+        out = b.copy()
+        bias = (out if bias_kind == 2 else b) if bias_kind else None
+        rc = lib.pkb_gemm_f32_host(out.ctypes.data, os_, w.ctypes.data + 64 * k0, ld, rows, n, x.ctypes.data, xs, T,
+                                   0 if bias is None else bias.ctypes.data, os_ if bias_kind == 2 else 0, relu, O.RN)
+        assert rc == 0, pkb.lib().pkb_last_error()
+        assert out.tobytes() == golden[f"gf/{i}/out"].tobytes(), meta
+    for i, s in enumerate(G.softmax_cases()):
+        x = s.copy()
+        assert lib.pkb_softmax_host(x.ctypes.data, x.size, ctypes.c_float(0.0883883476), O.RN) == 0
+        assert x.tobytes() == golden[f"sm/{i}/y"].tobytes(), s.size

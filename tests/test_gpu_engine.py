@@ -2,13 +2,16 @@
 
 oracle/_ref/pktito-c_cuda is the reference's CLI and engine (core/cli.c and
 every core/*.c), compiled unmodified from its sources, whose backend list is
-cuda-b200 then ref (oracle/Makefile). It transcribes the reference's test
-recording with its tiny model twice, once on each backend (PKTITO_KERNELS),
-at one and at eight pool threads and in fast mode, and the two transcripts
-must be the same bytes: every int8 product and quantization of the encoder
-and decoder then went through the GPU with the reference's call pattern
-(slices of 64/256 rows and column chunks from every pool thread at once,
-fused tile callbacks, chunks in lanes) and changed no bit of the result.
+cuda-b200-f32, cuda-b200, then ref (oracle/Makefile). It transcribes the
+reference's test recording with its tiny model on each backend
+(PKTITO_KERNELS), at one and at eight pool threads and in fast mode, and the
+transcripts must be the same bytes: every int8 product and quantization of
+the encoder and decoder then went through the GPU with the reference's call
+pattern (slices of 64/256 rows and column chunks from every pool thread at
+once, fused tile callbacks, chunks in lanes) and changed no bit of the
+result; with cuda-b200-f32 every float product (the attention's scores,
+positions and weighted values, a head and block of 16 queries a call, and
+the decoder's) and every softmax row did too.
 """
 import os
 import subprocess
@@ -36,3 +39,9 @@ def test_reference_engine_transcribes_the_same_bytes_on_cuda_b200(cuda_device, t
     got = transcribe("cuda-b200", threads, fast)
     assert b'"segments"' in want
     assert got == want
+
+
+@pytest.mark.skipif(not os.path.exists(CLI), reason="the reference's engine is not built (make -C oracle ref)")
+@pytest.mark.parametrize("threads", [1, 8])
+def test_reference_engine_with_the_float_kernels_on_the_gpu(cuda_device, threads):
+    assert transcribe("cuda-b200-f32", threads, False) == transcribe("ref", threads, False)
