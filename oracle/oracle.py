@@ -87,6 +87,11 @@ def olib() -> ctypes.CDLL:
         l.oracle_attention.argtypes = [vp, sz, vp, sz, vp, vp, vp, vp, vp, u32, u32, u32, i32]
         for f in (l.oracle_gemm_f32, l.oracle_softmax, l.oracle_attention):
             f.restype = None
+        l.oracle_tanhf.argtypes = [vp, vp, sz, i32]
+        l.oracle_lstm.argtypes = [vp, vp, vp, u32, i32]
+        l.oracle_tanhf.restype = l.oracle_lstm.restype = None
+        l.oracle_tdt_search.argtypes = [vp, vp, vp, ctypes.c_long, vp, u32, ctypes.POINTER(_Tdt), i32]
+        l.oracle_tdt_search.restype = ctypes.c_long
         for f in (l.oracle_set_rint_style, l.oracle_expf, l.oracle_sigmoidf, l.oracle_layernorm,
                   l.oracle_layernorm_quantize, l.oracle_silu_quantize, l.oracle_dwconv_quantize):
             f.restype = None
@@ -265,6 +270,83 @@ def attention(q: np.ndarray, qs: int, kp: np.ndarray, pp: np.ndarray, vp: np.nda
     olib().oracle_attention(_p(o), D, _p(_f32(q)), qs, _p(_f32(kp)), _p(_f32(pp)), _p(_f32(vp)), _p(_f32(bias_u)),
                             _p(_f32(bias_v)), T, D, H, rmode)
     return o
+
+
+class _Tdt(ctypes.Structure):
+    """oracle_tdt (oracle/q8_oracle.c): the decoder's weights"""
+    _fields_ = [(n, ctypes.c_uint32) for n in ("P", "L", "J", "V", "n_dur", "max_symbols", "n_out_pad")] + \
+               [(n, ctypes.c_void_p) for n in ("dur", "embed", "wx", "wh", "wxs", "whs", "lb", "jpred", "jpreds",
+                                               "jpredb", "jout", "jouts", "joutb")]
+
+
+def tdt_read(path: str) -> dict:
+    """A file tdt_ref wrote (oracle/tdt_ref.c): the reference's decoder
+    weights (PK_Q8 bytes and scales), the frames and the reference's tokens."""
+    b = open(path, "rb").read()
+    P, L, J, V, nd, ms, nop, T, nt = np.frombuffer(b, np.uint32, 9).tolist()
+    o = 36
+    out = dict(P=P, L=L, J=J, V=V, n_dur=nd, max_symbols=ms, n_out_pad=nop, T=T)
+
+    def take(name, dtype, count):
+        nonlocal o
+        a = np.frombuffer(b, dtype, count, o).copy()
+        o += a.nbytes
+        out[name] = a
+    take("dur", np.uint32, nd)
+    take("embed", np.float32, (V + 1) * P)
+    wx, wxs, wh, whs, lb = [], [], [], [], []
+    for _ in range(L):
+        for lst, dt, cnt in ((wx, np.int8, 16 * P * P // 4), (wxs, np.float32, 4 * P), (wh, np.int8, 16 * P * P // 4),
+                             (whs, np.float32, 4 * P), (lb, np.float32, 4 * P)):
+            lst.append(np.frombuffer(b, dt, cnt, o).copy())
+            o += lst[-1].nbytes
+    out.update(wx=np.concatenate(wx), wxs=np.concatenate(wxs), wh=np.concatenate(wh), whs=np.concatenate(whs),
+               lb=np.concatenate(lb))
+    take("jpred", np.int8, J * P)
+    take("jpreds", np.float32, J)
+    take("jpredb", np.float32, J)
+    take("jout", np.int8, nop * J)
+    take("jouts", np.float32, nop)
+    take("joutb", np.float32, nop)
+    take("f", np.float32, T * J)
+    take("toks", np.int32, 3 * nt)
+    out["toks"] = out["toks"].reshape(nt, 3)
+    assert o == len(b)
+    return out
+
+
+def tdt_search(m: dict, f: np.ndarray, T: int, rmode: int = RN, cap: int = 1 << 20) -> np.ndarray:
+    """TDT's greedy search (core/decoder.c:125-179) as restated: tokens as
+    rows of (id, frame, duration)."""
+    keep = {k: np.ascontiguousarray(m[k]) for k in ("dur", "embed", "wx", "wh", "wxs", "whs", "lb", "jpred",
+                                                      "jpreds", "jpredb", "jout", "jouts", "joutb")}
+    t = _Tdt(m["P"], m["L"], m["J"], m["V"], m["n_dur"], m["max_symbols"], m["n_out_pad"],
+             *[_p(keep[k]) for k in ("dur", "embed", "wx", "wh", "wxs", "whs", "lb", "jpred", "jpreds", "jpredb",
+                                     "jout", "jouts", "joutb")])
+    f = np.ascontiguousarray(f, np.float32)
+    cap = min(cap, 4 * T + 16)
+    ids, frames, durs = (np.zeros(cap, np.int32) for _ in range(3))
+    n = olib().oracle_tdt_search(_p(ids), _p(frames), _p(durs), cap, _p(f), T, ctypes.byref(t), rmode)
+    assert n >= 0, "more tokens than the cap"
+    return np.stack([ids[:n], frames[:n], durs[:n]], axis=1)
+
+
+def tanhf(x: np.ndarray, rmode: int = RN) -> np.ndarray:
+    """pk_tanhf (core/vmath.h:153-165), elementwise."""
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    olib().oracle_tanhf(_p(y), _p(x), x.size, rmode)
+    return y
+
+
+TDT_REF = os.path.join(REF_DIR, "tdt_ref")
+
+
+def ref_tdt(frames: int, seed: int, scale: float, path: str) -> dict:
+    """The reference's own search (oracle/_ref/tdt_ref over its tiny model)."""
+    subprocess.run([TDT_REF, os.path.join(REF_DIR, "tiny.pkf"), str(frames), str(seed), repr(float(scale)), path],
+                   check=True)
+    return tdt_read(path)
 
 
 def _f32(a: np.ndarray) -> np.ndarray:

@@ -511,3 +511,179 @@ void oracle_attention(float *o, size_t os, const float *q, size_t qs, const floa
     free(s);
     fesetround(was);
 }
+
+/* --------------------------------------------- the TDT decoder's search -- */
+
+/* pk_tanhf (core/vmath.h:153-165) with its constants (:108-116): below
+ * |x| = 0.625 x + x^3 p(x^2) by Horner in fused steps, else
+ * copysign(1 - 2 / (e^2|x| + 1), x) */
+static float or_tanhf(float x) {
+    const float a = fabsf(x);
+    if (a < 0.625f) {
+        const float x2 = x * x;
+        float p = -0x1.75e1cep-8f;
+        p = fmaf(p, x2, 0x1.52269cp-6f);
+        p = fmaf(p, x2, -0x1.b83c5ap-5f);
+        p = fmaf(p, x2, 0x1.110726p-3f);
+        p = fmaf(p, x2, -0x1.555532p-2f);
+        return fmaf(x * x2, p, x);
+    }
+    const float e = or_expf(2.0f * a);
+    return copysignf(1.0f - 2.0f / (e + 1.0f), x);
+}
+
+void oracle_tanhf(float *y, const float *x, size_t n, int rmode) {
+    const int was = fegetround();
+    fesetround(fe_of(rmode));
+    for (size_t i = 0; i < n; i++)
+        y[i] = or_tanhf(x[i]);
+    fesetround(was);
+}
+
+/* k_lstm (backend/ref/kernels.c:203-212): gates g = [i f u o] of H each */
+static void or_lstm(float *h, float *c, const float *g, uint32_t H) {
+    for (uint32_t j = 0; j < H; j++) {
+        const float i = or_sigmoidf(g[j]);
+        const float f = or_sigmoidf(g[H + j]);
+        const float u = or_tanhf(g[2 * H + j]);
+        const float o = or_sigmoidf(g[3 * H + j]);
+        c[j] = f * c[j] + i * u;
+        h[j] = o * or_tanhf(c[j]);
+    }
+}
+
+void oracle_lstm(float *h, float *c, const float *g, uint32_t H, int rmode) {
+    const int was = fegetround();
+    fesetround(fe_of(rmode));
+    or_lstm(h, c, g, H);
+    fesetround(was);
+}
+
+/* The decoder's weights, as core/model.c holds them: int8 matrices in PK_Q8
+ * panels with their row scales. */
+typedef struct {
+    uint32_t P, L, J, V, n_dur, max_symbols, n_out_pad;
+    const uint32_t *dur;          /* [n_dur] */
+    const float *embed;           /* [V + 1][P] */
+    const int8_t *wx, *wh;        /* [L][4P x P] */
+    const float *wxs, *whs, *lb;  /* [L][4P] */
+    const int8_t *jpred;          /* J x P */
+    const float *jpreds, *jpredb; /* [J] */
+    const int8_t *jout;           /* n_out_pad x J */
+    const float *jouts, *joutb;   /* [n_out_pad] */
+} oracle_tdt;
+
+typedef struct {
+    const oracle_tdt *m;
+    float *h, *c, *gates, *gp, *z, *logit, *d;
+    int8_t *q;
+    int rmode;
+} or_dec;
+
+/* gemv (core/decoder.c:53-63): x quantized as one block of cols, then the
+ * product of one column */
+static void or_gemv(or_dec *s, float *out, const int8_t *w, const float *ws, uint32_t rows, uint32_t cols,
+                    const float *bias, const float *x, int add) {
+    oracle_quantize(s->q, s->d, x, cols, 1, cols, cols, s->rmode);
+    oracle_gemm_q8(out, rows, w, ws, bias, rows, s->q, s->d, cols, cols, 1, add, s->rmode);
+}
+
+/* predict (core/decoder.c:67-79) */
+static void or_predict(or_dec *s, uint32_t label) {
+    const oracle_tdt *m = s->m;
+    const uint32_t P = m->P;
+    const float *x = m->embed + (size_t)label * P;
+    for (uint32_t l = 0; l < m->L; l++) {
+        float *h = s->h + (size_t)l * P, *c = s->c + (size_t)l * P;
+        const size_t wo = (size_t)l * 4 * P * P, so = (size_t)l * 4 * P;
+        or_gemv(s, s->gates, m->wx + wo, m->wxs + so, 4 * P, P, m->lb + so, x, 0);
+        or_gemv(s, s->gates, m->wh + wo, m->whs + so, 4 * P, P, NULL, h, 1);
+        oracle_lstm(h, c, s->gates, P, s->rmode);
+        x = h;
+    }
+    or_gemv(s, s->gp, m->jpred, m->jpreds, m->J, P, m->jpredb, x, 0);
+}
+
+/* joint (core/decoder.c:83-103): the best token and duration index */
+static void or_joint(or_dec *s, const float *f, uint32_t *k, uint32_t *di) {
+    const oracle_tdt *m = s->m;
+    const int was = fegetround();
+    fesetround(fe_of(s->rmode));
+    for (uint32_t j = 0; j < m->J; j++) {
+        const float v = f[j] + s->gp[j];
+        s->z[j] = v > 0 ? v : 0;
+    }
+    fesetround(was);
+    or_gemv(s, s->logit, m->jout, m->jouts, m->n_out_pad, m->J, m->joutb, s->z, 0);
+    uint32_t best = 0;
+    for (uint32_t i = 1; i <= m->V; i++)
+        if (s->logit[i] > s->logit[best])
+            best = i;
+    uint32_t bd = 0;
+    for (uint32_t i = 1; i < m->n_dur; i++)
+        if (s->logit[m->V + 1 + i] > s->logit[m->V + 1 + bd])
+            bd = i;
+    *k = best;
+    *di = bd;
+}
+
+/* pk_decode + search (core/decoder.c:125-179): TDT's greedy search over T
+ * frames of the joint's encoder half (f: [T][J]), from the blank's
+ * prediction of a zero state. Writes up to cap tokens (id, frame, duration)
+ * and returns their count (-1 past cap). */
+long oracle_tdt_search(int32_t *id, int32_t *frame, int32_t *durs, long cap, const float *f, uint32_t T,
+                       const oracle_tdt *m, int rmode) {
+    or_dec s = { m };
+    const uint32_t P = m->P;
+    s.rmode = rmode;
+    s.h = calloc((size_t)m->L * P, sizeof(float));
+    s.c = calloc((size_t)m->L * P, sizeof(float));
+    s.gates = malloc((size_t)4 * P * sizeof(float));
+    s.gp = malloc((size_t)m->J * sizeof(float));
+    s.z = malloc((size_t)m->J * sizeof(float));
+    s.logit = malloc((size_t)m->n_out_pad * sizeof(float));
+    const uint32_t big = (P > m->J ? P : m->J);
+    s.q = malloc(big);
+    s.d = malloc(sizeof(float));
+    long n = 0;
+    const uint32_t blank = m->V;
+    if (T) {
+        or_predict(&s, blank);
+        uint32_t t = 0, last = UINT32_MAX, lasts = 0;
+        while (t < T) {
+            uint32_t k, di, d, at;
+            do {
+                at = t;
+                or_joint(&s, f + (size_t)t * m->J, &k, &di);
+                d = m->dur[di];
+                if (k == blank && d == 0)
+                    d = 1;
+                t += d;
+            } while (k == blank && t < T);
+            if (k == blank)
+                break;
+            if (n >= cap) {
+                n = -1;
+                break;
+            }
+            id[n] = (int32_t)k;
+            frame[n] = (int32_t)at;
+            durs[n] = (int32_t)m->dur[di];
+            n++;
+            lasts = last == at ? lasts + 1 : 1;
+            last = at;
+            or_predict(&s, k);
+            if (lasts >= m->max_symbols && last == t)
+                t++;
+        }
+    }
+    free(s.h);
+    free(s.c);
+    free(s.gates);
+    free(s.gp);
+    free(s.z);
+    free(s.logit);
+    free(s.q);
+    free(s.d);
+    return n;
+}
