@@ -354,3 +354,47 @@ def test_live_reference_attention():
         q, kp, pp, vp, bu, bv = G.att_inputs(T, D, H, T + D)
         want = O.ref_attention(q, D, kp, pp, vp, bu, bv, T, D, H)
         assert O.attention(q, D, kp, pp, vp, bu, bv, T, D, H).tobytes() == want.tobytes(), (T, D, H)
+
+
+# ------------------------------------------------ the TDT decoder's search --
+
+TDT_GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "tdt_golden.npz")
+
+
+def test_golden_tdt_search():
+    """The search restated (predict, joint, the label-looping loop of
+    core/decoder.c:125-179, with the oracle's quantize, gemm_q8, sigmoid,
+    tanh and LSTM cell) gives the reference's own tokens on its tiny model
+    (tests/golden/make_tdt_golden.py): blanks that skip frames, durations 0
+    to 3, several tokens at one frame."""
+    from tests.golden import make_tdt_golden as G
+    g = np.load(TDT_GOLDEN)
+    m = G.model(g)
+    durs = set()
+    for i in range(len(G.CASES)):
+        T, seed = (int(v) for v in g[f"case/{i}/meta"])
+        f = G.frames(T, m["J"], seed, float(g[f"case/{i}/scale"][0]))
+        want = g[f"case/{i}/toks"]
+        got = O.tdt_search(m, f, T)
+        assert got.shape == want.shape and (got == want).all(), (T, seed)
+        durs |= set(want[:, 2].tolist())
+    assert {0, 1, 2, 3} <= durs
+
+
+@pytest.mark.skipif(not os.path.exists(O.TDT_REF), reason="oracle/_ref/tdt_ref not built")
+def test_live_reference_tdt_search(tmp_path):
+    for T, seed, scale in [(77, 11, 2.0), (250, 12, 6.0)]:
+        m = O.ref_tdt(T, seed, scale, str(tmp_path / "t.bin"))
+        got = O.tdt_search(m, m["f"], T)
+        assert got.shape == m["toks"].shape and (got == m["toks"]).all()
+
+
+def test_tanh_properties():
+    """pk_tanhf as restated: odd, within 2 ulp of tanh, 0 and the ends."""
+    x = np.linspace(-12, 12, 100001, dtype=np.float32)
+    y = O.tanhf(x)
+    ref = np.tanh(x.astype(np.float64)).astype(np.float32)
+    assert np.abs(y.view(np.int32).astype(np.int64) - ref.view(np.int32).astype(np.int64)).max() <= 2
+    assert (O.tanhf(-x) == -y).all()
+    e = O.tanhf(np.array([0.0, -0.0, 100.0, -100.0], np.float32))
+    assert e[0] == 0 and e[2] == 1.0 and e[3] == -1.0
