@@ -266,6 +266,51 @@ int pkb_attention_rows_dev(void *stream, float *o, size_t os, const float *q, si
                            const float *bias_v, uint32_t D, uint32_t H, const pkb_att_segment *segs, uint32_t nseg,
                            int rmode);
 
+/* ------------------------------------------ the TDT decoder (device) -- */
+
+#define PKB_TDT_MAX_LAYERS 4
+#define PKB_TDT_MAX_DUR 16
+
+/* The TDT decoder's weights on the device: the prediction network's
+ * embedding [(V + 1)][P] (row V the blank's) and L LSTM layers (wx, wh:
+ * 4P x P, gates i f u o; lb the two biases summed), the joint's jpred (J x P
+ * + jpredb) and jout (n_out_pad x J + joutb: V + 1 token logits then n_dur
+ * duration logits, rounded up to 16 rows). The int8 matrices are rows as
+ * pkb_repack_q8_dev makes them from PK_Q8 panels, with their row scales (the
+ * reference's core/model.h:120-128). P and J multiples of 32. */
+typedef struct {
+    uint32_t P, L, J, V, n_dur, max_symbols, n_out_pad;
+    uint32_t dur[PKB_TDT_MAX_DUR];
+    const float *embed;
+    const int8_t *wx[PKB_TDT_MAX_LAYERS], *wh[PKB_TDT_MAX_LAYERS];
+    const float *wxs[PKB_TDT_MAX_LAYERS], *whs[PKB_TDT_MAX_LAYERS], *lb[PKB_TDT_MAX_LAYERS];
+    const int8_t *jpred;
+    const float *jpreds, *jpredb;
+    const int8_t *jout;
+    const float *jouts, *joutb;
+} pkb_tdt_model;
+
+/* Device bytes pkb_tdt_search_dev's work area takes for S segments. */
+size_t pkb_tdt_work_bytes(const pkb_tdt_model *m, uint32_t S);
+
+/* TDT's greedy search (core/decoder.c:125-179, pk_decode) over S segments
+ * at once, bit for bit the reference's: segment s's T[s] frames of the
+ * joint's encoder half are rows of J floats at f + (f0[s] + t)*J (what the
+ * jenc product writes, the batch's segments one after another). Each round
+ * every segment still searching takes one joint step at its own frame (the
+ * rounds' products have the segments as their columns), and those that
+ * emitted a token step their prediction network before the next. Tokens go
+ * to toks + (s*cap + i)*3 as (id, frame, duration), their count to ntok[s].
+ * f, toks, ntok and work are device memory (work: pkb_tdt_work_bytes of it,
+ * 256-byte aligned); f0 and T host memory. Returns when every search has
+ * ended (it reads the segments' states back every few rounds); PKB_EINVAL if
+ * a segment found more than cap tokens. No counterpart in the backend table:
+ * the reference runs the search in core/decoder.c over the table's
+ * quantize, gemm_q8 and lstm, one segment at a time. */
+int pkb_tdt_search_dev(void *stream, const pkb_tdt_model *m, const float *f, const uint32_t *f0, const uint32_t *T,
+                       uint32_t S, int32_t *toks, uint32_t *ntok, uint32_t cap, void *work, size_t work_bytes,
+                       int rmode);
+
 /* Launches of libpktito_b200 kernels since the process started, on every
  * device: the evidence a benchmark reports for its own kernels' work. */
 uint64_t pkb_launch_count(void);

@@ -119,6 +119,10 @@ _SIGS = {
                                          ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int,
                                          ctypes.c_int]),
     "pkb_softmax_host": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_float, ctypes.c_int]),
+    "pkb_tdt_work_bytes": (ctypes.c_size_t, [ctypes.c_void_p, ctypes.c_uint32]),
+    "pkb_tdt_search_dev": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                          ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p,
+                                          ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]),
     "pkb_launch_count": (ctypes.c_uint64, []),
     "pkb_host_bytes": (None, [ctypes.c_void_p, ctypes.c_void_p]),
     "pkb_quantize_host_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,
@@ -325,6 +329,29 @@ def attention_rows_dev(o, os_: int, q, qs: int, k, ks: int, v, vs: int, p, ps: i
     _check(lib().pkb_attention_rows_dev(_stream(stream), _ptr(o), os_, _ptr(q), qs, _ptr(k), ks, _ptr(v), vs,
                                         _ptr(p), ps, _ptr(bias_u), _ptr(bias_v), D, H, ctypes.addressof(arr),
                                         len(segs), rmode))
+
+
+class TdtModel(ctypes.Structure):
+    """pkb_tdt_model (include/pktito_b200.h): the TDT decoder's device weights."""
+    _fields_ = [(n, ctypes.c_uint32) for n in ("P", "L", "J", "V", "n_dur", "max_symbols", "n_out_pad")] + \
+               [("dur", ctypes.c_uint32 * 16), ("embed", ctypes.c_void_p)] + \
+               [(n, ctypes.c_void_p * 4) for n in ("wx", "wh", "wxs", "whs", "lb")] + \
+               [(n, ctypes.c_void_p) for n in ("jpred", "jpreds", "jpredb", "jout", "jouts", "joutb")]
+
+
+def tdt_work_bytes(m: TdtModel, S: int) -> int:
+    return int(lib().pkb_tdt_work_bytes(ctypes.byref(m), S))
+
+
+def tdt_search_dev(m: TdtModel, f, f0: np.ndarray, T: np.ndarray, toks, ntok, cap: int, work, rmode: int = RN,
+                   stream=None) -> None:
+    """TDT's greedy search (core/decoder.c:125-179) over len(T) segments in
+    lockstep: f device rows of J, f0/T host arrays, toks/ntok/work device."""
+    f0 = np.ascontiguousarray(f0, np.uint32)
+    T = np.ascontiguousarray(T, np.uint32)
+    nbytes = work.numel() * work.element_size()
+    _check(lib().pkb_tdt_search_dev(_stream(stream), ctypes.byref(m), _ptr(f), f0.ctypes.data, T.ctypes.data, T.size,
+                                    _ptr(toks), _ptr(ntok), cap, _ptr(work), nbytes, rmode))
 
 
 def repack_q8_dev(wpack, w_pk, rows: int, n: int, stream=None) -> None:

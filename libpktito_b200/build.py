@@ -23,7 +23,7 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libpktito_b200.so")
 
 CU_SOURCES = ["pkb_api.cu", "pkb_host.cu", "pkb_gemm.cu", "pkb_quantize.cu", "pkb_noalloc.cu", "pkb_selftest.cu", "pkb_fused.cu",
-              "pkb_attn.cu"]
+              "pkb_attn.cu", "pkb_tdt.cu"]
 C_SOURCES = ["cuda_b200.c"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

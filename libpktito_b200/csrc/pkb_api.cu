@@ -526,6 +526,171 @@ int attention_dev(cudaStream_t stream, bool panels, float* o, size_t os, const f
     return PKB_OK;
 }
 
+// ------------------------------------------------------------- TDT search --
+
+// The work area's pieces, 256-byte aligned, in the order TdtArgs lists them.
+struct TdtLayout {
+    size_t seg, T, f0, qembed, dembed, qx, dx, h, c, qh, dh, gates, gp, gpn, qz, dz, logits, total;
+};
+
+TdtLayout tdt_layout(const pkb_tdt_model& m, uint32_t S) {
+    TdtLayout o = {};
+    size_t at = 0;
+    auto take = [&](size_t bytes) {
+        const size_t here = at;
+        at += (bytes + 255) & ~size_t(255);
+        return here;
+    };
+    const size_t P = m.P, J = m.J, L = m.L, V1 = m.V + 1;
+    o.seg = take(S * tdt_seg_bytes());
+    o.T = take(S * 4);
+    o.f0 = take(S * 4);
+    o.qembed = take(V1 * P);
+    o.dembed = take(V1 * 4);
+    o.qx = take(S * P);
+    o.dx = take(S * 4);
+    o.h = take(L * S * P * 4);
+    o.c = take(L * S * P * 4);
+    o.qh = take(L * S * P);
+    o.dh = take(L * S * 4);
+    o.gates = take(S * 4 * P * 4);
+    o.gp = take(S * J * 4);
+    o.gpn = take(S * J * 4);
+    o.qz = take(S * J);
+    o.dz = take(S * 4);
+    o.logits = take(S * size_t(m.n_out_pad) * 4);
+    o.total = at;
+    return o;
+}
+
+int check_tdt(const pkb_tdt_model* m) {
+    if (!m) return fail(PKB_EINVAL, "tdt: null model");
+    if (!m->P || m->P % 32 || m->P > PKB_MAX_N || !m->J || m->J % 32 || m->J > PKB_MAX_N)
+        return fail(PKB_EINVAL, "tdt: P = %u and J = %u, multiples of 32 up to %u", m->P, m->J, PKB_MAX_N);
+    if (!m->L || m->L > PKB_TDT_MAX_LAYERS) return fail(PKB_EINVAL, "tdt: %u LSTM layers", m->L);
+    if (!m->n_dur || m->n_dur > PKB_TDT_MAX_DUR) return fail(PKB_EINVAL, "tdt: %u durations", m->n_dur);
+    if (m->n_out_pad % 16 || m->n_out_pad < m->V + 1 + m->n_dur)
+        return fail(PKB_EINVAL, "tdt: n_out_pad = %u for %u tokens and %u durations", m->n_out_pad, m->V + 1, m->n_dur);
+    if (!m->max_symbols) return fail(PKB_EINVAL, "tdt: max_symbols 0");
+    if (!m->embed || !m->jpred || !m->jpreds || !m->jout || !m->jouts)
+        return fail(PKB_EINVAL, "tdt: null weights");
+    for (uint32_t l = 0; l < m->L; l++)
+        if (!m->wx[l] || !m->wh[l] || !m->wxs[l] || !m->whs[l] || !m->lb[l])
+            return fail(PKB_EINVAL, "tdt: null weights of layer %u", l);
+    return PKB_OK;
+}
+
+int tdt_search_dev(cudaStream_t st, const pkb_tdt_model* m, const float* f, const uint32_t* f0, const uint32_t* T,
+                   uint32_t S, int32_t* toks, uint32_t* ntok, uint32_t cap, void* work, size_t work_bytes, int rmode) {
+    int rc;
+    if ((rc = check_rmode(rmode)) || (rc = check_tdt(m))) return rc;
+    if (!S) return PKB_OK;
+    if (!f || !f0 || !T || !toks || !ntok || !work) return fail(PKB_EINVAL, "tdt: null pointer");
+    const TdtLayout o = tdt_layout(*m, S);
+    if (work_bytes < o.total || !aligned(work, 256))
+        return fail(PKB_EINVAL, "tdt: work area of %zu bytes (%zu needed, 256-byte aligned)", work_bytes, o.total);
+    Device* dev;
+    if ((rc = current_device(&dev))) return rc;
+    uint8_t* w = static_cast<uint8_t*>(work);
+    TdtArgs a = {};
+    a.S = S;
+    a.P = m->P;
+    a.J = m->J;
+    a.V = m->V;
+    a.n_dur = m->n_dur;
+    a.max_symbols = m->max_symbols;
+    a.nout = m->n_out_pad;
+    a.cap = cap;
+    for (uint32_t i = 0; i < m->n_dur; i++) a.dur[i] = m->dur[i];
+    a.T = reinterpret_cast<const uint32_t*>(w + o.T);
+    a.f0 = reinterpret_cast<const uint32_t*>(w + o.f0);
+    a.f = f;
+    a.seg = w + o.seg;
+    a.ntok = ntok;
+    a.toks = toks;
+    a.qembed = reinterpret_cast<const int8_t*>(w + o.qembed);
+    a.dembed = reinterpret_cast<const float*>(w + o.dembed);
+    a.qx = reinterpret_cast<int8_t*>(w + o.qx);
+    a.dx = reinterpret_cast<float*>(w + o.dx);
+    a.h = reinterpret_cast<float*>(w + o.h);
+    a.c = reinterpret_cast<float*>(w + o.c);
+    a.qh = reinterpret_cast<int8_t*>(w + o.qh);
+    a.dh = reinterpret_cast<float*>(w + o.dh);
+    a.gates = reinterpret_cast<float*>(w + o.gates);
+    a.gp = reinterpret_cast<float*>(w + o.gp);
+    a.gpn = reinterpret_cast<float*>(w + o.gpn);
+    a.qz = reinterpret_cast<int8_t*>(w + o.qz);
+    a.dz = reinterpret_cast<float*>(w + o.dz);
+    a.logits = reinterpret_cast<float*>(w + o.logits);
+    // a zero state: h, c and h quantized (a block of zeros quantizes to
+    // zeros with scale 0), and the joint's halves
+    PKB_CUDA(cudaMemsetAsync(w + o.h, 0, o.gates - o.h, st), "cudaMemsetAsync");
+    PKB_CUDA(cudaMemsetAsync(w + o.gp, 0, o.qz - o.gp, st), "cudaMemsetAsync");
+    PKB_CUDA(cudaMemcpyAsync(w + o.T, T, S * 4, cudaMemcpyHostToDevice, st), "upload");
+    PKB_CUDA(cudaMemcpyAsync(w + o.f0, f0, S * 4, cudaMemcpyHostToDevice, st), "upload");
+    uint32_t tmax = 0;
+    for (uint32_t s = 0; s < S; s++) tmax = T[s] > tmax ? T[s] : tmax;
+    // the embedding quantized once a row, as gemv quantizes its input
+    if ((rc = quantize_dev(st, reinterpret_cast<int8_t*>(w + o.qembed), reinterpret_cast<float*>(w + o.dembed),
+                           m->embed, m->P, m->V + 1, m->P, m->P, rmode)))
+        return rc;
+    PKB_CUDA(launch_tdt_init(a, st), "tdt launch");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    const uint32_t P = m->P, J = m->J, L = m->L;
+    auto product = [&](float* out, uint32_t rows, const int8_t* wq, const float* ws, const float* bias,
+                       const int8_t* q, const float* d, uint32_t n, int add) {
+        return gemm_dev(st, out, rows, wq, ws, bias, rows, q, d, n, n, S, add, rmode);
+    };
+    auto tdt = [&](int phase, uint32_t l) -> int {
+        PKB_CUDA(launch_tdt(a, phase, l, rmode, st), "tdt launch");
+        g_launches.fetch_add(1, std::memory_order_relaxed);
+        return PKB_OK;
+    };
+    // every round takes each running segment one joint step further (or one
+    // token), so T (max_symbols + 1) + 1 rounds end every search
+    const uint64_t max_rounds = static_cast<uint64_t>(tmax) * (m->max_symbols + 1) + 2;
+    std::vector<uint8_t> states(S * tdt_seg_bytes());
+    bool running = true;
+    for (uint64_t r = 0; running && r < max_rounds; r++) {
+        // the prediction network of the segments that emitted (all of them
+        // at the first round: the blank's), columns of the others unused
+        for (uint32_t l = 0; l < L; l++) {
+            const int8_t* qin = l ? a.qh + static_cast<size_t>(l - 1) * S * P : a.qx;
+            const float* din = l ? a.dh + static_cast<size_t>(l - 1) * S : a.dx;
+            if ((rc = product(a.gates, 4 * P, m->wx[l], m->wxs[l], m->lb[l], qin, din, P, 0))) return rc;
+            if ((rc = product(a.gates, 4 * P, m->wh[l], m->whs[l], nullptr, a.qh + static_cast<size_t>(l) * S * P,
+                              a.dh + static_cast<size_t>(l) * S, P, 1)))
+                return rc;
+            if ((rc = tdt(TDT_LSTM, l))) return rc;
+        }
+        if ((rc = product(a.gpn, J, m->jpred, m->jpreds, m->jpredb, a.qh + static_cast<size_t>(L - 1) * S * P,
+                          a.dh + static_cast<size_t>(L - 1) * S, P, 0)))
+            return rc;
+        // the joint at each running segment's frame, and the search's step
+        if ((rc = tdt(TDT_JOINT_IN, 0))) return rc;
+        if ((rc = product(a.logits, m->n_out_pad, m->jout, m->jouts, m->joutb, a.qz, a.dz, J, 0))) return rc;
+        if ((rc = tdt(TDT_STEP, 0))) return rc;
+        if (r % 8 == 7 || r + 1 == max_rounds) {
+            PKB_CUDA(cudaMemcpyAsync(states.data(), w + o.seg, states.size(), cudaMemcpyDeviceToHost, st), "download");
+            PKB_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+            running = false;
+            for (uint32_t s = 0; s < S; s++) {
+                const uint32_t* g = reinterpret_cast<const uint32_t*>(states.data() + s * tdt_seg_bytes());
+                if (g[TDT_SEG_ACTIVE]) running = true;
+            }
+        }
+    }
+    PKB_CUDA(cudaMemcpyAsync(states.data(), w + o.seg, states.size(), cudaMemcpyDeviceToHost, st), "download");
+    PKB_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+    for (uint32_t s = 0; s < S; s++) {
+        const uint32_t* g = reinterpret_cast<const uint32_t*>(states.data() + s * tdt_seg_bytes());
+        if (g[TDT_SEG_OVER]) return fail(PKB_EINVAL, "tdt: segment %u found more than %u tokens", s, cap);
+        if (g[TDT_SEG_ACTIVE]) return fail(PKB_ETIMEOUT, "tdt: segment %u still searching after %llu rounds", s,
+                              static_cast<unsigned long long>(max_rounds));
+    }
+    return PKB_OK;
+}
+
 }  // namespace
 
 int current_device_info(int* sms, uint32_t** err_word) {
@@ -638,6 +803,17 @@ int pkb_attention_rows_dev(void* stream, float* o, size_t os, const float* q, si
                            int rmode) {
     return pkb::attention_dev(static_cast<cudaStream_t>(stream), false, o, os, q, qs, k, ks, v, vs, p, ps, bias_u,
                               bias_v, D, H, segs, nseg, rmode);
+}
+
+size_t pkb_tdt_work_bytes(const pkb_tdt_model* m, uint32_t S) {
+    return m && S ? pkb::tdt_layout(*m, S).total : 0;
+}
+
+int pkb_tdt_search_dev(void* stream, const pkb_tdt_model* m, const float* f, const uint32_t* f0, const uint32_t* T,
+                       uint32_t S, int32_t* toks, uint32_t* ntok, uint32_t cap, void* work, size_t work_bytes,
+                       int rmode) {
+    return pkb::tdt_search_dev(static_cast<cudaStream_t>(stream), m, f, f0, T, S, toks, ntok, cap, work, work_bytes,
+                               rmode);
 }
 
 int pkb_gemm_q8_panels_dev(void* stream, float* panels, int kind, size_t ps, uint32_t dk, uint32_t tpad,

@@ -145,6 +145,41 @@ cudaError_t prepare_attention();
 // The dynamic shared memory an attention CTA may take (set by prepare_attention).
 size_t attention_smem_max();
 
+// ------------------------------------------------ the TDT search (pkb_tdt.cu) --
+
+enum { TDT_LSTM = 0, TDT_JOINT_IN = 1, TDT_STEP = 2 };
+
+// A lockstep search's buffers (device) and shapes; pkb_tdt.cu's kernels
+// take it by value.
+struct TdtArgs {
+    uint32_t S, P, J, V, n_dur, max_symbols, nout, cap;
+    uint32_t dur[16];
+    const uint32_t *T, *f0;  // [S] frames, first frame row
+    const float* f;          // the joint's encoder half, rows of J
+    void* seg;               // [S] search states
+    uint32_t* ntok;          // [S] tokens emitted
+    int32_t* toks;           // [S][cap][3] id, frame, duration
+    const int8_t* qembed;    // [V + 1][P] the embedding quantized a row a block
+    const float* dembed;     // [V + 1]
+    int8_t* qx;              // [S][P] the first layer's input
+    float* dx;               // [S]
+    float *h, *c;            // [L][S][P]
+    int8_t* qh;              // [L][S][P] h quantized
+    float* dh;               // [L][S]
+    float* gates;            // [S][4P]
+    float *gp, *gpn;         // [S][J] jpred of the prediction, and its next value
+    int8_t* qz;              // [S][J] the joint's input quantized
+    float* dz;               // [S]
+    float* logits;           // [S][nout]
+};
+
+cudaError_t launch_tdt_init(const TdtArgs& a, cudaStream_t stream);
+cudaError_t launch_tdt(const TdtArgs& a, int phase, uint32_t l, int rmode, cudaStream_t stream);
+size_t tdt_seg_bytes();  // one segment's search state
+// the 32-bit words of a search state the host reads back: still searching,
+// out of token room
+constexpr int TDT_SEG_ACTIVE = 4, TDT_SEG_OVER = 7;
+
 cudaError_t launch_repack_q8(int8_t* wpack, const int8_t* w_pk, uint32_t rows, uint32_t n, int num_sms,
                              cudaStream_t stream);
 
