@@ -722,6 +722,116 @@ def attention_timing(model, segs, sm_mhz) -> dict:
             "parity": attention_check(torch, o, q, k, v, p, bu, bv, sl, picks)}
 
 
+def tdt_model_synthetic(P_: int = 640, J: int = 640, V: int = 8192, layers: int = 2, seed: int = SEED + 321):
+    """The TDT decoder's weights at the model's shapes (pred_hidden 640,
+    joint 640, vocab 8192 + blank, durations 0-4: jout 8208 x 640), seeded:
+    PK_Q8 bytes uniform, scales and biases in small ranges; the blank's bias
+    raised and duration 0's lowered so that a segment emits about a token
+    every three frames, most of them moving on 2 frames or more (measured
+    with the oracle: 20 tokens over 60 seeded frames), as speech does."""
+    from oracle import oracle as O  # PK_Q8 packing of the seeded rows
+    g = np.random.default_rng(seed)
+    nd = 5
+    nop = (V + 1 + nd + 15) // 16 * 16
+
+    def q8(rows, n):
+        return O.pack_q8(g.integers(-127, 128, (rows, n), dtype=np.int8))
+
+    def sc(n):
+        return (1e-4 + 9e-4 * g.random(n)).astype(np.float32)
+    m = dict(P=P_, L=layers, J=J, V=V, n_dur=nd, max_symbols=10, n_out_pad=nop,
+             dur=np.arange(nd, dtype=np.uint32), embed=(g.standard_normal((V + 1) * P_) * 0.5).astype(np.float32))
+    m["wx"] = np.concatenate([q8(4 * P_, P_) for _ in range(layers)])
+    m["wh"] = np.concatenate([q8(4 * P_, P_) for _ in range(layers)])
+    m["wxs"], m["whs"] = sc(layers * 4 * P_), sc(layers * 4 * P_)
+    m["lb"] = (g.standard_normal(layers * 4 * P_) * 0.1).astype(np.float32)
+    m["jpred"], m["jpreds"], m["jpredb"] = q8(J, P_), sc(J), (g.standard_normal(J) * 0.1).astype(np.float32)
+    m["jout"], m["jouts"] = q8(nop, J), sc(nop)
+    m["joutb"] = (g.standard_normal(nop) * 0.1).astype(np.float32)
+    m["joutb"][V] += 7.0
+    m["joutb"][V + 1] -= 3.0
+    return m
+
+
+def tdt_device_model(torch, P, m: dict):
+    """pkb_tdt_model over device copies of m (PK_Q8 repacked to rows)."""
+    keep = []
+
+    def put(a):
+        t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        keep.append(t)
+        return t.data_ptr()
+
+    def q8(w_pk, rows, n):
+        src = torch.from_numpy(np.ascontiguousarray(w_pk)).cuda()
+        out = torch.empty(rows * n, dtype=torch.int8, device="cuda")
+        P.repack_q8_dev(out, src, rows, n)
+        keep.extend([src, out])
+        return out.data_ptr()
+    p_, l_, j_ = m["P"], m["L"], m["J"]
+    t = P.TdtModel()
+    t.P, t.L, t.J, t.V, t.n_dur, t.max_symbols, t.n_out_pad = p_, l_, j_, m["V"], m["n_dur"], m["max_symbols"], \
+        m["n_out_pad"]
+    for i, d in enumerate(m["dur"]):
+        t.dur[i] = int(d)
+    t.embed = put(m["embed"])
+    for l in range(l_):
+        sl, sv = slice(l * 4 * p_ * p_, (l + 1) * 4 * p_ * p_), slice(l * 4 * p_, (l + 1) * 4 * p_)
+        t.wx[l], t.wh[l] = q8(m["wx"][sl], 4 * p_, p_), q8(m["wh"][sl], 4 * p_, p_)
+        t.wxs[l], t.whs[l], t.lb[l] = put(m["wxs"][sv]), put(m["whs"][sv]), put(m["lb"][sv])
+    t.jpred, t.jpreds, t.jpredb = q8(m["jpred"], j_, p_), put(m["jpreds"]), put(m["jpredb"])
+    t.jout, t.jouts, t.joutb = q8(m["jout"], m["n_out_pad"], j_), put(m["jouts"]), put(m["joutb"])
+    return t, keep
+
+
+def decoder_search(model, segs) -> dict:
+    """TDT's greedy search (core/decoder.c:125-179) over the rank's segments
+    in lockstep on the device (pkb_tdt_search_dev): seeded weights at the
+    model's shapes, each segment's frames of the joint's encoder half seeded
+    (the jenc product's output), one call decoding the whole batch, timed
+    with CUDA events; then the shortest segment's tokens against the
+    oracle's search."""
+    torch, P = model.torch, model.P
+    m = tdt_model_synthetic()
+    t, keep = tdt_device_model(torch, P, m)
+    Ts = np.array([sg[3] for sg in segs], np.uint32)
+    f0 = np.concatenate([[0], np.cumsum(Ts)[:-1]]).astype(np.uint32)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED + 77)
+    f = 2.0 * torch.randn(int(Ts.sum() + 1) * m["J"], device="cuda", generator=g)
+    S, cap = len(Ts), int(Ts.max()) * (m["max_symbols"] + 1) + 8
+    toks = torch.empty(S * cap * 3, dtype=torch.int32, device="cuda")
+    ntok = torch.empty(S, dtype=torch.int32, device="cuda")
+    work = torch.empty(P.tdt_work_bytes(t, S) // 4 + 64, device="cuda")
+    l0 = P.launch_count()
+    P.tdt_search_dev(t, f, f0, Ts, toks, ntok, cap, work)  # warm
+    torch.cuda.synchronize()
+    launches = P.launch_count() - l0
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    e0.record(s)
+    for _ in range(reps):
+        P.tdt_search_dev(t, f, f0, Ts, toks, ntok, cap, work)
+    e1.record(s)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    n = ntok.cpu().numpy()
+    i = int(np.argmin(Ts))
+    from oracle import oracle as O
+    fh = f.view(-1, m["J"])[int(f0[i]):int(f0[i]) + int(Ts[i])].cpu().numpy().reshape(-1)
+    want = O.tdt_search(m, fh, int(Ts[i]))
+    got = toks.view(S, cap, 3)[i, :int(n[i])].cpu().numpy()
+    rounds = (launches - 2) // (3 * m["L"] + 4)  # the embedding's quantize and the initial state, then a round's launches
+    return {"ms": ms, "segments": S, "frames": int(Ts.sum()), "tokens": int(n.sum()), "rounds": int(rounds),
+            "us_per_round": ms * 1e3 / max(1, rounds), "launches_per_round": 3 * m["L"] + 4,
+            "frames_per_s": float(Ts.sum()) / (ms * 1e-3),
+            "shapes": "pred_hidden 640 x 2 LSTM layers, joint 640, jout 8208 x 640, durations 0-4; qb = n",
+            "parity": {"segment_frames": int(Ts[i]), "tokens": int(len(want)),
+                       "equal": bool(got.shape == want.shape and (got == want).all()),
+                       "checker": "the oracle's search (oracle_tdt_search), pinned to the reference's pk_decode"}}
+
+
 def decoder_batched(model, T: int, segs: int = SEGMENTS, layers: int = 2, P_: int = 640, J: int = 640,
                     vocab_out: int = 8208) -> dict:
     """The TDT decoder's int8 products with the batch's segments stepped in
@@ -1161,6 +1271,7 @@ def run_ours(args) -> None:
         roof["decoder_batched"] = decoder_batched(model, sum(sg[3] for sg in segs))
         roof["panels"] = panels_timing(model, sum(sg[3] for sg in segs))
         roof["attention"] = attention_timing(model, segs, clk.get("sm_mhz"))
+        roof["decoder_search"] = decoder_search(model, segs)
     e2e = None
     if not args.no_e2e:
         # every rank at once through the host table, each on its own
