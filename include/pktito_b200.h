@@ -302,9 +302,11 @@ size_t pkb_tdt_work_bytes(const pkb_tdt_model *m, uint32_t S);
  * emitted a token step their prediction network before the next. Tokens go
  * to toks + (s*cap + i)*3 as (id, frame, duration), their count to ntok[s].
  * f, toks, ntok and work are device memory (work: pkb_tdt_work_bytes of it,
- * 256-byte aligned); f0 and T host memory. Returns when every search has
- * ended (it reads the segments' states back every few rounds); PKB_EINVAL if
- * a segment found more than cap tokens. No counterpart in the backend table:
+ * 256-byte aligned); f0 and T host memory. Waits for the work already on
+ * stream, runs the search on a stream of its own (its rounds replayed as a
+ * CUDA graph of 8, the segments' states read back after each) and returns
+ * when every search has ended; PKB_EINVAL if a segment found more than cap
+ * tokens. No counterpart in the backend table:
  * the reference runs the search in core/decoder.c over the table's
  * quantize, gemm_q8 and lstm, one segment at a time. */
 int pkb_tdt_search_dev(void *stream, const pkb_tdt_model *m, const float *f, const uint32_t *f0, const uint32_t *T,

@@ -528,6 +528,10 @@ int attention_dev(cudaStream_t stream, bool panels, float* o, size_t os, const f
 
 // ------------------------------------------------------------- TDT search --
 
+#ifndef PKB_TDT_GRAPH
+#define PKB_TDT_GRAPH 1
+#endif
+
 // The work area's pieces, 256-byte aligned, in the order TdtArgs lists them.
 struct TdtLayout {
     size_t seg, T, f0, qembed, dembed, qx, dx, h, c, qh, dh, gates, gp, gpn, qz, dz, logits, total;
@@ -580,8 +584,18 @@ int check_tdt(const pkb_tdt_model* m) {
     return PKB_OK;
 }
 
-int tdt_search_dev(cudaStream_t st, const pkb_tdt_model* m, const float* f, const uint32_t* f0, const uint32_t* T,
-                   uint32_t S, int32_t* toks, uint32_t* ntok, uint32_t cap, void* work, size_t work_bytes, int rmode) {
+// A stream of the call's own (rounds are captured into a graph, which the
+// legacy default stream a caller may pass cannot be), destroyed on return.
+struct OwnStream {
+    cudaStream_t s = nullptr;
+    ~OwnStream() {
+        if (s) cudaStreamDestroy(s);
+    }
+};
+
+int tdt_search_dev(cudaStream_t caller, const pkb_tdt_model* m, const float* f, const uint32_t* f0,
+                   const uint32_t* T, uint32_t S, int32_t* toks, uint32_t* ntok, uint32_t cap, void* work,
+                   size_t work_bytes, int rmode) {
     int rc;
     if ((rc = check_rmode(rmode)) || (rc = check_tdt(m))) return rc;
     if (!S) return PKB_OK;
@@ -591,6 +605,12 @@ int tdt_search_dev(cudaStream_t st, const pkb_tdt_model* m, const float* f, cons
         return fail(PKB_EINVAL, "tdt: work area of %zu bytes (%zu needed, 256-byte aligned)", work_bytes, o.total);
     Device* dev;
     if ((rc = current_device(&dev))) return rc;
+    // the caller's work on f and the outputs ends first; the call's own runs
+    // on its own stream and has ended when it returns
+    PKB_CUDA(cudaStreamSynchronize(caller), "cudaStreamSynchronize");
+    OwnStream own;
+    PKB_CUDA(cudaStreamCreateWithFlags(&own.s, cudaStreamNonBlocking), "cudaStreamCreate");
+    const cudaStream_t st = own.s;
     uint8_t* w = static_cast<uint8_t*>(work);
     TdtArgs a = {};
     a.S = S;
@@ -646,14 +666,11 @@ int tdt_search_dev(cudaStream_t st, const pkb_tdt_model* m, const float* f, cons
         g_launches.fetch_add(1, std::memory_order_relaxed);
         return PKB_OK;
     };
-    // every round takes each running segment one joint step further (or one
-    // token), so T (max_symbols + 1) + 1 rounds end every search
-    const uint64_t max_rounds = static_cast<uint64_t>(tmax) * (m->max_symbols + 1) + 2;
-    std::vector<uint8_t> states(S * tdt_seg_bytes());
-    bool running = true;
-    for (uint64_t r = 0; running && r < max_rounds; r++) {
-        // the prediction network of the segments that emitted (all of them
-        // at the first round: the blank's), columns of the others unused
+    // one round: the prediction network of the segments that emitted (all of
+    // them at the first round: the blank's; the other columns' results are
+    // not used), then the joint at each running segment's frame and the
+    // search's step
+    auto round = [&]() -> int {
         for (uint32_t l = 0; l < L; l++) {
             const int8_t* qin = l ? a.qh + static_cast<size_t>(l - 1) * S * P : a.qx;
             const float* din = l ? a.dh + static_cast<size_t>(l - 1) * S : a.dx;
@@ -666,20 +683,60 @@ int tdt_search_dev(cudaStream_t st, const pkb_tdt_model* m, const float* f, cons
         if ((rc = product(a.gpn, J, m->jpred, m->jpreds, m->jpredb, a.qh + static_cast<size_t>(L - 1) * S * P,
                           a.dh + static_cast<size_t>(L - 1) * S, P, 0)))
             return rc;
-        // the joint at each running segment's frame, and the search's step
         if ((rc = tdt(TDT_JOINT_IN, 0))) return rc;
         if ((rc = product(a.logits, m->n_out_pad, m->jout, m->jouts, m->joutb, a.qz, a.dz, J, 0))) return rc;
-        if ((rc = tdt(TDT_STEP, 0))) return rc;
-        if (r % 8 == 7 || r + 1 == max_rounds) {
-            PKB_CUDA(cudaMemcpyAsync(states.data(), w + o.seg, states.size(), cudaMemcpyDeviceToHost, st), "download");
-            PKB_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize");
-            running = false;
-            for (uint32_t s = 0; s < S; s++) {
-                const uint32_t* g = reinterpret_cast<const uint32_t*>(states.data() + s * tdt_seg_bytes());
-                if (g[TDT_SEG_ACTIVE]) running = true;
-            }
-        }
+        return tdt(TDT_STEP, 0);
+    };
+    // ROUNDS rounds as one CUDA graph, replayed until every search has ended
+    // (a round past a segment's end does nothing to it); each round takes
+    // every running segment one joint step further or one token on, so
+    // T (max_symbols + 1) + 1 rounds end every search
+    constexpr uint32_t ROUNDS = 8;
+    const uint64_t max_rounds = static_cast<uint64_t>(tmax) * (m->max_symbols + 1) + 2;
+    std::vector<uint8_t> states(S * tdt_seg_bytes());
+#if !PKB_TDT_GRAPH
+    for (uint64_t r = 0; r < max_rounds; r += ROUNDS) {
+        for (uint32_t i = 0; i < ROUNDS; i++)
+            if ((rc = round())) return rc;
+        PKB_CUDA(cudaMemcpyAsync(states.data(), w + o.seg, states.size(), cudaMemcpyDeviceToHost, st), "download");
+        PKB_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+        bool running = false;
+        for (uint32_t s = 0; s < S; s++)
+            if (reinterpret_cast<const uint32_t*>(states.data() + s * tdt_seg_bytes())[TDT_SEG_ACTIVE]) running = true;
+        if (!running) break;
     }
+#else
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    PKB_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+    int crc = PKB_OK;
+    const uint64_t counted = g_launches.load();
+    for (uint32_t r = 0; r < ROUNDS && !crc; r++) crc = round();
+    // a captured launch runs when the graph does: counted at each replay
+    g_launches.fetch_sub(g_launches.load() - counted, std::memory_order_relaxed);
+    const cudaError_t ce = cudaStreamEndCapture(st, &graph);
+    if (crc) {
+        if (graph) cudaGraphDestroy(graph);
+        return crc;
+    }
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamEndCapture");
+    const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) return cuda_fail(ie, "cudaGraphInstantiate");
+    bool running = true;
+    cudaError_t le = cudaSuccess;
+    for (uint64_t r = 0; running && r < max_rounds && le == cudaSuccess; r += ROUNDS) {
+        le = cudaGraphLaunch(exec, st);
+        if (le == cudaSuccess) le = cudaMemcpyAsync(states.data(), w + o.seg, states.size(), cudaMemcpyDeviceToHost, st);
+        if (le == cudaSuccess) le = cudaStreamSynchronize(st);
+        g_launches.fetch_add(ROUNDS * (3 * L + 4), std::memory_order_relaxed);
+        running = false;
+        for (uint32_t s = 0; s < S; s++)
+            if (reinterpret_cast<const uint32_t*>(states.data() + s * tdt_seg_bytes())[TDT_SEG_ACTIVE]) running = true;
+    }
+    cudaGraphExecDestroy(exec);
+    if (le != cudaSuccess) return cuda_fail(le, "tdt rounds");
+#endif
     PKB_CUDA(cudaMemcpyAsync(states.data(), w + o.seg, states.size(), cudaMemcpyDeviceToHost, st), "download");
     PKB_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize");
     for (uint32_t s = 0; s < S; s++) {
