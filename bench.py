@@ -907,25 +907,30 @@ def decoder_batched(model, T: int, segs: int = SEGMENTS, layers: int = 2, P_: in
     jenc_b = torch.randn(J, device="cuda", generator=g)
     f = torch.empty(T * J, device="cuda")
 
-    def enc():
+    def quant():
         P.quantize_dev(qe, de, xe, D_, T, D_, D_)
+
+    def enc():
         P.gemm_q8_dev(f, J, jenc[0], jenc[1], jenc_b, J, qe, de, D_, D_, T, False)
 
-    for _ in range(3):
-        enc()
-    s.synchronize()
-    e0.record(s)
-    for _ in range(20):
-        enc()
-    e1.record(s)
-    e1.synchronize()
-    ems = e0.elapsed_time(e1) / 20
+    def timed(fn) -> float:
+        for _ in range(3):
+            fn()
+        s.synchronize()
+        e0.record(s)
+        for _ in range(20):
+            fn()
+        e1.record(s)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / 20
+    qms = timed(quant)
+    ems = timed(enc)
     eops = 2.0 * T * J * D_
     return {"segments": S, "step_us": ms * 1e3, "step_tops": ops / (ms * 1e-3) / 1e12,
             "steps_per_s": 1e3 / ms, "launches_per_step": 4 * (2 * layers + 2),
             "shapes": f"per layer wx, wh {G}x{P_}; jpred {J}x{P_}; jout {vocab_out}x{J}; M = {S}, qb = n",
-            "jenc_us": ems * 1e3, "jenc_tops": eops / (ems * 1e-3) / 1e12,
-            "jenc_shape": f"M {T} x N {J} x K {D_}, qb {D_}"}
+            "jenc_us": ems * 1e3, "jenc_tops": eops / (ems * 1e-3) / 1e12, "jenc_quantize_us": qms * 1e3,
+            "jenc_shape": f"M {T} x N {J} x K {D_}, qb {D_}; the product alone, its input's quantization beside it"}
 
 
 def panels_timing(model, T: int, dk: int = 128) -> dict:
