@@ -222,3 +222,33 @@ def test_host_entries_of_the_table(pkb, cuda_device, golden):
         x = s.copy()
         assert lib.pkb_softmax_host(x.ctypes.data, x.size, ctypes.c_float(0.0883883476), O.RN) == 0
         assert x.tobytes() == golden[f"sm/{i}/y"].tobytes(), s.size
+
+
+def test_attention_rows_more_segments_than_a_launch_takes(pkb, cuda_device):
+    """130 short segments (a launch takes 128): the call splits them over two
+    launches; every segment's o is the oracle's."""
+    D, H = 256, 4
+    dk = D // H
+    g = np.random.default_rng(77)
+    Ts = [1 + (i * 7) % 11 for i in range(130)]
+    M, Rsum = sum(Ts), sum(2 * t - 1 for t in Ts)
+    q, k, v = (g.standard_normal(M * D).astype(np.float32) for _ in range(3))
+    p = g.standard_normal(Rsum * D).astype(np.float32)
+    bu, bv = (g.standard_normal(D) * 0.1).astype(np.float32), (g.standard_normal(D) * 0.1).astype(np.float32)
+    segs, f, r = [], 0, 0
+    for T in Ts:
+        segs.append((T, f, r))
+        f += T
+        r += 2 * T - 1
+    launches = pkb.launch_count()
+    o = dev(np.full(M * D, 5.0, np.float32))
+    pkb.attention_rows_dev(o, D, dev(q), D, dev(k), D, dev(v), D, dev(p), D, dev(bu), dev(bv), D, H, segs)
+    got = host(o).reshape(M, D)
+    assert pkb.launch_count() - launches == 2
+    for T, f, r in segs:
+        R = 2 * T - 1
+        Tp, Pp = (T + 15) // 16 * 16, (R + 15) // 16 * 16 + 16
+        want = O.attention(q.reshape(M, D)[f:f + T], D, rows_to_panels(k.reshape(M, D)[f:f + T], T, D, dk, Tp),
+                           rows_to_panels(p.reshape(Rsum, D)[r:r + R], R, D, dk, Pp),
+                           rows_to_vpanels(v.reshape(M, D)[f:f + T], T, D), bu, bv, T, D, H)
+        assert got[f:f + T].tobytes() == want.tobytes(), T
