@@ -977,6 +977,49 @@ def panels_timing(model, T: int, dk: int = 128) -> dict:
             "v_panels_tops": ops / (t_v * 1e-3) / 1e12}
 
 
+def gpu_local_cpus(device: int):
+    """The host cores NVML reports as local to this GPU (its NUMA node), or
+    None where that cannot be read. Reading only: nothing of the GPU is set."""
+    try:
+        import torch
+        import pynvml
+        pr = torch.cuda.get_device_properties(device)
+        bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        pynvml.nvmlInit()
+        try:
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            words = (os.cpu_count() + 63) // 64
+            mask = pynvml.nvmlDeviceGetCpuAffinity(h, words)
+        finally:
+            pynvml.nvmlShutdown()
+        cpus = {64 * i + b for i, w in enumerate(mask) for b in range(64) if (int(w) >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        return cpus or None
+    except Exception:  # no NVML, no such attribute: leave the threads where they are
+        return None
+
+
+class near_gpu:
+    """Within the block the process's threads run on the GPU's own NUMA
+    node, and the page-locked buffers made there sit in its memory: the
+    host side of an engine deployed beside its GPU. The affinity is put back
+    after."""
+
+    def __init__(self, device: int):
+        self.cpus = gpu_local_cpus(device)
+        self.was = None
+
+    def __enter__(self):
+        if self.cpus and os.environ.get("PKB_BENCH_NO_BIND") != "1":
+            self.was = os.sched_getaffinity(0)
+            os.sched_setaffinity(0, self.cpus)
+        return self
+
+    def __exit__(self, *exc):
+        if self.was is not None:
+            os.sched_setaffinity(0, self.was)
+
+
 def e2e_host(prods, steps: int, seed: int, lanes: int) -> dict:
     """The same step through the reference-facing table (pk_kernels_cuda_b200:
     quantize and gemm_q8 on HOST buffers, copies inside each call), called
@@ -1284,7 +1327,8 @@ def run_ours(args) -> None:
         if dist:
             dist.barrier(device_ids=[local])
         e2e_steps = args.e2e_steps or (args.steps if WORKLOAD == "batched" else min(args.steps, 3))
-        e = e2e_host(prods, e2e_steps, SEED + 7 + rank, args.e2e_lanes)
+        with near_gpu(local) as near:
+            e = e2e_host(prods, e2e_steps, SEED + 7 + rank, args.e2e_lanes)
         sec, e_ops, e_audio = job_totals(dist, dev, e["seconds_per_step"], step_ops(prods), audio_seconds(segs))
         h2d, d2h = job_totals(dist, dev, 0.0, e["h2d_bytes_per_step"], e["d2h_bytes_per_step"])[1:]
         e2e = {"value": e_ops / sec / 1e12, "unit": "TOPS",
@@ -1296,12 +1340,14 @@ def run_ours(args) -> None:
                        "bytes as the library counts its copies (pkb_host_bytes): a product whose q and d "
                        "are a quantize result still held on the device does not upload them",
                "steps": e2e_steps,
-               "lanes": args.e2e_lanes}
+               "lanes": args.e2e_lanes,
+               "host_cpus": len(near.cpus) if near.was is not None else None}
     if e2e is not None and not args.no_sliced and world == 1:
         # the engine's call pattern (slices from a pool of host threads); one
         # GPU only, as the pool's threads of several ranks would share the
         # host's cores
-        sl = e2e_host_sliced(prods, max(1, min(args.steps, 3)), SEED + 11 + rank, args.e2e_threads)
+        with near_gpu(local):
+            sl = e2e_host_sliced(prods, max(1, min(args.steps, 3)), SEED + 11 + rank, args.e2e_threads)
         sec, e_ops, _ = job_totals(dist, dev, sl["seconds_per_step"], step_ops(prods), audio_seconds(segs))
         e2e["engine_sliced"] = {"value": e_ops / sec / 1e12, "unit": "TOPS", "calls_per_step": sl["calls_per_step"],
                                 "h2d_bytes_per_step": int(sl["h2d_bytes_per_step"]),
