@@ -178,6 +178,14 @@ int pkb_gemm_q8_panels_dev(void *stream, float *panels, int kind, size_t ps, uin
 int pkb_layernorm_quantize_dev(void *stream, int8_t *q, float *d, const float *x, size_t xs, uint32_t T,
                                uint32_t n, uint32_t qb, const float *w, const float *b, float eps, int rmode);
 
+/* k_layernorm alone (backend/ref/kernels.c:115-131), the floats out: the
+ * encoder's out norm (core/encoder.c:367, `norm`), which the next layer's
+ * residual reads. out rows at stride os; out may be x itself (in place,
+ * os == xs), as the reference runs it. n a multiple of 32, at most
+ * PKB_LN_MAX_N. */
+int pkb_layernorm_dev(void *stream, float *out, size_t os, const float *x, size_t xs, uint32_t T, uint32_t n,
+                      const float *w, const float *b, float eps, int rmode);
+
 /* siluq_tile (core/encoder.c:150-158): T rows of n floats (row t at
  * u + t*us) through k_silu (backend/ref/kernels.c:149-151: x * pk_sigmoidf(x),
  * core/vmath.h:134-151) and quantized into q [T][n], d [T][n/qb]. */

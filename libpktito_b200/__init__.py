@@ -123,6 +123,9 @@ _SIGS = {
     "pkb_tdt_search_dev": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                           ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p,
                                           ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]),
+    "pkb_layernorm_dev": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+                                         ctypes.c_size_t, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p,
+                                         ctypes.c_void_p, ctypes.c_float, ctypes.c_int]),
     "pkb_launch_count": (ctypes.c_uint64, []),
     "pkb_host_bytes": (None, [ctypes.c_void_p, ctypes.c_void_p]),
     "pkb_quantize_host_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,
@@ -272,6 +275,12 @@ def layernorm_quantize_dev(q, d, x, xs: int, T: int, n: int, qb: int, w, b, eps:
     and quantized in one kernel."""
     _check(lib().pkb_layernorm_quantize_dev(_stream(stream), _ptr(q), _ptr(d), _ptr(x), xs, T, n, qb, _ptr(w), _ptr(b),
                                             eps, rmode))
+
+
+def layernorm_dev(out, os_: int, x, xs: int, T: int, n: int, w, b, eps: float, rmode: int = RN,
+                  stream=None) -> None:
+    """k_layernorm (backend/ref/kernels.c:115-131) on device rows; out may be x."""
+    _check(lib().pkb_layernorm_dev(_stream(stream), _ptr(out), os_, _ptr(x), xs, T, n, _ptr(w), _ptr(b), eps, rmode))
 
 
 def silu_quantize_dev(q, d, u, us: int, T: int, n: int, qb: int, rmode: int = RN, stream=None) -> None:

@@ -273,6 +273,32 @@ int layernorm_quantize_dev(cudaStream_t stream, int8_t* q, float* d, const float
     return PKB_OK;
 }
 
+int layernorm_dev(cudaStream_t stream, float* out, size_t os, const float* x, size_t xs, uint32_t T, uint32_t n,
+                  const float* w, const float* b, float eps, int rmode) {
+    int rc;
+    if ((rc = check_rmode(rmode))) return rc;
+    if (n == 0 || n % 32 || n > PKB_LN_MAX_N)
+        return fail(PKB_EINVAL, "layernorm: n = %u, a multiple of 32 up to %u", n, PKB_LN_MAX_N);
+    if (!T) return PKB_OK;
+    if (!out || !x || !w || !b) return fail(PKB_EINVAL, "layernorm: null pointer");
+    if (T > 1 && (xs < n || os < n)) return fail(PKB_EINVAL, "layernorm: a row stride below n = %u", n);
+    if (T == 1) xs = os = n;
+    if (!aligned(out, 4) || !aligned(x, 4) || !aligned(w, 4) || !aligned(b, 4))
+        return fail(PKB_EINVAL, "layernorm: misaligned buffer");
+    if (out != x) {
+        const uintptr_t x0 = reinterpret_cast<uintptr_t>(x), x1 = x0 + ((T - 1) * xs + n) * sizeof(float);
+        const uintptr_t o0 = reinterpret_cast<uintptr_t>(out), o1 = o0 + ((T - 1) * os + n) * sizeof(float);
+        if (o0 < x1 && x0 < o1) return fail(PKB_EINVAL, "layernorm: out overlaps x (only out == x is allowed)");
+    } else if (os != xs) {
+        return fail(PKB_EINVAL, "layernorm: in place with os %zu != xs %zu", os, xs);
+    }
+    Device* dev;
+    if ((rc = current_device(&dev))) return rc;
+    PKB_CUDA(launch_layernorm(out, os, x, xs, T, n, w, b, eps, rmode, dev->sms, stream), "layernorm launch");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return PKB_OK;
+}
+
 int silu_quantize_dev(cudaStream_t stream, int8_t* q, float* d, const float* u, size_t us, uint32_t T, uint32_t n,
                       uint32_t qb, int rmode) {
     int rc;
@@ -822,6 +848,11 @@ size_t pkb_wpack_bytes(uint32_t rows, uint32_t n) { return static_cast<size_t>(r
 int pkb_layernorm_quantize_dev(void* stream, int8_t* q, float* d, const float* x, size_t xs, uint32_t T, uint32_t n,
                                uint32_t qb, const float* w, const float* b, float eps, int rmode) {
     return pkb::layernorm_quantize_dev(static_cast<cudaStream_t>(stream), q, d, x, xs, T, n, qb, w, b, eps, rmode);
+}
+
+int pkb_layernorm_dev(void* stream, float* out, size_t os, const float* x, size_t xs, uint32_t T, uint32_t n,
+                      const float* w, const float* b, float eps, int rmode) {
+    return pkb::layernorm_dev(static_cast<cudaStream_t>(stream), out, os, x, xs, T, n, w, b, eps, rmode);
 }
 
 int pkb_silu_quantize_dev(void* stream, int8_t* q, float* d, const float* u, size_t us, uint32_t T, uint32_t n,

@@ -55,12 +55,13 @@ constexpr uint32_t LN_NC = 64;
 // Block k of ROWS staged rows (the second pitch floats after the first, for
 // frames t0 and t0 + 1; the second only if live1): (x - mean) * r * w + b,
 // left to right, each chunk's w and b read once for the rows; then each
-// row's block quantized, its bytes stored 16 at a time where q16.
-template <int RM, int QB, int ROWS>
-__device__ __forceinline__ void ln_block(int8_t* __restrict__ q, float* __restrict__ d, const float* rows,
-                                         uint32_t pitch, const float* ws, const float* bs, uint32_t k, uint32_t t0,
-                                         bool live1, uint32_t n, uint32_t nb, float mean0, float rs0, float mean1,
-                                         float rs1, bool q16) {
+// row's block quantized, its bytes stored 16 at a time where q16 (FOUT: the
+// floats stored instead, at out + t os, 16 bytes at a time where ov).
+template <int RM, int QB, int ROWS, bool FOUT>
+__device__ __forceinline__ void ln_block(int8_t* __restrict__ q, float* __restrict__ d, float* out, size_t os,
+                                         const float* rows, uint32_t pitch, const float* ws, const float* bs,
+                                         uint32_t k, uint32_t t0, bool live1, uint32_t n, uint32_t nb, float mean0,
+                                         float rs0, float mean1, float rs1, bool q16) {
     float4 v[ROWS][QB / 4];
     uint32_t m[ROWS] = {};
     const uint64_t nm[2] = {pack2(-mean0, -mean0), pack2(-mean1, -mean1)};
@@ -83,6 +84,26 @@ __device__ __forceinline__ void ln_block(int8_t* __restrict__ q, float* __restri
             m[r] = max(m[r], max(max(abs_bits(v[r][c].x), abs_bits(v[r][c].y)),
                                  max(abs_bits(v[r][c].z), abs_bits(v[r][c].w))));
         }
+    }
+    if constexpr (FOUT) {
+#pragma unroll
+        for (int r = 0; r < ROWS; r++) {
+            if (r == 1 && !live1) break;
+            float* o = out + static_cast<size_t>(t0 + r) * os + k * QB;
+            if (q16) {  // out 16-byte aligned, os a multiple of 4
+#pragma unroll
+                for (int c = 0; c < QB / 4; c++) *reinterpret_cast<float4*>(o + 4 * c) = v[r][c];
+            } else {
+#pragma unroll
+                for (int c = 0; c < QB / 4; c++) {
+                    o[4 * c] = v[r][c].x;
+                    o[4 * c + 1] = v[r][c].y;
+                    o[4 * c + 2] = v[r][c].z;
+                    o[4 * c + 3] = v[r][c].w;
+                }
+            }
+        }
+        return;
     }
 #pragma unroll
     for (int r = 0; r < ROWS; r++) {
@@ -124,9 +145,15 @@ __device__ __forceinline__ void ln_block(int8_t* __restrict__ q, float* __restri
 // so that a block's maximum and its two divisions stay in one thread, the
 // arithmetic on pairs of inputs (f32x2, each half rounded as the scalar
 // operation), the bytes stored 16 at a time where q allows.
-template <int RM, int QB, uint32_t NC>
-__global__ void __launch_bounds__(256) layernorm_quantize(int8_t* __restrict__ q, float* __restrict__ d,
-                                                          const float* __restrict__ x, size_t xs, uint32_t T,
+//
+// FOUT: k_layernorm alone, the normalized floats stored at out + t os
+// instead of quantized. out may be x itself (the reference's out norm runs
+// in place): a row is read only by the asynchronous copies into shared
+// memory, which complete before the warp stores any of its floats, and no
+// other warp touches it.
+template <int RM, int QB, uint32_t NC, bool FOUT>
+__global__ void __launch_bounds__(256) layernorm_quantize(int8_t* __restrict__ q, float* __restrict__ d, float* out,
+                                                          size_t os, const float* x, size_t xs, uint32_t T,
                                                           uint32_t n, const float* __restrict__ w,
                                                           const float* __restrict__ b, float eps, bool xvec,
                                                           bool q16) {
@@ -212,13 +239,14 @@ __global__ void __launch_bounds__(256) layernorm_quantize(int8_t* __restrict__ q
         const bool live1 = 2 * pr + 1 < T;
         if (QB == 32 && nb >= 32) {
             for (uint32_t k = lane; k < nb; k += 32)
-                ln_block<RM, QB, 2>(q, d, rows, pitch, ws, bs, k, 2 * pr, live1, n, nb, mean0, rs0, mean1, rs1, q16);
+                ln_block<RM, QB, 2, FOUT>(q, d, out, os, rows, pitch, ws, bs, k, 2 * pr, live1, n, nb, mean0, rs0,
+                                          mean1, rs1, q16);
         } else {
             for (uint32_t item = lane; item < 2 * nb; item += 32) {
                 const uint32_t r = item >= nb, k = item - r * nb;
                 if (r && !live1) continue;
-                ln_block<RM, QB, 1>(q, d, rows + r * pitch, pitch, ws, bs, k, 2 * pr + r, false, n, nb,
-                                    r ? mean1 : mean0, r ? rs1 : rs0, 0.0f, 0.0f, q16);
+                ln_block<RM, QB, 1, FOUT>(q, d, out, os, rows + r * pitch, pitch, ws, bs, k, 2 * pr + r, false, n,
+                                          nb, r ? mean1 : mean0, r ? rs1 : rs0, 0.0f, 0.0f, q16);
             }
         }
         __syncwarp();  // the stage is refilled two pairs on
@@ -392,8 +420,8 @@ constexpr size_t LN_SMEM_PAIR_CTA = 110 * 1024;
 constexpr size_t LN_SMEM_MAX = 227 * 1024;
 
 template <int RM, int QB>
-cudaError_t ln_launch(int8_t* q, float* d, const float* x, size_t xs, uint32_t T, uint32_t n, const float* w,
-                      const float* b, float eps, int num_sms, cudaStream_t stream) {
+cudaError_t ln_launch(int8_t* q, float* d, float* out, size_t os, const float* x, size_t xs, uint32_t T, uint32_t n,
+                      const float* w, const float* b, float eps, int num_sms, cudaStream_t stream) {
     const size_t wb = 2 * static_cast<size_t>(ln_padded(n)) * sizeof(float);
     const size_t per_warp = 4 * static_cast<size_t>(ln_pitch(n)) * sizeof(float);
     size_t warps = LN_SMEM_PAIR_CTA > wb ? (LN_SMEM_PAIR_CTA - wb) / per_warp : 0;
@@ -401,7 +429,8 @@ cudaError_t ln_launch(int8_t* q, float* d, const float* x, size_t xs, uint32_t T
     if (warps < 1) warps = 1;
     const size_t smem = wb + warps * per_warp;
     if (smem > LN_SMEM_MAX) return cudaErrorInvalidValue;  // n beyond the checked maximum
-    auto kern = n == 16 * LN_NC ? layernorm_quantize<RM, QB, LN_NC> : layernorm_quantize<RM, QB, 0>;
+    auto kern = out ? (n == 16 * LN_NC ? layernorm_quantize<RM, QB, LN_NC, true> : layernorm_quantize<RM, QB, 0, true>)
+                    : (n == 16 * LN_NC ? layernorm_quantize<RM, QB, LN_NC, false> : layernorm_quantize<RM, QB, 0, false>);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     const size_t pairs = (static_cast<size_t>(T) + 1) / 2;
@@ -410,9 +439,10 @@ cudaError_t ln_launch(int8_t* q, float* d, const float* x, size_t xs, uint32_t T
     const size_t cap = static_cast<size_t>(num_sms) * (per_sm ? per_sm : 1);
     if (grid > cap) grid = cap;
     const bool xvec = reinterpret_cast<uintptr_t>(x) % 16 == 0 && xs % 4 == 0;
-    const bool q16 = reinterpret_cast<uintptr_t>(q) % 16 == 0;
+    const bool q16 = out ? reinterpret_cast<uintptr_t>(out) % 16 == 0 && os % 4 == 0
+                         : reinterpret_cast<uintptr_t>(q) % 16 == 0;
     return launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(static_cast<unsigned>(32 * warps)), smem, stream,
-                      q, d, x, xs, T, n, w, b, eps, xvec, q16);
+                      q, d, out, os, x, xs, T, n, w, b, eps, xvec, q16);
 }
 
 template <int RM, int QB>
@@ -438,8 +468,8 @@ cudaError_t dw_launch(int8_t* q, float* d, float* out, size_t os, const float* x
 template <int RM>
 cudaError_t ln_rm(int8_t* q, float* d, const float* x, size_t xs, uint32_t T, uint32_t n, uint32_t qb,
                   const float* w, const float* b, float eps, int num_sms, cudaStream_t stream) {
-    if (qb == 32) return ln_launch<RM, 32>(q, d, x, xs, T, n, w, b, eps, num_sms, stream);
-    if (qb == 64) return ln_launch<RM, 64>(q, d, x, xs, T, n, w, b, eps, num_sms, stream);
+    if (qb == 32) return ln_launch<RM, 32>(q, d, nullptr, 0, x, xs, T, n, w, b, eps, num_sms, stream);
+    if (qb == 64) return ln_launch<RM, 64>(q, d, nullptr, 0, x, xs, T, n, w, b, eps, num_sms, stream);
     return cudaErrorInvalidValue;
 }
 
@@ -461,6 +491,16 @@ cudaError_t launch_layernorm_quantize(int8_t* q, float* d, const float* x, size_
     case 2: return ln_rm<2>(q, d, x, xs, T, n, qb, w, b, eps, num_sms, stream);
     case 3: return ln_rm<3>(q, d, x, xs, T, n, qb, w, b, eps, num_sms, stream);
     default: return ln_rm<0>(q, d, x, xs, T, n, qb, w, b, eps, num_sms, stream);
+    }
+}
+
+cudaError_t launch_layernorm(float* out, size_t os, const float* x, size_t xs, uint32_t T, uint32_t n, const float* w,
+                             const float* b, float eps, int rmode, int num_sms, cudaStream_t stream) {
+    switch (rmode) {
+    case 1: return ln_launch<1, 32>(nullptr, nullptr, out, os, x, xs, T, n, w, b, eps, num_sms, stream);
+    case 2: return ln_launch<2, 32>(nullptr, nullptr, out, os, x, xs, T, n, w, b, eps, num_sms, stream);
+    case 3: return ln_launch<3, 32>(nullptr, nullptr, out, os, x, xs, T, n, w, b, eps, num_sms, stream);
+    default: return ln_launch<0, 32>(nullptr, nullptr, out, os, x, xs, T, n, w, b, eps, num_sms, stream);
     }
 }
 

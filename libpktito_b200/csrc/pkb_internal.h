@@ -96,6 +96,10 @@ cudaError_t launch_quantize(int8_t* q, float* d, const float* x, size_t xs, uint
 // device's set-up.
 void prepare_quantize();
 
+// k_layernorm alone, the floats out (out may be x with os == xs)
+cudaError_t launch_layernorm(float* out, size_t os, const float* x, size_t xs, uint32_t T, uint32_t n, const float* w,
+                             const float* b, float eps, int rmode, int num_sms, cudaStream_t stream);
+
 cudaError_t launch_silu_quantize(int8_t* q, float* d, const float* u, size_t us, uint32_t T, uint32_t n,
                                  uint32_t qb, int rmode, int num_sms, cudaStream_t stream);
 

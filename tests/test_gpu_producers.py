@@ -323,3 +323,25 @@ def test_sigmoid_reciprocal_exhaustive(pkb, cuda_device, rmode):
     mismatch over 1.07e9 floats."""
     mismatches, first = pkb.rcp_selftest(rmode)
     assert mismatches == 0, f"{mismatches} floats differ, the first 0x{first:08x}"
+
+
+@pytest.mark.parametrize("rmode", MODES)
+def test_layernorm_floats(pkb, cuda_device, rmode):
+    """k_layernorm alone (the encoder's out norm): the floats against the
+    oracle in every mode, at the model's width and an odd one, rows at a
+    stride, and in place as the reference runs it."""
+    import torch
+    g = np.random.default_rng(60 + rmode)
+    for T, n, xs in [(37, 1024, 1024), (9, 160, 200), (1, 4096, 4096)]:
+        x = (g.standard_normal(T * xs) * 3 + 500.0 * (n == 160)).astype(np.float32)
+        w, b = g.standard_normal(n).astype(np.float32), g.standard_normal(n).astype(np.float32)
+        want = O.layernorm(x, xs, T, n, w, b, 1e-5, rmode)
+        out = torch.full((T * (n + 8),), 7.0, device="cuda")
+        pkb.layernorm_dev(out, n + 8, dev(x), xs, T, n, dev(w), dev(b), 1e-5, rmode)
+        got = host(out).reshape(T, n + 8)
+        assert got[:, :n].tobytes() == want.tobytes(), (T, n)
+        assert (got[:, n:] == 7.0).all()
+        xi = dev(x)
+        pkb.layernorm_dev(xi, xs, xi, xs, T, n, dev(w), dev(b), 1e-5, rmode)
+        inplace = host(xi).reshape(T, xs)
+        assert inplace[:, :n].tobytes() == want.tobytes(), (T, n, "in place")
