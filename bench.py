@@ -722,6 +722,135 @@ def attention_timing(model, segs, sm_mhz) -> dict:
             "parity": attention_check(torch, o, q, k, v, p, bu, bv, sl, picks)}
 
 
+def encoder_layer_timing(model, segs) -> dict:
+    """One encoder layer on the device (libpktito_b200.encoder.layer_dev:
+    layer(), core/encoder.c:338-368) over the rank's segments: its 11
+    products, four LayerNorm -> quantize, two SiLU -> quantize, the
+    attention over every segment and head, the quantization of its output,
+    GLU + depthwise convolution -> quantize a segment at a time and the out
+    norm, seeded weights, captured as one CUDA graph and timed with CUDA
+    events; then the shortest segment's output against the oracle's
+    composition of the same steps."""
+    torch, P = model.torch, model.P
+    from libpktito_b200.encoder import PRODUCTS, Batch, Buffers, layer_dev, product_shapes
+    from oracle import oracle as O
+    K, EPS = 9, 1e-5
+    g = np.random.default_rng(SEED + 91)
+    L, Ld = {}, {}
+    for name in PRODUCTS:
+        rows, n = product_shapes(D, F)[name]
+        w_pk = O.pack_q8(g.integers(-127, 128, (rows, n), dtype=np.int8))
+        ws = (1e-4 + 9e-4 * g.random(rows)).astype(np.float32)
+        src = torch.from_numpy(w_pk).cuda()
+        wd = torch.empty(rows * n, dtype=torch.int8, device="cuda")
+        P.repack_q8_dev(wd, src, rows, n)
+        L[name], Ld[name] = (w_pk, ws), (wd, torch.from_numpy(ws).cuda())
+    for name in ("ff1", "att", "conv", "ff2", "out"):
+        L[name + "_nw"] = (1 + 0.1 * g.standard_normal(D)).astype(np.float32)
+        L[name + "_nb"] = (0.1 * g.standard_normal(D)).astype(np.float32)
+    L["bias_u"], L["bias_v"] = ((0.1 * g.standard_normal(D)).astype(np.float32) for _ in range(2))
+    L["dw"], L["dw_b"] = (0.3 * g.standard_normal(D * K)).astype(np.float32), (0.1 * g.standard_normal(D)).astype(
+        np.float32)
+    for k, v in L.items():
+        if not isinstance(v, tuple):
+            Ld[k] = torch.from_numpy(v).cuda()
+    sl, f, r = [], 0, 0
+    for sg in segs:
+        sl.append((sg[3], f, r))
+        f += sg[3]
+        r += 2 * sg[3] - 1
+    batch = Batch(sl)
+    x0 = torch.randn(batch.frames * D, device="cuda", generator=torch.Generator(device="cuda").manual_seed(SEED + 92))
+    ape = torch.randn(batch.positions * D, device="cuda", generator=torch.Generator(device="cuda").manual_seed(SEED + 93))
+    aq = torch.empty(batch.positions * D, dtype=torch.int8, device="cuda")
+    ad = torch.empty(batch.positions * D // QB, device="cuda")
+    P.quantize_dev(aq, ad, ape, D, batch.positions, D, QB)
+    buf = Buffers(torch, batch.frames, batch.positions, D, F, QB)
+    x = x0.clone()
+    s = torch.cuda.Stream()
+    l0 = P.launch_count()
+    with torch.cuda.stream(s):
+        layer_dev(x, Ld, batch, aq, ad, D, F, HEADS, K, QB, EPS, buf)
+    s.synchronize()
+    launches = P.launch_count() - l0
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s, capture_error_mode="relaxed"):
+        layer_dev(x, Ld, batch, aq, ad, D, F, HEADS, K, QB, EPS, buf)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10
+    with torch.cuda.stream(s):
+        x.copy_(x0)
+        graph.replay()
+        e0.record(s)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(s)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    # parity: one layer from x0, the shortest segment against the oracle
+    with torch.cuda.stream(s):
+        x.copy_(x0)
+        graph.replay()
+    s.synchronize()
+    del graph
+    i = min(range(len(sl)), key=lambda j: sl[j][0])
+    T, f, r = sl[i]
+    xh, ah = x0.view(-1, D)[f:f + T].cpu().numpy().reshape(-1), ape.view(-1, D)[r:r + 2 * T - 1].cpu().numpy()
+    want = encoder_layer_oracle(xh, T, L, ah.reshape(-1), K, EPS)
+    got = x.view(-1, D)[f:f + T].cpu().numpy().reshape(-1)
+    ops = 2.0 * (batch.frames * D * (4 * F + 7 * D) + batch.positions * D * D)
+    return {"ms": ms, "segments": len(sl), "frames": batch.frames, "launches": launches,
+            "int8_tops": ops / (ms * 1e-3) / 1e12, "encoder_ms_24_layers": 24 * ms,
+            "audio_s_per_s": audio_seconds(segs) / (24 * ms * 1e-3),
+            "note": "the layer's int8 products, its float steps (norms, SiLU, attention, GLU + depthwise "
+                    "convolution) and quantizations, all on the device; the subsampling and the position "
+                    "embeddings' quantization once a forward pass are not in it",
+            "parity": {"segment_frames": int(T), "equal": bool(got.tobytes() == want.tobytes()),
+                       "checker": "the oracle's composition of the layer's steps, each pinned to the reference's"}}
+
+
+def encoder_layer_oracle(x, T: int, L: dict, ape, K: int, eps: float):
+    """layer() (core/encoder.c:338-368) on one segment with the oracle."""
+    from oracle import oracle as O
+    x = x.copy()
+    qb = QB
+
+    def prod(out, name, q, d, n, add, Tn):
+        w, ws = L[name]
+        O.gemm_q8(out, ws.size, w, ws, None, ws.size, q, d, n, qb, Tn, add)
+
+    def ff(pre):
+        q, d = O.layernorm_quantize(x, D, T, D, qb, L[pre + "_nw"], L[pre + "_nb"], eps)
+        u = np.zeros(T * F, np.float32)
+        prod(u, pre + "_up", q, d, D, False, T)
+        q2, d2 = O.silu_quantize(u, F, T, F, qb)
+        prod(x, pre + "_down", q2, d2, F, True, T)
+
+    ff("ff1")
+    q, d = O.layernorm_quantize(x, D, T, D, qb, L["att_nw"], L["att_nb"], eps)
+    Q, Kr, V = (np.zeros(T * D, np.float32) for _ in range(3))
+    for name, out in (("q", Q), ("k", Kr), ("v", V)):
+        prod(out, name, q, d, D, False, T)
+    R = 2 * T - 1
+    aq, ad = O.quantize(ape, D, qb, R, D)
+    Pr = np.zeros(R * D, np.float32)
+    prod(Pr, "pos", aq, ad, D, False, R)
+    dk = D // HEADS
+    Tp, Pp = (T + 15) // 16 * 16, (R + 15) // 16 * 16 + 16
+    vp = np.ascontiguousarray(V.reshape(T, D // 16, 16).transpose(1, 0, 2)).reshape(-1)
+    o = O.attention(Q, D, O.panels_kp(Kr, T, Tp, D, dk), O.panels_kp(Pr, R, Pp, D, dk), vp, L["bias_u"], L["bias_v"],
+                    T, D, HEADS)
+    qo, do = O.quantize(o, D, qb, T, D)
+    prod(x, "o", qo, do, D, True, T)
+    q, d = O.layernorm_quantize(x, D, T, D, qb, L["conv_nw"], L["conv_nb"], eps)
+    U = np.zeros(T * 2 * D, np.float32)
+    prod(U, "pw1", q, d, D, False, T)
+    qc, dc, _ = O.dwconv_quantize(U, 2 * D, T, D, L["dw"], L["dw_b"], K, True, qb)
+    prod(x, "pw2", qc, dc, D, True, T)
+    ff("ff2")
+    return O.layernorm(x, D, T, D, L["out_nw"], L["out_nb"], eps).reshape(-1)
+
+
 def tdt_model_synthetic(P_: int = 640, J: int = 640, V: int = 8192, layers: int = 2, seed: int = SEED + 321):
     """The TDT decoder's weights at the model's shapes (pred_hidden 640,
     joint 640, vocab 8192 + blank, durations 0-4: jout 8208 x 640), seeded:
@@ -1320,6 +1449,10 @@ def run_ours(args) -> None:
         roof["panels"] = panels_timing(model, sum(sg[3] for sg in segs))
         roof["attention"] = attention_timing(model, segs, clk.get("sm_mhz"))
         roof["decoder_search"] = decoder_search(model, segs)
+        try:
+            roof["encoder_layer"] = encoder_layer_timing(model, segs)
+        except Exception as e:  # a measurement beside the headline: its failure is reported, not fatal
+            roof["encoder_layer"] = {"error": f"{type(e).__name__}: {e}"[:300]}
     e2e = None
     if not args.no_e2e:
         # every rank at once through the host table, each on its own
