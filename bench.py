@@ -22,11 +22,15 @@ product's input is a resident float32 activation ~N(0,1).
 A step is one pass over the batch: 267 products and 196 quantizations. value
 is whole-job int8 TOPS (2*M*N*K summed over the products, over every rank);
 audio-seconds per second is reported beside it. Multi-GPU: one process per
-GPU (torchrun); the batch of 64 segments is dealt across the GPUs longest
-first (strong scaling, the configuration's "data-partitioned across 1/2/4/8
-GPUs"; `--scaling weak` gives every GPU 64 segments of its own instead), no
-collective on the data path; the time is the max over ranks, the work the
-sum.
+GPU (torchrun), segments partitioned across the GPUs with no collective on
+the data path; the time is the max over ranks, the work the sum. Weak
+scaling (the default): every GPU takes a batch of 64 segments of its own, so
+the work per GPU is fixed as the GPUs are added (at 1 GPU the batch is the
+same one strong scaling splits). `--scaling strong`: the one batch of 64
+segments is dealt across the GPUs longest first, so each GPU's share shrinks
+as 1/N (at 8 GPUs about 1,440 frames a GPU, where an N = 1024 product has 96
+tiles of 128 x 128 for 148 SMs). The long-form workload always
+splits its one hour across the GPUs.
 
 `--impl reference` times the reference's own CPU backend (the one its picker
 chooses on this host, built from its sources into oracle/_ref) on a bounded
@@ -109,7 +113,7 @@ def partition(segs, world: int) -> list[list[int]]:
     return [sorted(s) for s in share]
 
 
-def segments(rank: int, world: int = 1, scaling: str = "strong") -> list[tuple[float, int, int, int]]:
+def segments(rank: int, world: int = 1, scaling: str = "weak") -> list[tuple[float, int, int, int]]:
     """The rank's segments. Strong scaling (configs[3]: one batch of 64
     segments partitioned across the GPUs): the rank's share of the one draw.
     Weak scaling: a draw of 64 of its own."""
@@ -1514,7 +1518,8 @@ def run_ours(args) -> None:
                     f"one input; the position input is quantized once), qb {QB}")
     line = {
         "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": args.scaling,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "strong" if WORKLOAD == "longform" else args.scaling,
         "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded segments, random int8 weights, N(0,1) activations)",
         "config": {"workload": workload,
                    "segments_rank0": len(segs), "encoder_frames_rank0": t3, "layers": LAYERS, "d_model": D,
@@ -1586,10 +1591,11 @@ def reference_step(prods, seed: int, threads: int):
 
 
 def run_reference(args) -> None:
-    """The reference arm: the same workload (this arm's rank 0 share at
-    --gpus 1, i.e. the whole batch) through the reference's own CPU int8 path
-    on all host cores, every one of the step's products each step. Under
-    torchrun only rank 0 runs."""
+    """The reference arm: one GPU's workload (the whole batch of 64 segments,
+    what rank 0 takes at every N under weak scaling and at N = 1 under
+    strong) through the reference's own CPU int8 path on all host cores,
+    every one of the step's products each step. Under torchrun only rank 0
+    runs."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -1616,7 +1622,7 @@ def run_reference(args) -> None:
                      f"{float(np.median(times)):.3f} s"}
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+            "scaling": "strong" if WORKLOAD == "longform" else args.scaling, "vs_baseline": None, "dtype": "int8",
             "data": "synthetic (seeded segments, random int8 weights, N(0,1) activations)",
             "config": {"workload": "configs[3] batched encoder (the GPU arm's whole batch): 64 segments of 2-30 s, "
                                    "24 layers x 11 products + 3 subsampling products, every product timed every "
@@ -1744,9 +1750,9 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-producers", action="store_true", help="skip timing the fused producers (rank 0)")
     ap.add_argument("--no-graph", action="store_true")
-    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
-                    help="strong: the one batch of 64 segments split across the GPUs (configs[3]); "
-                         "weak: 64 segments per GPU")
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="weak",
+                    help="weak: a batch of 64 segments per GPU (configs[3] on every GPU); "
+                         "strong: the one batch of 64 segments split across the GPUs")
     ap.add_argument("--kernel-only", action="store_true",
                     help="only the dominant product (FF up at the batch's M), 3 launches: the ncu capture's case")
     ap.add_argument("--producers-only", action="store_true",
