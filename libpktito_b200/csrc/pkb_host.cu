@@ -613,7 +613,9 @@ int weights_for(Pipe& p, const int8_t* w, uint32_t rows, uint32_t n, const int8_
 // same either way; what the cache saves is PCIe traffic, paid for with host
 // memory reads. A new quantize call over the same host bytes replaces the
 // old result. The device copies are capped (PKB_ACT_CACHE_MB, default 4096;
-// 0 turns the cache off), the oldest dropped first.
+// 0 turns the cache off), the oldest dropped first; a dropped copy no call
+// uses keeps its memory as a spare (capped the same) that a later quantize
+// call of a size it holds takes over.
 //
 // A call whose frames lie inside those of a call still in progress that
 // compared (or was itself covered so) skips the comparison: the caller may
@@ -645,8 +647,18 @@ struct ActCopy {
 struct ActCache {
     std::shared_mutex mu;
     std::map<uintptr_t, std::shared_ptr<ActCopy>> by_q;  // by q0; disjoint host ranges
-    std::deque<uintptr_t> order;                          // insertion order, for eviction
+    // insertion order, for eviction: each entry with the copy it named, so a
+    // key inserted again is not evicted for its older self
+    std::deque<std::pair<uintptr_t, const ActCopy*>> order;
     size_t bytes = 0;
+    // Copies that left the cache while no call used them, kept with their
+    // device and host memory for the next quantize call to take over: an
+    // encoder quantizes the same shapes every forward pass, and a step's
+    // results can outgrow the cap (FIFO then evicts every result before its
+    // next use), so without this each step would allocate its copies again
+    // and fault in and zero-fill fresh host pages for their comparison copies.
+    std::deque<std::shared_ptr<ActCopy>> spares;  // oldest first
+    size_t spare_bytes = 0;
 };
 
 ActCache g_acts[MAX_DEV];
@@ -659,24 +671,54 @@ size_t act_cache_cap() {
     return cap;
 }
 
-// Drops the results overlapping host bytes [q, q + qbytes) or scales [d, d + dbytes);
-// returns one of them that no call still uses, for its memory to be reused.
-std::shared_ptr<ActCopy> act_forget(ActCache& c, uintptr_t q, size_t qbytes, uintptr_t d, size_t dbytes) {
-    std::shared_ptr<ActCopy> spare;
+size_t act_bytes(const ActCopy& a) { return static_cast<size_t>(a.T) * (a.n + 4 * a.nb); }
+size_t act_held(const ActCopy& a) { return a.cap_q + a.cap_d + a.hq.capacity() + 4 * a.hd.capacity(); }
+
+// A copy that left the cache (c.mu held): kept as a spare where no call
+// uses it (the spares' memory capped as the cache is, the oldest freed
+// first), else freed by the last call that does.
+void act_retire(ActCache& c, std::shared_ptr<ActCopy> a) {
+    if (!a || a.use_count() != 1 || !a->dq) return;
+    c.spare_bytes += act_held(*a);
+    c.spares.push_back(std::move(a));
+    while (c.spare_bytes > act_cache_cap() && !c.spares.empty()) {
+        c.spare_bytes -= act_held(*c.spares.front());
+        c.spares.pop_front();
+    }
+}
+
+// The smallest spare whose device memory holds qbytes of bytes and dbytes
+// of scales, taken out of the spares; null where none does.
+std::shared_ptr<ActCopy> act_take_spare(ActCache& c, size_t qbytes, size_t dbytes) {
+    std::unique_lock<std::shared_mutex> lock(c.mu);
+    auto best = c.spares.end();
+    for (auto it = c.spares.begin(); it != c.spares.end(); ++it)
+        if ((*it)->cap_q >= qbytes && (*it)->cap_d >= dbytes &&
+            (best == c.spares.end() || (*it)->cap_q + (*it)->cap_d < (*best)->cap_q + (*best)->cap_d))
+            best = it;
+    if (best == c.spares.end()) return nullptr;
+    std::shared_ptr<ActCopy> a = std::move(*best);
+    c.spares.erase(best);
+    c.spare_bytes -= act_held(*a);
+    return a;
+}
+
+// Drops the results overlapping host bytes [q, q + qbytes) or scales
+// [d, d + dbytes); those no call still uses become spares.
+void act_forget(ActCache& c, uintptr_t q, size_t qbytes, uintptr_t d, size_t dbytes) {
     std::unique_lock<std::shared_mutex> lock(c.mu);
     for (auto it = c.by_q.begin(); it != c.by_q.end();) {
         const ActCopy& a = *it->second;
         const uintptr_t aq1 = a.q0 + static_cast<size_t>(a.T) * a.n, ad1 = a.d0 + static_cast<size_t>(a.T) * a.nb * 4;
         if ((a.q0 < q + qbytes && q < aq1) || (a.d0 < d + dbytes && d < ad1)) {
-            c.bytes -= static_cast<size_t>(a.T) * (a.n + 4 * a.nb);
-            if (it->second.use_count() == 1 && (!spare || a.T * static_cast<size_t>(a.n) > spare->hq.size()))
-                spare = it->second;
+            c.bytes -= act_bytes(a);
+            std::shared_ptr<ActCopy> gone = std::move(it->second);
             it = c.by_q.erase(it);
+            act_retire(c, std::move(gone));
         } else {
             ++it;
         }
     }
-    return spare;
 }
 
 // A call's hold on frames [f0, f0 + T) of a device copy, released when the
@@ -793,31 +835,36 @@ int pkb_quantize_host(int8_t* q, float* d, uint32_t n, uint32_t qb, uint32_t T, 
     auto frames = [&](uint32_t c) { return std::min(TC, T - c * TC); };
     // the host bytes this call rewrites: older results over them are stale
     ActCache& ac = g_acts[p->dev];
-    std::shared_ptr<ActCopy> spare =
-        act_forget(ac, reinterpret_cast<uintptr_t>(q), T * qrow, reinterpret_cast<uintptr_t>(d), T * drow);
-    // the result's device copy, kept for the products that read it; the
-    // memory of the result it replaces, where it is large enough and no call
-    // uses it, is taken over (no allocation, no fresh host pages)
+    act_forget(ac, reinterpret_cast<uintptr_t>(q), T * qrow, reinterpret_cast<uintptr_t>(d), T * drow);
+    // the result's device copy, kept for the products that read it: a spare
+    // copy's memory where one is large enough (no allocation, no fresh host
+    // pages), else new device memory
     std::shared_ptr<ActCopy> keep;
     if (act_cache_cap() && T * (qrow + drow) <= act_cache_cap()) {
-        const bool reuse = spare && spare->cap_q >= T * qrow && spare->cap_d >= T * drow;
-        keep = reuse ? spare : std::make_shared<ActCopy>();
+        keep = act_take_spare(ac, T * qrow, T * drow);
+        if (!keep) {
+            keep = std::make_shared<ActCopy>();
+            keep->dev = p->dev;
+            if (cudaMallocAsync(&keep->dq, T * qrow, p->s_comp) != cudaSuccess ||
+                cudaMallocAsync(&keep->dd, T * drow, p->s_comp) != cudaSuccess) {
+                cudaGetLastError();
+                keep.reset();  // no room: the call works as without the cache
+            } else {
+                keep->cap_q = T * qrow;
+                keep->cap_d = T * drow;
+            }
+        }
+    }
+    if (keep) {
         keep->q0 = reinterpret_cast<uintptr_t>(q);
         keep->d0 = reinterpret_cast<uintptr_t>(d);
         keep->n = n;
         keep->nb = nb;
         keep->T = T;
-        keep->dev = p->dev;
-        if (!reuse && (cudaMallocAsync(&keep->dq, T * qrow, p->s_comp) != cudaSuccess ||
-                       cudaMallocAsync(&keep->dd, T * drow, p->s_comp) != cudaSuccess)) {
-            cudaGetLastError();
-            keep.reset();  // no room: the call works as without the cache
-        } else if (!reuse) {
-            keep->cap_q = T * qrow;
-            keep->cap_d = T * drow;
-        }
+        // the host copy of what the call writes
+        if (keep->hq.size() < T * qrow) keep->hq.resize(T * qrow);
+        if (keep->hd.size() < static_cast<size_t>(T) * nb) keep->hd.resize(static_cast<size_t>(T) * nb);
     }
-    spare.reset();
     // declared after keep, so drained before keep's memory can go
     DrainOnReturn drain{p};
     // where chunk c's bytes and scales are made on the device
@@ -827,25 +874,31 @@ int pkb_quantize_host(int8_t* q, float* d, uint32_t n, uint32_t qb, uint32_t T, 
     auto dd_of = [&](uint32_t c) -> float* {
         return keep ? keep->dd + static_cast<size_t>(c) * TC * nb : reinterpret_cast<float*>(p->dev_out[c & 1] + off_d);
     };
-    // after the call's last copy: the host copy of what was written, and the entry
+    // chunk c's bytes and scales, once in the caller's memory, into the host copy
+    auto shadow = [&](uint32_t c) {
+        if (!keep) return;
+        const size_t t0 = static_cast<size_t>(c) * TC;
+        pool.copy(keep->hq.data() + t0 * qrow, q + t0 * qrow, frames(c) * qrow);
+        pool.copy(keep->hd.data() + t0 * nb, d + t0 * nb, frames(c) * drow);
+    };
+    // after the call's last copy: the entry, the oldest ones evicted past the cap
     auto remember = [&]() {
         if (!keep) return;
-        if (keep->hq.size() < T * qrow) keep->hq.resize(T * qrow);
-        if (keep->hd.size() < static_cast<size_t>(T) * nb) keep->hd.resize(static_cast<size_t>(T) * nb);
-        pool.copy(keep->hq.data(), q, T * qrow);
-        pool.copy(keep->hd.data(), d, T * drow);
         std::unique_lock<std::shared_mutex> lock(ac.mu);
-        const size_t sz = T * (qrow + drow);
+        const size_t sz = act_bytes(*keep);
         while (ac.bytes + sz > act_cache_cap() && !ac.order.empty()) {
-            auto it = ac.by_q.find(ac.order.front());
+            const auto old = ac.order.front();
             ac.order.pop_front();
-            if (it != ac.by_q.end()) {
-                ac.bytes -= static_cast<size_t>(it->second->T) * (it->second->n + 4 * it->second->nb);
+            auto it = ac.by_q.find(old.first);
+            if (it != ac.by_q.end() && it->second.get() == old.second) {
+                ac.bytes -= act_bytes(*it->second);
+                std::shared_ptr<ActCopy> gone = std::move(it->second);
                 ac.by_q.erase(it);
+                act_retire(ac, std::move(gone));
             }
         }
         ac.by_q[keep->q0] = keep;
-        ac.order.push_back(keep->q0);
+        ac.order.emplace_back(keep->q0, keep.get());
         ac.bytes += sz;
     };
     if (pinned(x, ((T - 1) * xs + n) * 4) && pinned(q, T * qrow) && pinned(d, T * drow)) {
@@ -872,6 +925,11 @@ int pkb_quantize_host(int8_t* q, float* d, uint32_t n, uint32_t qb, uint32_t T, 
         }
         count_host_bytes(T * xrow, T * (qrow + drow));
         if ((rc = p->finish(err))) return rc;
+        // the host copy after the last chunk (a chunk at a time during the
+        // loop would hold the next chunk's enqueue behind a copy that waits
+        // for the copy pool, which other calls' comparisons keep busy: the
+        // uploads then starve, measured on B200)
+        for (uint32_t c = 0; c < nchunks; c++) shadow(c);
         remember();
         return PKB_OK;
     }
@@ -880,6 +938,7 @@ int pkb_quantize_host(int8_t* q, float* d, uint32_t n, uint32_t qb, uint32_t T, 
         HOST_CUDA(cudaEventSynchronize(p->ev_out[s]), "cudaEventSynchronize");
         pool.copy(q + static_cast<size_t>(c) * TC * qrow, p->pin_out[s], frames(c) * qrow);
         pool.copy(d + static_cast<size_t>(c) * TC * nb, p->pin_out[s] + off_d, frames(c) * drow);
+        shadow(c);
         return PKB_OK;
     };
     for (uint32_t c = 0; c < nchunks; c++) {
