@@ -963,9 +963,9 @@ def decoder_search(model, segs) -> dict:
     fh = f.view(-1, m["J"])[int(f0[i]):int(f0[i]) + int(Ts[i])].cpu().numpy().reshape(-1)
     want = O.tdt_search(m, fh, int(Ts[i]))
     got = toks.view(S, cap, 3)[i, :int(n[i])].cpu().numpy()
-    rounds = (launches - 2) // (3 * m["L"] + 4)  # the embedding's quantize and the initial state, then a round's launches
+    rounds = P.tdt_last_rounds()
     return {"ms": ms, "segments": S, "frames": int(Ts.sum()), "tokens": int(n.sum()), "rounds": int(rounds),
-            "us_per_round": ms * 1e3 / max(1, rounds), "launches_per_round": 3 * m["L"] + 4,
+            "us_per_round": ms * 1e3 / max(1, rounds), "launches_per_search": int(launches),
             "frames_per_s": float(Ts.sum()) / (ms * 1e-3),
             "shapes": "pred_hidden 640 x 2 LSTM layers, joint 640, jout 8208 x 640, durations 0-4; qb = n",
             "parity": {"segment_frames": int(Ts[i]), "tokens": int(len(want)),

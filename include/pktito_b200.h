@@ -311,8 +311,7 @@ size_t pkb_tdt_work_bytes(const pkb_tdt_model *m, uint32_t S);
  * to toks + (s*cap + i)*3 as (id, frame, duration), their count to ntok[s].
  * f, toks, ntok and work are device memory (work: pkb_tdt_work_bytes of it,
  * 256-byte aligned); f0 and T host memory. Waits for the work already on
- * stream, runs the search on a stream of its own (its rounds replayed as a
- * CUDA graph of 8, the segments' states read back after each) and returns
+ * stream, runs the search on a stream of its own and returns
  * when every search has ended; PKB_EINVAL if a segment found more than cap
  * tokens. No counterpart in the backend table:
  * the reference runs the search in core/decoder.c over the table's
@@ -320,6 +319,10 @@ size_t pkb_tdt_work_bytes(const pkb_tdt_model *m, uint32_t S);
 int pkb_tdt_search_dev(void *stream, const pkb_tdt_model *m, const float *f, const uint32_t *f0, const uint32_t *T,
                        uint32_t S, int32_t *toks, uint32_t *ntok, uint32_t cap, void *work, size_t work_bytes,
                        int rmode);
+
+/* Rounds the calling thread's last pkb_tdt_search_dev ran: the joint steps
+ * of its longest-running segment. No counterpart in the reference. */
+uint64_t pkb_tdt_last_rounds(void);
 
 /* Launches of libpktito_b200 kernels since the process started, on every
  * device: the evidence a benchmark reports for its own kernels' work. */

@@ -127,6 +127,7 @@ _SIGS = {
                                          ctypes.c_size_t, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p,
                                          ctypes.c_void_p, ctypes.c_float, ctypes.c_int]),
     "pkb_launch_count": (ctypes.c_uint64, []),
+    "pkb_tdt_last_rounds": (ctypes.c_uint64, []),
     "pkb_host_bytes": (None, [ctypes.c_void_p, ctypes.c_void_p]),
     "pkb_quantize_host_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,
                                                  ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]),
@@ -346,6 +347,11 @@ class TdtModel(ctypes.Structure):
                [("dur", ctypes.c_uint32 * 16), ("embed", ctypes.c_void_p)] + \
                [(n, ctypes.c_void_p * 4) for n in ("wx", "wh", "wxs", "whs", "lb")] + \
                [(n, ctypes.c_void_p) for n in ("jpred", "jpreds", "jpredb", "jout", "jouts", "joutb")]
+
+
+def tdt_last_rounds() -> int:
+    """Rounds this thread's last tdt_search_dev ran (its longest segment's joint steps)."""
+    return int(lib().pkb_tdt_last_rounds())
 
 
 def tdt_work_bytes(m: TdtModel, S: int) -> int:

@@ -560,7 +560,7 @@ int attention_dev(cudaStream_t stream, bool panels, float* o, size_t os, const f
 
 // The work area's pieces, 256-byte aligned, in the order TdtArgs lists them.
 struct TdtLayout {
-    size_t seg, T, f0, qembed, dembed, qx, dx, h, c, qh, dh, gates, gp, gpn, qz, dz, logits, total;
+    size_t seg, T, f0, qembed, dembed, qx, dx, h, c, qh, dh, gates, gp, gpn, qz, dz, logits, bar, total;
 };
 
 TdtLayout tdt_layout(const pkb_tdt_model& m, uint32_t S) {
@@ -589,6 +589,7 @@ TdtLayout tdt_layout(const pkb_tdt_model& m, uint32_t S) {
     o.qz = take(S * J);
     o.dz = take(S * 4);
     o.logits = take(S * size_t(m.n_out_pad) * 4);
+    o.bar = take(8);  // the persistent search's barrier count and abort flag
     o.total = at;
     return o;
 }
@@ -618,6 +619,63 @@ struct OwnStream {
         if (s) cudaStreamDestroy(s);
     }
 };
+
+// The rounds as launches: ROUNDS rounds as one CUDA graph, replayed until
+// every search has ended (a round past a segment's end does nothing to it),
+// the segments' states read back after each replay.
+template <typename Round>
+int tdt_rounds(Round& round, cudaStream_t st, std::vector<uint8_t>& states, const uint8_t* seg, uint32_t S, uint32_t L,
+               uint64_t max_rounds) {
+    constexpr uint32_t ROUNDS = 8;
+#if !PKB_TDT_GRAPH
+    int rc;
+    for (uint64_t r = 0; r < max_rounds; r += ROUNDS) {
+        for (uint32_t i = 0; i < ROUNDS; i++)
+            if ((rc = round())) return rc;
+        PKB_CUDA(cudaMemcpyAsync(states.data(), seg, states.size(), cudaMemcpyDeviceToHost, st), "download");
+        PKB_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+        bool running = false;
+        for (uint32_t s = 0; s < S; s++)
+            if (reinterpret_cast<const uint32_t*>(states.data() + s * tdt_seg_bytes())[TDT_SEG_ACTIVE]) running = true;
+        if (!running) break;
+    }
+#else
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    PKB_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+    int crc = PKB_OK;
+    const uint64_t counted = g_launches.load();
+    for (uint32_t r = 0; r < ROUNDS && !crc; r++) crc = round();
+    // a captured launch runs when the graph does: counted at each replay
+    g_launches.fetch_sub(g_launches.load() - counted, std::memory_order_relaxed);
+    const cudaError_t ce = cudaStreamEndCapture(st, &graph);
+    if (crc) {
+        if (graph) cudaGraphDestroy(graph);
+        return crc;
+    }
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamEndCapture");
+    const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) return cuda_fail(ie, "cudaGraphInstantiate");
+    bool running = true;
+    cudaError_t le = cudaSuccess;
+    for (uint64_t r = 0; running && r < max_rounds && le == cudaSuccess; r += ROUNDS) {
+        le = cudaGraphLaunch(exec, st);
+        if (le == cudaSuccess) le = cudaMemcpyAsync(states.data(), seg, states.size(), cudaMemcpyDeviceToHost, st);
+        if (le == cudaSuccess) le = cudaStreamSynchronize(st);
+        g_launches.fetch_add(ROUNDS * (3 * L + 4), std::memory_order_relaxed);
+        running = false;
+        for (uint32_t s = 0; s < S; s++)
+            if (reinterpret_cast<const uint32_t*>(states.data() + s * tdt_seg_bytes())[TDT_SEG_ACTIVE]) running = true;
+    }
+    cudaGraphExecDestroy(exec);
+    if (le != cudaSuccess) return cuda_fail(le, "tdt rounds");
+#endif
+    return PKB_OK;
+}
+
+// rounds of the calling thread's last search: its longest segment's joint steps
+thread_local uint64_t tl_tdt_rounds = 0;
 
 int tdt_search_dev(cudaStream_t caller, const pkb_tdt_model* m, const float* f, const uint32_t* f0,
                    const uint32_t* T, uint32_t S, int32_t* toks, uint32_t* ntok, uint32_t cap, void* work,
@@ -713,66 +771,64 @@ int tdt_search_dev(cudaStream_t caller, const pkb_tdt_model* m, const float* f, 
         if ((rc = product(a.logits, m->n_out_pad, m->jout, m->jouts, m->joutb, a.qz, a.dz, J, 0))) return rc;
         return tdt(TDT_STEP, 0);
     };
-    // ROUNDS rounds as one CUDA graph, replayed until every search has ended
-    // (a round past a segment's end does nothing to it); each round takes
-    // every running segment one joint step further or one token on, so
-    // T (max_symbols + 1) + 1 rounds end every search
-    constexpr uint32_t ROUNDS = 8;
+    // each round takes every running segment one joint step further or one
+    // token on, so T (max_symbols + 1) + 1 rounds end every search
     const uint64_t max_rounds = static_cast<uint64_t>(tmax) * (m->max_symbols + 1) + 2;
     std::vector<uint8_t> states(S * tdt_seg_bytes());
-#if !PKB_TDT_GRAPH
-    for (uint64_t r = 0; r < max_rounds; r += ROUNDS) {
-        for (uint32_t i = 0; i < ROUNDS; i++)
-            if ((rc = round())) return rc;
-        PKB_CUDA(cudaMemcpyAsync(states.data(), w + o.seg, states.size(), cudaMemcpyDeviceToHost, st), "download");
+    // The whole search as one cooperative launch where its shared memory
+    // fits and the grid can be resident at once (pkb_tdt.cu); otherwise
+    // the rounds' launches below.
+    const size_t psmem = L <= TDT_MAX_L && max_rounds < (1ull << 31) ? tdt_persist_smem(a, attention_smem_max()) : 0;
+    const int pgrid = psmem ? tdt_persist_grid(a, rmode, dev->sms, psmem) : 0;
+    if (pgrid > 0) {
+        TdtPersist pp = {};
+        pp.L = L;
+        for (uint32_t l = 0; l < L; l++) {
+            pp.wx[l] = m->wx[l];
+            pp.wh[l] = m->wh[l];
+            pp.wxs[l] = m->wxs[l];
+            pp.whs[l] = m->whs[l];
+            pp.lb[l] = m->lb[l];
+        }
+        pp.jpred = m->jpred;
+        pp.jpreds = m->jpreds;
+        pp.jpredb = m->jpredb;
+        pp.jout = m->jout;
+        pp.jouts = m->jouts;
+        pp.joutb = m->joutb;
+        pp.bar = reinterpret_cast<unsigned*>(w + o.bar);
+        pp.abort = reinterpret_cast<int*>(w + o.bar + 4);
+        pp.err = dev->err;
+        pp.timeout = wait_limit();
+        pp.max_rounds = static_cast<uint32_t>(max_rounds);
+        PKB_CUDA(cudaMemsetAsync(w + o.bar, 0, 8, st), "cudaMemsetAsync");
+        PKB_CUDA(launch_tdt_persist(a, pp, rmode, pgrid, psmem, st), "tdt launch");
+        g_launches.fetch_add(1, std::memory_order_relaxed);
+        uint32_t word = 0;
+        PKB_CUDA(cudaMemcpyAsync(&word, dev->err, sizeof word, cudaMemcpyDeviceToHost, st), "download");
         PKB_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize");
-        bool running = false;
-        for (uint32_t s = 0; s < S; s++)
-            if (reinterpret_cast<const uint32_t*>(states.data() + s * tdt_seg_bytes())[TDT_SEG_ACTIVE]) running = true;
-        if (!running) break;
+        if (word) {
+            PKB_CUDA(cudaMemsetAsync(dev->err, 0, sizeof word, st), "cudaMemsetAsync");
+            PKB_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+            return fail(PKB_ETIMEOUT, "tdt: a barrier of the search gave up waiting (device error word 0x%x)", word);
+        }
+    } else {
+        if ((rc = tdt_rounds(round, st, states, w + o.seg, S, L, max_rounds))) return rc;
     }
-#else
-    cudaGraph_t graph = nullptr;
-    cudaGraphExec_t exec = nullptr;
-    PKB_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
-    int crc = PKB_OK;
-    const uint64_t counted = g_launches.load();
-    for (uint32_t r = 0; r < ROUNDS && !crc; r++) crc = round();
-    // a captured launch runs when the graph does: counted at each replay
-    g_launches.fetch_sub(g_launches.load() - counted, std::memory_order_relaxed);
-    const cudaError_t ce = cudaStreamEndCapture(st, &graph);
-    if (crc) {
-        if (graph) cudaGraphDestroy(graph);
-        return crc;
-    }
-    if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamEndCapture");
-    const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
-    cudaGraphDestroy(graph);
-    if (ie != cudaSuccess) return cuda_fail(ie, "cudaGraphInstantiate");
-    bool running = true;
-    cudaError_t le = cudaSuccess;
-    for (uint64_t r = 0; running && r < max_rounds && le == cudaSuccess; r += ROUNDS) {
-        le = cudaGraphLaunch(exec, st);
-        if (le == cudaSuccess) le = cudaMemcpyAsync(states.data(), w + o.seg, states.size(), cudaMemcpyDeviceToHost, st);
-        if (le == cudaSuccess) le = cudaStreamSynchronize(st);
-        g_launches.fetch_add(ROUNDS * (3 * L + 4), std::memory_order_relaxed);
-        running = false;
-        for (uint32_t s = 0; s < S; s++)
-            if (reinterpret_cast<const uint32_t*>(states.data() + s * tdt_seg_bytes())[TDT_SEG_ACTIVE]) running = true;
-    }
-    cudaGraphExecDestroy(exec);
-    if (le != cudaSuccess) return cuda_fail(le, "tdt rounds");
-#endif
     PKB_CUDA(cudaMemcpyAsync(states.data(), w + o.seg, states.size(), cudaMemcpyDeviceToHost, st), "download");
     PKB_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+    tl_tdt_rounds = 0;
     for (uint32_t s = 0; s < S; s++) {
         const uint32_t* g = reinterpret_cast<const uint32_t*>(states.data() + s * tdt_seg_bytes());
+        if (g[TDT_SEG_STEPS] > tl_tdt_rounds) tl_tdt_rounds = g[TDT_SEG_STEPS];
         if (g[TDT_SEG_OVER]) return fail(PKB_EINVAL, "tdt: segment %u found more than %u tokens", s, cap);
         if (g[TDT_SEG_ACTIVE]) return fail(PKB_ETIMEOUT, "tdt: segment %u still searching after %llu rounds", s,
                               static_cast<unsigned long long>(max_rounds));
     }
     return PKB_OK;
 }
+
+
 
 }  // namespace
 
@@ -892,6 +948,8 @@ int pkb_attention_rows_dev(void* stream, float* o, size_t os, const float* q, si
     return pkb::attention_dev(static_cast<cudaStream_t>(stream), false, o, os, q, qs, k, ks, v, vs, p, ps, bias_u,
                               bias_v, D, H, segs, nseg, rmode);
 }
+
+uint64_t pkb_tdt_last_rounds(void) { return pkb::tl_tdt_rounds; }
 
 size_t pkb_tdt_work_bytes(const pkb_tdt_model* m, uint32_t S) {
     return m && S ? pkb::tdt_layout(*m, S).total : 0;

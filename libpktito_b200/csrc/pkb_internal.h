@@ -179,10 +179,34 @@ struct TdtArgs {
 
 cudaError_t launch_tdt_init(const TdtArgs& a, cudaStream_t stream);
 cudaError_t launch_tdt(const TdtArgs& a, int phase, uint32_t l, int rmode, cudaStream_t stream);
+
+// The whole search as one cooperative launch (pkb_tdt.cu): the weights, the
+// grid barrier's words and the bound on rounds, beside TdtArgs.
+constexpr int TDT_MAX_L = 4;
+struct TdtPersist {
+    uint32_t L;
+    const int8_t *wx[TDT_MAX_L], *wh[TDT_MAX_L];  // [4P][P] rows
+    const float *wxs[TDT_MAX_L], *whs[TDT_MAX_L], *lb[TDT_MAX_L];
+    const int8_t* jpred;  // [J][P]
+    const float *jpreds, *jpredb;
+    const int8_t* jout;   // [nout][J]
+    const float *jouts, *joutb;
+    unsigned* bar;        // arrivals at the grid's barriers (zero at launch)
+    int* abort;           // set by a CTA whose wait gave up (zero at launch)
+    uint32_t* err;        // the device error word
+    long long timeout;    // SM clock cycles a barrier wait may last
+    uint32_t max_rounds;
+};
+// Shared memory a CTA of the persistent search takes (0: the shapes do not fit).
+size_t tdt_persist_smem(const TdtArgs& a, size_t smem_max);
+// CTAs the search may run (all resident at once) on a device of `sms` SMs; 0 where none fits.
+int tdt_persist_grid(const TdtArgs& a, int rmode, int sms, size_t smem);
+cudaError_t launch_tdt_persist(const TdtArgs& a, const TdtPersist& p, int rmode, int grid, size_t smem,
+                               cudaStream_t stream);
 size_t tdt_seg_bytes();  // one segment's search state
 // the 32-bit words of a search state the host reads back: still searching,
-// out of token room
-constexpr int TDT_SEG_ACTIVE = 4, TDT_SEG_OVER = 7;
+// out of token room, joint steps taken
+constexpr int TDT_SEG_ACTIVE = 4, TDT_SEG_OVER = 7, TDT_SEG_STEPS = 8;
 
 cudaError_t launch_repack_q8(int8_t* wpack, const int8_t* w_pk, uint32_t rows, uint32_t n, int num_sms,
                              cudaStream_t stream);

@@ -324,7 +324,7 @@ def tdt_search(m: dict, f: np.ndarray, T: int, rmode: int = RN, cap: int = 1 << 
              *[_p(keep[k]) for k in ("dur", "embed", "wx", "wh", "wxs", "whs", "lb", "jpred", "jpreds", "jpredb",
                                      "jout", "jouts", "joutb")])
     f = np.ascontiguousarray(f, np.float32)
-    cap = min(cap, 4 * T + 16)
+    cap = min(cap, T * (m["max_symbols"] + 1) + 16)  # at most max_symbols tokens a frame
     ids, frames, durs = (np.zeros(cap, np.int32) for _ in range(3))
     n = olib().oracle_tdt_search(_p(ids), _p(frames), _p(durs), cap, _p(f), T, ctypes.byref(t), rmode)
     assert n >= 0, "more tokens than the cap"

@@ -11,6 +11,10 @@ in lockstep, against the reference's own tokens and the oracle.
   a batch of 6 segments against the oracle's search, in two rounding modes.
 * The token capacity: a segment that finds more tokens than the room given
   makes the call fail.
+* Both ways the search runs: one cooperative launch for the whole search
+  where a batch's shapes fit its shared memory (the cases above), and the
+  rounds' launches replayed as a CUDA graph where they do not (a batch of
+  200 segments at the model's shapes).
 """
 import os
 
@@ -134,13 +138,37 @@ def test_the_oracles_tokens_at_the_models_shapes(pkb, cuda_device, rmode):
     g = np.random.default_rng(11 + rmode)
     Ts = [1, 9, 40, 64, 17, 100]
     frames = [(g.standard_normal(T * m["J"]) * 2.0).astype(np.float32) for T in Ts]
+    n0 = pkb.launch_count()
     got = search(pkb, t, frames, cap=1024, rmode=rmode)
+    # the embedding's quantization, the states' set-up, the search: one launch
+    assert pkb.launch_count() - n0 == 3
     total = 0
     for T, f, a in zip(Ts, frames, got):
         want = O.tdt_search(m, f, T, rmode)
         assert a.shape == want.shape and (a == want).all(), T
         total += len(want)
     assert total > 50  # the prediction network stepped on real tokens
+
+
+def test_a_batch_past_one_launchs_shared_memory_takes_the_rounds_launches(pkb, cuda_device):
+    """200 segments at the model's shapes: the persistent search's staging of
+    every segment's input would need more shared memory than a CTA has, so
+    the rounds run as launches; every segment's tokens are still the
+    oracle's."""
+    m = synthetic_model()
+    t, keep = device_model(pkb, m)
+    g = np.random.default_rng(23)
+    Ts = [int(x) for x in g.integers(0, 5, 200)]
+    frames = [(g.standard_normal(T * m["J"]) * 2.0).astype(np.float32) for T in Ts]
+    n0 = pkb.launch_count()
+    got = search(pkb, t, frames, cap=64)
+    assert pkb.launch_count() - n0 > 10
+    total = 0
+    for T, f, a in zip(Ts, frames, got):
+        want = O.tdt_search(m, f, T, O.RN)
+        assert a.shape == want.shape and (a == want).all(), T
+        total += len(want)
+    assert total > 20
 
 
 def test_a_segment_past_its_token_room_fails_the_call(pkb, cuda_device):
