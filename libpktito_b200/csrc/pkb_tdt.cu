@@ -31,6 +31,7 @@ namespace pkb {
 namespace {
 
 constexpr int TD_THREADS = 256;
+constexpr uint32_t TD_MAX_DUR = sizeof(TdtArgs::dur) / sizeof(uint32_t);
 
 // pk_sigmoidf (core/vmath.h:149-151): 1 / (1 + pk_expf(-x))
 template <int RM>
@@ -257,33 +258,46 @@ __device__ void step_seg(const TdtArgs& a, uint32_t s) {
                 b = bv[w];
                 k = bi[w];
             }
-        // the best duration, the first of equals (a handful: one thread)
+        // the best duration, the first of equals (a handful: one thread);
+        // its logits and the state loaded before any is used, so their
+        // round trips to L2 overlap
+        float dl[TD_MAX_DUR];
+#pragma unroll
+        for (uint32_t i = 0; i < TD_MAX_DUR; i++) dl[i] = i < a.n_dur ? __ldcg(lg + V + 1 + i) : 0.0f;
+        const uint32_t t0 = g->t, last = g->last, lasts = g->lasts, ntok = g->ntok, steps = g->steps;
+        const uint32_t Ts = a.T[s];
         uint32_t di = 0;
-        for (uint32_t i = 1; i < a.n_dur; i++)
-            if (__ldcg(lg + V + 1 + i) > __ldcg(lg + V + 1 + di)) di = i;
-        const uint32_t t0 = g->t;
-        uint32_t d = a.dur[di];
+        float bd = dl[0];
+#pragma unroll
+        for (uint32_t i = 1; i < TD_MAX_DUR; i++)
+            if (i < a.n_dur && dl[i] > bd) {
+                bd = dl[i];
+                di = i;
+            }
+        const uint32_t dur = a.dur[di];
         uint32_t emit = 0;
-        g->steps++;
+        g->steps = steps + 1;
         if (k == V) {
-            if (d == 0) d = 1;
-            g->t = t0 + d;
-            if (g->t >= a.T[s]) g->active = 0;  // a blank ran off the end: the search stops
-        } else if (g->ntok == a.cap) {
+            const uint32_t nt = t0 + (dur ? dur : 1);
+            g->t = nt;
+            if (nt >= Ts) g->active = 0;  // a blank ran off the end: the search stops
+        } else if (ntok == a.cap) {
             g->over = 1;  // no room for the token: the call fails
             g->active = 0;
         } else {
-            int32_t* tk = a.toks + (static_cast<size_t>(s) * a.cap + g->ntok) * 3;
+            int32_t* tk = a.toks + (static_cast<size_t>(s) * a.cap + ntok) * 3;
             tk[0] = static_cast<int32_t>(k);
             tk[1] = static_cast<int32_t>(t0);
-            tk[2] = static_cast<int32_t>(a.dur[di]);
-            g->ntok++;
-            a.ntok[s] = g->ntok;
-            g->t = t0 + d;
-            g->lasts = g->last == t0 ? g->lasts + 1 : 1;
+            tk[2] = static_cast<int32_t>(dur);
+            g->ntok = ntok + 1;
+            a.ntok[s] = ntok + 1;
+            uint32_t nt = t0 + dur;
+            const uint32_t nlasts = last == t0 ? lasts + 1 : 1;
+            g->lasts = nlasts;
             g->last = t0;
-            if (g->lasts >= a.max_symbols && g->last == g->t) g->t++;
-            if (g->t >= a.T[s]) {
+            if (nlasts >= a.max_symbols && t0 == nt) nt++;
+            g->t = nt;
+            if (nt >= Ts) {
                 g->active = 0;  // its prediction would change nothing
             } else {
                 g->pred = 1;
@@ -325,8 +339,8 @@ __global__ void __launch_bounds__(TD_THREADS) tdt_step(TdtArgs a) { step_seg(a, 
 // product kernel computes a block of qb = n. At 64 segments a product is
 // 64 columns, too few to feed tcgen05's 128-row tiles; the legacy MMA
 // reads its operands from registers loaded out of shared memory, where a
-// job's weight rows and every segment's input are staged (rows K + 16 bytes
-// apart, so the fragment loads of a warp hit 32 distinct banks).
+// job's weight rows and every segment's input are staged (rows ps_pitch(K)
+// bytes apart, so the fragment loads of a warp hit distinct banks).
 //
 // Everything a phase reads that another CTA wrote in an earlier phase is
 // read through L2 (__ldcg, or the state through a volatile pointer), and the
@@ -373,17 +387,27 @@ __device__ bool grid_barrier(const TdtPersist& p, uint32_t& epoch) {
     return s_ok != 0;
 }
 
-// Segments' quantized inputs [S][K] (written by other CTAs: copied through
-// L2 by cp.async.cg) into shared memory, KP = K + 16 bytes apart, segments
-// S..Spad-1 zeros. The copies are only issued: the caller commits and waits.
-__device__ void stage_inputs(int8_t* dst, const int8_t* x, uint32_t S, uint32_t Spad, uint32_t K) {
-    const uint32_t per = K / 16, KP = K + 16;
-    for (uint32_t i = threadIdx.x; i < Spad * per; i += blockDim.x) {
-        const uint32_t s = i / per, u = i % per;
-        if (s < S)
-            cp_async16(dst + s * KP + u * 16, x + static_cast<size_t>(s) * K + u * 16);
+// Bytes between rows of K int8 in shared memory: K rounded up so that the
+// pitch in 16-byte units is 4 modulo 8, so a quarter-warp's 16-byte loads of
+// two rows (lanes 4g + t, bytes 16t of row g) cover 8 distinct bank groups.
+__host__ __device__ __forceinline__ uint32_t ps_pitch(uint32_t K) {
+    const uint32_t u = K / 16;
+    return 16 * (u + ((4u - u % 8u) & 7u));
+}
+
+// The quantized inputs [K] of n segments, segment list[i] as row i
+// (written by other CTAs: copied through L2 by cp.async.cg), into shared
+// memory ps_pitch(K) bytes apart, rows n..npad-1 zeros. The copies are only
+// issued: the caller commits and waits.
+__device__ void stage_inputs(int8_t* dst, const int8_t* x, const uint32_t* list, uint32_t n, uint32_t npad,
+                             uint32_t K) {
+    const uint32_t per = K / 16, KP = ps_pitch(K);
+    for (uint32_t i = threadIdx.x; i < npad * per; i += blockDim.x) {
+        const uint32_t c = i / per, u = i % per;
+        if (c < n)
+            cp_async16(dst + c * KP + u * 16, x + static_cast<size_t>(list[c]) * K + u * 16);
         else
-            *reinterpret_cast<int4*>(dst + s * KP + u * 16) = make_int4(0, 0, 0, 0);
+            *reinterpret_cast<int4*>(dst + c * KP + u * 16) = make_int4(0, 0, 0, 0);
     }
 }
 
@@ -391,7 +415,7 @@ __device__ void stage_inputs(int8_t* dst, const int8_t* x, uint32_t S, uint32_t 
 // is row `row(lr)` of w, or zeros where that is past `rows`. Issued only.
 template <typename RowOf>
 __device__ void stage_weights(int8_t* dst, const int8_t* w, uint32_t K, uint32_t rows, RowOf row) {
-    const uint32_t per = K / 16, KP = K + 16;
+    const uint32_t per = K / 16, KP = ps_pitch(K);
     for (uint32_t i = threadIdx.x; i < PS_ROWS * per; i += blockDim.x) {
         const uint32_t lr = i / per, u = i % per, r = row(lr);
         if (r < rows)
@@ -401,9 +425,9 @@ __device__ void stage_weights(int8_t* dst, const int8_t* w, uint32_t K, uint32_t
     }
 }
 
-// A CTA's scales of every segment [S] (written by other CTAs) into shared memory.
-__device__ __forceinline__ void stage_scales(float* dst, const float* d, uint32_t S) {
-    for (uint32_t s = threadIdx.x; s < S; s += blockDim.x) dst[s] = __ldcg(d + s);
+// The scales of the n listed segments (written by other CTAs) into shared memory.
+__device__ __forceinline__ void stage_scales(float* dst, const float* d, const uint32_t* list, uint32_t n) {
+    for (uint32_t c = threadIdx.x; c < n; c += blockDim.x) dst[c] = __ldcg(d + list[c]);
 }
 
 // Everything staged by this thread's copies has landed, for every thread.
@@ -415,35 +439,53 @@ __device__ __forceinline__ void staged() {
 
 // The int32 sums of NT tiles, each weight rows [16 rt, 16 rt + 16) of W[i]
 // with the 8 segments of group sg[i] of X[i], over K (all in shared memory,
-// KP apart), their MMAs interleaved. Lane (g = lane / 4, t = lane % 4)
-// holds row 16 rt + g (c[i][0], c[i][1]) and + 8 (c[i][2], c[i][3]) of
+// ps_pitch(K) apart), their MMAs interleaved. Lane (g = lane / 4, t = lane
+// % 4) holds row 16 rt + g (c[i][0], c[i][1]) and + 8 (c[i][2], c[i][3]) of
 // segments 8 sg + 2t and + 1.
+//
+// A sum of integer products does not depend on the order of its terms, so
+// the MMA's k need only pair the same bytes of a weight row and of a
+// segment's input: of each 64 bytes of K, lane t takes bytes 16t..16t+15 of
+// its rows in one 16-byte load, bytes 0-7 as its k of one MMA (its fragment
+// registers 0 and 2, resp. 0 and 1 of B) and 8-15 of the next; a K that is
+// an odd multiple of 32 ends with 8-byte loads.
 template <int NT>
 __device__ __forceinline__ void mma_rows(int (&c)[NT][4], const int8_t* const (&W)[NT], const int8_t* const (&X)[NT],
                                          const uint32_t (&sg)[NT], uint32_t rt, uint32_t K) {
-    const uint32_t lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3, KP = K + 16;
+    const uint32_t lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3, KP = ps_pitch(K);
     const int8_t* alo[NT];
     const int8_t* b[NT];
 #pragma unroll
     for (int i = 0; i < NT; i++) {
-        alo[i] = W[i] + (16 * rt + g) * KP + 4 * t;
-        b[i] = X[i] + (8 * sg[i] + g) * KP + 4 * t;
+        alo[i] = W[i] + (16 * rt + g) * KP;
+        b[i] = X[i] + (8 * sg[i] + g) * KP;
         c[i][0] = c[i][1] = c[i][2] = c[i][3] = 0;
     }
-    for (uint32_t k = 0; k < K; k += 32) {
+    auto mma = [](int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    };
+    uint32_t k = 0;
+    for (; k + 64 <= K; k += 64) {
 #pragma unroll
         for (int i = 0; i < NT; i++) {
-            const uint32_t a0 = *reinterpret_cast<const uint32_t*>(alo[i] + k);
-            const uint32_t a1 = *reinterpret_cast<const uint32_t*>(alo[i] + 8 * KP + k);
-            const uint32_t a2 = *reinterpret_cast<const uint32_t*>(alo[i] + k + 16);
-            const uint32_t a3 = *reinterpret_cast<const uint32_t*>(alo[i] + 8 * KP + k + 16);
-            const uint32_t b0 = *reinterpret_cast<const uint32_t*>(b[i] + k);
-            const uint32_t b1 = *reinterpret_cast<const uint32_t*>(b[i] + k + 16);
-            asm volatile(
-                "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                "{%0,%1,%2,%3};"
-                : "+r"(c[i][0]), "+r"(c[i][1]), "+r"(c[i][2]), "+r"(c[i][3])
-                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+            const uint4 lo = *reinterpret_cast<const uint4*>(alo[i] + k + 16 * t);
+            const uint4 hi = *reinterpret_cast<const uint4*>(alo[i] + 8 * KP + k + 16 * t);
+            const uint4 bb = *reinterpret_cast<const uint4*>(b[i] + k + 16 * t);
+            mma(c[i], lo.x, hi.x, lo.y, hi.y, bb.x, bb.y);
+            mma(c[i], lo.z, hi.z, lo.w, hi.w, bb.z, bb.w);
+        }
+    }
+    if (k < K) {  // the last 32 bytes: 8 a lane
+#pragma unroll
+        for (int i = 0; i < NT; i++) {
+            const uint2 lo = *reinterpret_cast<const uint2*>(alo[i] + k + 8 * t);
+            const uint2 hi = *reinterpret_cast<const uint2*>(alo[i] + 8 * KP + k + 8 * t);
+            const uint2 bb = *reinterpret_cast<const uint2*>(b[i] + k + 8 * t);
+            mma(c[i], lo.x, hi.x, lo.y, hi.y, bb.x, bb.y);
         }
     }
 }
@@ -459,32 +501,34 @@ __device__ __forceinline__ float one_block(int s, float d, float ws, bool has_bi
 }
 
 struct PsShared {
-    uint8_t* base;  // the dynamic area
-    uint32_t* pred;  // [S] whose prediction steps this round
-    uint32_t* act;   // [S] still searching
+    uint8_t* base;    // the dynamic area
+    uint32_t* plist;  // [np] the segments whose prediction steps this round, in order
+    uint32_t* alist;  // [na] the segments still searching, in order
+    uint32_t np, na;
 };
 
-// Layer l's gates and cells for the segments whose prediction steps.
+// Layer l's gates and cells for the segments whose prediction steps, as
+// the columns of its products (column c: segment plist[c]).
 template <int RM>
 __device__ void ps_gates(const TdtArgs& a, const TdtPersist& p, uint32_t l, const PsShared& sh) {
-    const uint32_t S = a.S, P = a.P, Spad = (S + 7) & ~7u, KP = P + 16, njobs = P / 8;
+    const uint32_t S = a.S, P = a.P, n = sh.np, npad = (n + 7) & ~7u, KP = ps_pitch(P), njobs = P / 8;
     if (blockIdx.x >= njobs) return;  // the CTA's uniform choice
-    int8_t* x0 = reinterpret_cast<int8_t*>(sh.base);  // [Spad][KP] the layer's input
-    int8_t* x1 = x0 + Spad * KP;                       // [Spad][KP] its h of the last step
-    int8_t* wxs = x1 + Spad * KP;                      // [32][KP] the job's rows of wx
+    int8_t* x0 = reinterpret_cast<int8_t*>(sh.base);  // [npad][KP] the layer's input
+    int8_t* x1 = x0 + npad * KP;                       // [npad][KP] its h of the last step
+    int8_t* wxs = x1 + npad * KP;                      // [32][KP] the job's rows of wx
     int8_t* whs = wxs + PS_ROWS * KP;                  // [32][KP] of wh
-    float* gsm = reinterpret_cast<float*>(whs + PS_ROWS * KP);  // [32][Spad] the gates
-    float* d0 = gsm + PS_ROWS * Spad;                  // [Spad] the inputs' scales
-    float* d1 = d0 + Spad;                             // [Spad] the last h's
-    float* vs = d1 + Spad;                             // [3][32] the job's wxs, whs, lb
+    float* gsm = reinterpret_cast<float*>(whs + PS_ROWS * KP);  // [32][npad] the gates
+    float* d0 = gsm + PS_ROWS * npad;                  // [npad] the inputs' scales
+    float* d1 = d0 + npad;                             // [npad] the last h's
+    float* vs = d1 + npad;                             // [3][32] the job's wxs, whs, lb
     const int8_t* qin = l ? a.qh + static_cast<size_t>(l - 1) * S * P : a.qx;
     const float* din = l ? a.dh + static_cast<size_t>(l - 1) * S : a.dx;
     const int8_t* qhl = a.qh + static_cast<size_t>(l) * S * P;
     const float* dhl = a.dh + static_cast<size_t>(l) * S;
-    stage_inputs(x0, qin, S, Spad, P);
-    stage_inputs(x1, qhl, S, Spad, P);
-    stage_scales(d0, din, S);
-    stage_scales(d1, dhl, S);
+    stage_inputs(x0, qin, sh.plist, n, npad, P);
+    stage_inputs(x1, qhl, sh.plist, n, npad, P);
+    stage_scales(d0, din, sh.plist, n);
+    stage_scales(d1, dhl, sh.plist, n);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, rt = warp & 1;
     for (uint32_t job = blockIdx.x; job < njobs; job += gridDim.x) {
         const uint32_t j0 = 8 * job;
@@ -499,54 +543,44 @@ __device__ void ps_gates(const TdtArgs& a, const TdtPersist& p, uint32_t l, cons
             vs[PS_ROWS + threadIdx.x] = __ldg(p.whs[l] + r);
             vs[2 * PS_ROWS + threadIdx.x] = __ldg(p.lb[l] + r);
         }
+        // cell i (below) is unit j0 + i % 8 of column i / 8; the old c of
+        // this thread's first two, loaded while the copies land
+        auto cell_at = [&](uint32_t i) { return (static_cast<size_t>(l) * S + sh.plist[i >> 3]) * P + j0 + (i & 7); };
+        float cpre0 = 0.0f, cpre1 = 0.0f;
+        if (threadIdx.x < 8 * n) cpre0 = __ldcg(a.c + cell_at(threadIdx.x));
+        if (threadIdx.x + blockDim.x < 8 * n) cpre1 = __ldcg(a.c + cell_at(threadIdx.x + blockDim.x));
         staged();
-        const uint32_t sg0 = warp >> 1;
-        if (sg0 < Spad / 8) {
-            // the warp's two segment groups (the second may be past the last)
-            const uint32_t sg1 = sg0 + 4 < Spad / 8 ? sg0 + 4 : sg0;
+        // a warp: one row tile, column groups sg0, sg0 + 4, sg0 + 8, ...
+        for (uint32_t sg = warp >> 1; sg < npad / 8; sg += 8) {
+            const uint32_t sg1 = sg + 4 < npad / 8 ? sg + 4 : sg;
             int c[4][4];
-            mma_rows<4>(c, {wxs, whs, wxs, whs}, {x0, x1, x0, x1}, {sg0, sg0, sg1, sg1}, rt, P);
+            mma_rows<4>(c, {wxs, whs, wxs, whs}, {x0, x1, x0, x1}, {sg, sg, sg1, sg1}, rt, P);
 #pragma unroll
             for (int h = 0; h < 2; h++) {
-                if (h == 1 && sg1 == sg0) break;
-                const uint32_t sg = h ? sg1 : sg0;
+                if (h == 1 && sg1 == sg) break;
+                const uint32_t g = h ? sg1 : sg;
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
-                    const uint32_t lr = 16 * rt + (lane >> 2) + 8 * (e >> 1), sgm = 8 * sg + 2 * (lane & 3) + (e & 1);
-                    if (sgm < S && sh.pred[sgm]) {
+                    const uint32_t lr = 16 * rt + (lane >> 2) + 8 * (e >> 1), col = 8 * g + 2 * (lane & 3) + (e & 1);
+                    if (col < n) {
                         // gates = wx x + lb, then + wh h (the reference's two products, the second added)
-                        const float gx = one_block<RM>(c[2 * h][e], d0[sgm], vs[lr], true, vs[2 * PS_ROWS + lr]);
-                        const float gh = one_block<RM>(c[2 * h + 1][e], d1[sgm], vs[PS_ROWS + lr], false, 0.0f);
-                        gsm[lr * Spad + sgm] = add_r<RM>(gx, gh);
+                        const float gx = one_block<RM>(c[2 * h][e], d0[col], vs[lr], true, vs[2 * PS_ROWS + lr]);
+                        const float gh = one_block<RM>(c[2 * h + 1][e], d1[col], vs[PS_ROWS + lr], false, 0.0f);
+                        gsm[lr * npad + col] = add_r<RM>(gx, gh);
                     }
-                }
-            }
-        }
-        // the warps' remaining segment groups (more than 64 segments)
-        for (uint32_t sg = sg0 + 8; sg < Spad / 8; sg += 4) {
-            int c[2][4];
-            mma_rows<2>(c, {wxs, whs}, {x0, x1}, {sg, sg}, rt, P);
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const uint32_t lr = 16 * rt + (lane >> 2) + 8 * (e >> 1), sgm = 8 * sg + 2 * (lane & 3) + (e & 1);
-                if (sgm < S && sh.pred[sgm]) {
-                    const float gx = one_block<RM>(c[0][e], d0[sgm], vs[lr], true, vs[2 * PS_ROWS + lr]);
-                    const float gh = one_block<RM>(c[1][e], d1[sgm], vs[PS_ROWS + lr], false, 0.0f);
-                    gsm[lr * Spad + sgm] = add_r<RM>(gx, gh);
                 }
             }
         }
         __syncthreads();
         // k_lstm's cell for units j0..j0+7
-        for (uint32_t i = threadIdx.x; i < 8 * S; i += blockDim.x) {
-            const uint32_t u = i & 7, sg = i >> 3;
-            if (!sh.pred[sg]) continue;
-            const size_t at = (static_cast<size_t>(l) * S + sg) * P + j0 + u;
-            const float cold = __ldcg(a.c + at);
-            const float ig = pk_sigmoid<RM>(gsm[u * Spad + sg]);
-            const float fg = pk_sigmoid<RM>(gsm[(8 + u) * Spad + sg]);
-            const float ug = pk_tanh<RM>(gsm[(16 + u) * Spad + sg]);
-            const float og = pk_sigmoid<RM>(gsm[(24 + u) * Spad + sg]);
+        for (uint32_t i = threadIdx.x, q = 0; i < 8 * n; i += blockDim.x, q++) {
+            const uint32_t u = i & 7, col = i >> 3;
+            const size_t at = cell_at(i);
+            const float cold = q == 0 ? cpre0 : q == 1 ? cpre1 : __ldcg(a.c + at);
+            const float ig = pk_sigmoid<RM>(gsm[u * npad + col]);
+            const float fg = pk_sigmoid<RM>(gsm[(8 + u) * npad + col]);
+            const float ug = pk_tanh<RM>(gsm[(16 + u) * npad + col]);
+            const float og = pk_sigmoid<RM>(gsm[(24 + u) * npad + col]);
             const float cj = add_r<RM>(mul_r<RM>(fg, cold), mul_r<RM>(ig, ug));
             a.c[at] = cj;
             a.h[at] = mul_r<RM>(og, pk_tanh<RM>(cj));
@@ -559,9 +593,8 @@ template <int RM>
 __device__ void ps_quant_h(const TdtArgs& a, uint32_t l, const PsShared& sh, uint32_t* red) {
     const uint32_t S = a.S, P = a.P;
     float* hs = reinterpret_cast<float*>(sh.base);
-    for (uint32_t s = blockIdx.x; s < S; s += gridDim.x) {
-        if (!sh.pred[s]) continue;  // uniform
-        const size_t row = static_cast<size_t>(l) * S + s;
+    for (uint32_t i = blockIdx.x; i < sh.np; i += gridDim.x) {
+        const size_t row = static_cast<size_t>(l) * S + sh.plist[i];
         for (uint32_t j = threadIdx.x; j < P; j += blockDim.x) hs[j] = __ldcg(a.h + row * P + j);
         __syncthreads();
         quant_row<RM>(a.qh + row * P, a.dh + row, hs, P, red);
@@ -569,22 +602,22 @@ __device__ void ps_quant_h(const TdtArgs& a, uint32_t l, const PsShared& sh, uin
     }
 }
 
-// A product of PS_ROWS rows a job against every segment's input x [S][K]
-// (scales d), for the segments `want` marks: out[s * os + r] =
+// A product of PS_ROWS rows a job against the inputs x [S][K] (scales d) of
+// the n segments list names, as its columns: out[list[c] * os + r] =
 // one_block(...). Rows past `rows` are not written. A CTA stages the
 // inputs and the weights of two of its jobs at once.
 template <int RM>
 __device__ void ps_product(const int8_t* w, const float* ws, const float* bias, uint32_t rows, uint32_t K,
-                           const int8_t* x, const float* d, uint32_t S, const uint32_t* want, float* out, size_t os,
+                           const int8_t* x, const float* d, const uint32_t* list, uint32_t n, float* out, size_t os,
                            const PsShared& sh) {
-    const uint32_t Spad = (S + 7) & ~7u, KP = K + 16, njobs = (rows + PS_ROWS - 1) / PS_ROWS;
-    if (blockIdx.x >= njobs) return;  // uniform
-    int8_t* xs = reinterpret_cast<int8_t*>(sh.base);  // [Spad][KP]
-    int8_t* wsm = xs + Spad * KP;                     // [2][32][KP]
-    float* ds = reinterpret_cast<float*>(wsm + 2 * PS_ROWS * KP);  // [Spad]
-    float* vs = ds + Spad;                            // [2][2][32] row scales, biases
-    stage_inputs(xs, x, S, Spad, K);
-    stage_scales(ds, d, S);
+    const uint32_t npad = (n + 7) & ~7u, KP = ps_pitch(K), njobs = (rows + PS_ROWS - 1) / PS_ROWS;
+    if (blockIdx.x >= njobs || !n) return;  // uniform
+    int8_t* xs = reinterpret_cast<int8_t*>(sh.base);  // [npad][KP]
+    int8_t* wsm = xs + npad * KP;                     // [2][32][KP]
+    float* ds = reinterpret_cast<float*>(wsm + 2 * PS_ROWS * KP);  // [npad]
+    float* vs = ds + npad;                            // [2][2][32] row scales, biases
+    stage_inputs(xs, x, list, n, npad, K);
+    stage_scales(ds, d, list, n);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, rt = warp & 1;
     for (uint32_t job = blockIdx.x; job < njobs; job += 2 * gridDim.x) {
         const uint32_t job2 = job + gridDim.x, nj = job2 < njobs ? 2 : 1;
@@ -603,8 +636,8 @@ __device__ void ps_product(const int8_t* w, const float* ws, const float* bias, 
             const uint32_t r0 = PS_ROWS * (k ? job2 : job);
             const int8_t* W = wsm + k * PS_ROWS * KP;
             const float* v = vs + k * 2 * PS_ROWS;
-            for (uint32_t sg = warp >> 1; sg < Spad / 8; sg += 8) {
-                const uint32_t sg1 = sg + 4 < Spad / 8 ? sg + 4 : sg;
+            for (uint32_t sg = warp >> 1; sg < npad / 8; sg += 8) {
+                const uint32_t sg1 = sg + 4 < npad / 8 ? sg + 4 : sg;
                 int c[2][4];
                 mma_rows<2>(c, {W, W}, {xs, xs}, {sg, sg1}, rt, K);
 #pragma unroll
@@ -614,9 +647,10 @@ __device__ void ps_product(const int8_t* w, const float* ws, const float* bias, 
 #pragma unroll
                     for (int e = 0; e < 4; e++) {
                         const uint32_t lr = 16 * rt + (lane >> 2) + 8 * (e >> 1), r = r0 + lr;
-                        const uint32_t sgm = 8 * g + 2 * (lane & 3) + (e & 1);
-                        if (r < rows && sgm < S && want[sgm])
-                            out[sgm * os + r] = one_block<RM>(c[h][e], ds[sgm], v[lr], bias != nullptr, v[PS_ROWS + lr]);
+                        const uint32_t col = 8 * g + 2 * (lane & 3) + (e & 1);
+                        if (r < rows && col < n)
+                            out[list[col] * os + r] =
+                                one_block<RM>(c[h][e], ds[col], v[lr], bias != nullptr, v[PS_ROWS + lr]);
                     }
                 }
             }
@@ -628,32 +662,44 @@ template <int RM>
 __global__ void __launch_bounds__(TD_THREADS, 1) tdt_persist(TdtArgs a, TdtPersist p) {
     extern __shared__ __align__(16) uint8_t ps_smem[];
     __shared__ uint32_t red[TD_THREADS / 32];
-    __shared__ uint32_t s_any_act, s_any_pred;
+    __shared__ uint32_t s_np, s_na;
     const uint32_t S = a.S, P = a.P, J = a.J;
     PsShared sh;
-    sh.pred = reinterpret_cast<uint32_t*>(ps_smem);
-    sh.act = sh.pred + S;
+    sh.plist = reinterpret_cast<uint32_t*>(ps_smem);
+    sh.alist = sh.plist + S;
     sh.base = ps_smem + ((8 * static_cast<size_t>(S) + 15) & ~size_t(15));
     uint32_t epoch = 0;
     for (uint32_t round = 0; round < p.max_rounds; round++) {
-        // every CTA reads the same states: the last writes to them came
-        // before the barrier that ended the last round
-        if (threadIdx.x == 0) {
-            s_any_act = 0;
-            s_any_pred = 0;
+        // every CTA reads the same states (the last writes to them came
+        // before the barrier that ended the last round) and lists the
+        // segments still searching and those whose prediction steps, in order
+        if (threadIdx.x < 32) {
+            uint32_t np = 0, na = 0;
+            for (uint32_t s0 = 0; s0 < S; s0 += 32) {
+                const uint32_t s = s0 + threadIdx.x;
+                uint32_t act = 0, pred = 0;
+                if (s < S) {
+                    volatile TdtSeg* g = reinterpret_cast<volatile TdtSeg*>(a.seg) + s;
+                    act = g->active;
+                    pred = act && g->pred;
+                }
+                const uint32_t ma = __ballot_sync(0xffffffffu, act), mp = __ballot_sync(0xffffffffu, pred);
+                const uint32_t below = (1u << threadIdx.x) - 1;
+                if (act) sh.alist[na + __popc(ma & below)] = s;
+                if (pred) sh.plist[np + __popc(mp & below)] = s;
+                na += __popc(ma);
+                np += __popc(mp);
+            }
+            if (threadIdx.x == 0) {
+                s_np = np;
+                s_na = na;
+            }
         }
         __syncthreads();
-        for (uint32_t s = threadIdx.x; s < S; s += blockDim.x) {
-            volatile TdtSeg* g = reinterpret_cast<volatile TdtSeg*>(a.seg) + s;
-            const uint32_t act = g->active, pred = act && g->pred;
-            sh.act[s] = act;
-            sh.pred[s] = pred;
-            if (act) atomicOr(&s_any_act, 1u);
-            if (pred) atomicOr(&s_any_pred, 1u);
-        }
-        __syncthreads();
-        if (!s_any_act) break;  // every search has ended (the grid's uniform choice)
-        if (s_any_pred) {
+        sh.np = s_np;
+        sh.na = s_na;
+        if (!sh.na) break;  // every search has ended (the grid's uniform choice)
+        if (sh.np) {
             for (uint32_t l = 0; l < p.L; l++) {
                 ps_gates<RM>(a, p, l, sh);
                 if (!grid_barrier(p, epoch)) return;
@@ -661,17 +707,20 @@ __global__ void __launch_bounds__(TD_THREADS, 1) tdt_persist(TdtArgs a, TdtPersi
                 if (!grid_barrier(p, epoch)) return;
             }
             const size_t top = static_cast<size_t>(p.L - 1) * S;
-            ps_product<RM>(p.jpred, p.jpreds, p.jpredb, J, P, a.qh + top * P, a.dh + top, S, sh.pred, a.gpn, J, sh);
+            ps_product<RM>(p.jpred, p.jpreds, p.jpredb, J, P, a.qh + top * P, a.dh + top, sh.plist, sh.np, a.gpn, J,
+                           sh);
             if (!grid_barrier(p, epoch)) return;
         }
-        for (uint32_t s = blockIdx.x; s < S; s += gridDim.x) {
-            joint_in_seg<RM>(a, s, reinterpret_cast<float*>(sh.base), red);
+        // the joint's input of every running segment (a segment whose
+        // prediction steps is running)
+        for (uint32_t i = blockIdx.x; i < sh.na; i += gridDim.x) {
+            joint_in_seg<RM>(a, sh.alist[i], reinterpret_cast<float*>(sh.base), red);
             __syncthreads();
         }
         if (!grid_barrier(p, epoch)) return;
-        ps_product<RM>(p.jout, p.jouts, p.joutb, a.nout, J, a.qz, a.dz, S, sh.act, a.logits, a.nout, sh);
+        ps_product<RM>(p.jout, p.jouts, p.joutb, a.nout, J, a.qz, a.dz, sh.alist, sh.na, a.logits, a.nout, sh);
         if (!grid_barrier(p, epoch)) return;
-        for (uint32_t s = blockIdx.x; s < S; s += gridDim.x) step_seg(a, s);
+        for (uint32_t i = blockIdx.x; i < sh.na; i += gridDim.x) step_seg(a, sh.alist[i]);
         if (!grid_barrier(p, epoch)) return;
     }
 }
@@ -711,7 +760,7 @@ cudaError_t launch_tdt(const TdtArgs& a, int phase, uint32_t l, int rmode, cudaS
 size_t tdt_seg_bytes() { return sizeof(TdtSeg); }
 
 size_t tdt_persist_smem(const TdtArgs& a, size_t smem_max) {
-    const size_t S = a.S, Spad = (S + 7) & ~size_t(7), KP = a.P + 16, KJ = a.J + 16;
+    const size_t S = a.S, Spad = (S + 7) & ~size_t(7), KP = ps_pitch(a.P), KJ = ps_pitch(a.J);
     // gates: inputs and last h, the job's rows of wx and wh, the gates, two scale vectors, the job's vectors
     size_t need = 2 * Spad * KP + 2 * PS_ROWS * KP + 4 * PS_ROWS * Spad + 8 * Spad + 12 * PS_ROWS;
     // jpred, jout: inputs, two jobs' rows, the scales, the jobs' vectors
