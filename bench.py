@@ -24,9 +24,9 @@ is whole-job int8 TOPS (2*M*N*K summed over the products, over every rank);
 audio-seconds per second is reported beside it. Multi-GPU: one process per
 GPU (torchrun), segments partitioned across the GPUs with no collective on
 the data path; the time is the max over ranks, the work the sum. Weak
-scaling (the default): every GPU takes a batch of 64 segments of its own, so
-the work per GPU is fixed as the GPUs are added (at 1 GPU the batch is the
-same one strong scaling splits). `--scaling strong`: the one batch of 64
+scaling (the default): every GPU takes configs[3]'s batch of 64 segments
+(the same seeded lengths on each), so the work per GPU is fixed as the GPUs
+are added. `--scaling strong`: the one batch of 64
 segments is dealt across the GPUs longest first, so each GPU's share shrinks
 as 1/N (at 8 GPUs about 1,440 frames a GPU, where an N = 1024 product has 96
 tiles of 128 x 128 for 148 SMs). The long-form workload always
@@ -122,14 +122,16 @@ def partition(segs, world: int) -> list[list[int]]:
 
 
 def segments(rank: int, world: int = 1, scaling: str = "weak") -> list[tuple[float, int, int, int]]:
-    """The rank's segments. Strong scaling (configs[3]: one batch of 64
-    segments partitioned across the GPUs): the rank's share of the one draw.
-    Weak scaling: a draw of 64 of its own."""
+    """The rank's segments. Weak scaling: configs[3]'s batch of 64 segments
+    on every GPU (the same seeded lengths, so each GPU's work is the same and
+    fixed as GPUs are added; per-rank draws would make the job's time the
+    largest draw's, up to 6 % more work than the mean at 8 GPUs). Strong
+    scaling: the rank's share of the one batch, partitioned across the GPUs."""
     if WORKLOAD == "longform":
         segs = longform_chunks()
         return [segs[i] for i in partition(segs, world)[rank]]
     if scaling == "weak":
-        return draw_segments(SEED + rank)
+        return draw_segments(SEED)
     segs = draw_segments(SEED)
     return [segs[i] for i in partition(segs, world)[rank]]
 
@@ -1521,7 +1523,7 @@ def run_ours(args) -> None:
     else:
         workload = (("configs[3] batched encoder: one batch of 64 segments of 2-30 s dealt across the "
                      "GPUs longest first" if args.scaling == "strong" else
-                     "configs[3] batched encoder, weak scaling: 64 segments of 2-30 s per GPU") +
+                     "configs[3] batched encoder, weak scaling: the batch of 64 segments of 2-30 s on every GPU") +
                     ", 24 layers x 11 products + 3 subsampling products, 196 quantizations (q, k, v share "
                     f"one input; the position input is quantized once), qb {QB}")
     line = {
@@ -1759,7 +1761,7 @@ def main() -> None:
     ap.add_argument("--no-producers", action="store_true", help="skip timing the fused producers (rank 0)")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--scaling", choices=["strong", "weak"], default="weak",
-                    help="weak: a batch of 64 segments per GPU (configs[3] on every GPU); "
+                    help="weak: configs[3]'s batch of 64 segments on every GPU; "
                          "strong: the one batch of 64 segments split across the GPUs")
     ap.add_argument("--kernel-only", action="store_true",
                     help="only the dominant product (FF up at the batch's M), 3 launches: the ncu capture's case")

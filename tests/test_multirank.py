@@ -2,7 +2,7 @@
 
 The benchmark partitions the batched encoder by rank with no collective on
 the data path: the batch of 64 segments is dealt across the ranks longest
-first (strong scaling; with weak scaling every rank draws 64 of its own) and
+first (strong scaling; with weak scaling every rank takes the whole batch) and
 each rank runs its share on its own GPU; the job's figures come from one
 reduction at the end, the time as the max over ranks and the work (int8
 ops, audio seconds) as the sum. These tests run exactly that host code
@@ -97,12 +97,15 @@ def test_partition_at_every_width():
         assert max(loads) - min(loads) <= max(s[3] for s in segs)
 
 
-def test_weak_scaling_each_rank_its_own_segments(two_ranks_weak):
+def test_weak_scaling_every_rank_the_whole_batch(two_ranks_weak):
     a, b = two_ranks_weak
     assert len(a["frames"]) == bench.SEGMENTS and len(b["frames"]) == bench.SEGMENTS
-    assert a["frames"] != b["frames"]
-    # the draw is the rank's alone: the same rank draws the same segments again
-    assert [s[3] for s in bench.segments(1, 2, "weak")] == b["frames"]
+    # every GPU the same batch: the work a GPU is the same at every world size
+    assert a["frames"] == b["frames"] == [s[3] for s in bench.draw_segments(bench.SEED)]
+    assert a["ops"] == b["ops"]
+    # and the job's work is the world size times one batch's
+    one = bench.step_ops(bench.products(bench.draw_segments(bench.SEED)))
+    assert a["totals"][1] == pytest.approx(2 * one, rel=1e-12)
 
 
 def test_job_totals_max_time_sum_work(two_ranks):
