@@ -1741,6 +1741,32 @@ def run_attention_only() -> None:
                       "launches": P.launch_count(), "device_errors": P.device_errors(0)}))
 
 
+def run_decoder_only() -> None:
+    """TDT's search over the batch's 64 segments on the device, once (the ncu
+    capture's case: the search as one cooperative launch, after the
+    embedding's quantization and the states' set-up)."""
+    import torch
+    import libpktito_b200 as P
+    torch.cuda.set_device(0)
+    segs = segments(0)
+    m = tdt_model_synthetic()
+    t, keep = tdt_device_model(torch, P, m)
+    Ts = np.array([sg[3] for sg in segs], np.uint32)
+    f0 = np.concatenate([[0], np.cumsum(Ts)[:-1]]).astype(np.uint32)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED + 77)
+    f = 2.0 * torch.randn(int(Ts.sum() + 1) * m["J"], device="cuda", generator=g)
+    S, cap = len(Ts), int(Ts.max()) * (m["max_symbols"] + 1) + 8
+    toks = torch.empty(S * cap * 3, dtype=torch.int32, device="cuda")
+    ntok = torch.empty(S, dtype=torch.int32, device="cuda")
+    work = torch.empty(P.tdt_work_bytes(t, S) // 4 + 64, device="cuda")
+    P.tdt_search_dev(t, f, f0, Ts, toks, ntok, cap, work)
+    torch.cuda.synchronize()
+    print(json.dumps({"decoder_only": f"{S} segments, {int(Ts.sum())} frames", "rounds": P.tdt_last_rounds(),
+                      "tokens": int(ntok.sum().item()), "launches": P.launch_count(),
+                      "device_errors": P.device_errors(0)}))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -1767,6 +1793,8 @@ def main() -> None:
                     help="only the dominant product (FF up at the batch's M), 3 launches: the ncu capture's case")
     ap.add_argument("--producers-only", action="store_true",
                     help="only the fused producers at the batch's frame count, 2 launches each: the ncu capture's case")
+    ap.add_argument("--decoder-only", action="store_true",
+                    help="TDT's search over the batch once and exit (for an ncu capture of the search)")
     ap.add_argument("--attention-only", action="store_true",
                     help="only one layer's attention over the batch, 1 launch: the ncu capture's case")
     ap.add_argument("--panels-only", action="store_true",
@@ -1784,6 +1812,8 @@ def main() -> None:
         run_producers_only()
     elif args.attention_only:
         run_attention_only()
+    elif args.decoder_only:
+        run_decoder_only()
     elif args.impl == "reference":
         run_reference(args)
     else:
