@@ -89,8 +89,8 @@ constexpr int EPI_BYTES = EPI_WARPS * 32 * EPI_PITCH * 4 > EPI_WARPS * EPI_HALVE
                               ? EPI_WARPS * 32 * EPI_PITCH * 4
                               : EPI_WARPS * EPI_HALVES * STG_BYTES;
 constexpr int CHUNK = 4;           // blocks a turn of the TMEM ring
-constexpr int DBLK = 8;            // blocks of scales a TMA box of d carries (32 bytes a frame)
-constexpr int NDS = 4;             // slots of the scales ring (24 blocks ahead)
+constexpr int DBLK = 16;           // blocks of scales a TMA box of d carries (64 bytes a frame)
+constexpr int NDS = 2;             // slots of the scales ring (16 blocks ahead)
 constexpr int DS_BYTES = BM * DBLK * 4;
 constexpr int WS_BYTES = 2 * BN * 4;  // a tile's row scales, then its biases
 constexpr int NWS = 2;             // slots of their ring (a tile each)
@@ -578,7 +578,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
             if constexpr (DRING) {
                 // four blocks an iteration, two pairs; the frame's four scales
-                // one 16-byte shared load out of the chunk of eight blocks
+                // one 16-byte shared load out of the chunk of DBLK blocks
                 // the scales ring holds (one wait a chunk)
                 for (uint32_t b = 0; b < nb; b += CHUNK) {
                     const uint32_t ds = dcnt % NDS;
