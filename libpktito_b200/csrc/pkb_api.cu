@@ -560,7 +560,7 @@ int attention_dev(cudaStream_t stream, bool panels, float* o, size_t os, const f
 
 // The work area's pieces, 256-byte aligned, in the order TdtArgs lists them.
 struct TdtLayout {
-    size_t seg, T, f0, qembed, dembed, qx, dx, h, c, qh, dh, gates, gp, gpn, qz, dz, logits, bar, total;
+    size_t seg, T, f0, qembed, dembed, qx, dx, h, c, qh, dh, gates, gp, gpn, qz, dz, logits, keys, bar, total;
 };
 
 TdtLayout tdt_layout(const pkb_tdt_model& m, uint32_t S) {
@@ -589,7 +589,8 @@ TdtLayout tdt_layout(const pkb_tdt_model& m, uint32_t S) {
     o.qz = take(S * J);
     o.dz = take(S * 4);
     o.logits = take(S * size_t(m.n_out_pad) * 4);
-    o.bar = take(8);  // the persistent search's barrier count and abort flag
+    o.keys = take(2 * S * 2 * 8);  // the persistent search's argmax keys, two rounds' worth
+    o.bar = take(8);  // its barrier count and abort flag
     o.total = at;
     return o;
 }
@@ -796,6 +797,7 @@ int tdt_search_dev(cudaStream_t caller, const pkb_tdt_model* m, const float* f, 
         pp.jout = m->jout;
         pp.jouts = m->jouts;
         pp.joutb = m->joutb;
+        pp.keys = reinterpret_cast<unsigned long long*>(w + o.keys);
         pp.bar = reinterpret_cast<unsigned*>(w + o.bar);
         pp.abort = reinterpret_cast<int*>(w + o.bar + 4);
         pp.err = dev->err;

@@ -191,6 +191,7 @@ struct TdtPersist {
     const float *jpreds, *jpredb;
     const int8_t* jout;   // [nout][J]
     const float *jouts, *joutb;
+    unsigned long long* keys;  // [2][S][2] each running segment's best token and duration (jout's, by round parity)
     unsigned* bar;        // arrivals at the grid's barriers (zero at launch)
     int* abort;           // set by a CTA whose wait gave up (zero at launch)
     uint32_t* err;        // the device error word

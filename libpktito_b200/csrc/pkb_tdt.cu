@@ -395,17 +395,17 @@ __host__ __device__ __forceinline__ uint32_t ps_pitch(uint32_t K) {
     return 16 * (u + ((4u - u % 8u) & 7u));
 }
 
-// The quantized inputs [K] of n segments, segment list[i] as row i
-// (written by other CTAs: copied through L2 by cp.async.cg), into shared
-// memory ps_pitch(K) bytes apart, rows n..npad-1 zeros. The copies are only
+// n rows of K quantized inputs, row c from src(c) (written by other CTAs or
+// before the launch: copied through L2 by cp.async.cg), into shared memory
+// ps_pitch(K) bytes apart, rows n..npad-1 zeros. The copies are only
 // issued: the caller commits and waits.
-__device__ void stage_inputs(int8_t* dst, const int8_t* x, const uint32_t* list, uint32_t n, uint32_t npad,
-                             uint32_t K) {
+template <typename Src>
+__device__ void stage_inputs(int8_t* dst, Src src, uint32_t n, uint32_t npad, uint32_t K) {
     const uint32_t per = K / 16, KP = ps_pitch(K);
     for (uint32_t i = threadIdx.x; i < npad * per; i += blockDim.x) {
         const uint32_t c = i / per, u = i % per;
         if (c < n)
-            cp_async16(dst + c * KP + u * 16, x + static_cast<size_t>(list[c]) * K + u * 16);
+            cp_async16(dst + c * KP + u * 16, src(c) + u * 16);
         else
             *reinterpret_cast<int4*>(dst + c * KP + u * 16) = make_int4(0, 0, 0, 0);
     }
@@ -425,9 +425,10 @@ __device__ void stage_weights(int8_t* dst, const int8_t* w, uint32_t K, uint32_t
     }
 }
 
-// The scales of the n listed segments (written by other CTAs) into shared memory.
-__device__ __forceinline__ void stage_scales(float* dst, const float* d, const uint32_t* list, uint32_t n) {
-    for (uint32_t c = threadIdx.x; c < n; c += blockDim.x) dst[c] = __ldcg(d + list[c]);
+// n scales, scale c at *src(c) (written by other CTAs: through L2), into shared memory.
+template <typename Src>
+__device__ __forceinline__ void stage_scales(float* dst, Src src, uint32_t n) {
+    for (uint32_t c = threadIdx.x; c < n; c += blockDim.x) dst[c] = __ldcg(src(c));
 }
 
 // Everything staged by this thread's copies has landed, for every thread.
@@ -504,11 +505,14 @@ struct PsShared {
     uint8_t* base;    // the dynamic area
     uint32_t* plist;  // [np] the segments whose prediction steps this round, in order
     uint32_t* alist;  // [na] the segments still searching, in order
+    TdtSeg* st;       // [S] every segment's search state: each CTA's own copy, all updated alike
     uint32_t np, na;
 };
 
 // Layer l's gates and cells for the segments whose prediction steps, as
-// the columns of its products (column c: segment plist[c]).
+// the columns of its products (column c: segment plist[c]). Layer 0's
+// input is the embedding of the segment's label, quantized a row a block
+// once a call.
 template <int RM>
 __device__ void ps_gates(const TdtArgs& a, const TdtPersist& p, uint32_t l, const PsShared& sh) {
     const uint32_t S = a.S, P = a.P, n = sh.np, npad = (n + 7) & ~7u, KP = ps_pitch(P), njobs = P / 8;
@@ -521,14 +525,21 @@ __device__ void ps_gates(const TdtArgs& a, const TdtPersist& p, uint32_t l, cons
     float* d0 = gsm + PS_ROWS * npad;                  // [npad] the inputs' scales
     float* d1 = d0 + npad;                             // [npad] the last h's
     float* vs = d1 + npad;                             // [3][32] the job's wxs, whs, lb
-    const int8_t* qin = l ? a.qh + static_cast<size_t>(l - 1) * S * P : a.qx;
-    const float* din = l ? a.dh + static_cast<size_t>(l - 1) * S : a.dx;
+    const uint32_t* pl = sh.plist;
+    const TdtSeg* st = sh.st;
+    if (l == 0) {
+        stage_inputs(x0, [&](uint32_t c) { return a.qembed + static_cast<size_t>(st[pl[c]].label) * P; }, n, npad, P);
+        stage_scales(d0, [&](uint32_t c) { return a.dembed + st[pl[c]].label; }, n);
+    } else {
+        const int8_t* qin = a.qh + static_cast<size_t>(l - 1) * S * P;
+        const float* din = a.dh + static_cast<size_t>(l - 1) * S;
+        stage_inputs(x0, [&](uint32_t c) { return qin + static_cast<size_t>(pl[c]) * P; }, n, npad, P);
+        stage_scales(d0, [&](uint32_t c) { return din + pl[c]; }, n);
+    }
     const int8_t* qhl = a.qh + static_cast<size_t>(l) * S * P;
     const float* dhl = a.dh + static_cast<size_t>(l) * S;
-    stage_inputs(x0, qin, sh.plist, n, npad, P);
-    stage_inputs(x1, qhl, sh.plist, n, npad, P);
-    stage_scales(d0, din, sh.plist, n);
-    stage_scales(d1, dhl, sh.plist, n);
+    stage_inputs(x1, [&](uint32_t c) { return qhl + static_cast<size_t>(pl[c]) * P; }, n, npad, P);
+    stage_scales(d1, [&](uint32_t c) { return dhl + pl[c]; }, n);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, rt = warp & 1;
     for (uint32_t job = blockIdx.x; job < njobs; job += gridDim.x) {
         const uint32_t j0 = 8 * job;
@@ -545,12 +556,12 @@ __device__ void ps_gates(const TdtArgs& a, const TdtPersist& p, uint32_t l, cons
         }
         // cell i (below) is unit j0 + i % 8 of column i / 8; the old c of
         // this thread's first two, loaded while the copies land
-        auto cell_at = [&](uint32_t i) { return (static_cast<size_t>(l) * S + sh.plist[i >> 3]) * P + j0 + (i & 7); };
+        auto cell_at = [&](uint32_t i) { return (static_cast<size_t>(l) * S + pl[i >> 3]) * P + j0 + (i & 7); };
         float cpre0 = 0.0f, cpre1 = 0.0f;
         if (threadIdx.x < 8 * n) cpre0 = __ldcg(a.c + cell_at(threadIdx.x));
         if (threadIdx.x + blockDim.x < 8 * n) cpre1 = __ldcg(a.c + cell_at(threadIdx.x + blockDim.x));
         staged();
-        // a warp: one row tile, column groups sg0, sg0 + 4, sg0 + 8, ...
+        // a warp: one row tile, column groups sg, sg + 4, sg + 8, ...
         for (uint32_t sg = warp >> 1; sg < npad / 8; sg += 8) {
             const uint32_t sg1 = sg + 4 < npad / 8 ? sg + 4 : sg;
             int c[4][4];
@@ -602,22 +613,41 @@ __device__ void ps_quant_h(const TdtArgs& a, uint32_t l, const PsShared& sh, uin
     }
 }
 
+// The first largest of values compared as floats as one key that
+// atomicMax can combine: the larger value, and of equal ones (-0 and +0
+// equal) the lower index. The logits are finite.
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t i) {
+    uint32_t b = __float_as_uint(v == 0.0f ? 0.0f : v);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return (static_cast<unsigned long long>(b) << 32) | (0xFFFFFFFFu - i);
+}
+__device__ __forceinline__ uint32_t key_index(unsigned long long k) {
+    return 0xFFFFFFFFu - static_cast<uint32_t>(k);
+}
+
 // A product of PS_ROWS rows a job against the inputs x [S][K] (scales d) of
-// the n segments list names, as its columns: out[list[c] * os + r] =
-// one_block(...). Rows past `rows` are not written. A CTA stages the
-// inputs and the weights of two of its jobs at once.
+// the n segments list names, as its columns: one_block(...) of row r and
+// column c to out[list[c] * os + r] where out is given, and, where keys
+// is, into each column's two keys (keys[2 list[c]]: the first largest
+// token logit, rows 0..V; keys[2 list[c] + 1]: the first largest duration
+// logit, rows V+1..V+n_dur, its index counted from V+1), the CTA's columns
+// reduced in shared memory first. Rows past `rows` are skipped. A CTA
+// stages the inputs and the weights of two of its jobs at once.
 template <int RM>
 __device__ void ps_product(const int8_t* w, const float* ws, const float* bias, uint32_t rows, uint32_t K,
                            const int8_t* x, const float* d, const uint32_t* list, uint32_t n, float* out, size_t os,
-                           const PsShared& sh) {
+                           unsigned long long* keys, uint32_t V, uint32_t n_dur, const PsShared& sh) {
     const uint32_t npad = (n + 7) & ~7u, KP = ps_pitch(K), njobs = (rows + PS_ROWS - 1) / PS_ROWS;
     if (blockIdx.x >= njobs || !n) return;  // uniform
     int8_t* xs = reinterpret_cast<int8_t*>(sh.base);  // [npad][KP]
     int8_t* wsm = xs + npad * KP;                     // [2][32][KP]
     float* ds = reinterpret_cast<float*>(wsm + 2 * PS_ROWS * KP);  // [npad]
     float* vs = ds + npad;                            // [2][2][32] row scales, biases
-    stage_inputs(xs, x, list, n, npad, K);
-    stage_scales(ds, d, list, n);
+    unsigned long long* sk = reinterpret_cast<unsigned long long*>(vs + 4 * PS_ROWS);  // [npad][2] the keys
+    stage_inputs(xs, [&](uint32_t c) { return x + static_cast<size_t>(list[c]) * K; }, n, npad, K);
+    stage_scales(ds, [&](uint32_t c) { return d + list[c]; }, n);
+    if (keys)
+        for (uint32_t i = threadIdx.x; i < 2 * npad; i += blockDim.x) sk[i] = 0ull;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, rt = warp & 1;
     for (uint32_t job = blockIdx.x; job < njobs; job += 2 * gridDim.x) {
         const uint32_t job2 = job + gridDim.x, nj = job2 < njobs ? 2 : 1;
@@ -648,12 +678,83 @@ __device__ void ps_product(const int8_t* w, const float* ws, const float* bias, 
                     for (int e = 0; e < 4; e++) {
                         const uint32_t lr = 16 * rt + (lane >> 2) + 8 * (e >> 1), r = r0 + lr;
                         const uint32_t col = 8 * g + 2 * (lane & 3) + (e & 1);
-                        if (r < rows && col < n)
-                            out[list[col] * os + r] =
-                                one_block<RM>(c[h][e], ds[col], v[lr], bias != nullptr, v[PS_ROWS + lr]);
+                        if (r < rows && col < n) {
+                            const float y = one_block<RM>(c[h][e], ds[col], v[lr], bias != nullptr, v[PS_ROWS + lr]);
+                            if (out) out[list[col] * os + r] = y;
+                            if (keys) {
+                                if (r <= V)
+                                    atomicMax(&sk[2 * col], argmax_key(y, r));
+                                else if (r <= V + n_dur)
+                                    atomicMax(&sk[2 * col + 1], argmax_key(y, r - V - 1));
+                            }
+                        }
                     }
                 }
             }
+        }
+    }
+    if (keys) {
+        __syncthreads();
+        for (uint32_t i = threadIdx.x; i < 2 * n; i += blockDim.x)
+            if (sk[i]) atomicMax(keys + 2 * list[i >> 1] + (i & 1), sk[i]);
+    }
+}
+
+// The joint's input of running segment s (the whole CTA): relu(f_t + g),
+// g its prediction's jpred (just stepped where it emitted), quantized as
+// one block; zs J floats of shared memory.
+template <int RM>
+__device__ void ps_joint(const TdtArgs& a, uint32_t s, const TdtSeg& st, float* zs, uint32_t* red) {
+    const uint32_t J = a.J;
+    const bool fresh = st.pred;
+    float* gp = a.gp + static_cast<size_t>(s) * J;
+    const float* gn = a.gpn + static_cast<size_t>(s) * J;
+    const float* f = a.f + (static_cast<size_t>(a.f0[s]) + st.t) * J;
+    for (uint32_t j = threadIdx.x; j < J; j += blockDim.x) {
+        float gj;
+        if (fresh) {
+            gj = __ldcg(gn + j);
+            gp[j] = gj;
+        } else {
+            gj = __ldcg(gp + j);
+        }
+        const float v = add_r<RM>(f[j], gj);
+        zs[j] = v > 0.0f ? v : 0.0f;
+    }
+    __syncthreads();
+    quant_row<RM>(a.qz + static_cast<size_t>(s) * J, a.dz + s, zs, J, red);
+}
+
+// The search's step for segment s from its best token k and duration di
+// (tdt_step's, core/decoder.c:132-148) on state g; where `owner`, the token
+// is written out.
+__device__ __forceinline__ void ps_step(const TdtArgs& a, uint32_t s, TdtSeg& g, uint32_t k, uint32_t di, bool owner) {
+    const uint32_t t0 = g.t, dur = a.dur[di];
+    g.steps++;
+    if (k == a.V) {
+        g.t = t0 + (dur ? dur : 1);
+        if (g.t >= a.T[s]) g.active = 0;  // a blank ran off the end: the search stops
+    } else if (g.ntok == a.cap) {
+        g.over = 1;  // no room for the token: the call fails
+        g.active = 0;
+    } else {
+        if (owner) {
+            int32_t* tk = a.toks + (static_cast<size_t>(s) * a.cap + g.ntok) * 3;
+            tk[0] = static_cast<int32_t>(k);
+            tk[1] = static_cast<int32_t>(t0);
+            tk[2] = static_cast<int32_t>(dur);
+            a.ntok[s] = g.ntok + 1;
+        }
+        g.ntok++;
+        g.t = t0 + dur;
+        g.lasts = g.last == t0 ? g.lasts + 1 : 1;
+        g.last = t0;
+        if (g.lasts >= a.max_symbols && g.last == g.t) g.t++;
+        if (g.t >= a.T[s]) {
+            g.active = 0;  // its prediction would change nothing
+        } else {
+            g.pred = 1;
+            g.label = k;
         }
     }
 }
@@ -667,22 +768,37 @@ __global__ void __launch_bounds__(TD_THREADS, 1) tdt_persist(TdtArgs a, TdtPersi
     PsShared sh;
     sh.plist = reinterpret_cast<uint32_t*>(ps_smem);
     sh.alist = sh.plist + S;
-    sh.base = ps_smem + ((8 * static_cast<size_t>(S) + 15) & ~size_t(15));
+    sh.st = reinterpret_cast<TdtSeg*>(sh.alist + S);
+    sh.base = ps_smem + ((static_cast<size_t>(S) * (8 + sizeof(TdtSeg)) + 15) & ~size_t(15));
+    // every CTA's copy of the states, as tdt_init left them
+    for (uint32_t i = threadIdx.x; i < S * (sizeof(TdtSeg) / 4); i += blockDim.x)
+        reinterpret_cast<uint32_t*>(sh.st)[i] = reinterpret_cast<const uint32_t*>(a.seg)[i];
+    sh.na = 0;
     uint32_t epoch = 0;
     for (uint32_t round = 0; round < p.max_rounds; round++) {
-        // every CTA reads the same states (the last writes to them came
-        // before the barrier that ended the last round) and lists the
-        // segments still searching and those whose prediction steps, in order
+        __syncthreads();
+        if (round) {
+            // the last round's step, from its jout's keys, for each segment
+            // it ran: every CTA on its own copy, alike; the token written
+            // by the segment's owner CTA
+            const unsigned long long* kp = p.keys + ((round - 1) & 1) * 2 * S;
+            for (uint32_t i = threadIdx.x; i < sh.na; i += blockDim.x) {
+                const uint32_t s = sh.alist[i];
+                const uint32_t k = key_index(__ldcg(kp + 2 * s)), di = key_index(__ldcg(kp + 2 * s + 1));
+                ps_step(a, s, sh.st[s], k, di, s % gridDim.x == blockIdx.x);
+            }
+            __syncthreads();
+        }
+        // this round's jout keys start from zero (the buffer was last read at
+        // the start of the last round, two barriers ago at least)
+        if (blockIdx.x == 0)
+            for (uint32_t i = threadIdx.x; i < 2 * S; i += blockDim.x) p.keys[(round & 1) * 2 * S + i] = 0ull;
+        // the segments still searching and those whose prediction steps, in order
         if (threadIdx.x < 32) {
             uint32_t np = 0, na = 0;
             for (uint32_t s0 = 0; s0 < S; s0 += 32) {
                 const uint32_t s = s0 + threadIdx.x;
-                uint32_t act = 0, pred = 0;
-                if (s < S) {
-                    volatile TdtSeg* g = reinterpret_cast<volatile TdtSeg*>(a.seg) + s;
-                    act = g->active;
-                    pred = act && g->pred;
-                }
+                const uint32_t act = s < S && sh.st[s].active, pred = act && sh.st[s].pred;
                 const uint32_t ma = __ballot_sync(0xffffffffu, act), mp = __ballot_sync(0xffffffffu, pred);
                 const uint32_t below = (1u << threadIdx.x) - 1;
                 if (act) sh.alist[na + __popc(ma & below)] = s;
@@ -708,21 +824,28 @@ __global__ void __launch_bounds__(TD_THREADS, 1) tdt_persist(TdtArgs a, TdtPersi
             }
             const size_t top = static_cast<size_t>(p.L - 1) * S;
             ps_product<RM>(p.jpred, p.jpreds, p.jpredb, J, P, a.qh + top * P, a.dh + top, sh.plist, sh.np, a.gpn, J,
-                           sh);
+                           nullptr, 0, 0, sh);
             if (!grid_barrier(p, epoch)) return;
         }
-        // the joint's input of every running segment (a segment whose
-        // prediction steps is running)
+        // the joint's input of every running segment; then no prediction is fresh
         for (uint32_t i = blockIdx.x; i < sh.na; i += gridDim.x) {
-            joint_in_seg<RM>(a, sh.alist[i], reinterpret_cast<float*>(sh.base), red);
+            ps_joint<RM>(a, sh.alist[i], sh.st[sh.alist[i]], reinterpret_cast<float*>(sh.base), red);
             __syncthreads();
         }
+        __syncthreads();
+        for (uint32_t i = threadIdx.x; i < sh.np; i += blockDim.x) sh.st[sh.plist[i]].pred = 0;
         if (!grid_barrier(p, epoch)) return;
-        ps_product<RM>(p.jout, p.jouts, p.joutb, a.nout, J, a.qz, a.dz, sh.alist, sh.na, a.logits, a.nout, sh);
-        if (!grid_barrier(p, epoch)) return;
-        for (uint32_t i = blockIdx.x; i < sh.na; i += gridDim.x) step_seg(a, sh.alist[i]);
+        // the logits of every running segment, reduced to the keys of its step
+        ps_product<RM>(p.jout, p.jouts, p.joutb, a.nout, J, a.qz, a.dz, sh.alist, sh.na, nullptr, 0,
+                       p.keys + (round & 1) * 2 * S, a.V, a.n_dur, sh);
         if (!grid_barrier(p, epoch)) return;
     }
+    // the states for the host: each segment's by its owner
+    __syncthreads();
+    for (uint32_t s = blockIdx.x; s < S; s += gridDim.x)
+        for (uint32_t i = threadIdx.x; i < sizeof(TdtSeg) / 4; i += blockDim.x)
+            reinterpret_cast<uint32_t*>(a.seg)[s * (sizeof(TdtSeg) / 4) + i] =
+                reinterpret_cast<const uint32_t*>(sh.st + s)[i];
 }
 
 template <int RM>
@@ -763,10 +886,11 @@ size_t tdt_persist_smem(const TdtArgs& a, size_t smem_max) {
     const size_t S = a.S, Spad = (S + 7) & ~size_t(7), KP = ps_pitch(a.P), KJ = ps_pitch(a.J);
     // gates: inputs and last h, the job's rows of wx and wh, the gates, two scale vectors, the job's vectors
     size_t need = 2 * Spad * KP + 2 * PS_ROWS * KP + 4 * PS_ROWS * Spad + 8 * Spad + 12 * PS_ROWS;
-    // jpred, jout: inputs, two jobs' rows, the scales, the jobs' vectors
-    need = std::max(need, Spad * std::max(KP, KJ) + 2 * PS_ROWS * std::max(KP, KJ) + 4 * Spad + 16 * PS_ROWS);
+    // jpred, jout: inputs, two jobs' rows, the scales, the jobs' vectors, the columns' keys
+    need = std::max(need, Spad * std::max(KP, KJ) + 2 * PS_ROWS * std::max(KP, KJ) + 4 * Spad + 16 * PS_ROWS +
+                              16 * Spad);
     need = std::max(need, 4 * static_cast<size_t>(std::max(a.P, a.J)));  // quantized rows
-    need += (8 * S + 15) & ~size_t(15);                                  // the round's flags
+    need += (S * (8 + sizeof(TdtSeg)) + 15) & ~size_t(15);               // the lists, the states
     return need <= smem_max ? need : 0;
 }
 
