@@ -674,6 +674,8 @@ __device__ void ps_product(const int8_t* w, const float* ws, const float* bias, 
                 for (int h = 0; h < 2; h++) {
                     if (h == 1 && sg1 == sg) break;
                     const uint32_t g = h ? sg1 : sg;
+                    // the lane's keys of its two columns (token, duration)
+                    unsigned long long kt[2] = {0ull, 0ull}, kd[2] = {0ull, 0ull};
 #pragma unroll
                     for (int e = 0; e < 4; e++) {
                         const uint32_t lr = 16 * rt + (lane >> 2) + 8 * (e >> 1), r = r0 + lr;
@@ -683,11 +685,29 @@ __device__ void ps_product(const int8_t* w, const float* ws, const float* bias, 
                             if (out) out[list[col] * os + r] = y;
                             if (keys) {
                                 if (r <= V)
-                                    atomicMax(&sk[2 * col], argmax_key(y, r));
+                                    kt[e & 1] = max(kt[e & 1], argmax_key(y, r));
                                 else if (r <= V + n_dur)
-                                    atomicMax(&sk[2 * col + 1], argmax_key(y, r - V - 1));
+                                    kd[e & 1] = max(kd[e & 1], argmax_key(y, r - V - 1));
                             }
                         }
+                    }
+                    if (keys) {
+                        // the 8 lanes of a column (lane / 4 = the rows) reduced
+                        // by shuffles, then one shared atomic a column and key
+#pragma unroll
+                        for (int o = 4; o <= 16; o <<= 1)
+#pragma unroll
+                            for (int x = 0; x < 2; x++) {
+                                kt[x] = max(kt[x], __shfl_xor_sync(0xffffffffu, kt[x], o));
+                                kd[x] = max(kd[x], __shfl_xor_sync(0xffffffffu, kd[x], o));
+                            }
+                        if (lane < 4)
+#pragma unroll
+                            for (int x = 0; x < 2; x++) {
+                                const uint32_t col = 8 * g + 2 * lane + x;
+                                if (kt[x]) atomicMax(&sk[2 * col], kt[x]);
+                                if (kd[x]) atomicMax(&sk[2 * col + 1], kd[x]);
+                            }
                     }
                 }
             }
