@@ -781,6 +781,7 @@ int tdt_search_dev(cudaStream_t caller, const pkb_tdt_model* m, const float* f, 
     // the rounds' launches below.
     const size_t psmem = L <= TDT_MAX_L && max_rounds < (1ull << 31) ? tdt_persist_smem(a, attention_smem_max()) : 0;
     const int pgrid = psmem ? tdt_persist_grid(a, rmode, dev->sms, psmem) : 0;
+    bool searched = false;
     if (pgrid > 0) {
         TdtPersist pp = {};
         pp.L = L;
@@ -804,7 +805,17 @@ int tdt_search_dev(cudaStream_t caller, const pkb_tdt_model* m, const float* f, 
         pp.timeout = wait_limit();
         pp.max_rounds = static_cast<uint32_t>(max_rounds);
         PKB_CUDA(cudaMemsetAsync(w + o.bar, 0, 8, st), "cudaMemsetAsync");
-        PKB_CUDA(launch_tdt_persist(a, pp, rmode, pgrid, psmem, st), "tdt launch");
+        const cudaError_t le = launch_tdt_persist(a, pp, rmode, pgrid, psmem, st);
+        if (le == cudaErrorCooperativeLaunchTooLarge || le == cudaErrorNotSupported) {
+            // the grid cannot be resident at once here (another context's
+            // work, a restricted device): the rounds' launches instead
+            cudaGetLastError();
+        } else {
+            PKB_CUDA(le, "tdt launch");
+            searched = true;
+        }
+    }
+    if (searched) {
         g_launches.fetch_add(1, std::memory_order_relaxed);
         uint32_t word = 0;
         PKB_CUDA(cudaMemcpyAsync(&word, dev->err, sizeof word, cudaMemcpyDeviceToHost, st), "download");
