@@ -3,7 +3,7 @@
 // takes one joint step at its own frame, and the segments that emitted a
 // token step their prediction network before the next round. Two forms:
 // tdt_persist, the whole search as one cooperative launch (below, where the
-// batch's inputs fit a CTA's shared memory), and rounds of launches, whose
+// model's rows fit a CTA's shared memory), and rounds of launches, whose
 // int8 products (the LSTM layers' wx and wh, jpred, jout) are the product
 // kernel (pkb_gemm.cu) with the batch's segments as its columns and whose
 // float steps around them are these kernels:
@@ -349,6 +349,7 @@ __global__ void __launch_bounds__(TD_THREADS) tdt_step(TdtArgs a) { step_seg(a, 
 // the abort flag, and every CTA returns at its next barrier.
 
 constexpr uint32_t PS_ROWS = 32;  // weight rows a job: two MMA tiles of 16
+constexpr uint32_t PS_COLS = 64;  // segments a chunk of a product's columns: 8 MMA groups of 8
 
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const unsigned* p) {
     uint32_t v;
@@ -510,42 +511,34 @@ struct PsShared {
 };
 
 // Layer l's gates and cells for the segments whose prediction steps, as
-// the columns of its products (column c: segment plist[c]). Layer 0's
-// input is the embedding of the segment's label, quantized a row a block
-// once a call.
+// the columns of its products (column c: segment plist[c]), PS_COLS
+// columns at a time (the job's weight rows staged once, each chunk's
+// inputs then), so that shared memory does not grow with the batch. Layer
+// 0's input is the embedding of the segment's label, quantized a row a
+// block once a call.
 template <int RM>
 __device__ void ps_gates(const TdtArgs& a, const TdtPersist& p, uint32_t l, const PsShared& sh) {
-    const uint32_t S = a.S, P = a.P, n = sh.np, npad = (n + 7) & ~7u, KP = ps_pitch(P), njobs = P / 8;
-    if (blockIdx.x >= njobs) return;  // the CTA's uniform choice
-    int8_t* x0 = reinterpret_cast<int8_t*>(sh.base);  // [npad][KP] the layer's input
-    int8_t* x1 = x0 + npad * KP;                       // [npad][KP] its h of the last step
-    int8_t* wxs = x1 + npad * KP;                      // [32][KP] the job's rows of wx
+    const uint32_t S = a.S, P = a.P, n = sh.np, KP = ps_pitch(P), njobs = P / 8;
+    if (blockIdx.x >= njobs || !n) return;  // the CTA's uniform choice
+    int8_t* x0 = reinterpret_cast<int8_t*>(sh.base);  // [PS_COLS][KP] the chunk's inputs
+    int8_t* x1 = x0 + PS_COLS * KP;                    // [PS_COLS][KP] their h of the last step
+    int8_t* wxs = x1 + PS_COLS * KP;                   // [32][KP] the job's rows of wx
     int8_t* whs = wxs + PS_ROWS * KP;                  // [32][KP] of wh
-    float* gsm = reinterpret_cast<float*>(whs + PS_ROWS * KP);  // [32][npad] the gates
-    float* d0 = gsm + PS_ROWS * npad;                  // [npad] the inputs' scales
-    float* d1 = d0 + npad;                             // [npad] the last h's
-    float* vs = d1 + npad;                             // [3][32] the job's wxs, whs, lb
-    const uint32_t* pl = sh.plist;
+    float* gsm = reinterpret_cast<float*>(whs + PS_ROWS * KP);  // [32][PS_COLS] the gates
+    float* d0 = gsm + PS_ROWS * PS_COLS;               // [PS_COLS] the inputs' scales
+    float* d1 = d0 + PS_COLS;                          // [PS_COLS] the last h's
+    float* vs = d1 + PS_COLS;                          // [3][32] the job's wxs, whs, lb
     const TdtSeg* st = sh.st;
-    if (l == 0) {
-        stage_inputs(x0, [&](uint32_t c) { return a.qembed + static_cast<size_t>(st[pl[c]].label) * P; }, n, npad, P);
-        stage_scales(d0, [&](uint32_t c) { return a.dembed + st[pl[c]].label; }, n);
-    } else {
-        const int8_t* qin = a.qh + static_cast<size_t>(l - 1) * S * P;
-        const float* din = a.dh + static_cast<size_t>(l - 1) * S;
-        stage_inputs(x0, [&](uint32_t c) { return qin + static_cast<size_t>(pl[c]) * P; }, n, npad, P);
-        stage_scales(d0, [&](uint32_t c) { return din + pl[c]; }, n);
-    }
+    const int8_t* qin = l ? a.qh + static_cast<size_t>(l - 1) * S * P : nullptr;
+    const float* din = l ? a.dh + static_cast<size_t>(l - 1) * S : nullptr;
     const int8_t* qhl = a.qh + static_cast<size_t>(l) * S * P;
     const float* dhl = a.dh + static_cast<size_t>(l) * S;
-    stage_inputs(x1, [&](uint32_t c) { return qhl + static_cast<size_t>(pl[c]) * P; }, n, npad, P);
-    stage_scales(d1, [&](uint32_t c) { return dhl + pl[c]; }, n);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, rt = warp & 1;
     for (uint32_t job = blockIdx.x; job < njobs; job += gridDim.x) {
         const uint32_t j0 = 8 * job;
         // job row lr: gate lr / 8 of unit j0 + lr % 8
         auto row = [=](uint32_t lr) { return (lr >> 3) * P + j0 + (lr & 7); };
-        if (job != blockIdx.x) __syncthreads();  // the last job's rows and gates are done with
+        __syncthreads();  // the last job's rows and chunk are done with
         stage_weights(wxs, p.wx[l], P, 4 * P, row);
         stage_weights(whs, p.wh[l], P, 4 * P, row);
         if (threadIdx.x < PS_ROWS) {
@@ -554,47 +547,63 @@ __device__ void ps_gates(const TdtArgs& a, const TdtPersist& p, uint32_t l, cons
             vs[PS_ROWS + threadIdx.x] = __ldg(p.whs[l] + r);
             vs[2 * PS_ROWS + threadIdx.x] = __ldg(p.lb[l] + r);
         }
-        // cell i (below) is unit j0 + i % 8 of column i / 8; the old c of
-        // this thread's first two, loaded while the copies land
-        auto cell_at = [&](uint32_t i) { return (static_cast<size_t>(l) * S + pl[i >> 3]) * P + j0 + (i & 7); };
-        float cpre0 = 0.0f, cpre1 = 0.0f;
-        if (threadIdx.x < 8 * n) cpre0 = __ldcg(a.c + cell_at(threadIdx.x));
-        if (threadIdx.x + blockDim.x < 8 * n) cpre1 = __ldcg(a.c + cell_at(threadIdx.x + blockDim.x));
-        staged();
-        // a warp: one row tile, column groups sg, sg + 4, sg + 8, ...
-        for (uint32_t sg = warp >> 1; sg < npad / 8; sg += 8) {
-            const uint32_t sg1 = sg + 4 < npad / 8 ? sg + 4 : sg;
-            int c[4][4];
-            mma_rows<4>(c, {wxs, whs, wxs, whs}, {x0, x1, x0, x1}, {sg, sg, sg1, sg1}, rt, P);
+        for (uint32_t c0 = 0; c0 < n; c0 += PS_COLS) {
+            const uint32_t* pl = sh.plist + c0;
+            const uint32_t nc = n - c0 < PS_COLS ? n - c0 : PS_COLS, npad = (nc + 7) & ~7u;
+            if (c0) __syncthreads();  // the last chunk's inputs and gates are done with
+            if (l == 0) {
+                stage_inputs(x0, [&](uint32_t c) { return a.qembed + static_cast<size_t>(st[pl[c]].label) * P; }, nc,
+                             npad, P);
+                stage_scales(d0, [&](uint32_t c) { return a.dembed + st[pl[c]].label; }, nc);
+            } else {
+                stage_inputs(x0, [&](uint32_t c) { return qin + static_cast<size_t>(pl[c]) * P; }, nc, npad, P);
+                stage_scales(d0, [&](uint32_t c) { return din + pl[c]; }, nc);
+            }
+            stage_inputs(x1, [&](uint32_t c) { return qhl + static_cast<size_t>(pl[c]) * P; }, nc, npad, P);
+            stage_scales(d1, [&](uint32_t c) { return dhl + pl[c]; }, nc);
+            // cell i (below) is unit j0 + i % 8 of column i / 8; the old c of
+            // this thread's first two, loaded while the copies land
+            auto cell_at = [&](uint32_t i) { return (static_cast<size_t>(l) * S + pl[i >> 3]) * P + j0 + (i & 7); };
+            float cpre0 = 0.0f, cpre1 = 0.0f;
+            if (threadIdx.x < 8 * nc) cpre0 = __ldcg(a.c + cell_at(threadIdx.x));
+            if (threadIdx.x + blockDim.x < 8 * nc) cpre1 = __ldcg(a.c + cell_at(threadIdx.x + blockDim.x));
+            staged();
+            // a warp: one row tile, column groups sg and sg + 4
+            const uint32_t sg = warp >> 1;
+            if (sg < npad / 8) {
+                const uint32_t sg1 = sg + 4 < npad / 8 ? sg + 4 : sg;
+                int c[4][4];
+                mma_rows<4>(c, {wxs, whs, wxs, whs}, {x0, x1, x0, x1}, {sg, sg, sg1, sg1}, rt, P);
 #pragma unroll
-            for (int h = 0; h < 2; h++) {
-                if (h == 1 && sg1 == sg) break;
-                const uint32_t g = h ? sg1 : sg;
+                for (int h = 0; h < 2; h++) {
+                    if (h == 1 && sg1 == sg) break;
+                    const uint32_t g = h ? sg1 : sg;
 #pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const uint32_t lr = 16 * rt + (lane >> 2) + 8 * (e >> 1), col = 8 * g + 2 * (lane & 3) + (e & 1);
-                    if (col < n) {
-                        // gates = wx x + lb, then + wh h (the reference's two products, the second added)
-                        const float gx = one_block<RM>(c[2 * h][e], d0[col], vs[lr], true, vs[2 * PS_ROWS + lr]);
-                        const float gh = one_block<RM>(c[2 * h + 1][e], d1[col], vs[PS_ROWS + lr], false, 0.0f);
-                        gsm[lr * npad + col] = add_r<RM>(gx, gh);
+                    for (int e = 0; e < 4; e++) {
+                        const uint32_t lr = 16 * rt + (lane >> 2) + 8 * (e >> 1), col = 8 * g + 2 * (lane & 3) + (e & 1);
+                        if (col < nc) {
+                            // gates = wx x + lb, then + wh h (the reference's two products, the second added)
+                            const float gx = one_block<RM>(c[2 * h][e], d0[col], vs[lr], true, vs[2 * PS_ROWS + lr]);
+                            const float gh = one_block<RM>(c[2 * h + 1][e], d1[col], vs[PS_ROWS + lr], false, 0.0f);
+                            gsm[lr * PS_COLS + col] = add_r<RM>(gx, gh);
+                        }
                     }
                 }
             }
-        }
-        __syncthreads();
-        // k_lstm's cell for units j0..j0+7
-        for (uint32_t i = threadIdx.x, q = 0; i < 8 * n; i += blockDim.x, q++) {
-            const uint32_t u = i & 7, col = i >> 3;
-            const size_t at = cell_at(i);
-            const float cold = q == 0 ? cpre0 : q == 1 ? cpre1 : __ldcg(a.c + at);
-            const float ig = pk_sigmoid<RM>(gsm[u * npad + col]);
-            const float fg = pk_sigmoid<RM>(gsm[(8 + u) * npad + col]);
-            const float ug = pk_tanh<RM>(gsm[(16 + u) * npad + col]);
-            const float og = pk_sigmoid<RM>(gsm[(24 + u) * npad + col]);
-            const float cj = add_r<RM>(mul_r<RM>(fg, cold), mul_r<RM>(ig, ug));
-            a.c[at] = cj;
-            a.h[at] = mul_r<RM>(og, pk_tanh<RM>(cj));
+            __syncthreads();
+            // k_lstm's cell for units j0..j0+7 of the chunk's columns
+            for (uint32_t i = threadIdx.x, q = 0; i < 8 * nc; i += blockDim.x, q++) {
+                const uint32_t u = i & 7, col = i >> 3;
+                const size_t at = cell_at(i);
+                const float cold = q == 0 ? cpre0 : q == 1 ? cpre1 : __ldcg(a.c + at);
+                const float ig = pk_sigmoid<RM>(gsm[u * PS_COLS + col]);
+                const float fg = pk_sigmoid<RM>(gsm[(8 + u) * PS_COLS + col]);
+                const float ug = pk_tanh<RM>(gsm[(16 + u) * PS_COLS + col]);
+                const float og = pk_sigmoid<RM>(gsm[(24 + u) * PS_COLS + col]);
+                const float cj = add_r<RM>(mul_r<RM>(fg, cold), mul_r<RM>(ig, ug));
+                a.c[at] = cj;
+                a.h[at] = mul_r<RM>(og, pk_tanh<RM>(cj));
+            }
         }
     }
 }
@@ -630,28 +639,24 @@ __device__ __forceinline__ uint32_t key_index(unsigned long long k) {
 // column c to out[list[c] * os + r] where out is given, and, where keys
 // is, into each column's two keys (keys[2 list[c]]: the first largest
 // token logit, rows 0..V; keys[2 list[c] + 1]: the first largest duration
-// logit, rows V+1..V+n_dur, its index counted from V+1), the CTA's columns
-// reduced in shared memory first. Rows past `rows` are skipped. A CTA
-// stages the inputs and the weights of two of its jobs at once.
+// logit, rows V+1..V+n_dur, its index counted from V+1), reduced across a
+// warp and the CTA first. Rows past `rows` are skipped. A CTA stages the
+// weights of two of its jobs at once and the columns PS_COLS at a time.
 template <int RM>
 __device__ void ps_product(const int8_t* w, const float* ws, const float* bias, uint32_t rows, uint32_t K,
                            const int8_t* x, const float* d, const uint32_t* list, uint32_t n, float* out, size_t os,
                            unsigned long long* keys, uint32_t V, uint32_t n_dur, const PsShared& sh) {
-    const uint32_t npad = (n + 7) & ~7u, KP = ps_pitch(K), njobs = (rows + PS_ROWS - 1) / PS_ROWS;
+    const uint32_t KP = ps_pitch(K), njobs = (rows + PS_ROWS - 1) / PS_ROWS;
     if (blockIdx.x >= njobs || !n) return;  // uniform
-    int8_t* xs = reinterpret_cast<int8_t*>(sh.base);  // [npad][KP]
-    int8_t* wsm = xs + npad * KP;                     // [2][32][KP]
-    float* ds = reinterpret_cast<float*>(wsm + 2 * PS_ROWS * KP);  // [npad]
-    float* vs = ds + npad;                            // [2][2][32] row scales, biases
-    unsigned long long* sk = reinterpret_cast<unsigned long long*>(vs + 4 * PS_ROWS);  // [npad][2] the keys
-    stage_inputs(xs, [&](uint32_t c) { return x + static_cast<size_t>(list[c]) * K; }, n, npad, K);
-    stage_scales(ds, [&](uint32_t c) { return d + list[c]; }, n);
-    if (keys)
-        for (uint32_t i = threadIdx.x; i < 2 * npad; i += blockDim.x) sk[i] = 0ull;
+    int8_t* xs = reinterpret_cast<int8_t*>(sh.base);  // [PS_COLS][KP] the chunk's inputs
+    int8_t* wsm = xs + PS_COLS * KP;                  // [2][32][KP]
+    float* ds = reinterpret_cast<float*>(wsm + 2 * PS_ROWS * KP);  // [PS_COLS]
+    float* vs = ds + PS_COLS;                         // [2][2][32] row scales, biases
+    unsigned long long* sk = reinterpret_cast<unsigned long long*>(vs + 4 * PS_ROWS);  // [PS_COLS][2] the keys
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, rt = warp & 1;
     for (uint32_t job = blockIdx.x; job < njobs; job += 2 * gridDim.x) {
         const uint32_t job2 = job + gridDim.x, nj = job2 < njobs ? 2 : 1;
-        if (job != blockIdx.x) __syncthreads();
+        __syncthreads();  // the last jobs' rows and chunk are done with
         for (uint32_t k = 0; k < nj; k++) {
             const uint32_t r0 = PS_ROWS * (k ? job2 : job);
             stage_weights(wsm + k * PS_ROWS * KP, w, K, rows, [=](uint32_t lr) { return r0 + lr; });
@@ -661,12 +666,21 @@ __device__ void ps_product(const int8_t* w, const float* ws, const float* bias, 
                 vs[k * 2 * PS_ROWS + PS_ROWS + threadIdx.x] = r < rows && bias ? __ldg(bias + r) : 0.0f;
             }
         }
-        staged();
-        for (uint32_t k = 0; k < nj; k++) {
-            const uint32_t r0 = PS_ROWS * (k ? job2 : job);
-            const int8_t* W = wsm + k * PS_ROWS * KP;
-            const float* v = vs + k * 2 * PS_ROWS;
-            for (uint32_t sg = warp >> 1; sg < npad / 8; sg += 8) {
+        for (uint32_t c0 = 0; c0 < n; c0 += PS_COLS) {
+            const uint32_t* cl = list + c0;
+            const uint32_t nc = n - c0 < PS_COLS ? n - c0 : PS_COLS, npad = (nc + 7) & ~7u;
+            if (c0) __syncthreads();  // the last chunk's inputs and keys are done with
+            stage_inputs(xs, [&](uint32_t c) { return x + static_cast<size_t>(cl[c]) * K; }, nc, npad, K);
+            stage_scales(ds, [&](uint32_t c) { return d + cl[c]; }, nc);
+            if (keys)
+                for (uint32_t i = threadIdx.x; i < 2 * npad; i += blockDim.x) sk[i] = 0ull;
+            staged();
+            for (uint32_t k = 0; k < nj; k++) {
+                const uint32_t r0 = PS_ROWS * (k ? job2 : job);
+                const int8_t* W = wsm + k * PS_ROWS * KP;
+                const float* v = vs + k * 2 * PS_ROWS;
+                const uint32_t sg = warp >> 1;
+                if (sg >= npad / 8) continue;  // warp-uniform
                 const uint32_t sg1 = sg + 4 < npad / 8 ? sg + 4 : sg;
                 int c[2][4];
                 mma_rows<2>(c, {W, W}, {xs, xs}, {sg, sg1}, rt, K);
@@ -680,9 +694,9 @@ __device__ void ps_product(const int8_t* w, const float* ws, const float* bias, 
                     for (int e = 0; e < 4; e++) {
                         const uint32_t lr = 16 * rt + (lane >> 2) + 8 * (e >> 1), r = r0 + lr;
                         const uint32_t col = 8 * g + 2 * (lane & 3) + (e & 1);
-                        if (r < rows && col < n) {
+                        if (r < rows && col < nc) {
                             const float y = one_block<RM>(c[h][e], ds[col], v[lr], bias != nullptr, v[PS_ROWS + lr]);
-                            if (out) out[list[col] * os + r] = y;
+                            if (out) out[cl[col] * os + r] = y;
                             if (keys) {
                                 if (r <= V)
                                     kt[e & 1] = max(kt[e & 1], argmax_key(y, r));
@@ -697,26 +711,26 @@ __device__ void ps_product(const int8_t* w, const float* ws, const float* bias, 
 #pragma unroll
                         for (int o = 4; o <= 16; o <<= 1)
 #pragma unroll
-                            for (int x = 0; x < 2; x++) {
-                                kt[x] = max(kt[x], __shfl_xor_sync(0xffffffffu, kt[x], o));
-                                kd[x] = max(kd[x], __shfl_xor_sync(0xffffffffu, kd[x], o));
+                            for (int xx = 0; xx < 2; xx++) {
+                                kt[xx] = max(kt[xx], __shfl_xor_sync(0xffffffffu, kt[xx], o));
+                                kd[xx] = max(kd[xx], __shfl_xor_sync(0xffffffffu, kd[xx], o));
                             }
                         if (lane < 4)
 #pragma unroll
-                            for (int x = 0; x < 2; x++) {
-                                const uint32_t col = 8 * g + 2 * lane + x;
-                                if (kt[x]) atomicMax(&sk[2 * col], kt[x]);
-                                if (kd[x]) atomicMax(&sk[2 * col + 1], kd[x]);
+                            for (int xx = 0; xx < 2; xx++) {
+                                const uint32_t col = 8 * g + 2 * lane + xx;
+                                if (kt[xx]) atomicMax(&sk[2 * col], kt[xx]);
+                                if (kd[xx]) atomicMax(&sk[2 * col + 1], kd[xx]);
                             }
                     }
                 }
             }
+            if (keys) {
+                __syncthreads();
+                for (uint32_t i = threadIdx.x; i < 2 * nc; i += blockDim.x)
+                    if (sk[i]) atomicMax(keys + 2 * cl[i >> 1] + (i & 1), sk[i]);
+            }
         }
-    }
-    if (keys) {
-        __syncthreads();
-        for (uint32_t i = threadIdx.x; i < 2 * n; i += blockDim.x)
-            if (sk[i]) atomicMax(keys + 2 * list[i >> 1] + (i & 1), sk[i]);
     }
 }
 
@@ -903,12 +917,11 @@ cudaError_t launch_tdt(const TdtArgs& a, int phase, uint32_t l, int rmode, cudaS
 size_t tdt_seg_bytes() { return sizeof(TdtSeg); }
 
 size_t tdt_persist_smem(const TdtArgs& a, size_t smem_max) {
-    const size_t S = a.S, Spad = (S + 7) & ~size_t(7), KP = ps_pitch(a.P), KJ = ps_pitch(a.J);
-    // gates: inputs and last h, the job's rows of wx and wh, the gates, two scale vectors, the job's vectors
-    size_t need = 2 * Spad * KP + 2 * PS_ROWS * KP + 4 * PS_ROWS * Spad + 8 * Spad + 12 * PS_ROWS;
-    // jpred, jout: inputs, two jobs' rows, the scales, the jobs' vectors, the columns' keys
-    need = std::max(need, Spad * std::max(KP, KJ) + 2 * PS_ROWS * std::max(KP, KJ) + 4 * Spad + 16 * PS_ROWS +
-                              16 * Spad);
+    const size_t S = a.S, C = PS_COLS, KP = ps_pitch(a.P), KJ = ps_pitch(a.J);
+    // gates: a chunk's inputs and last h, the job's rows of wx and wh, the gates, two scale vectors, the job's vectors
+    size_t need = 2 * C * KP + 2 * PS_ROWS * KP + 4 * PS_ROWS * C + 8 * C + 12 * PS_ROWS;
+    // jpred, jout: a chunk's inputs, two jobs' rows, the scales, the jobs' vectors, the columns' keys
+    need = std::max(need, C * std::max(KP, KJ) + 2 * PS_ROWS * std::max(KP, KJ) + 4 * C + 16 * PS_ROWS + 16 * C);
     need = std::max(need, 4 * static_cast<size_t>(std::max(a.P, a.J)));  // quantized rows
     need += (S * (8 + sizeof(TdtSeg)) + 15) & ~size_t(15);               // the lists, the states
     return need <= smem_max ? need : 0;

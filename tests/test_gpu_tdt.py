@@ -12,9 +12,10 @@ in lockstep, against the reference's own tokens and the oracle.
 * The token capacity: a segment that finds more tokens than the room given
   makes the call fail.
 * Both ways the search runs: one cooperative launch for the whole search
-  where a batch's shapes fit its shared memory (the cases above), and the
-  rounds' launches replayed as a CUDA graph where they do not (a batch of
-  200 segments at the model's shapes).
+  (the cases above, and a batch of 200 segments, its products' columns
+  taken 64 at a time), and the rounds' launches replayed as a CUDA graph
+  where the model's shapes do not fit the one launch's shared memory
+  (pred_hidden 2048).
 """
 import os
 
@@ -150,15 +151,35 @@ def test_the_oracles_tokens_at_the_models_shapes(pkb, cuda_device, rmode):
     assert total > 50  # the prediction network stepped on real tokens
 
 
-def test_a_batch_past_one_launchs_shared_memory_takes_the_rounds_launches(pkb, cuda_device):
-    """200 segments at the model's shapes: the persistent search's staging of
-    every segment's input would need more shared memory than a CTA has, so
-    the rounds run as launches; every segment's tokens are still the
-    oracle's."""
+def test_a_batch_of_200_segments_in_one_launch(pkb, cuda_device):
+    """200 segments at the model's shapes: the one launch takes a product's
+    columns 64 segments at a time, so its shared memory does not grow with
+    the batch; every segment's tokens are still the oracle's."""
     m = synthetic_model()
     t, keep = device_model(pkb, m)
     g = np.random.default_rng(23)
     Ts = [int(x) for x in g.integers(0, 5, 200)]
+    frames = [(g.standard_normal(T * m["J"]) * 2.0).astype(np.float32) for T in Ts]
+    n0 = pkb.launch_count()
+    got = search(pkb, t, frames, cap=64)
+    assert pkb.launch_count() - n0 == 3
+    total = 0
+    for T, f, a in zip(Ts, frames, got):
+        want = O.tdt_search(m, f, T, O.RN)
+        assert a.shape == want.shape and (a == want).all(), T
+        total += len(want)
+    assert total > 20
+
+
+def test_a_prediction_network_past_one_launchs_shared_memory_takes_the_rounds_launches(pkb, cuda_device):
+    """pred_hidden 2048: a job's weight rows and a chunk's inputs would need
+    more shared memory than a CTA has, so the rounds run as launches (the
+    product kernel and the rounds' kernels); every segment's tokens are
+    still the oracle's."""
+    m = synthetic_model(P=2048, V=256, seed=5)
+    t, keep = device_model(pkb, m)
+    g = np.random.default_rng(29)
+    Ts = [1, 3, 4, 2]
     frames = [(g.standard_normal(T * m["J"]) * 2.0).astype(np.float32) for T in Ts]
     n0 = pkb.launch_count()
     got = search(pkb, t, frames, cap=64)
@@ -168,7 +189,7 @@ def test_a_batch_past_one_launchs_shared_memory_takes_the_rounds_launches(pkb, c
         want = O.tdt_search(m, f, T, O.RN)
         assert a.shape == want.shape and (a == want).all(), T
         total += len(want)
-    assert total > 20
+    assert total > 3
 
 
 def test_a_segment_past_its_token_room_fails_the_call(pkb, cuda_device):
